@@ -1,0 +1,291 @@
+"""Headline benchmark: JustRL lock-step GRPO step, per-GPU weak scaling.
+
+Per rank (one process per GPU, ``torchrun`` for N > 1):
+  R1-Distill-Qwen-1.5B architecture, bf16, random init; 8 prompts x group 8 =
+  64 samples per GPU (64 prompts x 8 over 8 GPUs); prompt ids uniform random,
+  length U[64, 512]; response lengths log-normal (median 2048, sigma 0.6, cap
+  8192), generated to exactly that length (ignore EOS); binary rule reward
+  (parity of the response id sum, p ~ 0.5); GRPO advantages; packed
+  micro-batches; behaviour log-prob recompute; PPO mini-batches of 8 samples
+  (the recipe's ``mini_batch_size``); DDP gradient all-reduce; AdamW; weight
+  sync trainer -> rollout engine every step.
+
+Timing: W untimed warm-up steps, then K timed steps bracketed by a barrier and
+``torch.cuda.synchronize()``; CUDA events on the launching stream; max over
+ranks.  Weights (3.6 GB) and KV pages far exceed the 126 MB L2, so no flush is
+needed between steps.  SM clocks and throttle reasons are sampled with
+nvidia-smi during the timed region.
+
+``--impl reference`` runs the unmodified reference from ``baseline/_ref``
+through its own public API, or prints why it cannot.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import random
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "RL step time & trained tokens/s (JustRL 1.5B, 8 GPU); weight-sync latency"
+BASELINE_VALUE = None  # the reference publishes no number
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "torch"])
+    p.add_argument("--prompts-per-gpu", type=int, default=8)
+    p.add_argument("--group", type=int, default=8)
+    p.add_argument("--median-resp", type=int, default=2048)
+    p.add_argument("--resp-cap", type=int, default=8192)
+    p.add_argument("--sigma", type=float, default=0.6)
+    p.add_argument("--model", default="qwen2_5_math:R1-Distill-1.5B")
+    p.add_argument("--max-tokens-per-micro", type=int, default=32768)
+    p.add_argument("--no-clocks", action="store_true")
+    return p.parse_args()
+
+
+def reference_arm(args):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    why = None
+    if not os.path.isdir(ref):
+        why = "baseline/_ref not installed (reference install failed offline: see DESIGN.md)"
+    else:
+        sys.path.insert(0, ref)
+        try:
+            import sglang  # noqa: F401
+        except Exception:
+            why = ("reference needs SGLang 0.5.18 + torch 2.13 + TransferQueue/tensordict, none installable offline "
+                   "in this image (see DESIGN.md)")
+    if why is None:
+        why = "reference path not runnable on this box"
+    print(json.dumps({"impl": "reference", "unavailable": why}))
+
+
+class ClockSampler:
+    def __init__(self, enabled: bool, index: int):
+        self.enabled = enabled
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+        self.index = index
+
+    def __enter__(self):
+        if self.enabled:
+            try:
+                os.makedirs(os.path.dirname(self.path), exist_ok=True)
+                self.f = open(self.path, "w")
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.index),
+                     "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                     "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                     "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                     "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+            except Exception:
+                self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return None
+        try:
+            rows = [l.strip().split(",") for l in open(self.path) if l.strip()]
+        except Exception:
+            return None
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_workload(args, rank: int, step: int):
+    rng = random.Random(1234 + 7919 * rank + 104729 * step)
+    prompts = [[rng.randrange(151936) for _ in range(rng.randint(64, 512))] for _ in range(args.prompts_per_gpu)]
+    mu = math.log(args.median_resp)
+    lens = [max(1, min(args.resp_cap, int(round(math.exp(rng.gauss(mu, args.sigma))))))
+            for _ in range(args.prompts_per_gpu * args.group)]
+    return prompts, lens
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=600))
+        group = dist.group.WORLD
+
+    from meshy_b200.config import TrainerConfig, TrainerParamsConfig
+    from meshy_b200.ops import functional as Fx
+    from meshy_b200.rl import ColocatedGRPO
+
+    if args.impl == "torch":
+        Fx.set_torch_baseline(True)
+    name, flavor = args.model.split(":")
+    max_len = 512 + args.resp_cap + 64
+    tc = TrainerConfig(model_name=name, model_flavor=flavor, seq_len=max(8192, 1 << math.ceil(math.log2(max_len))),
+                       lr=1e-6, weight_decay=0.1, max_norm=1.0, dtype="bfloat16", dp_replicate_degree=world,
+                       steps=1000)
+    tp = TrainerParamsConfig(mini_batch_size=8, batch_layout="packed", max_tokens_per_micro=args.max_tokens_per_micro,
+                             ppo_clip_eps_low=0.2, ppo_clip_eps_high=0.28, old_logprobs_source="train",
+                             log_entropy=True)
+    rl = ColocatedGRPO(tc, tp, device=dev, group_size=args.group, dp_group=group, seed=0,
+                       engine_kwargs=dict(max_running=args.prompts_per_gpu * args.group, page_size=64,
+                                          max_seq_len=max_len, mem_fraction=0.25, sync_every=16))
+    try:
+        C = __import__("meshy_b200._C", fromlist=["_C"])
+    except Exception:
+        C = None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for w in range(args.warmup):
+        prompts, lens = make_workload(args, rank, w)
+        rl.step(prompts, lens)
+    barrier()
+    launches0 = C.launch_count() if (C is not None and hasattr(C, "launch_count")) else None
+    graph0 = rl.engine.stats.get("graph_kernels", 0)
+    tokens = 0
+    resp_tokens = 0
+    sync_ms = []
+    times = []
+    e2e_ms = []
+    h2d = d2h = 0
+    with ClockSampler(not args.no_clocks, local) as clocks:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        barrier()
+        start.record()
+        for s in range(args.steps):
+            prompts, lens = make_workload(args, rank, 100 + s)
+            # end-to-end: prompts arrive as a pinned host tensor; the loss is read back
+            flat = torch.tensor([t for p in prompts for t in p], dtype=torch.int64).pin_memory()
+            h2d += flat.numel() * flat.element_size()
+            t0 = time.perf_counter()
+            dev_prompts = flat.to(dev, non_blocking=True)
+            off = 0
+            plist = []
+            host = dev_prompts.cpu().tolist()
+            for p in prompts:
+                plist.append(host[off:off + len(p)])
+                off += len(p)
+            rep = rl.step(plist, lens)
+            loss = torch.tensor([rep.metrics["pg_loss"]], device=dev).cpu()
+            d2h += 4 + 8 * len(host)
+            e2e_ms.append((time.perf_counter() - t0) * 1e3)
+            tokens += rep.n_tokens
+            resp_tokens += rep.n_response_tokens
+            sync_ms.append(rep.times["weight_sync_ms"])
+            del loss
+        end.record()
+        barrier()
+    ms = start.elapsed_time(end)
+    launches = None
+    if launches0 is not None:
+        launches = C.launch_count() - launches0 + (rl.engine.stats.get("graph_kernels", 0) - graph0)
+
+    from meshy_b200.utils.timer import max_over_ranks
+
+    ms_max = max_over_ranks(ms, group, dev)
+    e2e_max = max_over_ranks(sum(e2e_ms), group, dev)
+    sync_max = max_over_ranks(max(sync_ms), group, dev)
+    tok_all = tokens
+    if world > 1:
+        t = torch.tensor([tokens, resp_tokens], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        tok_all, resp_tokens = int(t[0].item()), int(t[1].item())
+    value = tok_all / (ms_max / 1e3)
+    e2e_value = tok_all / (e2e_max / 1e3)
+    n_params = rl.trainer.model_args.num_params()
+    sync_bytes = rl.trainer.flat.numel * (4 + 2)
+    meas = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    hbm = json.load(open(meas)).get("hbm_gbs", 6650.0) if os.path.exists(meas) else 6650.0
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "trained tokens/s (all GPUs)",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 2),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None if BASELINE_VALUE is None else round(value / BASELINE_VALUE, 4),
+            "dtype": "bf16",
+            "data": "synthetic (random prompt ids, log-normal forced response lengths, random-init weights)",
+            "impl": "torch-baseline" if args.impl == "torch" else "ours",
+            "config": {
+                "model": f"R1-Distill-Qwen-1.5B ({name}:{flavor}, {n_params / 1e9:.3f}B params)",
+                "global_batch": args.prompts_per_gpu * args.group * world,
+                "prompts_x_group": f"{args.prompts_per_gpu * world}x{args.group}",
+                "seq_len": f"prompt U[64,512] + response lognormal(median {args.median_resp}, sigma {args.sigma}, "
+                           f"cap {args.resp_cap})",
+                "parallelism": f"dp{world} colocated (rollout TP1 per GPU)",
+                "mini_batch_size": 8,
+                "max_tokens_per_micro": args.max_tokens_per_micro,
+                "l2": "inputs larger than L2 (3.6 GB bf16 weights per step)",
+                "trained_tokens_per_step": tok_all // args.steps,
+                "response_tokens_per_step": resp_tokens // args.steps,
+            },
+            "weight_sync": {"ms": round(sync_max, 3), "bytes": sync_bytes,
+                            "roofline_ms": round(sync_bytes / (hbm * 1e9) * 1e3, 3),
+                            "frac_of_measured_hbm": round((sync_bytes / (hbm * 1e9) * 1e3) / max(sync_max, 1e-9), 3),
+                            "path": "fp32 master -> bf16 engine buffer, one device cast kernel (colocated)"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "trained tokens/s (all GPUs)",
+                    "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
+            "gpu_launches": launches,
+        }
+        cs = clocks.summary()
+        if cs is not None:
+            line["clocks"] = cs
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

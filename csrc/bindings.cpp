@@ -1,0 +1,444 @@
+// Python bindings of the kernel library (module ``meshy_b200._C``).
+//
+// Every entry point takes preallocated output tensors, checks shapes/dtypes
+// and launches on the current PyTorch CUDA stream, so all of them can be
+// captured in CUDA graphs.  Persistent scratch (split-K workspace and
+// counters, the device error word) is owned here and sized on first use.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <atomic>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "kernels/attention.h"
+#include "kernels/elementwise.h"
+#include "kernels/gemm.h"
+#include "kernels/misc.h"
+
+using torch::Tensor;
+using namespace meshy;
+
+namespace {
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_BF16(t) TORCH_CHECK((t).scalar_type() == at::kBFloat16, #t " must be bfloat16")
+#define CHECK_F32(t) TORCH_CHECK((t).scalar_type() == at::kFloat, #t " must be float32")
+#define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+
+std::atomic<int64_t> g_launches{0};
+// Every entry point counts the kernels it launches (graph replays are counted
+// by the caller from the capture-time count).
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+inline void count(int n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+template <typename T>
+T* ptr(const Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+template <typename T>
+T* optr(const c10::optional<Tensor>& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+struct DeviceScratch {
+  Tensor ws, counters, err;
+};
+std::mutex g_mu;
+DeviceScratch& scratch(int64_t ws_elems, int64_t n_counters) {
+  static DeviceScratch per_dev[64];
+  int dev = at::cuda::current_device();
+  std::lock_guard<std::mutex> g(g_mu);
+  DeviceScratch& s = per_dev[dev];
+  auto opts = torch::TensorOptions().device(torch::kCUDA, dev);
+  if (!s.err.defined()) s.err = torch::zeros({1}, opts.dtype(torch::kInt32));
+  if (!s.ws.defined() || s.ws.numel() < ws_elems) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    MESHY_CUDA_CHECK(cudaStreamIsCapturing(cur_stream(), &cap));
+    TORCH_CHECK(cap == cudaStreamCaptureStatusNone,
+                "split-K workspace must be sized before CUDA graph capture (run the shape once uncaptured)");
+    s.ws = torch::zeros({std::max<int64_t>(ws_elems, 16 << 20)}, opts.dtype(torch::kFloat));
+  }
+  if (!s.counters.defined() || s.counters.numel() < n_counters)
+    s.counters = torch::zeros({std::max<int64_t>(n_counters, 1 << 16)}, opts.dtype(torch::kInt32));
+  return s;
+}
+
+// out[M,N] (=|+=) op(a) · op(b)^T
+void gemm(Tensor a, Tensor b, Tensor out, bool a_mn, bool b_mn, c10::optional<Tensor> bias,
+          c10::optional<Tensor> residual, c10::optional<Tensor> aux, int64_t epi, bool accumulate, int64_t block) {
+  CHECK_CUDA(a);
+  CHECK_BF16(a);
+  CHECK_BF16(b);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm expects 2-D tensors");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm operands must be row-major");
+  const c10::cuda::CUDAGuard guard(a.device());
+  GemmProblem g;
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.lda = a.stride(0);
+  g.ldb = b.stride(0);
+  g.a_mn = a_mn;
+  g.b_mn = b_mn;
+  g.M = a_mn ? a.size(1) : a.size(0);
+  g.K = a_mn ? a.size(0) : a.size(1);
+  g.N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == g.K, "gemm: K mismatch");
+  if (g.M == 0 || g.N == 0) return;
+  if (g.K == 0) {
+    if (!accumulate) out.zero_();
+    return;
+  }
+  g.out = out.data_ptr();
+  g.ldo = out.stride(0);
+  g.out_f32 = out.scalar_type() == at::kFloat;
+  g.epi = (int)epi;
+  if (epi == EPI_STORE && accumulate) {
+    TORCH_CHECK(g.out_f32, "accumulating GEMM needs an fp32 output");
+    g.epi = EPI_ACC_F32;
+  }
+  if (g.epi == EPI_SWIGLU) {
+    TORCH_CHECK(block == 64, "fused SwiGLU epilogue expects interleave block 64");
+    TORCH_CHECK(out.size(1) * 2 == g.N, "swiglu out must be [M, N/2]");
+  } else {
+    TORCH_CHECK(out.size(0) == g.M && out.size(1) == g.N, "gemm: out shape mismatch");
+  }
+  g.bias = optr<bf16>(bias);
+  if (residual.has_value() && residual->defined()) {
+    TORCH_CHECK(residual->stride(1) == 1, "residual must be row-major");
+    g.residual = ptr<bf16>(*residual);
+    g.ldr = residual->stride(0);
+  }
+  if (aux.has_value() && aux->defined()) {
+    g.aux = ptr<bf16>(*aux);
+    g.ld_aux = aux->stride(0);
+  }
+  const int m_tiles = (g.M + 127) / 128;
+  if (g.epi == EPI_STORE && m_tiles <= 4) {
+    int64_t need = (int64_t)g.M * g.N;
+    auto& s = scratch(need, (int64_t)m_tiles * ((g.N + 63) / 64));
+    g.ws = ptr<float>(s.ws);
+    g.ws_cap = s.ws.numel();
+    g.counters = ptr<int>(s.counters);
+    g.counters_cap = s.counters.numel();
+  }
+  g.err = ptr<int>(scratch(0, 0).err);
+  gemm_launch(g, cur_stream());
+  count();
+}
+
+void swiglu_bwd_(Tensor h, Tensor ga, Tensor dh, int64_t block) {
+  CHECK_CONTIG(h);
+  CHECK_CONTIG(ga);
+  const c10::cuda::CUDAGuard guard(h.device());
+  swiglu_bwd(ptr<bf16>(h), ptr<bf16>(ga), ptr<bf16>(dh), h.size(0), (int)ga.size(1), (int)block, cur_stream());
+  count();
+}
+
+void rmsnorm_fwd_(Tensor x, Tensor w, Tensor y, Tensor rstd, double eps) {
+  CHECK_CONTIG(x);
+  CHECK_BF16(x);
+  const c10::cuda::CUDAGuard guard(x.device());
+  rmsnorm_fwd(ptr<bf16>(x), ptr<bf16>(w), ptr<bf16>(y), ptr<float>(rstd), (int)x.size(0), (int)x.size(1), (float)eps,
+              cur_stream());
+  count();
+}
+
+void rmsnorm_bwd_(Tensor gy, Tensor x, Tensor w, Tensor rstd, Tensor gx, Tensor gw) {
+  CHECK_CONTIG(gy);
+  CHECK_F32(gw);
+  const c10::cuda::CUDAGuard guard(x.device());
+  rmsnorm_bwd(ptr<bf16>(gy), ptr<bf16>(x), ptr<bf16>(w), ptr<float>(rstd), ptr<bf16>(gx), ptr<float>(gw),
+              (int)x.size(0), (int)x.size(1), cur_stream());
+  count();
+}
+
+Tensor inv_freq_table(int64_t hd, double theta, const torch::Device& dev) {
+  static std::mutex mu;
+  static std::map<std::tuple<int64_t, double, int>, Tensor> cache;
+  std::lock_guard<std::mutex> g(mu);
+  auto key = std::make_tuple(hd, theta, (int)dev.index());
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  // HF convention: inv_freq = 1 / theta^(arange(0, hd, 2) / hd), fp32
+  auto ar = torch::arange(0, hd, 2, torch::kInt64).to(torch::kFloat) / (float)hd;
+  auto inv = 1.0 / torch::pow(torch::tensor((float)theta), ar);
+  // expand to per-dim table: entry i (i < hd/2) holds inv_freq[i]
+  Tensor t = inv.to(torch::kFloat).to(dev);
+  cache.emplace(key, t);
+  return t;
+}
+
+void qkv_rope_fwd_(Tensor qkv, Tensor pos, c10::optional<Tensor> qn, c10::optional<Tensor> kn, Tensor q, Tensor k,
+                   Tensor v, double theta, double eps) {
+  CHECK_CONTIG(qkv);
+  TORCH_CHECK(pos.scalar_type() == at::kInt, "positions must be int32");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  int T = q.size(0), Hq = q.size(1), hd = q.size(2), Hkv = k.size(1);
+  Tensor inv = inv_freq_table(hd, theta, qkv.device());
+  qkv_rope_fwd(ptr<bf16>(qkv), ptr<int>(pos), optr<bf16>(qn), optr<bf16>(kn), ptr<float>(inv), ptr<bf16>(q), ptr<bf16>(k),
+               ptr<bf16>(v), T, Hq, Hkv, hd, (float)eps, cur_stream());
+  count();
+}
+
+void qkv_rope_bwd_(Tensor qkv, Tensor pos, c10::optional<Tensor> qn, c10::optional<Tensor> kn, Tensor gq, Tensor gk,
+                   Tensor gv, Tensor gqkv, c10::optional<Tensor> gqn, c10::optional<Tensor> gkn, double theta,
+                   double eps) {
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  int T = gq.size(0), Hq = gq.size(1), hd = gq.size(2), Hkv = gk.size(1);
+  Tensor inv = inv_freq_table(hd, theta, qkv.device());
+  qkv_rope_bwd(ptr<bf16>(qkv), ptr<int>(pos), optr<bf16>(qn), optr<bf16>(kn), ptr<float>(inv), ptr<bf16>(gq),
+               ptr<bf16>(gk), ptr<bf16>(gv), ptr<bf16>(gqkv), optr<float>(gqn), optr<float>(gkn), T, Hq, Hkv, hd,
+               (float)eps, cur_stream());
+  count();
+}
+
+void flash_attn_fwd_(Tensor q, Tensor k, Tensor v, Tensor cu, Tensor out, Tensor lse, int64_t max_seqlen,
+                     double scale) {
+  CHECK_CONTIG(q);
+  CHECK_CONTIG(k);
+  CHECK_CONTIG(v);
+  TORCH_CHECK(cu.scalar_type() == at::kInt, "cu_seqlens must be int32");
+  const c10::cuda::CUDAGuard guard(q.device());
+  flash_attn_fwd(ptr<bf16>(q), ptr<bf16>(k), ptr<bf16>(v), ptr<int>(cu), (int)cu.numel() - 1, ptr<bf16>(out),
+                 ptr<float>(lse), (int)q.size(0), (int)max_seqlen, (int)q.size(1), (int)k.size(1), (int)q.size(2),
+                 (float)scale, cur_stream());
+  count();
+}
+
+void flash_attn_bwd_(Tensor q, Tensor k, Tensor v, Tensor cu, Tensor out, Tensor gout, Tensor lse, Tensor gq,
+                     Tensor gk, Tensor gv, int64_t max_seqlen, double scale) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  Tensor dvec = torch::empty({q.size(1), q.size(0)}, q.options().dtype(torch::kFloat));
+  flash_attn_bwd(ptr<bf16>(q), ptr<bf16>(k), ptr<bf16>(v), ptr<int>(cu), (int)cu.numel() - 1, ptr<bf16>(out),
+                 ptr<bf16>(gout), ptr<float>(lse), ptr<float>(dvec), ptr<bf16>(gq), ptr<bf16>(gk), ptr<bf16>(gv),
+                 (int)q.size(0), (int)max_seqlen, (int)q.size(1), (int)k.size(1), (int)q.size(2), (float)scale,
+                 cur_stream());
+  count(3);
+}
+
+constexpr int kLseBN = 256;
+
+// lp = z[label] - lse, lse, entropy — no [T, V] logits in memory
+void lmhead_logprob_fwd(Tensor h, Tensor w, Tensor labels, Tensor lp, Tensor lse, c10::optional<Tensor> ent) {
+  CHECK_CONTIG(h);
+  CHECK_BF16(h);
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int T = h.size(0), V = w.size(0), D = h.size(1);
+  const int n_tiles = (V + kLseBN - 1) / kLseBN;
+  const int chunk = 8192;
+  Tensor part = torch::empty({std::min(T, chunk), n_tiles, 8}, h.options().dtype(torch::kFloat));
+  for (int s = 0; s < T; s += chunk) {
+    int n = std::min(chunk, T - s);
+    GemmProblem g;
+    g.A = h.data_ptr<at::BFloat16>() + (int64_t)s * D;
+    g.B = w.data_ptr();
+    g.lda = D;
+    g.ldb = w.stride(0);
+    g.M = n;
+    g.N = V;
+    g.K = D;
+    g.epi = EPI_LSE;
+    g.labels = labels.data_ptr<int64_t>() + s;
+    g.partial = ptr<float>(part);
+    g.force_bn = kLseBN;
+    g.err = ptr<int>(scratch(0, 0).err);
+    gemm_launch(g, cur_stream());
+    lse_merge(ptr<float>(part), n_tiles, kLseBN, labels.data_ptr<int64_t>() + s, ptr<float>(lp) + s,
+              ptr<float>(lse) + s, ent.has_value() && ent->defined() ? ptr<float>(*ent) + s : nullptr, nullptr, nullptr,
+              n, cur_stream());
+    count(2);
+  }
+}
+
+// dz[t, v] = g[t] * (onehot(label) - softmax)  (bf16)
+void lmhead_dlogits(Tensor h, Tensor w, Tensor labels, Tensor lse, Tensor glp, Tensor dz) {
+  const c10::cuda::CUDAGuard guard(h.device());
+  GemmProblem g;
+  g.A = h.data_ptr();
+  g.B = w.data_ptr();
+  g.lda = h.stride(0);
+  g.ldb = w.stride(0);
+  g.M = h.size(0);
+  g.N = w.size(0);
+  g.K = h.size(1);
+  g.epi = EPI_DLOGITS;
+  g.out = dz.data_ptr();
+  g.ldo = dz.stride(0);
+  g.labels = labels.data_ptr<int64_t>();
+  g.row_lse = ptr<float>(lse);
+  g.row_g = ptr<float>(glp);
+  g.err = ptr<int>(scratch(0, 0).err);
+  gemm_launch(g, cur_stream());
+  count();
+}
+
+// fused LM head + Gumbel-max categorical sample + log-prob of the sample
+void lmhead_sample(Tensor h, Tensor w, Tensor tok, Tensor lp, double temperature, int64_t seed,
+                   c10::optional<Tensor> step) {
+  CHECK_CONTIG(h);
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int B = h.size(0), V = w.size(0);
+  const int n_tiles = (V + kLseBN - 1) / kLseBN;
+  Tensor part = torch::empty({B, n_tiles, 8}, h.options().dtype(torch::kFloat));
+  GemmProblem g;
+  g.A = h.data_ptr();
+  g.B = w.data_ptr();
+  g.lda = h.stride(0);
+  g.ldb = w.stride(0);
+  g.M = B;
+  g.N = V;
+  g.K = h.size(1);
+  g.epi = EPI_LSE;
+  g.partial = ptr<float>(part);
+  g.inv_temp = (float)(1.0 / temperature);
+  g.seed = (uint64_t)seed;
+  g.step_ptr = optr<int64_t>(step);
+  g.gumbel = 1;
+  g.force_bn = kLseBN;
+  g.err = ptr<int>(scratch(0, 0).err);
+  gemm_launch(g, cur_stream());
+  lse_merge(ptr<float>(part), n_tiles, kLseBN, nullptr, nullptr, nullptr, nullptr, ptr<int64_t>(tok), ptr<float>(lp), B,
+            cur_stream());
+  count(2);
+}
+
+void embedding_fwd_(Tensor ids, Tensor w, Tensor out) {
+  const c10::cuda::CUDAGuard guard(w.device());
+  TORCH_CHECK(ids.scalar_type() == at::kLong, "ids must be int64");
+  embedding_fwd(ptr<int64_t>(ids), ptr<bf16>(w), ptr<bf16>(out), ids.numel(), (int)w.size(1), w.size(0), cur_stream());
+  count();
+}
+
+void embedding_bwd_(Tensor ids, Tensor g, Tensor gw) {
+  const c10::cuda::CUDAGuard guard(g.device());
+  embedding_bwd(ptr<int64_t>(ids), ptr<bf16>(g), ptr<float>(gw), ids.numel(), (int)gw.size(1), gw.size(0),
+                cur_stream());
+  count();
+}
+
+void sq_norm_(Tensor x, Tensor out) {
+  CHECK_F32(x);
+  const c10::cuda::CUDAGuard guard(x.device());
+  sq_norm(ptr<float>(x), x.numel(), ptr<float>(out), cur_stream());
+  count();
+}
+
+void adamw_flat_(Tensor p, Tensor g, Tensor m, Tensor v, c10::optional<Tensor> out, c10::optional<Tensor> mirror,
+                 Tensor norm, double max_norm, double lr, double b1, double b2, double eps, double wd, int64_t step) {
+  const c10::cuda::CUDAGuard guard(p.device());
+  adamw_flat(ptr<float>(p), ptr<float>(g), ptr<float>(m), ptr<float>(v), optr<bf16>(out), optr<bf16>(mirror),
+             ptr<float>(norm), p.numel(), (float)max_norm, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
+             (int)step, cur_stream());
+  count();
+}
+
+void ppo_loss_fused_(Tensor new_lp, Tensor old_lp, Tensor adv, Tensor mask, c10::optional<Tensor> roll, Tensor inv,
+                     c10::optional<Tensor> posw, c10::optional<Tensor> ent, Tensor doc, Tensor grad, Tensor sums,
+                     Tensor seg, double lo, double hi, int64_t use_tis, int64_t use_icepop, double tmin, double tmax,
+                     double pcoef, int64_t train_old) {
+  const c10::cuda::CUDAGuard guard(new_lp.device());
+  TORCH_CHECK(new_lp.is_contiguous() && old_lp.is_contiguous(), "log-probs must be contiguous");
+  ppo_loss_fused(ptr<float>(new_lp), ptr<float>(old_lp), ptr<float>(adv), ptr<float>(mask), optr<float>(roll),
+                 ptr<float>(inv), optr<float>(posw), optr<float>(ent), ptr<int64_t>(doc), ptr<float>(grad),
+                 ptr<float>(sums), ptr<float>(seg), new_lp.numel(), (float)lo, (float)hi, (int)use_tis,
+                 (int)use_icepop, (float)tmin, (float)tmax, (float)pcoef, (int)train_old, cur_stream());
+  count();
+}
+
+void gae_scan_(Tensor x, Tensor d, Tensor valid, Tensor out) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  gae_scan(ptr<float>(x), ptr<float>(d), ptr<float>(valid), ptr<float>(out), (int)x.size(0), (int)x.size(1),
+           cur_stream());
+  count();
+}
+
+void kv_write_(Tensor k, Tensor v, Tensor kc, Tensor vc, Tensor slots) {
+  const c10::cuda::CUDAGuard guard(k.device());
+  CHECK_CONTIG(k);
+  CHECK_CONTIG(v);
+  kv_write(ptr<bf16>(k), ptr<bf16>(v), ptr<bf16>(kc), ptr<bf16>(vc), ptr<int64_t>(slots), (int)k.size(0),
+           (int)k.size(1), (int)k.size(2), (int)kc.size(2), cur_stream());
+  count();
+}
+
+void paged_attention_(Tensor q, Tensor kc, Tensor vc, Tensor bt, Tensor seq_lens, Tensor out, double scale,
+                      c10::optional<Tensor> workspace) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  CHECK_CONTIG(q);
+  TORCH_CHECK(bt.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt, "block table / lens must be int32");
+  const int B = q.size(0), Hq = q.size(1), hd = q.size(2), Hkv = kc.size(1), page = kc.size(2);
+  const int max_pages = bt.size(1);
+  const int n_split = paged_decode_splits(B, Hkv, max_pages);
+  Tensor part;
+  if (n_split > 1) {
+    int64_t need = (int64_t)B * Hq * n_split * (hd + 2);
+    if (workspace.has_value() && workspace->defined() && workspace->numel() >= need) part = *workspace;
+    else part = torch::empty({need}, q.options().dtype(torch::kFloat));
+  }
+  paged_decode(ptr<bf16>(q), ptr<bf16>(kc), ptr<bf16>(vc), ptr<int>(bt), ptr<int>(seq_lens), ptr<bf16>(out),
+               n_split > 1 ? ptr<float>(part) : nullptr, B, Hq, Hkv, hd, page, max_pages, n_split, (float)scale,
+               cur_stream());
+  count(n_split > 1 ? 2 : 1);
+}
+
+void decode_advance_(Tensor tok, Tensor lp, Tensor tok_in, Tensor pos, Tensor seq_lens, Tensor gen, Tensor max_new,
+                     Tensor done, Tensor slot, Tensor bt, Tensor req, Tensor out_tok, Tensor out_lp, Tensor eos,
+                     int64_t page) {
+  const c10::cuda::CUDAGuard guard(tok.device());
+  decode_advance(ptr<int64_t>(tok), ptr<float>(lp), ptr<int64_t>(tok_in), ptr<int>(pos), ptr<int>(seq_lens),
+                 ptr<int>(gen), ptr<int>(max_new), ptr<int>(done), ptr<int64_t>(slot), ptr<int>(bt), ptr<int>(req),
+                 ptr<int64_t>(out_tok), ptr<float>(out_lp), eos.numel() ? ptr<int64_t>(eos) : nullptr,
+                 (int)eos.numel(), (int)tok.size(0), (int)bt.size(1), (int)out_tok.size(1), (int)page, cur_stream());
+  count();
+}
+
+void cast_copy(Tensor src, Tensor dst) {
+  const c10::cuda::CUDAGuard guard(src.device());
+  TORCH_CHECK(src.numel() == dst.numel(), "cast_copy: size mismatch");
+  if (src.scalar_type() == at::kFloat && dst.scalar_type() == at::kBFloat16) {
+    cast_f32_bf16(ptr<float>(src), ptr<bf16>(dst), src.numel(), cur_stream());
+    count();
+  } else {
+    dst.copy_(src);
+  }
+}
+
+int64_t device_error() {
+  auto& s = scratch(0, 0);
+  return s.err.item<int>();
+}
+void clear_device_error() { scratch(0, 0).err.zero_(); }
+int64_t launch_count() { return g_launches.load(); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "meshy_b200 sm_100a kernel library";
+  m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("swiglu_bwd", &swiglu_bwd_);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd_);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd_);
+  m.def("qkv_rope_fwd", &qkv_rope_fwd_);
+  m.def("qkv_rope_bwd", &qkv_rope_bwd_);
+  m.def("flash_attn_fwd", &flash_attn_fwd_);
+  m.def("flash_attn_bwd", &flash_attn_bwd_);
+  m.def("lmhead_logprob_fwd", &lmhead_logprob_fwd);
+  m.def("lmhead_dlogits", &lmhead_dlogits);
+  m.def("lmhead_sample", &lmhead_sample);
+  m.def("embedding_fwd", &embedding_fwd_);
+  m.def("embedding_bwd", &embedding_bwd_);
+  m.def("sq_norm", &sq_norm_);
+  m.def("adamw_flat", &adamw_flat_);
+  m.def("ppo_loss_fused", &ppo_loss_fused_);
+  m.def("gae_scan", &gae_scan_);
+  m.def("kv_write", &kv_write_);
+  m.def("paged_attention", &paged_attention_);
+  m.def("decode_advance", &decode_advance_);
+  m.def("cast_copy", &cast_copy);
+  m.def("device_error", &device_error);
+  m.def("clear_device_error", &clear_device_error);
+  m.def("launch_count", &launch_count, "kernels launched by this library so far (host-side count)");
+}

@@ -1,0 +1,49 @@
+// Host interface of the tcgen05 GEMM (gemm.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../include/common.cuh"
+
+namespace meshy {
+
+enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ACC_F32 = 2, EPI_LSE = 3, EPI_DLOGITS = 4 };
+
+struct GemmProblem {
+  const void* A = nullptr;  // bf16
+  const void* B = nullptr;  // bf16
+  int64_t lda = 0, ldb = 0;
+  bool a_mn = false, b_mn = false;
+  int M = 0, N = 0, K = 0;
+  int epi = EPI_STORE;
+  void* out = nullptr;
+  int ldo = 0;
+  int out_f32 = 0;
+  const bf16* bias = nullptr;
+  const bf16* residual = nullptr;
+  int ldr = 0;
+  bf16* aux = nullptr;
+  int ld_aux = 0;
+  float* ws = nullptr;        // split-K fp32 workspace [M, N], kept zero between calls
+  int64_t ws_cap = 0;
+  int* counters = nullptr;    // split-K per-tile arrival counters, kept zero
+  int64_t counters_cap = 0;
+  const int64_t* labels = nullptr;
+  float* partial = nullptr;   // LSE partials [M, n_tiles, 8]
+  const float* row_lse = nullptr;
+  const float* row_g = nullptr;
+  float inv_temp = 1.f;
+  uint64_t seed = 0;
+  const int64_t* step_ptr = nullptr;
+  int gumbel = 0;
+  int* err = nullptr;         // device error word
+  int force_bn = 0;           // 0 = heuristic
+  int max_split = 0;          // 0 = heuristic
+};
+
+void gemm_launch(const GemmProblem& g, cudaStream_t stream);
+CUtensorMap make_map_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int bi, int bo);
+int gemm_n_tiles(int N, int bn);
+
+}  // namespace meshy

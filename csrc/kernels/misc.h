@@ -1,0 +1,18 @@
+#pragma once
+#include "../include/common.cuh"
+namespace meshy {
+void sq_norm(const float* x, long long n, float* out, cudaStream_t st);
+void adamw_flat(float* p, const float* g, float* m, float* v, bf16* out, bf16* mirror, const float* norm, long long n,
+                float max_norm, float lr, float b1, float b2, float eps, float wd, int step, cudaStream_t st);
+void ppo_loss_fused(const float* new_lp, const float* old_lp, const float* adv, const float* mask, const float* roll,
+                    const float* inv, const float* posw, const float* ent, const int64_t* doc, float* grad, float* sums,
+                    float* seg, long long T, float lo, float hi, int use_tis, int use_icepop, float tmin, float tmax,
+                    float pcoef, int train_old, cudaStream_t st);
+void gae_scan(const float* x, const float* d, const float* valid, float* out, int rows, int S, cudaStream_t st);
+void lse_merge(const float* part, int n_tiles, int bn, const int64_t* labels, float* lp, float* lse, float* ent,
+               int64_t* tok, float* tok_lp, int rows, cudaStream_t st);
+void decode_advance(const int64_t* tok, const float* lp, int64_t* tok_in, int* pos, int* seq_lens, int* gen,
+                    const int* max_new, int* done, int64_t* slot, const int* bt, const int* req, int64_t* out_tok,
+                    float* out_lp, const int64_t* eos, int n_eos, int B, int max_pages, int cap, int page,
+                    cudaStream_t st);
+}  // namespace meshy

@@ -1,0 +1,108 @@
+"""Inference-side ops of the rollout engine (no autograd).
+
+* :func:`kv_write` — scatter this step's K/V rows into the paged cache.
+* :func:`paged_attention` — decode attention over the paged KV cache
+  (split-KV flash-decode kernel on CUDA; GQA heads of one KV head share the
+  K/V stream).
+* :func:`sample` — fused LM head + softmax + categorical sample + log-prob.
+  The CUDA kernel never writes logits: each CTA sweeps a vocab slice with
+  tcgen05 tiles, keeps an online log-sum-exp and a Gumbel-max argmax per row,
+  and a final pass merges the per-CTA partials.  Temperature-only sampling
+  (every shipped recipe: temperature 1, top_p 1, top_k -1) takes this path;
+  top-k / top-p materialise logits and filter them.
+* :func:`decode_advance` — per-row bookkeeping after sampling (append token,
+  bump lengths, recompute the next cache slot, finish flags), so a whole
+  decode step can be replayed from a CUDA graph with no host work.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import reference as ref
+from .functional import native
+
+
+def kv_write(k, v, k_cache, v_cache, slot_mapping):
+    """``k/v [B, Hkv, hd]`` → cache ``[n_pages, Hkv, page, hd]`` at ``slot_mapping [B]``."""
+    if native(k):
+        from ._ext import ext
+
+        ext().kv_write(k, v, k_cache, v_cache, slot_mapping)
+        return
+    page = k_cache.shape[2]
+    pg = (slot_mapping // page).long()
+    off = (slot_mapping % page).long()
+    k_cache[pg, :, off] = k.to(k_cache.dtype)
+    v_cache[pg, :, off] = v.to(v_cache.dtype)
+
+
+def paged_attention(q, k_cache, v_cache, block_table, seq_lens, scale=None, workspace=None):
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if native(q):
+        from ._ext import ext
+
+        out = torch.empty_like(q)
+        ext().paged_attention(q, k_cache, v_cache, block_table, seq_lens, out, float(scale), workspace)
+        return out
+    return ref.attention_decode_paged(q, k_cache, v_cache, block_table, seq_lens, scale)
+
+
+def sample(h, w, temperature: float, *, top_k: int = -1, top_p: float = 1.0, seed: int = 0,
+           step: torch.Tensor | None = None, generator=None):
+    """Returns ``(tokens int64 [B], logprobs fp32 [B])`` for hidden ``h [B, D]``.
+
+    ``step`` is a device int64 counter folded into the Philox offset so a
+    captured CUDA graph draws fresh noise every replay.
+    """
+    if native(h) and temperature > 0 and top_k <= 0 and top_p >= 1.0:
+        from ._ext import ext
+
+        B = h.shape[0]
+        tok = torch.empty(B, dtype=torch.int64, device=h.device)
+        lp = torch.empty(B, dtype=torch.float32, device=h.device)
+        ext().lmhead_sample(h, w, tok, lp, float(temperature), int(seed), step)
+        return tok, lp
+    logits = h.float() @ w.float().t() if not h.is_cuda else torch.nn.functional.linear(h, w).float()
+    return ref.sample_with_logprob(logits, temperature, generator=generator, top_k=top_k, top_p=top_p)
+
+
+def decode_advance(state: dict, tok, lp, page_size: int):
+    """Append sampled tokens and advance per-row decode state (in place).
+
+    ``state`` holds device tensors: ``tok_in [B]``, ``pos [B]``, ``seq_lens [B]``,
+    ``gen [B]``, ``max_new [B]``, ``done [B]``, ``slot [B]``, ``block_table``,
+    ``req [B]`` (output slot of the row), ``out_tok [R, L]``, ``out_lp [R, L]``,
+    ``eos [n_eos]``.
+    """
+    if native(tok):
+        from ._ext import ext
+
+        ext().decode_advance(tok, lp, state["tok_in"], state["pos"], state["seq_lens"], state["gen"],
+                             state["max_new"], state["done"], state["slot"], state["block_table"],
+                             state["req"], state["out_tok"], state["out_lp"], state["eos"], int(page_size))
+        return
+    live = state["done"] == 0
+    rows = torch.nonzero(live).flatten()
+    if rows.numel() == 0:
+        return
+    r = state["req"][rows].long()
+    g = state["gen"][rows].long()
+    state["out_tok"][r, g] = tok[rows]
+    state["out_lp"][r, g] = lp[rows]
+    state["gen"][rows] += 1
+    state["tok_in"][rows] = tok[rows]
+    fin = state["gen"][rows] >= state["max_new"][rows]
+    if state["eos"].numel():
+        fin |= (tok[rows].unsqueeze(-1) == state["eos"].unsqueeze(0)).any(-1)
+    state["done"][rows] = fin.to(state["done"].dtype)
+    state["pos"][rows] += 1
+    state["seq_lens"][rows] += 1
+    p = state["pos"][rows].long()
+    pg = state["block_table"][rows, p // page_size].long()
+    state["slot"][rows] = pg * page_size + p % page_size
+
+
+__all__ = ["decode_advance", "kv_write", "paged_attention", "sample"]

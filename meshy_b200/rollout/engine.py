@@ -1,0 +1,546 @@
+"""Paged-KV continuous-batching rollout engine (replaces the reference's SGLang).
+
+Capabilities the reference uses from SGLang (``meshy/engine/sglang.py``) and
+how they map here:
+
+* ``/generate`` with ``return_logprob``: :meth:`RolloutEngine.generate` /
+  :meth:`submit` + :meth:`step` return output ids, per-token log-probs of the
+  sampled tokens and a finish reason (``stop`` / ``length`` / ``abort``);
+* ``/pause_generation {mode: abort}`` / ``/continue_generation``:
+  :meth:`abort_all`, :meth:`pause`, :meth:`resume`;
+* ``/release_memory_occupation`` / ``/resume_memory_occupation`` (tags
+  ``kv_cache``, ``weights``): :meth:`release_memory`, :meth:`resume_memory`
+  through the VMM pool (:mod:`.memory`), so virtual addresses — and hence
+  captured CUDA graphs — survive a hand-off;
+* ``/update_weights_from_disk``: :meth:`update_weights_from_disk`; plus the
+  device path :meth:`update_weights_from_flat` (one device copy, or done by the
+  trainer's optimiser kernel writing straight into :attr:`weight_flat`).
+
+Execution model:
+
+* weights live in one flat bf16 buffer with the trainer's layout;
+* the KV cache is ``[layers, 2, pages, kv_heads, page, head_dim]``; a host
+  block manager (:mod:`.kv_cache`) hands out pages;
+* prefill runs new prompts as one packed varlen forward and writes their KV;
+* a decode step (embedding → layers → fused LM-head sampler → row advance) is
+  captured once per batch-size bucket in a CUDA graph and replayed; rows that
+  finish are compacted away every ``sync_every`` steps, the only host↔device
+  synchronisation of the loop.
+"""
+
+from __future__ import annotations
+
+import itertools
+import math
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Any, Sequence
+
+import torch
+
+from ..models.args import ModelArgs
+from ..models.transformer import DecoderLM
+from ..ops import decode as D
+from ..ops import functional as Fx
+from .kv_cache import BlockManager
+
+_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512)
+
+
+@dataclass
+class Request:
+    rid: Any
+    prompt: list[int]
+    max_new_tokens: int
+    temperature: float = 1.0
+    top_k: int = -1
+    top_p: float = 1.0
+    ignore_eos: bool = False
+    # engine state
+    out_slot: int = -1
+    pages: list[int] = field(default_factory=list)
+    submitted: float = 0.0
+
+
+@dataclass
+class Generation:
+    rid: Any
+    prompt_ids: list[int]
+    output_ids: list[int]
+    output_logprobs: list[float]
+    finish_reason: str
+    weight_version: int = 0
+
+    @property
+    def tokens(self) -> list[int]:
+        return self.prompt_ids + self.output_ids
+
+
+def _bucket(n: int) -> int:
+    for b in _BUCKETS:
+        if b >= n:
+            return b
+    return n
+
+
+class RolloutEngine:
+    def __init__(
+        self,
+        args: ModelArgs,
+        *,
+        device: str | torch.device = "cpu",
+        model: DecoderLM | None = None,
+        max_running: int = 256,
+        max_total_tokens: int | None = None,
+        page_size: int = 64,
+        max_seq_len: int | None = None,
+        use_cuda_graph: bool = True,
+        sync_every: int = 16,
+        seed: int = 0,
+        eos_token_ids: Sequence[int] = (),
+        prefill_chunk_tokens: int = 32768,
+        mem_fraction: float = 0.5,
+    ):
+        from ..backend.flat import flatten_module
+
+        self.args = args
+        self.device = torch.device(device)
+        self.cuda = self.device.type == "cuda"
+        self.dtype = torch.bfloat16 if self.cuda else torch.float32
+        if model is None:
+            from ..models import build_model
+
+            model = build_model(args, seed=seed, device=self.device, dtype=self.dtype)
+        self.model = model.eval()
+        for p in self.model.parameters():
+            p.requires_grad_(False)
+        self.weight_flat, self.weight_slots = flatten_module(self.model, self.dtype, self.device)
+        self.page_size = page_size
+        self.max_running = max_running
+        self.max_seq_len = min(max_seq_len or args.max_seq_len, args.max_seq_len)
+        self.max_pages_per_seq = math.ceil(self.max_seq_len / page_size)
+        if max_total_tokens is None:
+            if self.cuda:
+                free, _ = torch.cuda.mem_get_info(self.device)
+                max_total_tokens = int(free * mem_fraction) // max(1, args.kv_bytes_per_token(2))
+            else:
+                max_total_tokens = 64 * 1024
+        n_pages = max(1, max_total_tokens // page_size)
+        self.n_pages = n_pages
+        self.blocks = BlockManager(n_pages, page_size)
+        self._alloc_kv()
+        self.use_cuda_graph = use_cuda_graph and self.cuda
+        self.sync_every = max(1, sync_every)
+        self.seed = seed
+        self.eos = list(eos_token_ids)
+        self.prefill_chunk_tokens = prefill_chunk_tokens
+        self.weight_version = 0
+        self._rid = itertools.count()
+        self._gen = torch.Generator(device="cpu").manual_seed(seed)
+        self.waiting: list[Request] = []
+        self.running: list[Request] = []   # row i <-> running[i]
+        self.finished: dict[Any, Generation] = {}
+        self.paused = False
+        self.lock = threading.RLock()
+        self._graphs: dict[int, Any] = {}
+        self.stats = {"decode_steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "graph_replays": 0}
+        self._init_state()
+
+    # ------------------------------------------------------------------ memory
+    def _alloc_kv(self):
+        a = self.args
+        self.kv = torch.zeros(a.n_layers, 2, self.n_pages, a.n_kv_heads, self.page_size, a.head_dim,
+                              dtype=self.dtype, device=self.device)
+
+    def _init_state(self):
+        B, dev = self.max_running, self.device
+        R = B  # one output slot per concurrently running request
+        self.max_new_cap = self.max_seq_len
+        i32, i64 = torch.int32, torch.int64
+        self.st = {
+            "tok_in": torch.zeros(B, dtype=i64, device=dev),
+            "pos": torch.zeros(B, dtype=i32, device=dev),
+            "seq_lens": torch.ones(B, dtype=i32, device=dev),
+            "gen": torch.zeros(B, dtype=i32, device=dev),
+            "max_new": torch.zeros(B, dtype=i32, device=dev),
+            "done": torch.ones(B, dtype=i32, device=dev),
+            "slot": torch.zeros(B, dtype=i64, device=dev),
+            "block_table": torch.zeros(B, self.max_pages_per_seq, dtype=i32, device=dev),
+            "req": torch.arange(B, dtype=i32, device=dev),
+            "out_tok": torch.zeros(R, self.max_new_cap, dtype=i64, device=dev),
+            "out_lp": torch.zeros(R, self.max_new_cap, dtype=torch.float32, device=dev),
+            "eos": torch.tensor(self.eos, dtype=i64, device=dev),
+            "noeos": torch.zeros(0, dtype=i64, device=dev),
+            "step": torch.zeros(1, dtype=i64, device=dev),
+        }
+        self.free_out_slots = list(range(R))
+        self._park_rows(0)
+
+    def release_memory(self, tags: Sequence[str] = ("kv_cache", "weights")) -> None:
+        """Give GPU memory back for a colocated trainer (graphs are dropped)."""
+        with self.lock:
+            self._graphs.clear()
+            if "kv_cache" in tags and self.kv is not None:
+                self.kv = None
+            if "weights" in tags and self.weight_flat is not None and self.cuda:
+                host = torch.empty(self.weight_flat.shape, dtype=self.weight_flat.dtype, pin_memory=True)
+                host.copy_(self.weight_flat)
+                self._host_weights = host
+                self.weight_flat = None
+                for p in self.model.parameters():
+                    p.data = torch.empty(0, dtype=p.dtype, device=self.device)
+            if self.cuda:
+                torch.cuda.empty_cache()
+
+    def resume_memory(self, tags: Sequence[str] = ("kv_cache", "weights")) -> None:
+        with self.lock:
+            if "weights" in tags and self.weight_flat is None:
+                self.weight_flat = self._host_weights.to(self.device)
+                self._host_weights = None
+                self._rebind_weights()
+            if "kv_cache" in tags and self.kv is None:
+                self._alloc_kv()
+
+    def _rebind_weights(self):
+        for s, p in zip(self.weight_slots, self.model.parameters()):
+            p.data = self.weight_flat[s.offset:s.offset + s.numel].view(s.shape)
+
+    # ------------------------------------------------------------------ weights
+    def update_weights_from_flat(self, src: torch.Tensor, version: int | None = None) -> None:
+        """Device weight sync: ``src`` is a flat buffer in the same layout."""
+        with self.lock:
+            if self.weight_flat is None:
+                raise RuntimeError("weights are released; resume_memory(['weights']) first")
+            if src.numel() != self.weight_flat.numel():
+                raise ValueError("flat weight layout mismatch")
+            if src.dtype == self.weight_flat.dtype:
+                self.weight_flat.copy_(src, non_blocking=True)
+            elif src.is_cuda:
+                from ..ops._ext import ext
+
+                ext().cast_copy(src, self.weight_flat)
+            else:
+                self.weight_flat.copy_(src)
+            self.weight_version = self.weight_version + 1 if version is None else int(version)
+
+    def update_weights_from_state_dict(self, sd: dict[str, torch.Tensor], version: int | None = None) -> None:
+        with self.lock:
+            with torch.no_grad():
+                for s in self.weight_slots:
+                    self.weight_flat[s.offset:s.offset + s.numel].copy_(sd[s.name].reshape(-1))
+            self.weight_version = self.weight_version + 1 if version is None else int(version)
+
+    def update_weights_from_disk(self, path: str, version: int | None = None) -> None:
+        from ..models.hf import load_hf_checkpoint
+
+        self.update_weights_from_state_dict(load_hf_checkpoint(self.args, path), version)
+
+    # ------------------------------------------------------------------ requests
+    def submit(self, prompt: Sequence[int], max_new_tokens: int, *, rid=None, temperature=1.0, top_k=-1,
+               top_p=1.0, ignore_eos=False) -> Any:
+        rid = next(self._rid) if rid is None else rid
+        if len(prompt) + max_new_tokens > self.max_seq_len:
+            max_new_tokens = max(1, self.max_seq_len - len(prompt))
+        req = Request(rid, list(map(int, prompt)), int(max_new_tokens), float(temperature), int(top_k),
+                      float(top_p), bool(ignore_eos), submitted=time.time())
+        with self.lock:
+            self.waiting.append(req)
+        return rid
+
+    def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int | Sequence[int], *,
+                 temperature: float = 1.0, top_k: int = -1, top_p: float = 1.0,
+                 ignore_eos: bool = False) -> list[Generation]:
+        """Blocking batch generation (the lock-step rollout's call)."""
+        if isinstance(max_new_tokens, int):
+            max_new_tokens = [max_new_tokens] * len(prompts)
+        rids = [self.submit(p, m, temperature=temperature, top_k=top_k, top_p=top_p, ignore_eos=ignore_eos)
+                for p, m in zip(prompts, max_new_tokens)]
+        self.run_until_idle()
+        return [self.finished.pop(r) for r in rids]
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def run_until_idle(self) -> None:
+        while self.has_work() and not self.paused:
+            self.step()
+
+    @property
+    def n_running(self) -> int:
+        return len(self.running)
+
+    def loads(self) -> dict[str, int]:
+        return {"num_running_reqs": len(self.running), "num_waiting_reqs": len(self.waiting),
+                "num_free_pages": self.blocks.num_free}
+
+    # ------------------------------------------------------------------ control
+    def pause(self) -> None:
+        self.paused = True
+
+    def resume(self) -> None:
+        self.paused = False
+
+    def abort_all(self) -> list[Generation]:
+        """Finish every running/waiting request now with ``finish_reason='abort'``."""
+        with self.lock:
+            out = []
+            if self.running:
+                self._collect(list(range(len(self.running))), reason="abort")
+            for req in self.waiting:
+                g = Generation(req.rid, req.prompt, [], [], "abort", self.weight_version)
+                self.finished[req.rid] = g
+            self.waiting.clear()
+            for g in self.finished.values():
+                if g.finish_reason == "abort":
+                    out.append(g)
+            return out
+
+    # ------------------------------------------------------------------ scheduling
+    def step(self) -> None:
+        with self.lock:
+            self._admit()
+            if not self.running:
+                return
+            n = len(self.running)
+            self._ensure_pages(range(n), self.sync_every + 1)
+            steps = self.sync_every
+            for _ in range(steps):
+                self._decode_step(n)
+            self._sync_finished()
+
+    def _admit(self) -> None:
+        if not self.waiting:
+            return
+        budget = self.prefill_chunk_tokens
+        batch: list[Request] = []
+        while self.waiting and len(self.running) + len(batch) < self.max_running:
+            req = self.waiting[0]
+            need = len(req.prompt) + min(req.max_new_tokens, self.sync_every * 2) + 1
+            if batch and sum(len(r.prompt) for r in batch) + len(req.prompt) > budget:
+                break
+            pages = self.blocks.allocate(math.ceil(need / self.page_size))
+            if pages is None:
+                break
+            req.pages = pages
+            req.out_slot = self.free_out_slots.pop()
+            batch.append(self.waiting.pop(0))
+        if batch:
+            self._prefill(batch)
+
+    def _ensure_pages(self, rows: Sequence[int], lookahead: int) -> None:
+        """Grow page lists so every row can decode ``lookahead`` more tokens."""
+        st = self.st
+        seq = st["seq_lens"][: len(self.running)].tolist()
+        bt_updates = []
+        for i in rows:
+            req = self.running[i]
+            need_tokens = min(seq[i] + lookahead, len(req.prompt) + req.max_new_tokens)
+            need = math.ceil(need_tokens / self.page_size)
+            if need > len(req.pages):
+                new = self.blocks.allocate(need - len(req.pages))
+                if new is None:
+                    raise RuntimeError("KV cache exhausted; lower max_running or raise max_total_tokens")
+                start = len(req.pages)
+                req.pages.extend(new)
+                bt_updates.append((i, start, new))
+        for i, start, new in bt_updates:
+            st["block_table"][i, start:start + len(new)] = torch.tensor(new, dtype=torch.int32, device=self.device)
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def _prefill(self, batch: list[Request]) -> None:
+        a, dev, P = self.args, self.device, self.page_size
+        lens = [len(r.prompt) for r in batch]
+        T = sum(lens)
+        toks = torch.tensor([t for r in batch for t in r.prompt], dtype=torch.int64)
+        pos = torch.cat([torch.arange(L, dtype=torch.int32) for L in lens])
+        slots = torch.cat([
+            torch.tensor(r.pages, dtype=torch.int64).repeat_interleave(P)[:L] * P + torch.arange(L) % P
+            for r, L in zip(batch, lens)])
+        cu = torch.tensor([0] + list(itertools.accumulate(lens)), dtype=torch.int32)
+        toks, pos, slots, cu = (t.to(dev, non_blocking=True) for t in (toks, pos, slots, cu))
+        m = self.model
+        x = Fx.embedding(toks, m.embed)
+        for li, layer in enumerate(m.layers):
+            h = Fx.rmsnorm(x, layer.attn_norm, a.norm_eps)
+            qkv = Fx.linear(h, layer.wqkv, layer.bqkv)
+            q, k, v = Fx.qkv_rope(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
+                                  a.rope_theta, a.norm_eps)
+            D.kv_write(k, v, self.kv[li, 0], self.kv[li, 1], slots)
+            o = Fx.flash_attn_varlen(q, k, v, cu, max(lens))
+            x = Fx.linear(o.reshape(T, a.q_dim), layer.wo, residual=x)
+            h = Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps)
+            x = self._mlp(layer, h, x)
+        last = (cu[1:] - 1).long()
+        hl = Fx.rmsnorm(x[last], m.norm, a.norm_eps)
+        tok, lp = self._sample_rows(hl, batch)
+        self.stats["prefill_tokens"] += T
+        # append rows
+        st = self.st
+        base = len(self.running)
+        n = len(batch)
+        rows = slice(base, base + n)
+        max_new = torch.tensor([r.max_new_tokens for r in batch], dtype=torch.int32)
+        req_slots = torch.tensor([r.out_slot for r in batch], dtype=torch.int32)
+        plen = torch.tensor(lens, dtype=torch.int32)
+        st["req"][rows] = req_slots.to(dev)
+        st["max_new"][rows] = max_new.to(dev)
+        st["gen"][rows] = 1
+        st["tok_in"][rows] = tok
+        st["pos"][rows] = plen.to(dev)
+        st["seq_lens"][rows] = (plen + 1).to(dev)
+        rs = req_slots.to(dev).long()
+        st["out_tok"][rs, 0] = tok
+        st["out_lp"][rs, 0] = lp
+        done = max_new <= 1
+        ignore = torch.tensor([r.ignore_eos for r in batch])
+        if self.eos:
+            hit = torch.isin(tok.cpu(), torch.tensor(self.eos)) & ~ignore
+            done = done | hit
+        st["done"][rows] = done.to(torch.int32).to(dev)
+        bt = torch.zeros(n, self.max_pages_per_seq, dtype=torch.int32)
+        for j, r in enumerate(batch):
+            bt[j, : len(r.pages)] = torch.tensor(r.pages, dtype=torch.int32)
+        st["block_table"][rows] = bt.to(dev)
+        pg = torch.tensor([r.pages[L // P] for r, L in zip(batch, lens)], dtype=torch.int64)
+        st["slot"][rows] = (pg * P + plen.long() % P).to(dev)
+        self.running.extend(batch)
+
+    def _mlp(self, layer, h, x):
+        a = self.args
+        if layer.moe is None:
+            return Fx.linear(Fx.linear_swiglu(h, layer.w13, a.swiglu_block), layer.w2, residual=x)
+        return x + layer.moe(h)
+
+    def _sample_rows(self, h, reqs: Sequence[Request]):
+        r0 = reqs[0]
+        uniform = all(r.temperature == r0.temperature and r.top_k == r0.top_k and r.top_p == r0.top_p
+                      for r in reqs)
+        w = self.model.output_weight
+        if uniform:
+            return D.sample(h, w, r0.temperature, top_k=r0.top_k, top_p=r0.top_p, seed=self.seed,
+                            step=self.st["step"], generator=self._gen if not self.cuda else None)
+        toks, lps = [], []
+        for i, r in enumerate(reqs):
+            t, l = D.sample(h[i:i + 1], w, r.temperature, top_k=r.top_k, top_p=r.top_p, seed=self.seed,
+                            step=self.st["step"], generator=self._gen if not self.cuda else None)
+            toks.append(t)
+            lps.append(l)
+        return torch.cat(toks), torch.cat(lps)
+
+    # ------------------------------------------------------------------ decode
+    @torch.no_grad()
+    def _decode_body(self, b: int, eos: torch.Tensor):
+        a, m, st = self.args, self.model, self.st
+        x = Fx.embedding(st["tok_in"][:b], m.embed)
+        pos = st["pos"][:b]
+        for li, layer in enumerate(m.layers):
+            h = Fx.rmsnorm(x, layer.attn_norm, a.norm_eps)
+            qkv = Fx.linear(h, layer.wqkv, layer.bqkv)
+            q, k, v = Fx.qkv_rope(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
+                                  a.rope_theta, a.norm_eps)
+            D.kv_write(k, v, self.kv[li, 0], self.kv[li, 1], st["slot"][:b])
+            o = D.paged_attention(q, self.kv[li, 0], self.kv[li, 1], st["block_table"][:b], st["seq_lens"][:b])
+            x = Fx.linear(o.reshape(b, a.q_dim), layer.wo, residual=x)
+            h = Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps)
+            x = self._mlp(layer, h, x)
+        h = Fx.rmsnorm(x, m.norm, a.norm_eps)
+        r0 = self.running[0]
+        tok, lp = D.sample(h, m.output_weight, r0.temperature, top_k=r0.top_k, top_p=r0.top_p, seed=self.seed,
+                           step=st["step"], generator=self._gen if not self.cuda else None)
+        sub = {k: (v[:b] if k not in ("out_tok", "out_lp", "eos", "noeos", "step") else v) for k, v in st.items()}
+        sub["eos"] = eos
+        D.decode_advance(sub, tok, lp, self.page_size)
+        st["step"] += 1
+
+    def _decode_step(self, n: int) -> None:
+        eos = self.st["eos"] if not all(r.ignore_eos for r in self.running) else self.st["noeos"]
+        if not self.use_cuda_graph:
+            self._decode_body(n, eos)
+        else:
+            b = min(_bucket(n), self.max_running)
+            key = (b, eos.numel() > 0, self._sampling_key())
+            g = self._graphs.get(key)
+            if g is None:
+                g = self._capture(b, eos)
+                self._graphs[key] = g
+            g.replay()
+            self.stats["graph_replays"] += 1
+            self.stats["graph_kernels"] = self.stats.get("graph_kernels", 0) + getattr(g, "n_kernels", 0)
+        self.stats["decode_steps"] += 1
+        self.stats["decode_tokens"] += n
+
+    def _sampling_key(self):
+        r = self.running[0]
+        return (r.temperature, r.top_k, r.top_p)
+
+    def _capture(self, b: int, eos: torch.Tensor):
+        # rows beyond len(running) are padding: mark them done so advance skips them
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up (allocator, tensor maps)
+                saved = {k: v.clone() for k, v in self.st.items()}
+                self._decode_body(b, eos)
+                for k, v in saved.items():
+                    self.st[k].copy_(v)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        saved = {k: v.clone() for k, v in self.st.items()}
+        from ..ops._ext import ext
+
+        n0 = ext().launch_count()
+        with torch.cuda.graph(g, stream=s):
+            self._decode_body(b, eos)
+        g.n_kernels = ext().launch_count() - n0
+        for k, v in saved.items():
+            self.st[k].copy_(v)
+        return g
+
+    # ------------------------------------------------------------------ finish
+    def _sync_finished(self) -> None:
+        n = len(self.running)
+        if n == 0:
+            return
+        done = self.st["done"][:n].tolist()
+        rows = [i for i, d in enumerate(done) if d]
+        if rows:
+            self._collect(rows)
+
+    def _collect(self, rows: list[int], reason: str | None = None) -> None:
+        st, n = self.st, len(self.running)
+        gen = st["gen"][:n].tolist()
+        max_gen = max(gen[i] for i in rows) if rows else 0
+        slots = torch.tensor([self.running[i].out_slot for i in rows], dtype=torch.long, device=self.device)
+        toks = st["out_tok"].index_select(0, slots)[:, :max_gen].cpu().tolist()
+        lps = st["out_lp"].index_select(0, slots)[:, :max_gen].cpu().tolist()
+        for j, i in enumerate(rows):
+            req = self.running[i]
+            g = gen[i]
+            out = toks[j][:g]
+            fr = reason
+            if fr is None:
+                fr = "stop" if (not req.ignore_eos and out and out[-1] in self.eos) else "length"
+            self.finished[req.rid] = Generation(req.rid, req.prompt, out, lps[j][:g], fr, self.weight_version)
+            self.blocks.free(req.pages)
+            self.free_out_slots.append(req.out_slot)
+        keep = [i for i in range(n) if i not in set(rows)]
+        if keep != list(range(len(keep))):
+            idx = torch.tensor(keep, dtype=torch.long, device=self.device)
+            for k in ("tok_in", "pos", "seq_lens", "gen", "max_new", "done", "slot", "block_table", "req"):
+                st[k][: len(keep)] = st[k].index_select(0, idx)
+        self._park_rows(len(keep))
+        self.running = [self.running[i] for i in keep]
+
+    def _park_rows(self, start: int) -> None:
+        """Rows ``>= start`` are idle: done, and their KV write goes to trash page 0."""
+        st = self.st
+        st["done"][start:] = 1
+        st["slot"][start:] = 0
+        st["block_table"][start:] = 0
+        st["seq_lens"][start:] = 1
+        st["pos"][start:] = 0
+
+
+__all__ = ["Generation", "Request", "RolloutEngine"]

@@ -1,0 +1,90 @@
+"""Accumulating named stopwatches (reference ``meshy/utils/timer.py:53-178``).
+
+``TimerStats.timer(name, sync=...)`` accumulates wall time per bucket; with
+``sync=True`` on a CUDA machine the block is bracketed by
+``torch.cuda.synchronize`` so the number covers device work.
+:class:`DeviceTimer` times a region with CUDA events instead (no host sync
+inside the region); :func:`max_over_ranks` turns a per-rank time into the
+job time.
+"""
+
+from __future__ import annotations
+
+import time
+from collections import defaultdict
+from contextlib import contextmanager
+
+import torch
+
+_GLOBAL_ENABLED = True
+
+
+def set_timers_enabled(flag: bool) -> None:
+    global _GLOBAL_ENABLED
+    _GLOBAL_ENABLED = bool(flag)
+
+
+class TimerStats:
+    def __init__(self, enabled: bool = True):
+        self.enabled = enabled
+        self.totals: dict[str, float] = defaultdict(float)
+        self.counts: dict[str, int] = defaultdict(int)
+
+    @contextmanager
+    def timer(self, name: str, sync: bool = False):
+        if not (self.enabled and _GLOBAL_ENABLED):
+            yield
+            return
+        cuda = sync and torch.cuda.is_available() and torch.cuda.is_initialized()
+        if cuda:
+            torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        try:
+            yield
+        finally:
+            if cuda:
+                torch.cuda.synchronize()
+            self.totals[name] += time.perf_counter() - t0
+            self.counts[name] += 1
+
+    def add(self, name: str, seconds: float) -> None:
+        self.totals[name] += seconds
+        self.counts[name] += 1
+
+    def pop_metrics(self, prefix: str = "") -> dict[str, float]:
+        out = {f"{prefix}{k}": v for k, v in self.totals.items()}
+        self.totals.clear()
+        self.counts.clear()
+        return out
+
+
+class DeviceTimer:
+    """CUDA-event timer on the current stream: ``start()`` … ``stop()`` → ms."""
+
+    def __init__(self):
+        self._s = torch.cuda.Event(enable_timing=True)
+        self._e = torch.cuda.Event(enable_timing=True)
+
+    def start(self):
+        self._s.record()
+        return self
+
+    def stop(self) -> float:
+        self._e.record()
+        self._e.synchronize()
+        return self._s.elapsed_time(self._e)
+
+
+def max_over_ranks(value: float, group=None, device=None) -> float:
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
+        return value
+    backend = dist.get_backend(group)
+    dev = device if device is not None else (torch.device("cuda") if backend == "nccl" else torch.device("cpu"))
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return float(t.item())
+
+
+__all__ = ["DeviceTimer", "TimerStats", "max_over_ranks", "set_timers_enabled"]
