@@ -215,6 +215,13 @@ def main():
             loss = torch.tensor([rep.metrics["pg_loss"]], device=dev).cpu()
             d2h += 4 + 8 * len(host)
             e2e_ms.append((time.perf_counter() - t0) * 1e3)
+            if rank == 0:
+                st = rl.engine.stats
+                print(f"[bench] step {s}: rollout {rep.times['rollout_s']:.2f}s train {rep.times['train_s']:.2f}s "
+                      f"sync {rep.times['weight_sync_ms']:.2f}ms tokens {rep.n_tokens} resp {rep.n_response_tokens} "
+                      f"decode_steps {st['decode_steps']} "
+                      + " ".join(f"{k}={v:.3f}" for k, v in rep.metrics.items() if k.startswith("time/")),
+                      file=sys.stderr, flush=True)
             tokens += rep.n_tokens
             resp_tokens += rep.n_response_tokens
             sync_ms.append(rep.times["weight_sync_ms"])

@@ -25,8 +25,8 @@ cuda_sources = [
 ]
 extra_cuda = [s for s in ("csrc/kernels/symm.cu",) if os.path.exists(os.path.join(ROOT, s))]
 
-native_sources = [s for s in ("csrc/native/bindings.cpp", "csrc/native/column_store.cpp",
-                              "csrc/native/page_allocator.cpp") if os.path.exists(os.path.join(ROOT, s))]
+native_sources = [s for s in ("csrc/native/bindings.cpp", "csrc/native/column_store.cpp")
+                  if os.path.exists(os.path.join(ROOT, s))]
 
 ext_modules = [
     CUDAExtension(

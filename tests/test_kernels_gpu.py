@@ -63,9 +63,11 @@ def test_gemm_dgrad_wgrad(T, N, K):
     gw = torch.ones(N, K, dtype=torch.float32, device=DEV)
     C().gemm(gy, x, gw, True, True, None, None, None, 0, True, 0)  # dW += dY^T X
     assert rel_err(gw, 1.0 + gy.float().t() @ x.float()) < 5e-3
-    # A MN-major, B K-major
-    out = torch.empty(N, N, dtype=torch.float32, device=DEV)
-    C().gemm(gy, w[:, :N].contiguous() if K >= N else bf(N, N), out, True, False, None, None, None, 0, False, 0)
+    # A MN-major, B K-major: out[N, K2] = gy^T [N, T] · y[K2, T]^T with y = x^T stored [K2, T]
+    y = x.t().contiguous()
+    out = torch.empty(N, K, dtype=torch.float32, device=DEV)
+    C().gemm(gy, y, out, True, False, None, None, None, 0, False, 0)
+    assert rel_err(out, gy.float().t() @ x.float()) < 5e-3
 
 
 def test_gemm_swiglu():
