@@ -1,0 +1,167 @@
+"""Actor training engine (the reference's ``TitanEngine``, ``meshy/engine/titan.py:126-560``).
+
+``step(samples, sync)`` on rank 0 broadcasts the window, every rank plans the
+global batch identically and trains its DP slice (:class:`PPOTrainer`), then
+on ``sync`` the engine bumps the weight version, publishes weights (device IPC
+handle for same-node engines, or an HF safetensors export), takes the global
+checkpoint when due and rotates old exports while protecting versions a
+retained checkpoint still points at.  Offload/restore implement the
+colocation hand-off.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+import shutil
+import time
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+from ..backend.trainer import PPOTrainer
+from ..config import GlobalCheckpointConfig, TrainerConfig, TrainerParamsConfig
+from .spmd import SpmdEngine
+
+log = logging.getLogger(__name__)
+
+
+@dataclass
+class StepResult:
+    metrics: dict = field(default_factory=dict)
+    weight_version: int = 0
+    weights_ref: str | None = None
+    global_step: int = 0
+
+
+class TrainerEngine(SpmdEngine):
+    def __init__(self, trainer_config: TrainerConfig, trainer_params: TrainerParamsConfig | None, *, service_name: str,
+                 runtime=None, checkpoint: GlobalCheckpointConfig | None = None, weight_sync_mode: str = "auto",
+                 weights_keep_latest_k: int = 5, critic_cold_start_windows: int = 0, model_path: str | None = None,
+                 **kw):
+        super().__init__(**kw)
+        self.tc, self.tp = trainer_config, trainer_params
+        self.service_name = service_name
+        self.runtime = runtime
+        self.checkpoint = GlobalCheckpointConfig.coerce(checkpoint)
+        self.weight_sync_mode = weight_sync_mode
+        self.weights_keep_latest_k = weights_keep_latest_k
+        self.cold = int(critic_cold_start_windows)
+        self.model_path = model_path
+        self.trainer: PPOTrainer | None = None
+        self.version = 0
+        self.step_index = 0
+
+    def setup(self) -> None:
+        if self.world_size > 1 and not torch.distributed.is_initialized():
+            self.init_process_group()
+        self.trainer = PPOTrainer(self.tc, self.tp, device=self.device,
+                                  dp_group=self.compute_group if self.world_size > 1 else None)
+        if self.model_path and os.path.isdir(self.model_path):
+            from ..models.hf import load_hf_checkpoint
+
+            self.trainer.flat.load_state_dict(load_hf_checkpoint(self.trainer.model_args, self.model_path))
+
+    @property
+    def global_step(self) -> int:
+        return self.step_index + self.cold
+
+    # ------------------------------------------------------------------ public (rank 0)
+    def step(self, samples: list[dict], sync: bool = True) -> StepResult:
+        return self.submit_command("step", {"samples": samples, "sync": sync})
+
+    def offload(self) -> None:
+        self.submit_command("offload", None)
+
+    def restore(self) -> None:
+        self.submit_command("restore", None)
+
+    # ------------------------------------------------------------------ collective commands
+    def cmd_step(self, payload) -> StepResult:
+        samples, sync = payload["samples"], payload["sync"]
+        t = self.trainer
+        plan = t.plan_batch(samples, t.dp_size)
+        local = plan.local_samples(samples, t.dp_rank)
+        t0 = time.perf_counter()
+        metrics = t.train_step(local, plan=plan.per_rank[t.dp_rank], step_schedule=sync)
+        metrics["time/train/step"] = time.perf_counter() - t0
+        res = StepResult(metrics=metrics)
+        if sync:
+            self.step_index += 1
+            self.version += 1
+            res.weight_version = self.version
+            res.global_step = self.global_step
+            res.weights_ref = self.publish_weights()
+            if self.checkpoint.due(self.global_step):
+                self.save_global_checkpoint(self.global_step)
+        return res
+
+    def cmd_offload(self, payload) -> None:
+        self.trainer.offload_to_cpu()
+
+    def cmd_restore(self, payload) -> None:
+        self.trainer.restore_to_gpu()
+
+    # ------------------------------------------------------------------ weights
+    def publish_weights(self) -> str | None:
+        mode = self.weight_sync_mode
+        if mode in ("auto", "device") and self.device.type == "cuda" and self.world_size == 1:
+            from ..rollout.weight_sync import export_ipc_flat
+
+            return "ipc:" + export_ipc_flat(self.trainer.flat.master)
+        if self.runtime is None:
+            return None
+        path = self.runtime.checkpoint_path(self.service_name, self.version)
+        if self.rank == 0:
+            self.trainer.export_hf(path)
+            self.prune_weights()
+        self.barrier()
+        return path
+
+    def prune_weights(self) -> list[int]:
+        if self.runtime is None or self.weights_keep_latest_k <= 0:
+            return []
+        wdir = self.runtime.weights_dir(self.service_name)
+        try:
+            versions = sorted(int(d[1:]) for d in os.listdir(wdir) if d.startswith("v") and d[1:].isdigit())
+        except FileNotFoundError:
+            return []
+        protected = set()
+        store = self.runtime.state_store()
+        for step in store.complete_steps(self.service_name):
+            v = store.payload(self.service_name, step).get("weight_version")
+            if v is not None:
+                protected.add(int(v))
+        stale = [v for v in versions[:-self.weights_keep_latest_k] if v not in protected]
+        for v in stale:
+            shutil.rmtree(os.path.join(wdir, f"v{v}"), ignore_errors=True)
+        return stale
+
+    # ------------------------------------------------------------------ checkpoints
+    def save_global_checkpoint(self, step: int) -> None:
+        store = self.runtime.state_store()
+        self.trainer.save_checkpoint(store.shard_dir(self.service_name, step), step)
+        if self.rank == 0:
+            store.write_meta(self.service_name, step, {"step_index": self.step_index, "weight_version": self.version,
+                                                       "trainer_step": self.trainer.step})
+            store.mark_complete(self.service_name, step)
+            store.prune(self.service_name, self.checkpoint.keep_latest_k)
+        self.barrier()
+
+    def restore_counters(self, resume_step: int) -> None:
+        if resume_step <= 0 or self.runtime is None:
+            return
+        store = self.runtime.state_store()
+        if not store.is_complete(self.service_name, resume_step):
+            if resume_step <= self.cold:  # trainer idle during the critic cold start
+                self.step_index = 0
+                return
+            raise FileNotFoundError(f"no trainer shard at global step {resume_step}")
+        p = store.payload(self.service_name, resume_step)
+        self.trainer.load_checkpoint(store.shard_dir(self.service_name, resume_step))
+        self.step_index = int(p["step_index"])
+        self.version = int(p["weight_version"])
+
+
+__all__ = ["StepResult", "TrainerEngine"]

@@ -34,7 +34,7 @@ class Columns(dict):
 
     @property
     def batch_size(self) -> tuple[int]:
-        n = len(next(iter(self.values()))) if self else 0
+        n = len(next(iter(self.values()))) if dict.__len__(self) else 0
         return (n,)
 
     def __len__(self) -> int:  # number of rows, like TensorDict's batch dim
