@@ -66,6 +66,11 @@ def test_gemm_dgrad_wgrad(T, N, K):
     # A MN-major, B K-major: out[N, K2] = gy^T [N, T] · y[K2, T]^T with y = x^T stored [K2, T]
     y = x.t().contiguous()
     out = torch.empty(N, K, dtype=torch.float32, device=DEV)
+    if (T * 2) % 16 != 0:
+        # a [K2, T] bf16 row of 600 bytes is not a legal TMA stride: the op must refuse, not misread
+        with pytest.raises(RuntimeError, match="multiple of 16 bytes"):
+            C().gemm(gy, y, out, True, False, None, None, None, 0, False, 0)
+        return
     C().gemm(gy, y, out, True, False, None, None, None, 0, False, 0)
     assert rel_err(out, gy.float().t() @ x.float()) < 5e-3
 
