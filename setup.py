@@ -22,6 +22,7 @@ cuda_sources = [
     "csrc/kernels/elementwise.cu",
     "csrc/kernels/attention.cu",
     "csrc/kernels/misc.cu",
+    "csrc/kernels/decode_noalloc.cu",
 ]
 extra_cuda = [s for s in ("csrc/kernels/symm.cu",) if os.path.exists(os.path.join(ROOT, s))]
 
