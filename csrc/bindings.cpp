@@ -368,20 +368,22 @@ void paged_attention_(Tensor q, Tensor kc, Tensor vc, Tensor bt, Tensor seq_lens
                       c10::optional<Tensor> workspace) {
   const c10::cuda::CUDAGuard guard(q.device());
   CHECK_CONTIG(q);
+  CHECK_CONTIG(kc);
+  CHECK_CONTIG(vc);
   TORCH_CHECK(bt.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt, "block table / lens must be int32");
   const int B = q.size(0), Hq = q.size(1), hd = q.size(2), Hkv = kc.size(1), page = kc.size(2);
   const int max_pages = bt.size(1);
-  const int n_split = paged_decode_splits(B, Hkv, max_pages);
+  const int n_split = paged_decode_tma_splits(B, Hkv, max_pages);
   Tensor part;
-  if (n_split > 1) {
+  if (n_split > kMaxClusterSplits) {
     int64_t need = (int64_t)B * Hq * n_split * (hd + 2);
     if (workspace.has_value() && workspace->defined() && workspace->numel() >= need) part = *workspace;
     else part = torch::empty({need}, q.options().dtype(torch::kFloat));
   }
-  paged_decode(ptr<bf16>(q), ptr<bf16>(kc), ptr<bf16>(vc), ptr<int>(bt), ptr<int>(seq_lens), ptr<bf16>(out),
-               n_split > 1 ? ptr<float>(part) : nullptr, B, Hq, Hkv, hd, page, max_pages, n_split, (float)scale,
-               cur_stream());
-  count(n_split > 1 ? 2 : 1);
+  paged_decode_tma(ptr<bf16>(q), ptr<bf16>(kc), ptr<bf16>(vc), (int)kc.size(0), ptr<int>(bt), ptr<int>(seq_lens),
+                   ptr<bf16>(out), part.defined() ? ptr<float>(part) : nullptr, B, Hq, Hkv, hd, page, max_pages,
+                   n_split, (float)scale, ptr<int>(scratch(0, 0).err), cur_stream());
+  count(n_split > kMaxClusterSplits ? 2 : 1);
 }
 
 void decode_advance_(Tensor tok, Tensor lp, Tensor tok_in, Tensor pos, Tensor seq_lens, Tensor gen, Tensor max_new,
@@ -418,6 +420,8 @@ int64_t launch_count() { return g_launches.load(); }
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "meshy_b200 sm_100a kernel library";
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("gemm_small_config", [](int64_t enabled, int64_t cluster) { gemm_small_config((int)enabled, (int)cluster); },
+        "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");
   m.def("swiglu_bwd", &swiglu_bwd_);
   m.def("rmsnorm_fwd", &rmsnorm_fwd_);
   m.def("rmsnorm_bwd", &rmsnorm_bwd_);
@@ -436,6 +440,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gae_scan", &gae_scan_);
   m.def("kv_write", &kv_write_);
   m.def("paged_attention", &paged_attention_);
+  m.def("paged_decode_force_splits", [](int64_t n) { paged_decode_force_splits((int)n); },
+        "decode attention split count override (0 = heuristic); for tests and benchmarks");
   m.def("decode_advance", &decode_advance_);
   m.def("cast_copy", &cast_copy);
   m.def("device_error", &device_error);

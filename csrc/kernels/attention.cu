@@ -822,6 +822,12 @@ void paged_decode(const bf16* q, const bf16* kc, const bf16* vc, const int* bt, 
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 
+void paged_decode_combine(const float* part, bf16* o, int B, int Hq, int hd, int n_split, cudaStream_t st) {
+  if (B == 0) return;
+  paged_decode_combine_kernel<<<B * Hq, 128, 0, st>>>(part, o, Hq, hd, n_split);
+  MESHY_CUDA_CHECK(cudaGetLastError());
+}
+
 void kv_write(const bf16* k, const bf16* v, bf16* kc, bf16* vc, const int64_t* slots, int n, int Hkv, int hd, int page,
               cudaStream_t st) {
   long long total = (long long)n * Hkv * hd / 8;

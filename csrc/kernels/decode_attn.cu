@@ -1,0 +1,400 @@
+// Split-KV paged decode attention with TMA page loads and a cluster reduction.
+//
+// One CTA per (sequence b, KV head hk, split sp). The rep = Hq/Hkv query
+// heads of a KV head form the rows of a 16-row MMA tile, so every K/V page is
+// read once for the whole GQA group.
+//
+//   warp 4     producer: reads the block table and brings each 64-token page
+//              of K and V (one [64, HD] bf16 tile each, contiguous in the
+//              cache) into a STAGES-deep shared-memory ring with 2-D TMA
+//              tiles (128-byte swizzle), completing on an mbarrier;
+//   warps 0-3  consumers: warp w scores keys [16w, 16w+16) of every page
+//              against the query rows (m16n8k16 bf16 MMA, ldmatrix from the
+//              swizzled tile), keeps an online softmax in the exp2 domain and
+//              accumulates P·V; the four warp states merge in shared memory.
+//
+// The n_split CTAs of one (b, hk) form a thread-block cluster along z. Each
+// writes its merged (max, sum, O) to its own shared memory; after a cluster
+// barrier every CTA combines a disjoint slice of the output across all splits
+// through distributed shared memory and writes bf16 O. No global partials and
+// no second kernel. Above kMaxClusterSplits splits the CTAs write partials to
+// a caller-provided fp32 buffer and paged_decode_combine_kernel merges them.
+//
+// Every mbarrier wait is bounded; a CTA that gives up records an error code
+// and still reaches both cluster barriers.
+#include <cuda.h>
+
+#include "../include/common.cuh"
+#include "../include/sm100.cuh"
+#include "attention.h"
+#include "gemm.h"
+
+namespace meshy {
+
+namespace {
+
+constexpr int kPage = 64;
+constexpr int kThreadsDec = 160;
+
+template <int HD>
+struct DCfg {
+  static constexpr int TILE_BYTES = kPage * HD * 2;   // one K or V page of one head
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;  // K + V
+  static constexpr int STAGES = HD == 128 ? 3 : 4;
+  static constexpr int Q_BYTES = 16 * HD * 2;
+  static constexpr int MERGE_BYTES = (128 + 4 * 16 * HD) * 4;   // rm, rl, ro of the 4 warps
+  static constexpr int RED_BYTES = (32 + 16 * HD) * 4;           // cm, cl, co of this CTA
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static_assert(MERGE_BYTES + RED_BYTES <= RING_BYTES, "merge buffers alias the stage ring");
+  static constexpr int SMEM_BYTES = RING_BYTES + Q_BYTES + 1024 + 256;
+};
+
+// Element offset of (row r, column c) in a [64, HD] tile stored as HD/64
+// 128-byte-swizzled [64 rows][64 cols] boxes (the TMA SWIZZLE_128B layout).
+__device__ __forceinline__ int sw128(int r, int c) {
+  return (c >> 6) * (64 * 64) + r * 64 + ((((c & 63) >> 3) ^ (r & 7)) << 3) + (c & 7);
+}
+
+__device__ __forceinline__ void ldsm4(uint32_t* d, const bf16* p) {
+  uint32_t a = smem_u32(p);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+               : "r"(a));
+}
+__device__ __forceinline__ void ldsm4t(uint32_t* d, const bf16* p) {
+  uint32_t a = smem_u32(p);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+               : "r"(a));
+}
+__device__ __forceinline__ void mma_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+constexpr float kLog2eD = 1.4426950408889634f;
+
+template <int HD, bool CLUSTER>
+__global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
+    const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV, const bf16* __restrict__ Q,
+    const int* __restrict__ bt, const int* __restrict__ seq_lens, bf16* __restrict__ O, float* __restrict__ part,
+    int Hq, int Hkv, int max_pages, int n_split, float scale, int* err) {
+  using C = DCfg<HD>;
+  extern __shared__ __align__(1024) uint8_t smraw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  bf16* Qs = reinterpret_cast<bf16*>(ring + C::RING_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::RING_BYTES + C::Q_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + C::STAGES);
+
+  const int b = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
+  const int rep = Hq / Hkv;
+  const int L = seq_lens[b];
+  const int n_pages = (L + kPage - 1) / kPage;
+  const int per = (n_pages + n_split - 1) / n_split;
+  const int p0 = min(n_pages, sp * per), p1 = min(n_pages, p0 + per);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const float sl2 = scale * kLog2eD;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mapK);
+    tma_prefetch_desc(&mapV);
+  }
+  // query rows of this GQA group → Qs[16][HD] (XOR swizzle of 16-byte chunks), rows >= rep zero
+  for (int i = threadIdx.x; i < 16 * HD / 8; i += kThreadsDec) {
+    int r = i / (HD / 8), c = (i % (HD / 8)) * 8;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (r < rep) val = *reinterpret_cast<const uint4*>(Q + ((size_t)b * Hq + hk * rep + r) * HD + c);
+    int ch = (c >> 3) ^ (r & 7);
+    *reinterpret_cast<uint4*>(Qs + r * HD + ch * 8) = val;
+  }
+  __syncthreads();
+
+  float o[HD / 8][4];
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+
+  if (warp == 4) {
+    // ───────────────────────────── producer ─────────────────────────────
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0, last_stage = 0;
+      uint32_t last_phase = 0;
+      for (int pi = p0; pi < p1; ++pi) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+        const int pg = bt[(size_t)b * max_pages + pi];
+        const int row = (pg * Hkv + hk) * kPage;
+        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+        uint8_t* sk = ring + stage * C::STAGE_BYTES;
+#pragma unroll
+        for (int h = 0; h < HD / 64; ++h) {
+          tma_load_2d(sk + h * 8192, &mapK, &full[stage], h * 64, row);
+          tma_load_2d(sk + C::TILE_BYTES + h * 8192, &mapV, &full[stage], h * 64, row);
+        }
+        issued++;
+        last_stage = stage;
+        last_phase = phase;
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (*abort_flag && issued) {
+        long long t0 = clock64();
+        while (!mbar_try_wait(&full[last_stage], last_phase) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {
+    // ───────────────────────────── consumers ────────────────────────────
+    uint32_t qf[HD / 16][4];
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      int r = (lane % 8) + 8 * ((lane / 8) % 2), c = kk * 16 + 8 * (lane / 16);
+      ldsm4(qf[kk], Qs + r * HD + (((c >> 3) ^ (r & 7)) << 3));
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int pi = p0; pi < p1; ++pi) {
+      if (!mbar_wait(&full[stage], phase, abort_flag, err, kErrTimeoutMma)) break;
+      const bf16* Kb = reinterpret_cast<const bf16*>(ring + stage * C::STAGE_BYTES);
+      const bf16* Vb = reinterpret_cast<const bf16*>(ring + stage * C::STAGE_BYTES + C::TILE_BYTES);
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        uint32_t bb[4];
+        int r = warp * 16 + (lane % 8) + 8 * (lane / 16), c = kk * 16 + 8 * ((lane / 8) % 2);
+        ldsm4(bb, Kb + sw128(r, c));
+        mma_16816(sc[0], qf[kk], bb[0], bb[1]);
+        mma_16816(sc[1], qf[kk], bb[2], bb[3]);
+      }
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          int key = pi * kPage + warp * 16 + j * 8 + 2 * (lane % 4) + (t & 1);
+          float v = key < L ? sc[j][t] * sl2 : -INFINITY;
+          sc[j][t] = v;
+          mx[t >> 1] = fmaxf(mx[t >> 1], v);
+        }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      }
+      float alpha[2], mnew[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mnew[r] = fmaxf(m_r[r], mx[r]);
+        alpha[r] = (mnew[r] == -INFINITY) ? 1.f : exp2f(m_r[r] - mnew[r]);
+        m_r[r] = mnew[r];
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float pv = (mnew[t >> 1] == -INFINITY) ? 0.f : exp2f(sc[j][t] - mnew[t >> 1]);
+          sc[j][t] = pv;
+          rs[t >> 1] += pv;
+        }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+        l_r[r] = l_r[r] * alpha[r] + rs[r];
+      }
+#pragma unroll
+      for (int i = 0; i < HD / 8; ++i) {
+        o[i][0] *= alpha[0];
+        o[i][1] *= alpha[0];
+        o[i][2] *= alpha[1];
+        o[i][3] *= alpha[1];
+      }
+      uint32_t pf[4] = {pack_bf16x2(sc[0][0], sc[0][1]), pack_bf16x2(sc[0][2], sc[0][3]),
+                        pack_bf16x2(sc[1][0], sc[1][1]), pack_bf16x2(sc[1][2], sc[1][3])};
+#pragma unroll
+      for (int i = 0; i < HD / 8; i += 2) {
+        uint32_t bb[4];
+        int r = warp * 16 + (lane % 8) + 8 * ((lane / 8) % 2), c = i * 8 + 8 * (lane / 16);
+        ldsm4t(bb, Vb + sw128(r, c));
+        mma_16816(o[i], pf, bb[0], bb[1]);
+        mma_16816(o[i + 1], pf, bb[2], bb[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == C::STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  }
+  __syncthreads();  // every page consumed: the stage ring is free for the merge buffers
+
+  // merge the 4 consumer warps: rows lane/4 (+8)
+  float* rm = reinterpret_cast<float*>(ring);
+  float* rl = rm + 64;
+  float* ro = rm + 128;
+  float* cm = rm + 128 + 4 * 16 * HD;  // this CTA's merged state
+  float* cl = cm + 16;
+  float* co = cm + 32;
+  if (warp < 4) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      int row = lane / 4 + 8 * r;
+      if (lane % 4 == 0) {
+        rm[warp * 16 + row] = m_r[r];
+        rl[warp * 16 + row] = l_r[r];
+      }
+#pragma unroll
+      for (int i = 0; i < HD / 8; ++i) {
+        int c = i * 8 + 2 * (lane % 4);
+        ro[(warp * 16 + row) * HD + c] = o[i][2 * r];
+        ro[(warp * 16 + row) * HD + c + 1] = o[i][2 * r + 1];
+      }
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < rep * HD; idx += kThreadsDec) {
+    int row = idx / HD, c = idx % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, rm[w * 16 + row]);
+    float Ls = 0.f, acc = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      float mw = rm[w * 16 + row];
+      float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      Ls += rl[w * 16 + row] * f;
+      acc += ro[(w * 16 + row) * HD + c] * f;
+    }
+    const int h = hk * rep + row;
+    if (n_split == 1) {
+      O[((size_t)b * Hq + h) * HD + c] = __float2bfloat16(Ls > 0.f ? acc / Ls : 0.f);
+    } else if (CLUSTER) {
+      co[row * HD + c] = acc;
+      if (c == 0) {
+        cm[row] = M;
+        cl[row] = Ls;
+      }
+    } else {
+      float* pp = part + (((size_t)b * Hq + h) * n_split + sp) * (HD + 2);
+      pp[c] = acc;
+      if (c == 0) {
+        pp[HD] = M;
+        pp[HD + 1] = Ls;
+      }
+    }
+  }
+  if constexpr (CLUSTER) {
+    if (n_split > 1) {
+      __syncwarp();
+      cluster_sync_all();
+      const uint32_t base_m = smem_u32(cm), base_l = smem_u32(cl), base_o = smem_u32(co);
+      for (int idx = sp * kThreadsDec + threadIdx.x; idx < rep * HD; idx += n_split * kThreadsDec) {
+        int row = idx / HD, c = idx % HD;
+        float ms[8];
+        float M = -INFINITY;
+        for (int r = 0; r < n_split; ++r) {
+          float v;
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(mapa_shared(base_m + row * 4, r)) : "memory");
+          ms[r] = v;
+          M = fmaxf(M, v);
+        }
+        float Ls = 0.f, acc = 0.f;
+        for (int r = 0; r < n_split; ++r) {
+          float f = (ms[r] == -INFINITY) ? 0.f : exp2f(ms[r] - M);
+          float lv, ov;
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(lv) : "r"(mapa_shared(base_l + row * 4, r)) : "memory");
+          asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                       : "=f"(ov)
+                       : "r"(mapa_shared(base_o + (row * HD + c) * 4, r))
+                       : "memory");
+          Ls += lv * f;
+          acc += ov * f;
+        }
+        O[((size_t)b * Hq + hk * rep + row) * HD + c] = __float2bfloat16(Ls > 0.f ? acc / Ls : 0.f);
+      }
+      __syncwarp();
+      cluster_sync_all();
+    }
+  }
+}
+
+template <int HD, bool CLUSTER>
+void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, const int* bt, const int* seq_lens,
+                bf16* o, float* part, int B, int Hq, int Hkv, int max_pages, int n_split, float scale, int* err,
+                cudaStream_t st) {
+  using C = DCfg<HD>;
+  auto k = paged_decode_tma_kernel<HD, CLUSTER>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(B, Hkv, n_split);
+  cfg.blockDim = dim3(kThreadsDec, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = CLUSTER ? n_split : 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MESHY_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, mk, mv, q, bt, seq_lens, o, part, Hq, Hkv, max_pages, n_split, scale,
+                                      err));
+}
+
+}  // namespace
+
+static int g_force_splits = 0;
+void paged_decode_force_splits(int n) { g_force_splits = n < 0 ? 0 : n; }
+
+int paged_decode_tma_splits(int B, int Hkv, int max_pages) {
+  if (g_force_splits > 0) return std::min(g_force_splits, 64);
+  // at most two CTAs per SM are resident (100 KB of shared memory each at head_dim 128), so
+  // aim for one wave of them; stay within a cluster (no partial buffer) unless that leaves
+  // most SMs idle
+  const int slots = 2 * 148;
+  const int ctas = std::max(1, B * Hkv);
+  int want = std::max(1, slots / ctas);
+  if (want > kMaxClusterSplits && ctas * kMaxClusterSplits >= 148) want = kMaxClusterSplits;
+  return std::max(1, std::min({want, max_pages, 64}));
+}
+
+void paged_decode_tma(const bf16* q, const bf16* kc, const bf16* vc, int n_cache_pages, const int* bt,
+                      const int* seq_lens, bf16* o, float* part, int B, int Hq, int Hkv, int hd, int page,
+                      int max_pages, int n_split, float scale, int* err, cudaStream_t st) {
+  MESHY_CHECK(hd == 64 || hd == 128, "paged_decode: head_dim must be 64 or 128");
+  MESHY_CHECK(page == kPage, "paged_decode: page size must be 64");
+  MESHY_CHECK(Hq % Hkv == 0 && Hq / Hkv <= 16, "paged_decode: at most 16 query heads per KV head");
+  MESHY_CHECK(n_split >= 1, "paged_decode: n_split must be >= 1");
+  const bool cluster = n_split <= kMaxClusterSplits;
+  MESHY_CHECK(cluster || part != nullptr, "paged_decode: more than 8 splits need a partial buffer");
+  if (B == 0) return;
+  const int64_t rows = (int64_t)n_cache_pages * Hkv * kPage;
+  CUtensorMap mk = make_map_bf16(kc, rows, hd, hd, 64, kPage);
+  CUtensorMap mv = make_map_bf16(vc, rows, hd, hd, 64, kPage);
+  if (hd == 128) {
+    if (cluster) launch_dec<128, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, st);
+    else launch_dec<128, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, st);
+  } else {
+    if (cluster) launch_dec<64, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, st);
+    else launch_dec<64, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, st);
+  }
+  if (!cluster) paged_decode_combine(part, o, B, Hq, hd, n_split, st);
+}
+
+}  // namespace meshy

@@ -8,11 +8,12 @@
 // latency-critical decode loop where cudaMalloc's implicit device
 // synchronisation is not acceptable.
 //
-// The regular entry point (meshy::paged_decode, reached from Python through
-// ``meshy_b200._C.paged_attention``) takes its split-KV partial buffer from
-// the caller or from torch.  This one uses a fixed file-scope device array of
-// kPagedDecodeNoAllocScratchBytes instead; every GPU that loads the library
-// keeps that array until the process exits.
+// It runs the split-KV decode kernels of meshy::paged_decode, whose regular
+// entry point takes the partial buffer from the caller.  This one uses a fixed
+// file-scope device array of MESHY_PAGED_DECODE_NOALLOC_SCRATCH_BYTES instead;
+// every GPU that loads the library keeps that array until the process exits.
+// (``meshy_b200._C.paged_attention`` computes the same op with the TMA /
+// cluster-reduction kernel of decode_attn.cu.)
 //
 // Contract:
 //  * All pointers are device pointers on the current device; ``stream`` is a

@@ -265,14 +265,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ncol = min(32, p.N - col0);
           if (p.split_k > 1 && p.epi == EPI_STORE) {
             float* w = p.ws + (size_t)row * p.N + col0;
-            for (int i = 0; i < ncol; ++i) atomicAdd(w + i, v[i]);
+            if (ncol == 32 && (p.N % 4) == 0) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4)
+                atomicAdd(reinterpret_cast<float4*>(w + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+            } else {
+              for (int i = 0; i < ncol; ++i) atomicAdd(w + i, v[i]);
+            }
             continue;
           }
           if (p.epi == EPI_ACC_F32) {
             float* o = reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + col0;
             if (p.split_k > 1) {
-              for (int i = 0; i < ncol; ++i) atomicAdd(o + i, v[i]);
-            } else if (ncol == 32) {
+              if (ncol == 32 && (p.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                  atomicAdd(reinterpret_cast<float4*>(o + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+              } else {
+                for (int i = 0; i < ncol; ++i) atomicAdd(o + i, v[i]);
+              }
+            } else if (ncol == 32 && (p.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) {
 #pragma unroll
               for (int i = 0; i < 32; i += 4) {
                 float4 x = *reinterpret_cast<float4*>(o + i);
@@ -459,12 +471,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         named_bar_sync(1, 128);
         if (*last_flag && row_ok) {
+          // the whole row slice is read with independent 16-byte loads before anything is
+          // written back, so the fix-up costs a few L2 round trips, not one per column
           for (int col0 = n0; col0 < min(n0 + BN, p.N); col0 += 32) {
             const int ncol = min(32, p.N - col0);
             float* w = p.ws + (size_t)row * p.N + col0;
-            for (int i = 0; i < ncol; ++i) {
-              v[i] = __ldcg(w + i);
-              __stcg(w + i, 0.f);
+            const bool vec = ncol == 32 && (p.N % 4) == 0;
+            if (vec) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4) {
+                float4 x = __ldcg(reinterpret_cast<const float4*>(w + i));
+                v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
+              }
+#pragma unroll
+              for (int i = 0; i < 32; i += 4) __stcg(reinterpret_cast<float4*>(w + i), make_float4(0.f, 0.f, 0.f, 0.f));
+            } else {
+              for (int i = 0; i < ncol; ++i) v[i] = __ldcg(w + i);
+              for (int i = 0; i < ncol; ++i) __stcg(w + i, 0.f);
             }
             if (p.bias)
               for (int i = 0; i < ncol; ++i) v[i] += __bfloat162float(p.bias[col0 + i]);
@@ -475,7 +498,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < ncol; ++i) o[i] = v[i];
             } else {
               bf16* o = reinterpret_cast<bf16*>(p.out) + (size_t)row * p.ldo + col0;
-              for (int i = 0; i < ncol; ++i) o[i] = __float2bfloat16(v[i]);
+              if (vec && (p.ldo % 8) == 0) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 8)
+                  *reinterpret_cast<uint4*>(o + i) =
+                      make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                                 pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+              } else {
+                for (int i = 0; i < ncol; ++i) o[i] = __float2bfloat16(v[i]);
+              }
             }
           }
         }
@@ -580,6 +611,15 @@ static void launch_bn(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtenso
 
 void gemm_launch(const GemmProblem& g, cudaStream_t stream) {
   MESHY_CHECK(g.M > 0 && g.N > 0 && g.K > 0, "empty GEMM");
+  if (g.force_bn == 0 && gemm_small_eligible(g)) {
+    gemm_small_launch(g, stream);
+    return;
+  }
+  // the epilogue writes 16-byte vectors of a row (and reads the residual that way)
+  MESHY_CHECK((reinterpret_cast<uintptr_t>(g.out) & 15) == 0 && (g.ldo * (g.out_f32 ? 4 : 2)) % 16 == 0,
+              "gemm: output rows must start on 16-byte boundaries");
+  MESHY_CHECK(!g.residual || ((reinterpret_cast<uintptr_t>(g.residual) & 15) == 0 && (g.ldr * 2) % 16 == 0),
+              "gemm: residual rows must start on 16-byte boundaries");
   int BN = g.force_bn;
   const int sms = num_sms();
   const int m_tiles = (g.M + BM - 1) / BM;

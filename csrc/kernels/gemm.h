@@ -40,9 +40,19 @@ struct GemmProblem {
   int* err = nullptr;         // device error word
   int force_bn = 0;           // 0 = heuristic
   int max_split = 0;          // 0 = heuristic
+  int force_cs = 0;           // small-M path: cluster split-K size (0 = heuristic)
 };
 
 void gemm_launch(const GemmProblem& g, cudaStream_t stream);
+
+// Small-M (decode) path, gemm_small.cu: TN problems with M <= kSmallMaxM and a
+// STORE or SwiGLU epilogue run with swapped operands and cluster split-K.
+constexpr int kSmallMaxM = 256;
+constexpr int kSmallMaxCluster = 8;
+bool gemm_small_eligible(const GemmProblem& g);
+void gemm_small_launch(const GemmProblem& g, cudaStream_t stream);
+// enabled: 1/0 (-1 keeps); force_cs: cluster size override, 0 = heuristic (-1 keeps)
+void gemm_small_config(int enabled, int force_cs);
 CUtensorMap make_map_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int bi, int bo);
 int gemm_n_tiles(int N, int bn);
 

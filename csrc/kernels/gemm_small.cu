@@ -1,0 +1,487 @@
+// Small-M GEMM for sm_100a (decode-time linears):
+//
+//   out[M, N] = X[M, K] · W[N, K]^T (+bias[n]) (+residual[m, n]),  M <= 256
+//
+// At decode M is the number of running sequences (8-256) while N and K are
+// model dimensions, so the op streams the weight once and is bound by HBM.
+// With the regular 128-row MMA tile the token dimension would fill at most
+// half of the M=128 MMA, and the few N tiles of a narrow projection (QKV,
+// o_proj, down_proj: 12-16 tiles of 128) would leave most SMs idle.  Here the
+// operands are swapped: the MMA computes D^T[n, m] = W[n, :] · X[m, :]^T with
+// the weight rows as the 128-lane MMA M dimension and the (padded) token count
+// MP as the MMA N dimension, so every MMA is full and the accumulator is only
+// MP TMEM columns wide.
+//
+// Two schedules:
+//  * split-K over a thread-block cluster (n_tiles <= #SMs): cluster (cs,1,1)
+//    of CTAs shares one 128-row weight tile and splits K cs ways.  Each CTA
+//    drains its fp32 partial from TMEM into its own shared memory; after a
+//    cluster barrier every CTA sums a disjoint set of token columns across all
+//    cs partials through distributed shared memory (ld.shared::cluster) and
+//    applies the epilogue.  No global workspace, no atomics, no second kernel.
+//  * persistent (n_tiles > #SMs, e.g. a 152k-row LM head): one CTA per SM
+//    walks the N tiles with two TMEM accumulators, so the epilogue of one tile
+//    overlaps the MMAs of the next.
+//
+// Roles (192 threads): warp 0 TMA producer, warp 1 TMEM allocator + single
+// thread MMA issuer, warps 2-5 epilogue (warp w owns TMEM lanes 32*(w%4)...).
+// Every mbarrier wait is bounded; on a timeout the kernel records an error
+// code and still reaches both cluster barriers, so no CTA of a cluster waits
+// on one that left.
+#include <cuda.h>
+
+#include <cstdlib>
+
+#include "../include/common.cuh"
+#include "../include/sm100.cuh"
+#include "gemm.h"
+
+namespace meshy {
+
+namespace {
+
+constexpr int SBK = 64;
+constexpr int kSmallThreads = 192;
+constexpr int W_TILE_BYTES = 128 * SBK * 2;
+
+struct SmallArgs {
+  int M, N, K;
+  int n_tiles, k_blocks, kb_per, cs;
+  int epi;
+  void* out;
+  int ldo;
+  int out_f32;
+  const bf16* bias;
+  const bf16* residual;
+  int ldr;
+  int* err;
+};
+
+template <int MP, bool PERSIST>
+struct SCfg {
+  static constexpr int X_TILE_BYTES = MP * SBK * 2;
+  static constexpr int STAGE_BYTES = W_TILE_BYTES + X_TILE_BYTES;
+  static constexpr int STAGES_FIT = (192 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int N_ACC = PERSIST ? 2 : 1;
+  static constexpr int TMEM_COLS = (N_ACC * MP < 32) ? 32 : N_ACC * MP;
+  static constexpr int RED_BYTES = 128 * MP * 4;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "reduction buffer must fit in the stage ring");
+  static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
+};
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// Load 32 (or 16 for MP == 16) accumulator columns starting at ``col`` for this thread's TMEM lane.
+template <int MP>
+__device__ __forceinline__ void ld_cols(uint32_t taddr, float* v) {
+  if constexpr (MP == 16) tmem_ld16(taddr, v);
+  else tmem_ld32(taddr, v);
+}
+
+__device__ __forceinline__ void store_val(const SmallArgs& p, int m, int n, float x) {
+  if (p.bias) x += __bfloat162float(p.bias[n]);
+  if (p.residual) x += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
+  if (p.out_f32) reinterpret_cast<float*>(p.out)[(size_t)m * p.ldo + n] = x;
+  else reinterpret_cast<bf16*>(p.out)[(size_t)m * p.ldo + n] = __float2bfloat16(x);
+}
+
+template <int MP, bool PERSIST>
+__global__ void __launch_bounds__(kSmallThreads, 1)
+    gemm_small_kernel(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapX,
+                      SmallArgs p) {
+  using C = SCfg<MP, PERSIST>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = PERSIST ? 0u : cluster_ctarank();
+  const int first = blockIdx.x / p.cs, stride = gridDim.x / p.cs;
+  const int kb0 = (int)rank * p.kb_per, kb1 = min(p.k_blocks, kb0 + p.kb_per);
+  const bool has_k = kb1 > kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mapW);
+    tma_prefetch_desc(&mapX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ─────────────────────────────── TMA producer ───────────────────────────────
+    if (lane == 0 && has_k) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0, last_stage = 0;
+      uint32_t last_phase = 0;
+      for (int nt = first; nt < p.n_tiles && !*abort_flag; nt += stride) {
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          uint8_t* sw = smem + stage * C::STAGE_BYTES;
+          tma_load_2d(sw, &mapW, &full[stage], kb * SBK, nt * 128);
+          tma_load_2d(sw + W_TILE_BYTES, &mapX, &full[stage], kb * SBK, 0);
+          issued++;
+          last_stage = stage;
+          last_phase = phase;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag && issued) {
+        long long t0 = clock64();
+        while (!mbar_try_wait(&full[last_stage], last_phase) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ─────────────────────────────── MMA issuer ─────────────────────────────────
+    if (lane == 0 && has_k) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, MP, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool any = false;
+      for (int nt = first; nt < p.n_tiles && !*abort_flag; nt += stride) {
+        if (PERSIST && !mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * MP;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sw = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sx = sw + W_TILE_BYTES;
+#pragma unroll
+          for (int k = 0; k < SBK / 16; ++k) {
+            mma_bf16(d_tmem, smem_desc_sw128(sw + k * 32, 16, 1024), smem_desc_sw128(sx + k * 32, 16, 1024), idesc,
+                     (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          any = true;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (PERSIST && ++acc == C::N_ACC) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (any) {
+        mma_commit(drain);
+        long long t0 = clock64();
+        while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {
+    // ─────────────────────────────── epilogue ───────────────────────────────────
+    const int q = warp & 3;
+    const int f = q * 32 + lane;  // weight row within the tile = TMEM lane
+    const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
+    constexpr int CH = MP < 32 ? MP : 32;
+    if constexpr (PERSIST) {
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int nt = first; nt < p.n_tiles; nt += stride) {
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        tc_fence_after();
+        const int n = nt * 128 + f;
+        float v[32];
+#pragma unroll 1
+        for (int c = 0; c < MP / CH; ++c) {
+          ld_cols<MP>(t_lane + acc * MP + c * CH, v);
+          if (n < p.N) {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+              const int m = c * CH + i;
+              if (m < p.M) store_val(p, m, n, v[i]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        if (++acc == C::N_ACC) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    } else {
+      // drain this CTA's partial into the (now idle) stage ring: layout [MP/4][128][4] fp32
+      float* red = reinterpret_cast<float*>(smem);
+      bool ok = true;
+      if (has_k) {
+        ok = mbar_wait(&tfull[0], 0, abort_flag, p.err, kErrTimeoutEpilogue);
+        tc_fence_after();
+      }
+      float v[32];
+#pragma unroll 1
+      for (int c = 0; c < MP / CH; ++c) {
+        if (has_k && ok) {
+          ld_cols<MP>(t_lane + c * CH, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < CH; i += 4) {
+          const int g = (c * CH + i) / 4;
+          *reinterpret_cast<float4*>(red + ((size_t)g * 128 + f) * 4) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
+      }
+      tc_fence_before();
+    }
+  }
+
+  if constexpr (!PERSIST) {
+    __syncwarp();
+    cluster_sync_all();  // every partial of the cluster is in shared memory
+    if (warp >= 2) {
+      const int q = warp & 3;
+      const int f = q * 32 + lane;
+      const int nt = first;
+      const uint32_t red_addr = smem_u32(smem);
+      const bool swiglu = p.epi == EPI_SWIGLU;
+      constexpr int G = MP / 4;
+      for (int g = (int)rank; g < G; g += p.cs) {
+        if (4 * g >= p.M) break;
+        if (swiglu && f >= 64) break;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
+        const uint32_t off_a = red_addr + (uint32_t)((g * 128 + f) * 16);
+        const uint32_t off_b = red_addr + (uint32_t)((g * 128 + f + 64) * 16);
+        for (int r = 0; r < p.cs; ++r) {
+          float4 x = ld_dsmem_f4(mapa_shared(off_a, (uint32_t)r));
+          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+          if (swiglu) {
+            float4 y = ld_dsmem_f4(mapa_shared(off_b, (uint32_t)r));
+            b.x += y.x; b.y += y.y; b.z += y.z; b.w += y.w;
+          }
+        }
+        const float av[4] = {a.x, a.y, a.z, a.w};
+        const float bv[4] = {b.x, b.y, b.z, b.w};
+        if (!swiglu) {
+          const int n = nt * 128 + f;
+          if (n < p.N) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (4 * g + i < p.M) store_val(p, 4 * g + i, n, av[i]);
+          }
+        } else {
+          // rows [128 nt, 128 nt + 64) are gate, the next 64 the matching up rows
+          const int n = nt * 64 + f;
+          bf16* o = reinterpret_cast<bf16*>(p.out);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = 4 * g + i;
+            if (m >= p.M) break;
+            // round the pre-activations to bf16 as the regular GEMM epilogue does
+            float gg = __bfloat162float(__float2bfloat16(av[i]));
+            float uu = __bfloat162float(__float2bfloat16(bv[i]));
+            o[(size_t)m * p.ldo + n] = __float2bfloat16(silu_f(gg) * uu);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    MESHY_CUDA_CHECK(cudaGetDevice(&dev));
+    MESHY_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return n;
+}
+
+template <int MP, bool PERSIST>
+void launch_small(const CUtensorMap& mw, const CUtensorMap& mx, const SmallArgs& a, int grid, int cs,
+                  cudaStream_t st) {
+  using C = SCfg<MP, PERSIST>;
+  auto k = gemm_small_kernel<MP, PERSIST>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kSmallThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MESHY_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, mw, mx, a));
+}
+
+// How many clusters of ``cs`` CTAs of this kernel can be resident at once (GPC limits).
+template <int MP>
+int max_active_clusters(int cs) {
+  using C = SCfg<MP, false>;
+  static int cache[kSmallMaxCluster + 1] = {};
+  if (cache[cs]) return cache[cs];
+  auto k = gemm_small_kernel<MP, false>;
+  MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cs * 64, 1, 1);
+  cfg.blockDim = dim3(kSmallThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    n = sm_count() / cs;
+  }
+  cache[cs] = n;
+  return n;
+}
+
+int max_clusters_mp(int MP, int cs) {
+  switch (MP) {
+    case 16: return max_active_clusters<16>(cs);
+    case 32: return max_active_clusters<32>(cs);
+    case 64: return max_active_clusters<64>(cs);
+    case 128: return max_active_clusters<128>(cs);
+    default: return max_active_clusters<256>(cs);
+  }
+}
+
+template <bool PERSIST>
+void launch_mp(int MP, const CUtensorMap& mw, const CUtensorMap& mx, const SmallArgs& a, int grid, int cs,
+               cudaStream_t st) {
+  switch (MP) {
+    case 16: launch_small<16, PERSIST>(mw, mx, a, grid, cs, st); break;
+    case 32: launch_small<32, PERSIST>(mw, mx, a, grid, cs, st); break;
+    case 64: launch_small<64, PERSIST>(mw, mx, a, grid, cs, st); break;
+    case 128: launch_small<128, PERSIST>(mw, mx, a, grid, cs, st); break;
+    default: launch_small<256, PERSIST>(mw, mx, a, grid, cs, st); break;
+  }
+}
+
+// Process-wide switches (tests and the op benchmark compare schedules with them).
+int g_small_enabled = -1;  // -1: from MESHY_GEMM_SMALL_M (default on)
+int g_small_force_cs = 0;
+
+bool small_enabled() {
+  if (g_small_enabled < 0) {
+    const char* e = std::getenv("MESHY_GEMM_SMALL_M");
+    g_small_enabled = (e && e[0] == '0') ? 0 : 1;
+  }
+  return g_small_enabled == 1;
+}
+
+}  // namespace
+
+void gemm_small_config(int enabled, int force_cs) {
+  if (enabled >= 0) g_small_enabled = enabled ? 1 : 0;
+  if (force_cs >= 0) g_small_force_cs = force_cs;
+}
+
+bool gemm_small_eligible(const GemmProblem& g) {
+  if (!small_enabled()) return false;
+  if (g.a_mn || g.b_mn || g.M > kSmallMaxM || g.M <= 0) return false;
+  if (g.epi != EPI_STORE && g.epi != EPI_SWIGLU) return false;
+  const int n_tiles = (g.N + 127) / 128;
+  if (g.epi == EPI_SWIGLU) {
+    // above 128 tokens the regular 128 x 256 tiling fills its MMA and wins
+    if (g.aux != nullptr || g.N % 128 != 0 || g.out_f32 || g.M > 128 || n_tiles > sm_count()) return false;
+  }
+  // the persistent schedule stores 2-byte scalars per token column; above 64 tokens the
+  // regular tiling writes the output faster
+  if (n_tiles > sm_count() && g.M > 64) return false;
+  return true;
+}
+
+void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
+  MESHY_CHECK(gemm_small_eligible(g), "gemm_small: problem not eligible");
+  const int MP = g.M <= 16 ? 16 : g.M <= 32 ? 32 : g.M <= 64 ? 64 : g.M <= 128 ? 128 : 256;
+  SmallArgs a{};
+  a.M = g.M; a.N = g.N; a.K = g.K;
+  a.n_tiles = (g.N + 127) / 128;
+  a.k_blocks = (g.K + SBK - 1) / SBK;
+  a.epi = g.epi;
+  a.out = g.out; a.ldo = g.ldo; a.out_f32 = g.out_f32;
+  a.bias = g.bias; a.residual = g.residual; a.ldr = g.ldr;
+  a.err = g.err;
+  const int sms = sm_count();
+  CUtensorMap mw = make_map_bf16(g.B, g.N, g.K, g.ldb, SBK, 128);
+  CUtensorMap mx = make_map_bf16(g.A, g.M, g.K, g.lda, SBK, MP);
+  if (a.n_tiles <= sms) {
+    // largest split whose clusters all fit in one wave (clusters are placed per GPC, so fewer
+    // than sms / cs of them may be resident)
+    int cs = 1;
+    for (int c = std::min(kSmallMaxCluster, a.k_blocks); c >= 2; --c) {
+      if (a.n_tiles * c <= sms && a.n_tiles <= max_clusters_mp(MP, c)) {
+        cs = c;
+        break;
+      }
+    }
+    const int want = g.force_cs > 0 ? g.force_cs : g_small_force_cs;
+    if (want > 0) cs = std::max(1, std::min({want, kSmallMaxCluster, a.k_blocks}));
+    a.kb_per = (a.k_blocks + cs - 1) / cs;
+    cs = (a.k_blocks + a.kb_per - 1) / a.kb_per;  // every rank gets at least one k-block
+    a.cs = cs;
+    launch_mp<false>(MP, mw, mx, a, a.n_tiles * cs, cs, st);
+  } else {
+    a.cs = 1;
+    a.kb_per = a.k_blocks;
+    launch_mp<true>(MP, mw, mx, a, sms, 1, st);
+  }
+}
+
+}  // namespace meshy

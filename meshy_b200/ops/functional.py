@@ -120,8 +120,8 @@ class _LinearSwiGLU(torch.autograd.Function):
         C = ext()
         x2 = x.reshape(-1, x.shape[-1])
         T = x2.shape[0]
-        h = torch.empty(T, w13.shape[0], dtype=x.dtype, device=x.device)
         a = torch.empty(T, w13.shape[0] // 2, dtype=x.dtype, device=x.device)
+        h = torch.empty(T, w13.shape[0], dtype=x.dtype, device=x.device)
         C.gemm(x2, w13, a, False, False, None, None, h, EPI_SWIGLU, False, block)
         ctx.save_for_backward(x2, w13, h)
         ctx.block = block
@@ -144,7 +144,13 @@ class _LinearSwiGLU(torch.autograd.Function):
 def linear_swiglu(x, w13, block: int):
     """``silu(x Wg^T) * (x Wu^T)`` with the block-interleaved fused weight."""
     if native(x):
-        return _LinearSwiGLU.apply(x, w13, block)
+        if torch.is_grad_enabled() and (x.requires_grad or w13.requires_grad):
+            return _LinearSwiGLU.apply(x, w13, block)
+        # inference: the pre-activation is only needed by backward, so it is never written
+        x2 = x.reshape(-1, x.shape[-1])
+        a = torch.empty(x2.shape[0], w13.shape[0] // 2, dtype=x.dtype, device=x.device)
+        ext().gemm(x2, w13, a, False, False, None, None, None, EPI_SWIGLU, False, block)
+        return a.reshape(*x.shape[:-1], a.shape[-1])
     return ref.swiglu(F.linear(x, w13), block)
 
 

