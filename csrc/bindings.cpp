@@ -183,6 +183,24 @@ void qkv_rope_fwd_(Tensor qkv, Tensor pos, c10::optional<Tensor> qn, c10::option
   count();
 }
 
+// decode / prefill: rope'd q out, K and V straight into the paged cache (and optionally k / v tensors)
+void qkv_rope_cache_(Tensor qkv, Tensor pos, c10::optional<Tensor> qn, c10::optional<Tensor> kn, Tensor q,
+                     c10::optional<Tensor> k, c10::optional<Tensor> v, Tensor kc, Tensor vc, Tensor slots, double theta,
+                     double eps) {
+  CHECK_CONTIG(qkv);
+  CHECK_CONTIG(kc);
+  CHECK_CONTIG(vc);
+  TORCH_CHECK(pos.scalar_type() == at::kInt, "positions must be int32");
+  TORCH_CHECK(slots.scalar_type() == at::kLong, "slot map must be int64");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  int T = q.size(0), Hq = q.size(1), hd = q.size(2), Hkv = kc.size(1);
+  Tensor inv = inv_freq_table(hd, theta, qkv.device());
+  qkv_rope_fwd(ptr<bf16>(qkv), ptr<int>(pos), optr<bf16>(qn), optr<bf16>(kn), ptr<float>(inv), ptr<bf16>(q),
+               optr<bf16>(k), optr<bf16>(v), T, Hq, Hkv, hd, (float)eps, cur_stream(), ptr<bf16>(kc), ptr<bf16>(vc),
+               ptr<int64_t>(slots), (int)kc.size(2));
+  count();
+}
+
 void qkv_rope_bwd_(Tensor qkv, Tensor pos, c10::optional<Tensor> qn, c10::optional<Tensor> kn, Tensor gq, Tensor gk,
                    Tensor gv, Tensor gqkv, c10::optional<Tensor> gqn, c10::optional<Tensor> gkn, double theta,
                    double eps) {
@@ -427,6 +445,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bwd", &rmsnorm_bwd_);
   m.def("qkv_rope_fwd", &qkv_rope_fwd_);
   m.def("qkv_rope_bwd", &qkv_rope_bwd_);
+  m.def("qkv_rope_cache", &qkv_rope_cache_, "QK-norm + RoPE with K/V written straight into the paged cache");
   m.def("flash_attn_fwd", &flash_attn_fwd_);
   m.def("flash_attn_bwd", &flash_attn_bwd_);
   m.def("lmhead_logprob_fwd", &lmhead_logprob_fwd);

@@ -370,7 +370,9 @@ int paged_decode_tma_splits(int B, int Hkv, int max_pages) {
   const int slots = 2 * 148;
   const int ctas = std::max(1, B * Hkv);
   int want = std::max(1, slots / ctas);
-  if (want > kMaxClusterSplits && ctas * kMaxClusterSplits >= 148) want = kMaxClusterSplits;
+  // a merge kernel costs more than the idle SMs of a cluster-capped grid unless fewer than half
+  // of the SMs would get a CTA
+  if (want > kMaxClusterSplits && ctas * kMaxClusterSplits >= 74) want = kMaxClusterSplits;
   return std::max(1, std::min({want, max_pages, 64}));
 }
 

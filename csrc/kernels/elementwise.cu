@@ -177,13 +177,20 @@ void rmsnorm_bwd(const bf16* gy, const bf16* x, const bf16* w, const float* rstd
 __global__ void qkv_rope_fwd_kernel(const bf16* __restrict__ qkv, const int* __restrict__ pos,
                                     const bf16* __restrict__ qn, const bf16* __restrict__ kn,
                                     const float* __restrict__ inv_freq, bf16* __restrict__ q, bf16* __restrict__ k,
-                                    bf16* __restrict__ v, int T, int Hq, int Hkv, int hd, float eps) {
+                                    bf16* __restrict__ v, int T, int Hq, int Hkv, int hd, float eps,
+                                    bf16* __restrict__ kc, bf16* __restrict__ vc, const int64_t* __restrict__ slots,
+                                    int page) {
   const int H = Hq + 2 * Hkv;
   const int lane = threadIdx.x % 32;
   const long long gw = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (gw >= (long long)T * H) return;
   const int t = (int)(gw / H), h = (int)(gw % H);
   const int half = hd / 2;
+  // paged-cache row of this token for head hh: [n_pages, Hkv, page, hd]
+  auto cache_row = [&](bf16* base, int hh) -> bf16* {
+    const int64_t slot = slots[t];
+    return base + (((size_t)(slot / page) * Hkv + hh) * page + (size_t)(slot % page)) * hd;
+  };
   const bf16* src = qkv + (size_t)t * H * hd + (size_t)h * hd;
   const int i0 = 2 * lane;
   const bool act = i0 < half;
@@ -193,11 +200,19 @@ __global__ void qkv_rope_fwd_kernel(const bf16* __restrict__ qkv, const int* __r
     float2 fb = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src + i0 + half));
     a0 = fa.x; a1 = fa.y; b0 = fb.x; b1 = fb.y;
   }
-  if (h >= Hq + Hkv) {  // V: plain copy
+  if (h >= Hq + Hkv) {  // V: plain copy (to the v tensor and/or the paged cache)
     if (act) {
-      bf16* dst = v + ((size_t)t * Hkv + (h - Hq - Hkv)) * hd;
-      *reinterpret_cast<uint32_t*>(dst + i0) = pack_bf16x2(a0, a1);
-      *reinterpret_cast<uint32_t*>(dst + i0 + half) = pack_bf16x2(b0, b1);
+      const uint32_t lo = pack_bf16x2(a0, a1), hi = pack_bf16x2(b0, b1);
+      if (v) {
+        bf16* dst = v + ((size_t)t * Hkv + (h - Hq - Hkv)) * hd;
+        *reinterpret_cast<uint32_t*>(dst + i0) = lo;
+        *reinterpret_cast<uint32_t*>(dst + i0 + half) = hi;
+      }
+      if (vc) {
+        bf16* dst = cache_row(vc, h - Hq - Hkv);
+        *reinterpret_cast<uint32_t*>(dst + i0) = lo;
+        *reinterpret_cast<uint32_t*>(dst + i0 + half) = hi;
+      }
     }
     return;
   }
@@ -221,9 +236,17 @@ __global__ void qkv_rope_fwd_kernel(const bf16* __restrict__ qkv, const int* __r
   sincosf(p * inv_freq[i0 + 1], &s1, &c1);
   float o_a0 = a0 * c0 - b0 * s0, o_b0 = b0 * c0 + a0 * s0;
   float o_a1 = a1 * c1 - b1 * s1, o_b1 = b1 * c1 + a1 * s1;
-  bf16* dst = is_q ? q + ((size_t)t * Hq + h) * hd : k + ((size_t)t * Hkv + (h - Hq)) * hd;
-  *reinterpret_cast<uint32_t*>(dst + i0) = pack_bf16x2(o_a0, o_a1);
-  *reinterpret_cast<uint32_t*>(dst + i0 + half) = pack_bf16x2(o_b0, o_b1);
+  const uint32_t lo = pack_bf16x2(o_a0, o_a1), hi = pack_bf16x2(o_b0, o_b1);
+  bf16* dst = is_q ? q + ((size_t)t * Hq + h) * hd : (k ? k + ((size_t)t * Hkv + (h - Hq)) * hd : nullptr);
+  if (dst) {
+    *reinterpret_cast<uint32_t*>(dst + i0) = lo;
+    *reinterpret_cast<uint32_t*>(dst + i0 + half) = hi;
+  }
+  if (!is_q && kc) {
+    bf16* c = cache_row(kc, h - Hq);
+    *reinterpret_cast<uint32_t*>(c + i0) = lo;
+    *reinterpret_cast<uint32_t*>(c + i0 + half) = hi;
+  }
 }
 
 __global__ void qkv_rope_bwd_kernel(const bf16* __restrict__ qkv, const int* __restrict__ pos,
@@ -300,12 +323,17 @@ __global__ void qkv_rope_bwd_kernel(const bf16* __restrict__ qkv, const int* __r
 }
 
 void qkv_rope_fwd(const bf16* qkv, const int* pos, const bf16* qn, const bf16* kn, const float* inv_freq, bf16* q,
-                  bf16* k, bf16* v, int T, int Hq, int Hkv, int hd, float eps, cudaStream_t st) {
+                  bf16* k, bf16* v, int T, int Hq, int Hkv, int hd, float eps, cudaStream_t st, bf16* kc, bf16* vc,
+                  const int64_t* slots, int page) {
   MESHY_CHECK(hd % 4 == 0 && hd <= 128, "qkv_rope: head_dim must be <= 128 and a multiple of 4");
+  MESHY_CHECK((kc == nullptr) == (vc == nullptr) && (kc == nullptr || (slots != nullptr && page > 0)),
+              "qkv_rope: cache write needs both caches, the slot map and the page size");
+  MESHY_CHECK((k != nullptr || kc != nullptr) && (v != nullptr || vc != nullptr), "qkv_rope: K/V have no destination");
   long long warps = (long long)T * (Hq + 2 * Hkv);
   int grid = (int)((warps + 7) / 8);
   if (grid == 0) return;
-  qkv_rope_fwd_kernel<<<grid, 256, 0, st>>>(qkv, pos, qn, kn, inv_freq, q, k, v, T, Hq, Hkv, hd, eps);
+  qkv_rope_fwd_kernel<<<grid, 256, 0, st>>>(qkv, pos, qn, kn, inv_freq, q, k, v, T, Hq, Hkv, hd, eps, kc, vc, slots,
+                                            page);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -48,7 +48,7 @@ void gemm_launch(const GemmProblem& g, cudaStream_t stream);
 // Small-M (decode) path, gemm_small.cu: TN problems with M <= kSmallMaxM and a
 // STORE or SwiGLU epilogue run with swapped operands and cluster split-K.
 constexpr int kSmallMaxM = 256;
-constexpr int kSmallMaxCluster = 8;
+constexpr int kSmallMaxCluster = 16;  // above 8 the kernel opts in to non-portable cluster sizes
 bool gemm_small_eligible(const GemmProblem& g);
 void gemm_small_launch(const GemmProblem& g, cudaStream_t stream);
 // enabled: 1/0 (-1 keeps); force_cs: cluster size override, 0 = heuristic (-1 keeps)

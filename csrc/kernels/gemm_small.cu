@@ -285,12 +285,23 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
         const uint32_t off_a = red_addr + (uint32_t)((g * 128 + f) * 16);
         const uint32_t off_b = red_addr + (uint32_t)((g * 128 + f + 64) * 16);
-        for (int r = 0; r < p.cs; ++r) {
-          float4 x = ld_dsmem_f4(mapa_shared(off_a, (uint32_t)r));
-          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
-          if (swiglu) {
-            float4 y = ld_dsmem_f4(mapa_shared(off_b, (uint32_t)r));
-            b.x += y.x; b.y += y.y; b.z += y.z; b.w += y.w;
+        // issue the peers' loads in batches before summing, so the DSMEM latency is paid once
+        // per batch instead of once per peer
+        for (int r0 = 0; r0 < p.cs; r0 += 4) {
+          float4 xa[4], xb[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (r0 + j < p.cs) {
+              xa[j] = ld_dsmem_f4(mapa_shared(off_a, (uint32_t)(r0 + j)));
+              if (swiglu) xb[j] = ld_dsmem_f4(mapa_shared(off_b, (uint32_t)(r0 + j)));
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (r0 + j < p.cs) {
+              a.x += xa[j].x; a.y += xa[j].y; a.z += xa[j].z; a.w += xa[j].w;
+              if (swiglu) { b.x += xb[j].x; b.y += xb[j].y; b.z += xb[j].z; b.w += xb[j].w; }
+            }
           }
         }
         const float av[4] = {a.x, a.y, a.z, a.w};
@@ -346,6 +357,7 @@ void launch_small(const CUtensorMap& mw, const CUtensorMap& mx, const SmallArgs&
   static bool attr_set = false;
   if (!attr_set) {
     MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -371,6 +383,7 @@ int max_active_clusters(int cs) {
   if (cache[cs]) return cache[cs];
   auto k = gemm_small_kernel<MP, false>;
   MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+  MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs * 64, 1, 1);
   cfg.blockDim = dim3(kSmallThreads, 1, 1);

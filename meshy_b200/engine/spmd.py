@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import logging
 import os
+import threading
 from datetime import timedelta
 from typing import Any
 
@@ -37,6 +38,9 @@ class SpmdEngine:
         self.control_group = None
         self.compute_group = None
         self._running = False
+        # rank 0 submits from the worker thread and from the colocation manager's callbacks; one
+        # lock keeps the broadcast order (and so the collective order) identical on every rank
+        self._cmd_lock = threading.Lock()
 
     def init_process_group(self) -> None:
         for v in _ELASTIC_VARS:
@@ -54,7 +58,8 @@ class SpmdEngine:
     def submit_command(self, name: str, payload: Any = None) -> Any:
         if self.rank != 0:
             raise RuntimeError("only rank 0 submits commands")
-        return self._broadcast_and_run([name, payload])
+        with self._cmd_lock:
+            return self._broadcast_and_run([name, payload])
 
     def _broadcast_and_run(self, obj) -> Any:
         if self.world_size > 1:
@@ -72,9 +77,14 @@ class SpmdEngine:
         while self._running:
             self._broadcast_and_run([None, None])
 
+    def setup(self) -> None:
+        if self.world_size > 1 and not dist.is_initialized():
+            self.init_process_group()
+
     def stop(self) -> None:
         if self.rank == 0 and self.world_size > 1:
-            self._broadcast_and_run(["__stop__", None])
+            with self._cmd_lock:
+                self._broadcast_and_run(["__stop__", None])
 
     def barrier(self) -> None:
         if self.world_size > 1:

@@ -97,6 +97,13 @@ class TrainerEngine(SpmdEngine):
                 self.save_global_checkpoint(self.global_step)
         return res
 
+    # colocation ring callbacks (rank 0, manager thread): every rank changes residency together
+    def on_colocate_acquire(self, grant) -> None:
+        self.restore()
+
+    def on_colocate_release(self, target: str) -> None:
+        self.offload()
+
     def cmd_offload(self, payload) -> None:
         self.trainer.offload_to_cpu()
 

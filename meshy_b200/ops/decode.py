@@ -1,6 +1,8 @@
 """Inference-side ops of the rollout engine (no autograd).
 
 * :func:`kv_write` — scatter this step's K/V rows into the paged cache.
+* :func:`qkv_rope_to_cache` — QK-norm + RoPE with the K/V rows written
+  straight into the paged cache (one kernel).
 * :func:`paged_attention` — decode attention over the paged KV cache
   (split-KV flash-decode kernel on CUDA; GQA heads of one KV head share the
   K/V stream).
@@ -37,6 +39,30 @@ def kv_write(k, v, k_cache, v_cache, slot_mapping):
     off = (slot_mapping % page).long()
     k_cache[pg, :, off] = k.to(k_cache.dtype)
     v_cache[pg, :, off] = v.to(v_cache.dtype)
+
+
+def qkv_rope_to_cache(qkv, positions, q_norm, k_norm, n_heads, n_kv, hd, theta, eps, k_cache, v_cache,
+                      slot_mapping, *, keep_kv: bool = False):
+    """QK-norm + RoPE of a fused ``qkv [T, (Hq + 2 Hkv) hd]`` row block with K and V written straight
+    into the paged cache at ``slot_mapping`` (one kernel instead of rope + scatter).
+
+    Returns ``q [T, Hq, hd]`` and, with ``keep_kv`` (prefill needs them for attention), ``k, v``.
+    """
+    T = qkv.shape[0]
+    if native(qkv):
+        from ._ext import ext
+
+        q = torch.empty(T, n_heads, hd, dtype=qkv.dtype, device=qkv.device)
+        k = torch.empty(T, n_kv, hd, dtype=qkv.dtype, device=qkv.device) if keep_kv else None
+        v = torch.empty(T, n_kv, hd, dtype=qkv.dtype, device=qkv.device) if keep_kv else None
+        ext().qkv_rope_cache(qkv, positions, q_norm, k_norm, q, k, v, k_cache, v_cache, slot_mapping, float(theta),
+                             float(eps))
+        return (q, k, v) if keep_kv else (q, None, None)
+    from .functional import qkv_rope
+
+    q, k, v = qkv_rope(qkv, positions, q_norm, k_norm, n_heads, n_kv, hd, theta, eps)
+    kv_write(k, v, k_cache, v_cache, slot_mapping)
+    return (q, k, v) if keep_kv else (q, None, None)
 
 
 def paged_attention(q, k_cache, v_cache, block_table, seq_lens, scale=None, workspace=None):
@@ -105,4 +131,4 @@ def decode_advance(state: dict, tok, lp, page_size: int):
     state["slot"][rows] = pg * page_size + p % page_size
 
 
-__all__ = ["decode_advance", "kv_write", "paged_attention", "sample"]
+__all__ = ["decode_advance", "kv_write", "paged_attention", "qkv_rope_to_cache", "sample"]

@@ -365,9 +365,9 @@ class RolloutEngine:
         for li, layer in enumerate(m.layers):
             h = Fx.rmsnorm(x, layer.attn_norm, a.norm_eps)
             qkv = Fx.linear(h, layer.wqkv, layer.bqkv)
-            q, k, v = Fx.qkv_rope(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
-                                  a.rope_theta, a.norm_eps)
-            D.kv_write(k, v, self.kv[li, 0], self.kv[li, 1], slots)
+            q, k, v = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
+                                          a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1], slots,
+                                          keep_kv=True)
             o = Fx.flash_attn_varlen(q, k, v, cu, max(lens))
             x = Fx.linear(o.reshape(T, a.q_dim), layer.wo, residual=x)
             h = Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps)
@@ -438,9 +438,8 @@ class RolloutEngine:
         for li, layer in enumerate(m.layers):
             h = Fx.rmsnorm(x, layer.attn_norm, a.norm_eps)
             qkv = Fx.linear(h, layer.wqkv, layer.bqkv)
-            q, k, v = Fx.qkv_rope(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
-                                  a.rope_theta, a.norm_eps)
-            D.kv_write(k, v, self.kv[li, 0], self.kv[li, 1], st["slot"][:b])
+            q, _, _ = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
+                                          a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1], st["slot"][:b])
             o = D.paged_attention(q, self.kv[li, 0], self.kv[li, 1], st["block_table"][:b], st["seq_lens"][:b])
             x = Fx.linear(o.reshape(b, a.q_dim), layer.wo, residual=x)
             h = Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps)

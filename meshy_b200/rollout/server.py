@@ -216,7 +216,11 @@ def main(argv=None):
     p.add_argument("--mem-fraction", type=float, default=0.5)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--eos", type=int, nargs="*", default=[])
+    p.add_argument("--tp-size", type=int, default=1, help="tensor-parallel degree of this replica")
+    p.add_argument("--ep-size", type=int, default=1, help="expert-parallel degree of this replica")
     a = p.parse_args(argv)
+    if a.tp_size > 1 or a.ep_size > 1:
+        raise SystemExit("this server runs one card per replica (tp_size = ep_size = 1); use more replicas")
     from ..models import get_model_args
     from .engine import RolloutEngine
 

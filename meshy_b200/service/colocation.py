@@ -182,7 +182,7 @@ class StoreLedger:
     def _rows(self):
         meta = self.client.get_meta(self.FIELDS, 0, self.partition, mode="force_fetch")
         if meta.size == 0:
-            return meta, []
+            return meta, {}
         return meta, self.client.get_data(meta)
 
     def _find(self, request_id: str):

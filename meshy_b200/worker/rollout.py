@@ -13,6 +13,7 @@ also drive the rollout's checkpoint shard.
 from __future__ import annotations
 
 import asyncio
+import time
 import copy
 import json
 import logging
@@ -347,6 +348,24 @@ class RolloutWorker(TQWorker):
                     t.add_done_callback(tasks.discard)
         if tasks:
             await asyncio.gather(*tasks)
+        await self.drain()
+
+    async def drain(self, timeout: float | None = None) -> None:
+        """After the last epoch: wait until consumers have cleared every row written to the data
+        partition, so the run ends after the final trainer step instead of before it."""
+        out = self.tq_outputs.get("rollouts")
+        part = out.partition if out is not None else None
+        if not part:
+            return
+        deadline = None if timeout is None else time.monotonic() + timeout
+        while not self.stopped:
+            n = await self.tq_call(lambda: self._aclient.num_rows(part))
+            if n == 0:
+                return
+            if deadline is not None and time.monotonic() > deadline:
+                log.warning("drain: %d rows still unconsumed in %s", n, part)
+                return
+            await asyncio.sleep(self.poll_interval)
 
 
 __all__ = ["GRPO_FIELDS", "GRPO_FIELDS_NO_ADVANTAGE", "RAW_REWARD_FIELD", "RolloutWorker", "TrajectoryLogger",

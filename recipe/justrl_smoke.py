@@ -1,0 +1,64 @@
+"""Smoke recipe: the JustRL service graph on a tiny Qwen3 (2 cards, CPU or GPU).
+
+Same shape as ``recipe.justrl`` -- per-card inference replicas colocated with
+one DDP trainer in a FALLBACK / ON_DEMAND ring, plus the CPU rollout driver --
+on ``qwen3:debugmodel`` with synthetic token prompts and the parity reward,
+for a few steps.  ``XRL_DEVICE=cpu`` runs it without a GPU (gloo):
+
+    XRL_DEVICE=cpu python -m meshy_b200.launch --recipe recipe.justrl_smoke
+"""
+
+from __future__ import annotations
+
+import os
+
+from meshy_b200.config import (GlobalCheckpointConfig, InferenceServiceConfig, RolloutServiceConfig, SamplingParams,
+                               TrainerConfig, TrainerParamsConfig, TrainingServiceConfig)
+from meshy_b200.service.base import ServiceGroup
+from meshy_b200.service.colocation import ColocationRing, SchedulingMode
+from meshy_b200.service.ignite import Ignitor
+
+MODEL = "qwen3:debugmodel"
+CARDS = int(os.environ.get("XRL_SMOKE_CARDS", "2"))
+PROMPTS = int(os.environ.get("XRL_SMOKE_PROMPTS", "4"))
+GROUP = 2
+STEPS = int(os.environ.get("XRL_SMOKE_STEPS", "3"))
+CKPT = GlobalCheckpointConfig(enabled=os.environ.get("XRL_SMOKE_CKPT", "0") == "1", interval=1, keep_latest_k=2)
+
+
+def _trainer_config() -> TrainerConfig:
+    return TrainerConfig(model_name="qwen3", model_flavor="debugmodel", seq_len=512, lr=1e-5, weight_decay=0.0,
+                         max_norm=1.0, steps=1000, dtype="bfloat16", dp_replicate_degree=CARDS)
+
+
+SERVICE_GROUPS = [
+    ServiceGroup(id="actor_infer", n_replicas=CARDS, n_gpus_per_replica=1,
+                 config=InferenceServiceConfig(model_path=None, server_args={
+                     "model": MODEL, "max_running_requests": 16, "max_total_tokens": 8192, "context_length": 512})),
+    ServiceGroup(id="actor_train", n_replicas=1, n_gpus_per_replica=CARDS, colocate_with="actor_infer",
+                 wait_until=["actor_infer"],
+                 config=TrainingServiceConfig(
+                     model_path=None, trainer_config=_trainer_config(),
+                     trainer_params=TrainerParamsConfig(mini_batch_size=PROMPTS * GROUP, batch_layout="packed",
+                                                        max_tokens_per_micro=2048, old_logprobs_source="train"),
+                     batch_size=PROMPTS * GROUP, weight_sync_mode="disk", checkpoint=CKPT)),
+    ServiceGroup(id="rollout", n_replicas=1, n_gpus_per_replica=0, wait_until=["actor_train", "actor_infer"],
+                 config=RolloutServiceConfig(
+                     model_path=None, dataset="meshy_b200.dataset.synthetic:SyntheticPrompts",
+                     dataset_kwargs={"batch_size": PROMPTS, "n_prompts": PROMPTS * STEPS, "vocab_size": 2048,
+                                     "min_len": 8, "max_len": 24, "seed": 1},
+                     reward="meshy_b200.dataset.synthetic:SyntheticPrompts.reward",
+                     sampling_params=SamplingParams(max_new_tokens=24).as_dict(), group_size=GROUP,
+                     poll_interval=0.2, pacing_window=1, num_epochs=1, checkpoint=CKPT)),
+]
+
+COLOCATIONS = [ColocationRing(group_id="actor", ring=(("actor_infer", SchedulingMode.FALLBACK),
+                                                      ("actor_train", SchedulingMode.ON_DEMAND)))]
+
+
+def main() -> None:
+    Ignitor(SERVICE_GROUPS, COLOCATIONS).run()
+
+
+if __name__ == "__main__":
+    main()

@@ -343,7 +343,7 @@ def test_gemm_small_m(M, N, K):
     assert rel_err(out32, a.float() @ b.float().t()) < 5e-3
 
 
-@pytest.mark.parametrize("cs", [1, 2, 3, 8])
+@pytest.mark.parametrize("cs", [1, 2, 3, 8, 12, 16])
 def test_gemm_small_m_cluster_sizes(cs):
     torch.manual_seed(11)
     M, N, K = 48, 1536, 8960
@@ -406,3 +406,24 @@ def test_paged_decode_tma_splits(splits, hd, Hq, Hkv):
     assert C().device_error() == 0
     o_ref = ref.attention_decode_paged(q.float(), kc.float(), vc.float(), bt, seq, 1 / math.sqrt(hd))
     assert rel_err(out, o_ref) < 1e-2
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_qkv_rope_cache_matches_rope_then_scatter(qk_norm):
+    torch.manual_seed(22)
+    T, Hq, Hkv, hd, page, n_pages = 37, 12, 2, 128, 64, 8
+    qkv = bf(T, (Hq + 2 * Hkv) * hd)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=DEV)
+    qn = bf(hd) if qk_norm else None
+    kn = bf(hd) if qk_norm else None
+    slots = torch.randperm(n_pages * page, device=DEV)[:T].long()
+    q1, k1, v1 = (torch.empty(T, h, hd, dtype=torch.bfloat16, device=DEV) for h in (Hq, Hkv, Hkv))
+    C().qkv_rope_fwd(qkv, pos, qn, kn, q1, k1, v1, 1e4, 1e-6)
+    kc1 = torch.zeros(n_pages, Hkv, page, hd, dtype=torch.bfloat16, device=DEV)
+    vc1 = torch.zeros_like(kc1)
+    C().kv_write(k1, v1, kc1, vc1, slots)
+    q2 = torch.empty_like(q1)
+    kc2, vc2 = torch.zeros_like(kc1), torch.zeros_like(vc1)
+    C().qkv_rope_cache(qkv, pos, qn, kn, q2, None, None, kc2, vc2, slots, 1e4, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q2) and torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
