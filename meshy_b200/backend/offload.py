@@ -14,8 +14,16 @@ _BUFS = ("master", "grad", "exp_avg", "exp_avg_sq", "compute")
 
 
 def offload(trainer) -> None:
-    f = trainer.flat
-    if f.master.device.type != "cuda":
+    offload_flat(trainer.flat)
+
+
+def restore(trainer) -> None:
+    restore_flat(trainer.flat)
+
+
+def offload_flat(f) -> None:
+    """Move every flat buffer of a :class:`~.flat.FlatParams` to pinned host memory."""
+    if f.master is None or f.master.device.type != "cuda":
         return
     host = {}
     for name in _BUFS:
@@ -35,8 +43,8 @@ def offload(trainer) -> None:
     torch.cuda.empty_cache()
 
 
-def restore(trainer) -> None:
-    f = trainer.flat
+def restore_flat(f) -> None:
+    """Inverse of :func:`offload_flat`: buffers back on the device, parameter views re-pointed."""
     host = getattr(f, "_host", None)
     if not host:
         return
@@ -55,4 +63,4 @@ def restore(trainer) -> None:
     f._host = None
 
 
-__all__ = ["offload", "restore"]
+__all__ = ["offload", "offload_flat", "restore", "restore_flat"]

@@ -47,3 +47,24 @@ def test_launcher_runs_colocated_grpo_on_cpu(tmp_path):
     assert (rt / "trajectories.jsonl").exists()
     state = rt / "state"
     assert (state / "actor_train-0").exists() and (state / "rollout-0").exists(), detail
+
+
+@pytest.mark.timeout(600)
+def test_launcher_runs_critic_ppo_on_cpu(tmp_path):
+    """Ring of inference → critic → trainer on one card: the critic cold-starts for one window (it raises
+    the gate itself), then publishes values that the trainer turns into VAPO-GAE advantages."""
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", XRL_SMOKE_COLD="1", PYTHONPATH=ROOT)
+    rt = tmp_path / "rt"
+    r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_ii_smoke",
+                        "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=540)
+    logs = rt / "logs"
+    detail = r.stderr[-2000:]
+    if logs.exists():
+        for f in sorted(logs.iterdir()):
+            detail += f"\n==== {f.name}\n" + f.read_text(errors="replace")[-1500:]
+    assert r.returncode == 0, detail
+    critic_log = (logs / "critic-0-0.log").read_text()
+    assert "critic cold start 1" in critic_log and "critic window 3" in critic_log, detail
+    rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
+    assert len(rows) == 2 and all("critic/value_mean" in x for x in rows), detail
