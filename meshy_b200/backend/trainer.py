@@ -167,7 +167,7 @@ class PPOTrainer:
                 gae_metrics = self.attach_gae_advantages(samples)
 
         old_per_mini: list[list[torch.Tensor] | None] = [None] * len(plan)
-        if self.params.old_logprobs_source == "train":
+        if self.params.old_logprobs_source == "train" and self.needs_behaviour_logprobs:
             with timer.timer("train/old_logprobs", sync=True):
                 old_per_mini = [self.compute_old_logprobs(samples, mini) for mini in plan]
 

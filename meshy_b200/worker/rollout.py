@@ -299,6 +299,12 @@ class RolloutWorker(TQWorker):
             await self._run_rollouts()
         finally:
             await self.close_tq()
+            close = getattr(self.engine, "close", None)
+            if close is not None:
+                try:
+                    await close()
+                except Exception:
+                    pass
 
     async def _run_rollouts(self) -> None:
         if self.builder is None:

@@ -68,3 +68,22 @@ def test_launcher_runs_critic_ppo_on_cpu(tmp_path):
     assert "critic cold start 1" in critic_log and "critic window 3" in critic_log, detail
     rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
     assert len(rows) == 2 and all("critic/value_mean" in x for x in rows), detail
+
+
+@pytest.mark.timeout(600)
+def test_launcher_runs_topk_distillation_on_cpu(tmp_path):
+    """Inference → teacher (Top-K columns appended in place) → student trainer (forward KL over the teacher's
+    Top-K), all ring members of one card."""
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", PYTHONPATH=ROOT)
+    rt = tmp_path / "rt"
+    r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.student_topk_opd_smoke",
+                        "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=540)
+    detail = r.stderr[-2000:]
+    logs = rt / "logs"
+    if logs.exists():
+        for f in sorted(logs.iterdir()):
+            detail += f"\n==== {f.name}\n" + f.read_text(errors="replace")[-1500:]
+    assert r.returncode == 0, detail
+    rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
+    assert len(rows) == 2 and all("train/distill_loss" in x and x["train/teacher_topk_mass"] > 0 for x in rows), detail
