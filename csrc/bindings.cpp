@@ -17,6 +17,7 @@
 #include "kernels/elementwise.h"
 #include "kernels/gemm.h"
 #include "kernels/misc.h"
+#include "kernels/symm.h"
 
 using torch::Tensor;
 using namespace meshy;
@@ -426,6 +427,65 @@ void cast_copy(Tensor src, Tensor dst) {
   }
 }
 
+// ─── symmetric peer memory ────────────────────────────────────────────────────
+int64_t symm_alloc_(int64_t nbytes) {
+  const c10::cuda::CUDAGuard guard(at::cuda::current_device());
+  return reinterpret_cast<int64_t>(symm_malloc((size_t)nbytes));
+}
+void symm_free_(int64_t p) { symm_free(reinterpret_cast<void*>(p)); }
+pybind11::bytes symm_export_(int64_t p) { return pybind11::bytes(symm_export(reinterpret_cast<void*>(p))); }
+int64_t symm_import_(pybind11::bytes h) { return reinterpret_cast<int64_t>(symm_import(std::string(h))); }
+void symm_close_(int64_t p) { symm_close(reinterpret_cast<void*>(p)); }
+
+// A tensor view of ``numel`` elements at ``ptr + offset_bytes`` (no ownership: the heap object keeps the memory).
+Tensor symm_view_(int64_t ptr, int64_t offset_bytes, int64_t numel, c10::ScalarType dtype) {
+  auto opts = torch::TensorOptions().device(torch::kCUDA, at::cuda::current_device()).dtype(dtype);
+  return torch::from_blob(reinterpret_cast<char*>(ptr) + offset_bytes, {numel}, opts);
+}
+
+void symm_barrier_(Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch, double timeout_s) {
+  TORCH_CHECK(flag_ptrs.scalar_type() == at::kLong && flag_ptrs.is_cuda(), "flag_ptrs: int64 CUDA tensor");
+  symm_barrier(reinterpret_cast<const unsigned long long*>(flag_ptrs.data_ptr()), (int)rank, (int)world,
+               (unsigned)epoch, timeout_s, ptr<int>(scratch(0, 0).err), cur_stream());
+  count();
+}
+
+void symm_dp_adamw_(Tensor grad_ptrs, Tensor master_ptrs, c10::optional<Tensor> compute_ptrs, Tensor flag_ptrs,
+                    Tensor slot_ptrs, Tensor master_local, Tensor grad_local, Tensor exp_avg, Tensor exp_avg_sq,
+                    Tensor scalars, int64_t rank, int64_t world, int64_t lo, int64_t hi, int64_t epoch, double max_norm,
+                    double lr, double b1, double b2, double eps, double wd, int64_t step, double timeout_s) {
+  TORCH_CHECK(scalars.scalar_type() == at::kFloat && scalars.numel() >= 2, "scalars: fp32 [2] (sumsq, norm)");
+  SymmAdamWArgs a;
+  auto tab = [](const Tensor& t) { return reinterpret_cast<const unsigned long long*>(t.data_ptr()); };
+  a.grad_ptrs = tab(grad_ptrs);
+  a.master_ptrs = tab(master_ptrs);
+  a.compute_ptrs = compute_ptrs.has_value() && compute_ptrs->defined() ? tab(*compute_ptrs) : nullptr;
+  a.flag_ptrs = tab(flag_ptrs);
+  a.slot_ptrs = tab(slot_ptrs);
+  a.master_local = ptr<float>(master_local);
+  a.local_grad = ptr<float>(grad_local);
+  a.exp_avg = ptr<float>(exp_avg);
+  a.exp_avg_sq = ptr<float>(exp_avg_sq);
+  a.sumsq = ptr<float>(scalars);
+  a.norm = ptr<float>(scalars) + 1;
+  a.err = ptr<int>(scratch(0, 0).err);
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.lo = lo;
+  a.hi = hi;
+  a.epoch = (unsigned)epoch;
+  a.max_norm = (float)max_norm;
+  a.lr = (float)lr;
+  a.b1 = (float)b1;
+  a.b2 = (float)b2;
+  a.eps = (float)eps;
+  a.wd = (float)wd;
+  a.step = (int)step;
+  a.timeout_s = timeout_s;
+  symm_dp_adamw_step(a, cur_stream());
+  count(5);
+}
+
 int64_t device_error() {
   auto& s = scratch(0, 0);
   return s.err.item<int>();
@@ -463,6 +523,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "decode attention split count override (0 = heuristic); for tests and benchmarks");
   m.def("decode_advance", &decode_advance_);
   m.def("cast_copy", &cast_copy);
+  m.def("symm_alloc", &symm_alloc_, "cudaMalloc a symmetric-heap buffer (zeroed); returns the pointer");
+  m.def("symm_free", &symm_free_);
+  m.def("symm_export", &symm_export_, "CUDA IPC handle bytes of a symmetric-heap buffer");
+  m.def("symm_import", &symm_import_, "map a peer's symmetric-heap buffer; returns the local pointer");
+  m.def("symm_close", &symm_close_);
+  m.def("symm_view", &symm_view_, "non-owning tensor view into a symmetric-heap buffer");
+  m.def("symm_barrier", &symm_barrier_, "device barrier over the ranks' flag arrays (bounded wait)");
+  m.def("symm_dp_adamw", &symm_dp_adamw_,
+        "fused DP optimiser step over NVLink: reduce-scatter + grad norm + AdamW + all-gather by P2P stores");
   m.def("device_error", &device_error);
   m.def("clear_device_error", &clear_device_error);
   m.def("launch_count", &launch_count, "kernels launched by this library so far (host-side count)");

@@ -1,0 +1,44 @@
+// Symmetric peer memory (CUDA IPC over NVLink) and the fused data-parallel optimiser step (symm.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "../include/common.cuh"
+
+namespace meshy {
+
+void* symm_malloc(size_t bytes);
+void symm_free(void* p);
+std::string symm_export(void* p);          // cudaIpcMemHandle bytes
+void* symm_import(const std::string& h);   // peer pointer in this process
+void symm_close(void* p);
+
+// One-CTA barrier over the ranks' flag arrays (bounded spin; err := kErrTimeoutPeer on timeout).
+void symm_barrier(const unsigned long long* flag_ptrs, int rank, int world, unsigned int epoch, double timeout_s,
+                  int* err, cudaStream_t st);
+
+struct SymmAdamWArgs {
+  const unsigned long long* grad_ptrs = nullptr;     // [world] device table
+  const unsigned long long* master_ptrs = nullptr;   // [world]
+  const unsigned long long* compute_ptrs = nullptr;  // [world] or null (no bf16 copy)
+  const unsigned long long* flag_ptrs = nullptr;     // [world] u32[world] flag arrays
+  const unsigned long long* slot_ptrs = nullptr;     // [world] f32[world] norm slots
+  const float* master_local = nullptr;
+  float* local_grad = nullptr;
+  float* exp_avg = nullptr;
+  float* exp_avg_sq = nullptr;
+  float* sumsq = nullptr;  // device scratch scalar
+  float* norm = nullptr;   // device scalar: global gradient norm (output)
+  int* err = nullptr;
+  int rank = 0, world = 1;
+  long long lo = 0, hi = 0;  // this rank's shard
+  unsigned int epoch = 0;    // uses epoch, epoch + 1, epoch + 2
+  float max_norm = 1.f, lr = 0.f, b1 = 0.9f, b2 = 0.999f, eps = 1e-8f, wd = 0.f;
+  int step = 1;
+  double timeout_s = 10.0;
+};
+
+void symm_dp_adamw_step(const SymmAdamWArgs& a, cudaStream_t st);
+
+}  // namespace meshy

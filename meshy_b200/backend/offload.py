@@ -26,7 +26,10 @@ def offload_flat(f) -> None:
     if f.master is None or f.master.device.type != "cuda":
         return
     host = {}
+    keep = set(getattr(f, "resident", ()))  # buffers that must stay mapped (symmetric heap)
     for name in _BUFS:
+        if name in keep:
+            continue
         t = getattr(f, name)
         if t is None or (name == "compute" and not f.separate_compute):
             continue
@@ -37,9 +40,10 @@ def offload_flat(f) -> None:
     f._host = host
     for name in host:
         setattr(f, name, None)
-    for p in f.params:
-        p.data = torch.empty(0, dtype=p.dtype, device=p.device)
-        p.main_grad = None
+    if not keep:
+        for p in f.params:
+            p.data = torch.empty(0, dtype=p.dtype, device=p.device)
+            p.main_grad = None
     torch.cuda.empty_cache()
 
 

@@ -90,7 +90,31 @@ class PPOTrainer:
         from ..parallel.ddp import GradReducer
 
         self.reducer = GradReducer(self.flat, dp_group)
+        self.fused_dp = False
+        if self._use_fused_dp():
+            # DDP gradient reduction + AdamW as one NVLink pipeline (reduce-scatter, norm, shard update,
+            # all-gather by P2P stores); the reducer has nothing left to do
+            from ..parallel.symm import FusedDPAdamW
+
+            self.optimizer = FusedDPAdamW(self.flat, dp_group, lr=config.lr, betas=(config.beta1, config.beta2),
+                                          eps=config.eps, weight_decay=config.weight_decay, max_norm=config.max_norm)
+            self.flat.resident = ("master", "grad", "compute")
+            self.reducer.backend = "none"
+            self.fused_dp = True
         self.h2d_bytes = 0
+
+    def _use_fused_dp(self) -> bool:
+        import os
+
+        if os.environ.get("MESHY_DP_FUSED", "auto") == "0" or self.device.type != "cuda":
+            return False
+        if self.dp_group is None or not dist.is_initialized() or dist.get_world_size(self.dp_group) < 2:
+            return False
+        if dist.get_backend(self.dp_group) != "nccl":
+            return False
+        from ..parallel.symm import SymmetricHeap
+
+        return SymmetricHeap.supported(self.dp_group)
 
     # ------------------------------------------------------------------ planning
     @property

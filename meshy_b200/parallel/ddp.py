@@ -6,10 +6,10 @@ divided by global denominators, so the reduction is a plain SUM).  Here the
 gradient is one flat buffer, so the reduction is a handful of large
 collectives:
 
-* within one node with peer access, the fused NVLink kernel
-  (:mod:`meshy_b200.parallel.symm` ``all_reduce``): each rank reduces its
-  slice straight from every peer's buffer and writes the result back into
-  every peer (P2P loads/stores, no staging copy);
+* within one node the trainer normally skips this class: the fused NVLink
+  optimiser (:class:`meshy_b200.parallel.symm.FusedDPAdamW`) reduces,
+  clips, updates and all-gathers in one device pipeline (backend ``none``
+  here);
 * otherwise NCCL ``all_reduce`` on the flat buffer in buckets.
 """
 
@@ -29,36 +29,16 @@ class GradReducer:
         self.group = group
         self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
         self.backend = backend or os.environ.get("MESHY_GRAD_REDUCE", "auto")
-        self._symm = None
         self.last_bytes = 0
 
     def arm(self) -> None:
         """Called before the last micro-batch's backward of a mini-batch."""
 
-    def _fused(self):
-        if self._symm is None:
-            from .symm import SymmetricAllReduce
-
-            self._symm = SymmetricAllReduce.create(self.flat.grad, self.group)
-        return self._symm
-
     def finish(self) -> None:
-        if self.world <= 1:
+        if self.world <= 1 or self.backend == "none":
             return
         g = self.flat.grad
         self.last_bytes = g.numel() * g.element_size()
-        use_fused = g.is_cuda and self.backend in ("auto", "fused")
-        if use_fused:
-            try:
-                ar = self._fused()
-            except Exception:
-                if self.backend == "fused":
-                    raise
-                ar = None
-                self.backend = "nccl"
-            if ar is not None:
-                ar.all_reduce_()
-                return
         for s in range(0, g.numel(), BUCKET_ELEMS):
             dist.all_reduce(g[s:s + BUCKET_ELEMS], group=self.group)
 
