@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #define MESHY_CUDA_CHECK(expr)                                                                  \
   do {                                                                                          \
@@ -25,7 +26,35 @@ namespace meshy {
 
 using bf16 = __nv_bfloat16;
 
+// ─── programmatic dependent launch (PDL) ────────────────────────────────────
+// Kernels of the decode step are launched with programmatic stream
+// serialisation: a kernel may start (prologue, barrier init, TMEM alloc, weight
+// prefetch) while its predecessor in the stream finishes, and calls pdl_wait()
+// before it touches anything the predecessor wrote.  pdl_trigger() lets the
+// successor start early.  Both are no-ops for a kernel launched normally.
+bool pdl_enabled();  // env MESHY_PDL (default on)
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(e) + " in launch_pdl");
+}
+
 #if defined(__CUDACC__)
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -92,6 +92,8 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
 
   const int b = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
   const int rep = Hq / Hkv;
+  pdl_wait();  // Q, the cache rows of this step and the lengths come from the kernels before
+  pdl_trigger();
   const int L = seq_lens[b];
   const int n_pages = (L + kPage - 1) / kPage;
   const int per = (n_pages + n_split - 1) / n_split;
@@ -346,13 +348,15 @@ void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, con
   cfg.blockDim = dim3(kThreadsDec, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = CLUSTER ? n_split : 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   MESHY_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, mk, mv, q, bt, seq_lens, o, part, Hq, Hkv, max_pages, n_split, scale,
                                       err));
 }

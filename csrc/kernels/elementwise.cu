@@ -16,6 +16,8 @@ __global__ void rmsnorm_fwd_kernel(const bf16* __restrict__ x, const bf16* __res
                                    float* __restrict__ rstd, int rows, int D, float eps) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
+  pdl_wait();
+  pdl_trigger();
   for (int r = blockIdx.x * warps + threadIdx.x / 32; r < rows; r += gridDim.x * warps) {
     const bf16* xr = x + (size_t)r * D;
     float v[VPT * 8];
@@ -141,7 +143,7 @@ void rmsnorm_fwd(const bf16* x, const bf16* w, bf16* y, float* rstd, int rows, i
   const int vpt = (D + 255) / 256;
   dim3 block(256);
   int grid = grid_for(rows, 8);
-#define RMS_F(V) rmsnorm_fwd_kernel<V><<<grid, block, 0, st>>>(x, w, y, rstd, rows, D, eps)
+#define RMS_F(V) launch_pdl(rmsnorm_fwd_kernel<V>, dim3(grid), block, 0, st, x, w, y, rstd, rows, D, eps)
   if (vpt <= 1) RMS_F(1);
   else if (vpt <= 2) RMS_F(2);
   else if (vpt <= 4) RMS_F(4);
@@ -183,6 +185,8 @@ __global__ void qkv_rope_fwd_kernel(const bf16* __restrict__ qkv, const int* __r
   const int H = Hq + 2 * Hkv;
   const int lane = threadIdx.x % 32;
   const long long gw = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  pdl_wait();
+  pdl_trigger();
   if (gw >= (long long)T * H) return;
   const int t = (int)(gw / H), h = (int)(gw % H);
   const int half = hd / 2;
@@ -332,8 +336,8 @@ void qkv_rope_fwd(const bf16* qkv, const int* pos, const bf16* qn, const bf16* k
   long long warps = (long long)T * (Hq + 2 * Hkv);
   int grid = (int)((warps + 7) / 8);
   if (grid == 0) return;
-  qkv_rope_fwd_kernel<<<grid, 256, 0, st>>>(qkv, pos, qn, kn, inv_freq, q, k, v, T, Hq, Hkv, hd, eps, kc, vc, slots,
-                                            page);
+  launch_pdl(qkv_rope_fwd_kernel, dim3(grid), dim3(256), 0, st, qkv, pos, qn, kn, inv_freq, q, k, v, T, Hq, Hkv, hd,
+             eps, kc, vc, slots, page);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -391,6 +395,8 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const bf16
                                      long long T, int D, long long V) {
   long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   long long per = D / 8;
+  pdl_wait();
+  pdl_trigger();
   if (idx >= T * per) return;
   long long t = idx / per;
   int c = (int)(idx % per) * 8;
@@ -417,7 +423,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const bf16
 void embedding_fwd(const int64_t* ids, const bf16* w, bf16* out, long long T, int D, long long V, cudaStream_t st) {
   long long n = T * (D / 8);
   if (n == 0) return;
-  embedding_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ids, w, out, T, D, V);
+  launch_pdl(embedding_fwd_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, ids, w, out, T, D, V);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 

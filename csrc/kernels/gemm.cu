@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -143,6 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ───────────────────────────── TMA producer ─────────────────────────────
     if (lane == 0) {
+      pdl_wait();  // the A operand comes from the kernel before
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0, last_stage = 0;
@@ -246,6 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const int et = threadIdx.x - 64;  // 0..127
+    pdl_wait();  // residual / labels / workspace may come from the kernels before
+    pdl_trigger();
     for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
       int mt, nt, ks;
       unit_coords(p, u, mt, nt, ks);
@@ -523,6 +527,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ════════════════════════════════ host side ══════════════════════════════════
 
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MESHY_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -596,8 +609,7 @@ static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
     MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_set = true;
   }
-  k<<<grid, kThreads, C::SMEM_BYTES, st>>>(ma, mb, a);
-  MESHY_CUDA_CHECK(cudaGetLastError());
+  launch_pdl(k, dim3(grid), dim3(kThreads), C::SMEM_BYTES, st, ma, mb, a);
 }
 
 template <int BN>

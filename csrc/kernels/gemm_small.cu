@@ -140,8 +140,26 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       uint32_t phase = 0;
       int issued = 0, last_stage = 0;
       uint32_t last_phase = 0;
+      // The weights do not depend on the kernel before this one: under programmatic dependent
+      // launch the first STAGES weight tiles stream in while that kernel finishes; the activation
+      // tiles of those stages follow once it has completed.
+      const int npre = PERSIST ? 0 : min(kb1 - kb0, C::STAGES);
+      for (int j = 0; j < npre; ++j) {
+        mbar_arrive_expect_tx(&full[j], C::STAGE_BYTES);
+        tma_load_2d(smem + j * C::STAGE_BYTES, &mapW, &full[j], (kb0 + j) * SBK, first * 128);
+      }
+      pdl_wait();
+      for (int j = 0; j < npre; ++j)
+        tma_load_2d(smem + j * C::STAGE_BYTES + W_TILE_BYTES, &mapX, &full[j], (kb0 + j) * SBK, 0);
+      if (npre > 0) {
+        issued = npre;
+        last_stage = npre - 1;
+        last_phase = 0;
+        stage = npre % C::STAGES;
+        phase = (npre == C::STAGES) ? 1u : 0u;
+      }
       for (int nt = first; nt < p.n_tiles && !*abort_flag; nt += stride) {
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = (nt == first ? kb0 + npre : kb0); kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           uint8_t* sw = smem + stage * C::STAGE_BYTES;
@@ -156,6 +174,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
           }
         }
       }
+      pdl_trigger();
       if (*abort_flag && issued) {
         long long t0 = clock64();
         while (!mbar_try_wait(&full[last_stage], last_phase) && clock64() - t0 < kWaitCycles) {
@@ -212,6 +231,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     }
   } else {
     // ─────────────────────────────── epilogue ───────────────────────────────────
+    pdl_wait();  // bias / residual / output may be touched by the kernels before
     const int q = warp & 3;
     const int f = q * 32 + lane;  // weight row within the tile = TMEM lane
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
@@ -365,13 +385,15 @@ void launch_small(const CUtensorMap& mw, const CUtensorMap& mx, const SmallArgs&
   cfg.blockDim = dim3(kSmallThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cs;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   MESHY_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, mw, mx, a));
 }
 

@@ -244,6 +244,8 @@ __global__ void lse_merge_kernel(const float* __restrict__ part, int n_tiles, in
                                  int64_t* __restrict__ tok, float* __restrict__ tok_lp, int rows) {
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  pdl_wait();
+  pdl_trigger();
   if (row >= rows) return;
   const float* pr = part + (size_t)row * n_tiles * 8;
   float M = -INFINITY;
@@ -295,7 +297,8 @@ __global__ void lse_merge_kernel(const float* __restrict__ part, int n_tiles, in
 void lse_merge(const float* part, int n_tiles, int bn, const int64_t* labels, float* lp, float* lse, float* ent,
                int64_t* tok, float* tok_lp, int rows, cudaStream_t st) {
   if (rows == 0) return;
-  lse_merge_kernel<<<(rows + 7) / 8, 256, 0, st>>>(part, n_tiles, bn, labels, lp, lse, ent, tok, tok_lp, rows);
+  launch_pdl(lse_merge_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, part, n_tiles, bn, labels, lp, lse, ent, tok,
+             tok_lp, rows);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -308,6 +311,8 @@ __global__ void decode_advance_kernel(const int64_t* __restrict__ tok, const flo
                                       const int64_t* __restrict__ eos, int n_eos, int B, int max_pages, int cap,
                                       int page) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
   if (i >= B || done[i]) return;
   int r = req[i], g = gen[i];
   int64_t t = tok[i];
@@ -333,8 +338,8 @@ void decode_advance(const int64_t* tok, const float* lp, int64_t* tok_in, int* p
                     float* out_lp, const int64_t* eos, int n_eos, int B, int max_pages, int cap, int page,
                     cudaStream_t st) {
   if (B == 0) return;
-  decode_advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(tok, lp, tok_in, pos, seq_lens, gen, max_new, done, slot, bt,
-                                                         req, out_tok, out_lp, eos, n_eos, B, max_pages, cap, page);
+  launch_pdl(decode_advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, tok, lp, tok_in, pos, seq_lens, gen,
+             max_new, done, slot, bt, req, out_tok, out_lp, eos, n_eos, B, max_pages, cap, page);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 
