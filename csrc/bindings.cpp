@@ -130,6 +130,44 @@ void gemm(Tensor a, Tensor b, Tensor out, bool a_mn, bool b_mn, c10::optional<Te
   count();
 }
 
+// Decode-time fused RMSNorm -> linear (optionally SwiGLU): out = epi(rmsnorm(x; w_norm, eps) . W^T (+bias)).
+// Returns false (and does nothing) when the problem is not eligible for the fused small-M path.
+bool gemm_norm(Tensor x, Tensor norm_w, double eps, Tensor w, Tensor out, c10::optional<Tensor> bias,
+               c10::optional<Tensor> residual, int64_t epi, int64_t block) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(norm_w);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1, "gemm_norm: row-major 2-D");
+  const c10::cuda::CUDAGuard guard(x.device());
+  GemmProblem g;
+  g.A = x.data_ptr();
+  g.B = w.data_ptr();
+  g.lda = x.stride(0);
+  g.ldb = w.stride(0);
+  g.M = x.size(0);
+  g.K = x.size(1);
+  g.N = w.size(0);
+  TORCH_CHECK(w.size(1) == g.K && norm_w.numel() == g.K, "gemm_norm: K mismatch");
+  g.out = out.data_ptr();
+  g.ldo = out.stride(0);
+  g.out_f32 = out.scalar_type() == at::kFloat;
+  g.epi = (int)epi;
+  if (g.epi == EPI_SWIGLU) TORCH_CHECK(block == 64 && out.size(1) * 2 == g.N, "gemm_norm: swiglu out [M, N/2]");
+  g.bias = optr<bf16>(bias);
+  if (residual.has_value() && residual->defined()) {
+    g.residual = ptr<bf16>(*residual);
+    g.ldr = residual->stride(0);
+  }
+  g.norm_w = ptr<bf16>(norm_w);
+  g.norm_eps = (float)eps;
+  g.err = ptr<int>(scratch(0, 0).err);
+  if (g.M == 0 || !gemm_small_norm_eligible(g)) return false;
+  gemm_small_launch(g, cur_stream());
+  count();
+  return true;
+}
+
 void swiglu_bwd_(Tensor h, Tensor ga, Tensor dh, int64_t block) {
   CHECK_CONTIG(h);
   CHECK_CONTIG(ga);
@@ -498,6 +536,7 @@ int64_t launch_count() { return g_launches.load(); }
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "meshy_b200 sm_100a kernel library";
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("gemm_norm", &gemm_norm, "decode: fused input RMSNorm + small-M GEMM (returns False if not eligible)");
   m.def("gemm_small_config", [](int64_t enabled, int64_t cluster) { gemm_small_config((int)enabled, (int)cluster); },
         "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");
   m.def("swiglu_bwd", &swiglu_bwd_);

@@ -41,6 +41,8 @@ struct GemmProblem {
   int force_bn = 0;           // 0 = heuristic
   int max_split = 0;          // 0 = heuristic
   int force_cs = 0;           // small-M path: cluster split-K size (0 = heuristic)
+  const bf16* norm_w = nullptr;  // small-M path: fused input RMSNorm gain (A is the raw stream)
+  float norm_eps = 1e-6f;
 };
 
 void gemm_launch(const GemmProblem& g, cudaStream_t stream);
@@ -50,6 +52,8 @@ void gemm_launch(const GemmProblem& g, cudaStream_t stream);
 constexpr int kSmallMaxM = 256;
 constexpr int kSmallMaxCluster = 16;  // above 8 the kernel opts in to non-portable cluster sizes
 bool gemm_small_eligible(const GemmProblem& g);
+// Whether the small-M path can also fuse the input RMSNorm for this problem.
+bool gemm_small_norm_eligible(const GemmProblem& g);
 void gemm_small_launch(const GemmProblem& g, cudaStream_t stream);
 // enabled: 1/0 (-1 keeps); force_cs: cluster size override, 0 = heuristic (-1 keeps)
 void gemm_small_config(int enabled, int force_cs);

@@ -55,6 +55,12 @@ struct SmallArgs {
   const bf16* residual;
   int ldr;
   int* err;
+  // fused input RMSNorm: X is the raw residual stream; every row is scaled by its own rstd and the
+  // gain before the MMA reads it (null: X is used as is)
+  const bf16* norm_w;
+  float norm_eps;
+  const bf16* x_raw;
+  int ldx;
 };
 
 template <int MP, bool PERSIST>
@@ -66,7 +72,8 @@ struct SCfg {
   static constexpr int N_ACC = PERSIST ? 2 : 1;
   static constexpr int TMEM_COLS = (N_ACC * MP < 32) ? 32 : N_ACC * MP;
   static constexpr int RED_BYTES = 128 * MP * 4;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + MP * 4;
   static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "reduction buffer must fit in the stage ring");
   static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
 };
@@ -87,6 +94,72 @@ __device__ __forceinline__ void store_val(const SmallArgs& p, int m, int n, floa
   else reinterpret_cast<bf16*>(p.out)[(size_t)m * p.ldo + n] = __float2bfloat16(x);
 }
 
+// Fused input RMSNorm, run by the four epilogue warps while the producer and MMA warps stream the
+// K loop.  First every row's rstd = rsqrt(mean(x^2) + eps) -- one warp per row, summed in the same
+// order as rmsnorm_fwd_kernel (lane l owns 8-element chunks l, l+32, ...; pairs accumulated in
+// order; xor-butterfly warp sum), so the result is bitwise that of the unfused op.  Then, stage by
+// stage, the landed X tile is rewritten in place as bf16((x * rstd) * g) and handed to the MMA
+// (generic-proxy writes fenced to the async proxy before the arrive).
+template <int MP>
+__device__ __forceinline__ void norm_stages(const SmallArgs& p, uint8_t* smem, uint64_t* full, uint64_t* normed,
+                                            float* rstd_s, int kb0, int kb1, volatile int* abort_flag) {
+  using C = SCfg<MP, false>;
+  const int ew = (threadIdx.x / 32) - 2;  // 0..3
+  const int lane = threadIdx.x % 32;
+  const int et = threadIdx.x - 64;        // 0..127
+  for (int m = ew; m < MP; m += 4) {
+    float ss = 0.f;
+    if (m < p.M) {
+      const bf16* xr = p.x_raw + (size_t)m * p.ldx;
+      for (int c = lane * 8; c < p.K; c += 32 * 8) {
+        uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+        uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float2 f = unpack_bf16x2(uu[t]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) rstd_s[m] = (m < p.M) ? rsqrtf(ss / p.K + p.norm_eps) : 0.f;
+  }
+  named_bar_sync(1, 128);
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int kb = kb0; kb < kb1; ++kb) {
+    if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrTimeoutEpilogue)) return;
+    bf16* xs = reinterpret_cast<bf16*>(smem + stage * C::STAGE_BYTES + W_TILE_BYTES);
+    for (int i = et; i < MP * 8; i += 128) {
+      const int m = i >> 3, pc = i & 7;
+      const int lc = pc ^ (m & 7);  // 128-byte swizzle: physical 16-byte chunk -> logical
+      const int k = kb * SBK + lc * 8;
+      uint4* ptr = reinterpret_cast<uint4*>(xs + m * 64 + pc * 8);
+      uint4 u = *ptr;
+      uint4 o = make_uint4(0, 0, 0, 0);
+      if (m < p.M && k < p.K) {
+        const float rs = rstd_s[m];
+        const uint4 gu = *reinterpret_cast<const uint4*>(p.norm_w + k);
+        uint32_t uu[4] = {u.x, u.y, u.z, u.w}, gg[4] = {gu.x, gu.y, gu.z, gu.w}, oo[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float2 x = unpack_bf16x2(uu[t]), g = unpack_bf16x2(gg[t]);
+          oo[t] = pack_bf16x2(x.x * rs * g.x, x.y * rs * g.y);
+        }
+        o = make_uint4(oo[0], oo[1], oo[2], oo[3]);
+      }
+      *ptr = o;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&normed[stage]);
+    if (++stage == C::STAGES) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+}
+
 template <int MP, bool PERSIST>
 __global__ void __launch_bounds__(kSmallThreads, 1)
     gemm_small_kernel(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapX,
@@ -99,8 +172,11 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* normed = drain + 1;  // [STAGES]: X tile of the stage normalised (fused RMSNorm)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(normed + C::STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* rstd_s = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+  const bool fuse_norm = p.norm_w != nullptr;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -119,6 +195,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       mbar_init(&tempty[i], 128);
     }
     mbar_init(drain, 1);
+    for (int s = 0; s < C::STAGES; ++s) mbar_init(&normed[s], 4);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&mapW);
@@ -196,7 +273,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         const uint32_t d_tmem = tmem_base + acc * MP;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+          if (!mbar_wait(fuse_norm ? &normed[stage] : &full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -232,6 +309,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   } else {
     // ─────────────────────────────── epilogue ───────────────────────────────────
     pdl_wait();  // bias / residual / output may be touched by the kernels before
+    if (!PERSIST && fuse_norm && has_k) norm_stages<MP>(p, smem, full, normed, rstd_s, kb0, kb1, abort_flag);
     const int q = warp & 3;
     const int f = q * 32 + lane;  // weight row within the tile = TMEM lane
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
@@ -482,8 +560,18 @@ bool gemm_small_eligible(const GemmProblem& g) {
   return true;
 }
 
+bool gemm_small_norm_eligible(const GemmProblem& g) {
+  if (!gemm_small_eligible(g)) return false;
+  const int n_tiles = (g.N + 127) / 128;
+  return n_tiles <= sm_count() && g.K % 8 == 0 && g.lda % 8 == 0 &&
+         (reinterpret_cast<uintptr_t>(g.A) & 15) == 0;
+}
+
 void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
   MESHY_CHECK(gemm_small_eligible(g), "gemm_small: problem not eligible");
+  MESHY_CHECK(g.norm_w == nullptr || gemm_small_norm_eligible(g), "gemm_small: fused RMSNorm not eligible");
+  MESHY_CHECK(g.norm_w == nullptr || (reinterpret_cast<uintptr_t>(g.norm_w) & 15) == 0,
+              "gemm_small: RMSNorm gain must be 16-byte aligned");
   const int MP = g.M <= 16 ? 16 : g.M <= 32 ? 32 : g.M <= 64 ? 64 : g.M <= 128 ? 128 : 256;
   SmallArgs a{};
   a.M = g.M; a.N = g.N; a.K = g.K;
@@ -493,6 +581,10 @@ void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
   a.out = g.out; a.ldo = g.ldo; a.out_f32 = g.out_f32;
   a.bias = g.bias; a.residual = g.residual; a.ldr = g.ldr;
   a.err = g.err;
+  a.norm_w = g.norm_w;
+  a.norm_eps = g.norm_eps;
+  a.x_raw = static_cast<const bf16*>(g.A);
+  a.ldx = (int)g.lda;
   const int sms = sm_count();
   CUtensorMap mw = make_map_bf16(g.B, g.N, g.K, g.ldb, SBK, 128);
   CUtensorMap mx = make_map_bf16(g.A, g.M, g.K, g.lda, SBK, MP);

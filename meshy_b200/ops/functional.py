@@ -154,6 +154,29 @@ def linear_swiglu(x, w13, block: int):
     return ref.swiglu(F.linear(x, w13), block)
 
 
+_FUSED_NORM = __import__("os").environ.get("MESHY_FUSED_NORM", "0") == "1"
+
+
+def rmsnorm_linear(x, norm_w, eps, w, b=None, *, swiglu_block: int = 0):
+    """Inference: ``linear(rmsnorm(x), w, b)`` (or the SwiGLU linear with ``swiglu_block``).
+
+    With ``MESHY_FUSED_NORM=1`` the norm runs inside the small-M GEMM (each CTA recomputes the row
+    rstd and rewrites its X tiles in shared memory).  Measured on B200 for the 1.5B model it is no
+    faster at batch 8 and 33% slower at batch 64 than the separate RMSNorm kernel (the per-CTA rstd
+    pass over the whole row block is on the critical path), so the two-kernel form is the default."""
+    if _FUSED_NORM and native(x) and not torch.is_grad_enabled():
+        x2 = x.reshape(-1, x.shape[-1])
+        n_out = w.shape[0] // 2 if swiglu_block else w.shape[0]
+        out = torch.empty(x2.shape[0], n_out, dtype=x.dtype, device=x.device)
+        if ext().gemm_norm(x2, norm_w, float(eps), w, out, b, None, EPI_SWIGLU if swiglu_block else EPI_NONE,
+                           int(swiglu_block)):
+            return out.reshape(*x.shape[:-1], n_out)
+    h = rmsnorm(x, norm_w, eps)
+    if swiglu_block:
+        return linear_swiglu(h, w, swiglu_block)
+    return linear(h, w, b)
+
+
 # ═══════════════════════════════ RMSNorm ═════════════════════════════════════
 
 class _RMSNorm(torch.autograd.Function):

@@ -436,14 +436,16 @@ class RolloutEngine:
         x = Fx.embedding(st["tok_in"][:b], m.embed)
         pos = st["pos"][:b]
         for li, layer in enumerate(m.layers):
-            h = Fx.rmsnorm(x, layer.attn_norm, a.norm_eps)
-            qkv = Fx.linear(h, layer.wqkv, layer.bqkv)
+            qkv = Fx.rmsnorm_linear(x, layer.attn_norm, a.norm_eps, layer.wqkv, layer.bqkv)
             q, _, _ = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
                                           a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1], st["slot"][:b])
             o = D.paged_attention(q, self.kv[li, 0], self.kv[li, 1], st["block_table"][:b], st["seq_lens"][:b])
             x = Fx.linear(o.reshape(b, a.q_dim), layer.wo, residual=x)
-            h = Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps)
-            x = self._mlp(layer, h, x)
+            if layer.moe is None:
+                act = Fx.rmsnorm_linear(x, layer.mlp_norm, a.norm_eps, layer.w13, swiglu_block=a.swiglu_block)
+                x = Fx.linear(act, layer.w2, residual=x)
+            else:
+                x = self._mlp(layer, Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps), x)
         h = Fx.rmsnorm(x, m.norm, a.norm_eps)
         r0 = self.running[0]
         tok, lp = D.sample(h, m.output_weight, r0.temperature, top_k=r0.top_k, top_p=r0.top_p, seed=self.seed,

@@ -427,3 +427,30 @@ def test_qkv_rope_cache_matches_rope_then_scatter(qk_norm):
     C().qkv_rope_cache(qkv, pos, qn, kn, q2, None, None, kc2, vc2, slots, 1e4, 1e-6)
     torch.cuda.synchronize()
     assert torch.equal(q1, q2) and torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+
+
+@pytest.mark.parametrize("M", [1, 8, 64, 130])
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_gemm_norm_fused_matches_rmsnorm_then_gemm(M, swiglu):
+    torch.manual_seed(23)
+    K, N = 1536, 2048
+    x, g, w, b = bf(M, K), bf(K), bf(N, K, scale=0.05), bf(N)
+    h = torch.empty_like(x)
+    rstd = torch.empty(M, device=DEV)
+    C().rmsnorm_fwd(x, g, h, rstd, 1e-6)
+    n_out = N // 2 if swiglu else N
+    want = torch.empty(M, n_out, dtype=torch.bfloat16, device=DEV)
+    got = torch.empty_like(want)
+    if swiglu:
+        C().gemm(h, w, want, False, False, None, None, None, 1, False, 64)
+        ok = C().gemm_norm(x, g, 1e-6, w, got, None, None, 1, 64)
+    else:
+        C().gemm(h, w, want, False, False, b, None, None, 0, False, 0)
+        ok = C().gemm_norm(x, g, 1e-6, w, got, b, None, 0, 0)
+    torch.cuda.synchronize()
+    if M > 128 and swiglu:
+        assert not ok  # large-M SwiGLU stays on the regular tiling
+        return
+    assert ok
+    assert C().device_error() == 0
+    assert torch.equal(got, want) or rel_err(got, want) < 2e-3
