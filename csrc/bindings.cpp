@@ -276,6 +276,35 @@ void flash_attn_bwd_(Tensor q, Tensor k, Tensor v, Tensor cu, Tensor out, Tensor
   count(3);
 }
 
+// Query chunks against a separate key stream (context parallelism): doc d = queries cu_q[d]..cu_q[d+1] at key
+// positions q_off[d].., keys cu_k[d]..cu_k[d+1].
+void flash_attn_fwd_kv_(Tensor q, Tensor k, Tensor v, Tensor cu_q, Tensor cu_k, Tensor q_off, Tensor out, Tensor lse,
+                        int64_t max_seqlen_q, double scale) {
+  CHECK_CONTIG(q);
+  CHECK_CONTIG(k);
+  CHECK_CONTIG(v);
+  TORCH_CHECK(cu_q.scalar_type() == at::kInt && cu_k.scalar_type() == at::kInt && q_off.scalar_type() == at::kInt,
+              "cu_q / cu_k / q_off must be int32");
+  TORCH_CHECK(cu_q.numel() == cu_k.numel() && q_off.numel() == cu_q.numel() - 1, "cu_q / cu_k / q_off sizes");
+  const c10::cuda::CUDAGuard guard(q.device());
+  flash_attn_fwd(ptr<bf16>(q), ptr<bf16>(k), ptr<bf16>(v), ptr<int>(cu_q), (int)cu_q.numel() - 1, ptr<bf16>(out),
+                 ptr<float>(lse), (int)q.size(0), (int)max_seqlen_q, (int)q.size(1), (int)k.size(1), (int)q.size(2),
+                 (float)scale, cur_stream(), ptr<int>(cu_k), ptr<int>(q_off));
+  count();
+}
+
+void flash_attn_bwd_kv_(Tensor q, Tensor k, Tensor v, Tensor cu_q, Tensor cu_k, Tensor q_off, Tensor out, Tensor gout,
+                        Tensor lse, Tensor gq, Tensor gk, Tensor gv, int64_t max_seqlen_q, int64_t max_seqlen_k,
+                        double scale) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  Tensor dvec = torch::empty({q.size(1), q.size(0)}, q.options().dtype(torch::kFloat));
+  flash_attn_bwd(ptr<bf16>(q), ptr<bf16>(k), ptr<bf16>(v), ptr<int>(cu_q), (int)cu_q.numel() - 1, ptr<bf16>(out),
+                 ptr<bf16>(gout), ptr<float>(lse), ptr<float>(dvec), ptr<bf16>(gq), ptr<bf16>(gk), ptr<bf16>(gv),
+                 (int)q.size(0), (int)max_seqlen_q, (int)q.size(1), (int)k.size(1), (int)q.size(2), (float)scale,
+                 cur_stream(), ptr<int>(cu_k), ptr<int>(q_off), (int)max_seqlen_k);
+  count(3);
+}
+
 constexpr int kLseBN = 256;
 
 // lp = z[label] - lse, lse, entropy — no [T, V] logits in memory
@@ -547,6 +576,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_rope_cache", &qkv_rope_cache_, "QK-norm + RoPE with K/V written straight into the paged cache");
   m.def("flash_attn_fwd", &flash_attn_fwd_);
   m.def("flash_attn_bwd", &flash_attn_bwd_);
+  m.def("flash_attn_fwd_kv", &flash_attn_fwd_kv_, "causal attention of query chunks against a separate key stream");
+  m.def("flash_attn_bwd_kv", &flash_attn_bwd_kv_);
   m.def("lmhead_logprob_fwd", &lmhead_logprob_fwd);
   m.def("lmhead_dlogits", &lmhead_dlogits);
   m.def("lmhead_sample", &lmhead_sample);

@@ -104,6 +104,7 @@ constexpr float kLn2 = 0.6931471805599453f;
 template <int HD>
 __global__ void __launch_bounds__(NT) fa_fwd_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
                                                     const bf16* __restrict__ V, const int* __restrict__ cu,
+                                                    const int* __restrict__ cu_k, const int* __restrict__ q_off,
                                                     bf16* __restrict__ O, float* __restrict__ LSE, int T, int max_blocks,
                                                     int Hq, int Hkv, float scale) {
   extern __shared__ __align__(128) uint8_t smraw[];
@@ -114,16 +115,20 @@ __global__ void __launch_bounds__(NT) fa_fwd_kernel(const bf16* __restrict__ Q, 
   const int qb = max_blocks - 1 - blockIdx.x % max_blocks;
   const int h = blockIdx.y, hk = h / (Hq / Hkv);
   const int s = cu[doc], e = cu[doc + 1], L = e - s;
+  // key document (the query document itself unless a separate key stream is given) and the
+  // position of the first query inside it: query i attends keys [0, qo + i]
+  const int ks = cu_k ? cu_k[doc] : s, ke = cu_k ? cu_k[doc + 1] : e, Lk = ke - ks;
+  const int qo = q_off ? q_off[doc] : 0;
   const int q0 = qb * BQ;
   if (q0 >= L) return;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const float sl2 = scale * kLog2e;
 
   load_tile<HD>(Qs, Q, s + q0, e, Hq, h);
-  load_tile<HD>(Ks, K, s, e, Hkv, hk);
-  load_tile<HD>(Vs, V, s, e, Hkv, hk);
+  load_tile<HD>(Ks, K, ks, ke, Hkv, hk);
+  load_tile<HD>(Vs, V, ks, ke, Hkv, hk);
   cp_commit();
-  const int n_kb = min((L + BKV - 1) / BKV, qb + 1);
+  const int n_kb = max(0, min((Lk + BKV - 1) / BKV, (qo + q0 + BQ - 1) / BKV + 1));
 
   uint32_t qf[HD / 16][4];
   float o[HD / 8][4];
@@ -136,8 +141,8 @@ __global__ void __launch_bounds__(NT) fa_fwd_kernel(const bf16* __restrict__ Q, 
   for (int kb = 0; kb < n_kb; ++kb) {
     const int buf = kb & 1;
     if (kb + 1 < n_kb) {
-      load_tile<HD>(Ks + (buf ^ 1) * BKV * HD, K, s + (kb + 1) * BKV, e, Hkv, hk);
-      load_tile<HD>(Vs + (buf ^ 1) * BKV * HD, V, s + (kb + 1) * BKV, e, Hkv, hk);
+      load_tile<HD>(Ks + (buf ^ 1) * BKV * HD, K, ks + (kb + 1) * BKV, ke, Hkv, hk);
+      load_tile<HD>(Vs + (buf ^ 1) * BKV * HD, V, ks + (kb + 1) * BKV, ke, Hkv, hk);
       cp_commit();
       cp_wait<1>();
     } else {
@@ -172,7 +177,7 @@ __global__ void __launch_bounds__(NT) fa_fwd_kernel(const bf16* __restrict__ Q, 
         int key = kb * BKV + j * 8 + 2 * (lane % 4) + (t & 1);
         int row = (t < 2) ? row_a : row_b;
         float v = sc[j][t] * sl2;
-        if (key > row || key >= L) v = -INFINITY;
+        if (key > row + qo || key >= Lk) v = -INFINITY;
         sc[j][t] = v;
         mx[t >> 1] = fmaxf(mx[t >> 1], v);
       }
@@ -275,7 +280,8 @@ template <int HD>
 __global__ void __launch_bounds__(NT) fa_bwd_dkdv_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
                                                          const bf16* __restrict__ V, const bf16* __restrict__ dO,
                                                          const float* __restrict__ LSE, const float* __restrict__ Dv,
-                                                         const int* __restrict__ cu, bf16* __restrict__ dK,
+                                                         const int* __restrict__ cu, const int* __restrict__ cu_k,
+                                                         const int* __restrict__ q_off, bf16* __restrict__ dK,
                                                          bf16* __restrict__ dV, int T, int max_blocks, int Hq, int Hkv,
                                                          float scale) {
   extern __shared__ __align__(128) uint8_t smraw[];
@@ -290,12 +296,14 @@ __global__ void __launch_bounds__(NT) fa_bwd_dkdv_kernel(const bf16* __restrict_
   const int hk = blockIdx.y;
   const int rep = Hq / Hkv;
   const int s = cu[doc], e = cu[doc + 1], L = e - s;
+  const int ks = cu_k ? cu_k[doc] : s, ke = cu_k ? cu_k[doc + 1] : e, Lk = ke - ks;
+  const int qo = q_off ? q_off[doc] : 0;
   const int k0 = kb * BKV;
-  if (k0 >= L) return;
+  if (k0 >= Lk) return;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const float sl2 = scale * kLog2e;
-  load_tile<HD>(Ks, K, s + k0, e, Hkv, hk);
-  load_tile<HD>(Vs, V, s + k0, e, Hkv, hk);
+  load_tile<HD>(Ks, K, ks + k0, ke, Hkv, hk);
+  load_tile<HD>(Vs, V, ks + k0, ke, Hkv, hk);
   cp_commit();
 
   float dk[HD / 8][4], dv[HD / 8][4];
@@ -305,7 +313,7 @@ __global__ void __launch_bounds__(NT) fa_bwd_dkdv_kernel(const bf16* __restrict_
     for (int t = 0; t < 4; ++t) dk[i][t] = dv[i][t] = 0.f;
 
   const int n_qb = (L + BQ - 1) / BQ;
-  const int qb_first = kb;  // causal: queries >= keys
+  const int qb_first = min(n_qb, max(0, k0 - qo) / BQ);  // causal: query positions >= keys
   const int n_iter = rep * (n_qb - qb_first);
   auto issue = [&](int it, int buf) {
     int hh = hk * rep + it / (n_qb - qb_first);
@@ -370,7 +378,7 @@ __global__ void __launch_bounds__(NT) fa_bwd_dkdv_kernel(const bf16* __restrict_
         int qrow = qb * BQ + ql;
         int key = (t < 2) ? key_a : key_b;
         float p = 0.f;
-        if (qrow < L && key <= qrow && key < L) p = exp2f(st[j][t] * sl2 - lse_b[ql] * kLog2e);
+        if (qrow < L && key <= qrow + qo && key < Lk) p = exp2f(st[j][t] * sl2 - lse_b[ql] * kLog2e);
         st[j][t] = p;
         dpt[j][t] = p * (dpt[j][t] - d_b[ql]);
       }
@@ -405,9 +413,9 @@ __global__ void __launch_bounds__(NT) fa_bwd_dkdv_kernel(const bf16* __restrict_
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     int key = r == 0 ? key_a : key_b;
-    if (key >= L) continue;
-    bf16* dkr = dK + ((size_t)(s + key) * Hkv + hk) * HD;
-    bf16* dvr = dV + ((size_t)(s + key) * Hkv + hk) * HD;
+    if (key >= Lk) continue;
+    bf16* dkr = dK + ((size_t)(ks + key) * Hkv + hk) * HD;
+    bf16* dvr = dV + ((size_t)(ks + key) * Hkv + hk) * HD;
 #pragma unroll
     for (int i = 0; i < HD / 8; ++i) {
       int c = i * 8 + 2 * (lane % 4);
@@ -421,7 +429,8 @@ template <int HD>
 __global__ void __launch_bounds__(NT) fa_bwd_dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
                                                        const bf16* __restrict__ V, const bf16* __restrict__ dO,
                                                        const float* __restrict__ LSE, const float* __restrict__ Dv,
-                                                       const int* __restrict__ cu, bf16* __restrict__ dQ, int T,
+                                                       const int* __restrict__ cu, const int* __restrict__ cu_k,
+                                                       const int* __restrict__ q_off, bf16* __restrict__ dQ, int T,
                                                        int max_blocks, int Hq, int Hkv, float scale) {
   extern __shared__ __align__(128) uint8_t smraw[];
   bf16* Qs = reinterpret_cast<bf16*>(smraw);
@@ -432,21 +441,23 @@ __global__ void __launch_bounds__(NT) fa_bwd_dq_kernel(const bf16* __restrict__ 
   const int qb = max_blocks - 1 - blockIdx.x % max_blocks;
   const int h = blockIdx.y, hk = h / (Hq / Hkv);
   const int s = cu[doc], e = cu[doc + 1], L = e - s;
+  const int ks = cu_k ? cu_k[doc] : s, ke = cu_k ? cu_k[doc + 1] : e, Lk = ke - ks;
+  const int qo = q_off ? q_off[doc] : 0;
   const int q0 = qb * BQ;
   if (q0 >= L) return;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const float sl2 = scale * kLog2e;
   load_tile<HD>(Qs, Q, s + q0, e, Hq, h);
   load_tile<HD>(dOs, dO, s + q0, e, Hq, h);
-  load_tile<HD>(Ks, K, s, e, Hkv, hk);
-  load_tile<HD>(Vs, V, s, e, Hkv, hk);
+  load_tile<HD>(Ks, K, ks, ke, Hkv, hk);
+  load_tile<HD>(Vs, V, ks, ke, Hkv, hk);
   cp_commit();
   const int row_a = q0 + warp * 16 + lane / 4, row_b = row_a + 8;
   const float lse_a = row_a < L ? LSE[(size_t)h * T + s + row_a] * kLog2e : 0.f;
   const float lse_b = row_b < L ? LSE[(size_t)h * T + s + row_b] * kLog2e : 0.f;
   const float d_a = row_a < L ? Dv[(size_t)h * T + s + row_a] : 0.f;
   const float d_b = row_b < L ? Dv[(size_t)h * T + s + row_b] : 0.f;
-  const int n_kb = min((L + BKV - 1) / BKV, qb + 1);
+  const int n_kb = max(0, min((Lk + BKV - 1) / BKV, (qo + q0 + BQ - 1) / BKV + 1));
   uint32_t qf[HD / 16][4];
   float dq[HD / 8][4];
 #pragma unroll
@@ -454,8 +465,8 @@ __global__ void __launch_bounds__(NT) fa_bwd_dq_kernel(const bf16* __restrict__ 
   for (int kb = 0; kb < n_kb; ++kb) {
     const int buf = kb & 1;
     if (kb + 1 < n_kb) {
-      load_tile<HD>(Ks + (buf ^ 1) * BKV * HD, K, s + (kb + 1) * BKV, e, Hkv, hk);
-      load_tile<HD>(Vs + (buf ^ 1) * BKV * HD, V, s + (kb + 1) * BKV, e, Hkv, hk);
+      load_tile<HD>(Ks + (buf ^ 1) * BKV * HD, K, ks + (kb + 1) * BKV, ke, Hkv, hk);
+      load_tile<HD>(Vs + (buf ^ 1) * BKV * HD, V, ks + (kb + 1) * BKV, ke, Hkv, hk);
       cp_commit();
       cp_wait<1>();
     } else {
@@ -496,7 +507,7 @@ __global__ void __launch_bounds__(NT) fa_bwd_dq_kernel(const bf16* __restrict__ 
         int key = kb * BKV + j * 8 + 2 * (lane % 4) + (t & 1);
         int row = t < 2 ? row_a : row_b;
         float p = 0.f;
-        if (row < L && key <= row) p = exp2f(sc[j][t] * sl2 - (t < 2 ? lse_a : lse_b));
+        if (row < L && key <= row + qo && key < Lk) p = exp2f(sc[j][t] * sl2 - (t < 2 ? lse_a : lse_b));
         dp[j][t] = p * (dp[j][t] - (t < 2 ? d_a : d_b));
       }
     }
@@ -747,7 +758,8 @@ static void set_smem(F f, int bytes) {
 }
 
 void flash_attn_fwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, bf16* o, float* lse, int T,
-                    int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st) {
+                    int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st, const int* cu_k,
+                    const int* q_off) {
   MESHY_CHECK(hd == 64 || hd == 128, "flash_attn: head_dim must be 64 or 128");
   MESHY_CHECK(Hq % Hkv == 0, "flash_attn: Hq must be a multiple of Hkv");
   int mb = (max_seqlen + BQ - 1) / BQ;
@@ -756,38 +768,42 @@ void flash_attn_fwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, 
   if (hd == 128) {
     int sm = (BQ + 4 * BKV) * 128 * 2;
     set_smem(fa_fwd_kernel<128>, sm);
-    fa_fwd_kernel<128><<<grid, NT, sm, st>>>(q, k, v, cu, o, lse, T, mb, Hq, Hkv, scale);
+    fa_fwd_kernel<128><<<grid, NT, sm, st>>>(q, k, v, cu, cu_k, q_off, o, lse, T, mb, Hq, Hkv, scale);
   } else {
     int sm = (BQ + 4 * BKV) * 64 * 2;
     set_smem(fa_fwd_kernel<64>, sm);
-    fa_fwd_kernel<64><<<grid, NT, sm, st>>>(q, k, v, cu, o, lse, T, mb, Hq, Hkv, scale);
+    fa_fwd_kernel<64><<<grid, NT, sm, st>>>(q, k, v, cu, cu_k, q_off, o, lse, T, mb, Hq, Hkv, scale);
   }
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 
 void flash_attn_bwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, const bf16* o,
                     const bf16* dout, const float* lse, float* dvec, bf16* dq, bf16* dk, bf16* dv, int T,
-                    int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st) {
+                    int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st, const int* cu_k,
+                    const int* q_off, int max_seqlen_k) {
   MESHY_CHECK(hd == 64 || hd == 128, "flash_attn: head_dim must be 64 or 128");
   long long warps = (long long)T * Hq;
   if (warps == 0) return;
   fa_bwd_prep_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(o, dout, dvec, T, Hq, hd);
   int mb = (max_seqlen + BQ - 1) / BQ;
-  dim3 g_kv(n_docs * mb, Hkv), g_q(n_docs * mb, Hq);
+  int mbk = ((cu_k ? max_seqlen_k : max_seqlen) + BKV - 1) / BKV;
+  dim3 g_kv(n_docs * mbk, Hkv), g_q(n_docs * mb, Hq);
   if (hd == 128) {
     int sm1 = (2 * BKV + 4 * BQ) * 128 * 2 + 4 * BQ * 4;
     set_smem(fa_bwd_dkdv_kernel<128>, sm1);
-    fa_bwd_dkdv_kernel<128><<<g_kv, NT, sm1, st>>>(q, k, v, dout, lse, dvec, cu, dk, dv, T, mb, Hq, Hkv, scale);
+    fa_bwd_dkdv_kernel<128><<<g_kv, NT, sm1, st>>>(q, k, v, dout, lse, dvec, cu, cu_k, q_off, dk, dv, T, mbk, Hq, Hkv,
+                                                   scale);
     int sm2 = (2 * BQ + 4 * BKV) * 128 * 2;
     set_smem(fa_bwd_dq_kernel<128>, sm2);
-    fa_bwd_dq_kernel<128><<<g_q, NT, sm2, st>>>(q, k, v, dout, lse, dvec, cu, dq, T, mb, Hq, Hkv, scale);
+    fa_bwd_dq_kernel<128><<<g_q, NT, sm2, st>>>(q, k, v, dout, lse, dvec, cu, cu_k, q_off, dq, T, mb, Hq, Hkv, scale);
   } else {
     int sm1 = (2 * BKV + 4 * BQ) * 64 * 2 + 4 * BQ * 4;
     set_smem(fa_bwd_dkdv_kernel<64>, sm1);
-    fa_bwd_dkdv_kernel<64><<<g_kv, NT, sm1, st>>>(q, k, v, dout, lse, dvec, cu, dk, dv, T, mb, Hq, Hkv, scale);
+    fa_bwd_dkdv_kernel<64><<<g_kv, NT, sm1, st>>>(q, k, v, dout, lse, dvec, cu, cu_k, q_off, dk, dv, T, mbk, Hq, Hkv,
+                                                  scale);
     int sm2 = (2 * BQ + 4 * BKV) * 64 * 2;
     set_smem(fa_bwd_dq_kernel<64>, sm2);
-    fa_bwd_dq_kernel<64><<<g_q, NT, sm2, st>>>(q, k, v, dout, lse, dvec, cu, dq, T, mb, Hq, Hkv, scale);
+    fa_bwd_dq_kernel<64><<<g_q, NT, sm2, st>>>(q, k, v, dout, lse, dvec, cu, cu_k, q_off, dq, T, mb, Hq, Hkv, scale);
   }
   MESHY_CUDA_CHECK(cudaGetLastError());
 }

@@ -1,11 +1,18 @@
 #pragma once
 #include "../include/common.cuh"
 namespace meshy {
+// Causal GQA flash attention over packed documents.  Document d's queries are rows [cu[d], cu[d+1])
+// of q; its keys are rows [cu_k[d], cu_k[d+1]) of k/v (cu_k null: the same rows) and its first query
+// sits at key position q_off[d] (null: 0), so query i attends keys [0, q_off[d] + i].  The second
+// form is what context parallelism uses: local query chunks against the gathered sequence.
 void flash_attn_fwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, bf16* o, float* lse, int T,
-                    int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st);
+                    int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st,
+                    const int* cu_k = nullptr, const int* q_off = nullptr);
+// dk / dv are written for every key row of every key document (zero where no query attends).
 void flash_attn_bwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, const bf16* o,
                     const bf16* dout, const float* lse, float* dvec, bf16* dq, bf16* dk, bf16* dv, int T,
-                    int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st);
+                    int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st,
+                    const int* cu_k = nullptr, const int* q_off = nullptr, int max_seqlen_k = 0);
 int paged_decode_splits(int B, int Hkv, int max_pages);
 void paged_decode(const bf16* q, const bf16* kc, const bf16* vc, const int* bt, const int* seq_lens, bf16* o,
                   float* part, int B, int Hq, int Hkv, int hd, int page, int max_pages, int n_split, float scale,

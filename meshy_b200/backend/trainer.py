@@ -54,11 +54,21 @@ class PPOTrainer:
         seed: int = 0,
         model=None,
         timer_enabled: bool = True,
+        cp_group=None,
+        loss_group=None,
     ):
         self.config = config
         self.params = params or TrainerParamsConfig()
         self.device = torch.device(device)
         self.dp_group = dp_group
+        # context parallelism: sequences split head-tail over cp_group; gradients and loss sums then
+        # reduce over the loss group (DP x CP), the data split stays over DP
+        self.cp = None
+        if cp_group is not None and dist.is_initialized() and dist.get_world_size(cp_group) > 1:
+            from ..parallel.cp import CpSharder
+
+            self.cp = CpSharder(cp_group)
+        self.loss_group = loss_group if loss_group is not None else dp_group
         self.model_args = get_model_args(config.model_name, config.model_flavor)
         cdt = torch.bfloat16 if (self.device.type == "cuda" and config.dtype == "bfloat16") else torch.float32
         self.compute_dtype = cdt
@@ -89,14 +99,14 @@ class PPOTrainer:
         )
         from ..parallel.ddp import GradReducer
 
-        self.reducer = GradReducer(self.flat, dp_group)
+        self.reducer = GradReducer(self.flat, self.loss_group)
         self.fused_dp = False
         if self._use_fused_dp():
             # DDP gradient reduction + AdamW as one NVLink pipeline (reduce-scatter, norm, shard update,
             # all-gather by P2P stores); the reducer has nothing left to do
             from ..parallel.symm import FusedDPAdamW
 
-            self.optimizer = FusedDPAdamW(self.flat, dp_group, lr=config.lr, betas=(config.beta1, config.beta2),
+            self.optimizer = FusedDPAdamW(self.flat, self.loss_group, lr=config.lr, betas=(config.beta1, config.beta2),
                                           eps=config.eps, weight_decay=config.weight_decay, max_norm=config.max_norm)
             self.flat.resident = ("master", "grad", "compute")
             self.reducer.backend = "none"
@@ -108,13 +118,14 @@ class PPOTrainer:
 
         if os.environ.get("MESHY_DP_FUSED", "auto") == "0" or self.device.type != "cuda":
             return False
-        if self.dp_group is None or not dist.is_initialized() or dist.get_world_size(self.dp_group) < 2:
+        g = self.loss_group
+        if g is None or not dist.is_initialized() or dist.get_world_size(g) < 2:
             return False
-        if dist.get_backend(self.dp_group) != "nccl":
+        if dist.get_backend(g) != "nccl":
             return False
         from ..parallel.symm import SymmetricHeap
 
-        return SymmetricHeap.supported(self.dp_group)
+        return SymmetricHeap.supported(g)
 
     # ------------------------------------------------------------------ planning
     @property
@@ -147,11 +158,17 @@ class PPOTrainer:
     # ------------------------------------------------------------------ forward
     def _build(self, samples, micro, need_rollout_lp=True) -> Batch:
         b = build_micro_batch(samples, micro, layout=self.batch_layout, device=self.device,
-                              need_rollout_lp=need_rollout_lp)
+                              need_rollout_lp=need_rollout_lp, sharder=self.cp)
         self.h2d_bytes += b.h2d_bytes
         return b
 
     def forward_batch(self, b: Batch, with_entropy: bool = False):
+        if self.cp is not None and "cp" in b.extra:
+            from ..parallel.cp import cp_attention
+
+            with cp_attention(self.cp, b.extra["cp"]):
+                return self.model.logprobs(b.input_ids, b.labels, b.positions, b.cu_seqlens, b.max_seqlen,
+                                           with_entropy=with_entropy, chunk=self.params.logprob_chunk_size * 4)
         return self.model.logprobs(b.input_ids, b.labels, b.positions, b.cu_seqlens, b.max_seqlen,
                                    with_entropy=with_entropy, chunk=self.params.logprob_chunk_size * 4)
 
@@ -253,7 +270,7 @@ class PPOTrainer:
             self.reducer.finish()
         with timer.timer("train/optim_step"):
             gn = self.optimizer.step()
-        return reduce_sums(sums, self.dp_group), gn
+        return reduce_sums(sums, self.loss_group), gn
 
     # ------------------------------------------------------------------ weights
     def named_weights(self):

@@ -56,12 +56,27 @@ class TrainerEngine(SpmdEngine):
     def setup(self) -> None:
         if self.world_size > 1 and not torch.distributed.is_initialized():
             self.init_process_group()
-        self.trainer = PPOTrainer(self.tc, self.tp, device=self.device,
-                                  dp_group=self.compute_group if self.world_size > 1 else None)
+        groups = self.parallel_groups()
+        self.trainer = PPOTrainer(self.tc, self.tp, device=self.device, **groups)
         if self.model_path and os.path.isdir(self.model_path):
             from ..models.hf import load_hf_checkpoint
 
             self.trainer.flat.load_state_dict(load_hf_checkpoint(self.trainer.model_args, self.model_path))
+
+    def parallel_groups(self) -> dict:
+        """DP / CP / loss groups of this replica from the trainer config's parallel degrees."""
+        if self.world_size == 1:
+            return {"dp_group": None}
+        from ..parallel.mesh import build_parallel_dims
+
+        tc = self.tc
+        cp = max(1, int(getattr(tc, "cp_degree", 1)))
+        if cp == 1 and int(getattr(tc, "tp_degree", 1)) <= 1:
+            return {"dp_group": self.compute_group}
+        pd = build_parallel_dims(self.world_size, self.rank, dp_replicate=-1, dp_shard=1, cp=cp,
+                                 tp=max(1, int(getattr(tc, "tp_degree", 1))))
+        self.parallel_dims = pd
+        return {"dp_group": pd.batch_group, "cp_group": pd.cp_group, "loss_group": pd.loss_group}
 
     @property
     def global_step(self) -> int:
@@ -82,7 +97,7 @@ class TrainerEngine(SpmdEngine):
         samples, sync = payload["samples"], payload["sync"]
         t = self.trainer
         plan = t.plan_batch(samples, t.dp_size)
-        local = plan.local_samples(samples, t.dp_rank)
+        local = plan.local_samples(samples, t.dp_rank)  # CP / TP ranks of one DP index get the same share
         t0 = time.perf_counter()
         metrics = t.train_step(local, plan=plan.per_rank[t.dp_rank], step_schedule=sync)
         metrics["time/train/step"] = time.perf_counter() - t0

@@ -291,14 +291,62 @@ class _FlashAttnVarlen(torch.autograd.Function):
         return gq, gk, gv, None, None, None
 
 
+_ATTN_OVERRIDE: list = []
+
+
+@contextmanager
+def attention_override(fn):
+    """Within the block, :func:`flash_attn_varlen` calls ``fn(q, k, v, cu_seqlens, max_seqlen, scale)``
+    instead (context parallelism routes the model's attention through its sharder this way)."""
+    _ATTN_OVERRIDE.append(fn)
+    try:
+        yield
+    finally:
+        _ATTN_OVERRIDE.pop()
+
+
 def flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen: int, scale: float | None = None):
     """Causal GQA attention over packed documents ``q [T,Hq,hd]``."""
+    if _ATTN_OVERRIDE:
+        return _ATTN_OVERRIDE[-1](q, k, v, cu_seqlens, max_seqlen, scale)
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if native(q):
         return _FlashAttnVarlen.apply(q, k, v, cu_seqlens, max_seqlen, scale)
     if q.is_cuda:  # torch baseline: SDPA per document batch
         return _sdpa_varlen(q, k, v, cu_seqlens, scale)
     return _RefAttn.apply(q, k, v, cu_seqlens, scale)
+
+
+class _FlashAttnKV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, cu_q, cu_k, q_off, max_q, max_k, scale):
+        C = ext()
+        out = torch.empty_like(q)
+        lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
+        C.flash_attn_fwd_kv(q, k, v, cu_q, cu_k, q_off, out, lse, int(max_q), float(scale))
+        ctx.save_for_backward(q, k, v, cu_q, cu_k, q_off, out, lse)
+        ctx.meta = (int(max_q), int(max_k), float(scale))
+        return out
+
+    @staticmethod
+    def backward(ctx, gout):
+        C = ext()
+        q, k, v, cu_q, cu_k, q_off, out, lse = ctx.saved_tensors
+        max_q, max_k, scale = ctx.meta
+        gq, gk, gv = torch.empty_like(q), torch.zeros_like(k), torch.zeros_like(v)
+        C.flash_attn_bwd_kv(q, k, v, cu_q, cu_k, q_off, out, gout.contiguous(), lse, gq, gk, gv, max_q, max_k, scale)
+        return gq, gk, gv, None, None, None, None, None, None
+
+
+def flash_attn_chunks(q, k, v, cu_q, cu_k, q_off, max_q: int, max_k: int, scale: float | None = None):
+    """Causal attention of query chunks ``q [Tq, Hq, hd]`` against key documents ``k/v [Tk, Hkv, hd]``:
+    chunk ``d`` = rows ``cu_q[d]..cu_q[d+1]`` sitting at key positions ``q_off[d]..`` of document
+    ``cu_k[d]..cu_k[d+1]``.  Context parallelism runs its local head/tail chunks against the gathered
+    sequence with it."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if native(q):
+        return _FlashAttnKV.apply(q, k, v, cu_q, cu_k, q_off, max_q, max_k, scale)
+    return ref.attention_chunks(q, k, v, cu_q, cu_k, q_off, scale).to(q.dtype)
 
 
 class _RefAttn(torch.autograd.Function):

@@ -81,6 +81,29 @@ def swiglu(h: torch.Tensor, block: int) -> torch.Tensor:
 
 # ── attention ────────────────────────────────────────────────────────────────
 
+def attention_chunks(q, k, v, cu_q, cu_k, q_off, scale: float | None = None) -> torch.Tensor:
+    """Causal GQA attention of query chunks against separate key documents: chunk ``d`` holds queries
+    ``cu_q[d]..`` at key positions ``q_off[d]..`` of keys ``cu_k[d]..cu_k[d+1]`` (fp32 oracle)."""
+    T, Hq, hd = q.shape
+    rep = Hq // k.shape[1]
+    scale = scale if scale is not None else 1.0 / math.sqrt(hd)
+    out = torch.zeros(T, Hq, hd, dtype=torch.float32, device=q.device)
+    cq, ck, qo = cu_q.tolist(), cu_k.tolist(), q_off.tolist()
+    for d in range(len(cq) - 1):
+        s, e, ks, ke = cq[d], cq[d + 1], ck[d], ck[d + 1]
+        if e <= s:
+            continue
+        qd = q[s:e].float().transpose(0, 1)
+        kd = k[ks:ke].float().transpose(0, 1).repeat_interleave(rep, 0)
+        vd = v[ks:ke].float().transpose(0, 1).repeat_interleave(rep, 0)
+        sc = torch.matmul(qd, kd.transpose(1, 2)) * scale
+        qpos = torch.arange(e - s, device=q.device).unsqueeze(1) + qo[d]
+        kpos = torch.arange(ke - ks, device=q.device).unsqueeze(0)
+        sc = sc.masked_fill(kpos > qpos, float("-inf"))
+        out[s:e] = torch.matmul(torch.softmax(sc, -1), vd).transpose(0, 1)
+    return out
+
+
 def attention_varlen(
     q: torch.Tensor,          # [T, Hq, hd]
     k: torch.Tensor,          # [T, Hkv, hd]

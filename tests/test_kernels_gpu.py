@@ -454,3 +454,29 @@ def test_gemm_norm_fused_matches_rmsnorm_then_gemm(M, swiglu):
     assert ok
     assert C().device_error() == 0
     assert torch.equal(got, want) or rel_err(got, want) < 2e-3
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_flash_attn_chunks_offsets_fwd_bwd(hd):
+    """Query chunks at key offsets against separate key documents (the context-parallel form)."""
+    from meshy_b200.ops import functional as Fx
+
+    torch.manual_seed(24)
+    Hq, Hkv, S, c = 8, 2, 256, 64
+    rows = 2
+    cu_q = torch.tensor([0, c, 2 * c], dtype=torch.int32, device=DEV)
+    cu_k = torch.tensor([0, S, 2 * S], dtype=torch.int32, device=DEV)
+    q_off = torch.tensor([64, 192], dtype=torch.int32, device=DEV)
+    q = bf(rows * c, Hq, hd).requires_grad_(True)
+    k = bf(rows * S, Hkv, hd).requires_grad_(True)
+    v = bf(rows * S, Hkv, hd).requires_grad_(True)
+    out = Fx.flash_attn_chunks(q, k, v, cu_q, cu_k, q_off, c, S)
+    go = bf(*out.shape)
+    out.backward(go)
+    qr, kr, vr = (t.detach().float().cpu().requires_grad_(True) for t in (q, k, v))
+    o_ref = ref.attention_chunks(qr, kr, vr, cu_q.cpu(), cu_k.cpu(), q_off.cpu())
+    o_ref.backward(go.float().cpu())
+    assert rel_err(out.cpu(), o_ref) < 1e-2
+    assert rel_err(q.grad.cpu(), qr.grad) < 3e-2
+    assert rel_err(k.grad.cpu(), kr.grad) < 3e-2
+    assert rel_err(v.grad.cpu(), vr.grad) < 3e-2
