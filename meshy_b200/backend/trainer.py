@@ -56,6 +56,7 @@ class PPOTrainer:
         timer_enabled: bool = True,
         cp_group=None,
         loss_group=None,
+        ep_group=None,
     ):
         self.config = config
         self.params = params or TrainerParamsConfig()
@@ -74,6 +75,13 @@ class PPOTrainer:
         self.compute_dtype = cdt
         if model is None:
             model = build_model(self.model_args, seed=seed, device=self.device, dtype=torch.float32)
+        # expert parallelism: this rank keeps 1/ep of every MoE layer's experts (ep_group = the DP ranks
+        # that split the experts); their gradients are never summed over that group
+        self.ep_group = ep_group
+        if ep_group is not None and dist.is_initialized() and dist.get_world_size(ep_group) > 1:
+            from ..parallel.ep import shard_experts
+
+            shard_experts(model, ep_group)
         self.model = model
         self.model.activation_checkpoint = config.activation_checkpoint_mode == "full"
         self.flat = FlatParams(self.model, compute_dtype=cdt, device=self.device)
@@ -99,7 +107,9 @@ class PPOTrainer:
         )
         from ..parallel.ddp import GradReducer
 
-        self.reducer = GradReducer(self.flat, self.loss_group)
+        expert_slots = [(sl.offset, sl.numel) for sl in self.flat.slots
+                        if ".moe.w13" in sl.name or ".moe.w2" in sl.name] if self.ep_group is not None else []
+        self.reducer = GradReducer(self.flat, self.loss_group, skip=expert_slots)
         self.fused_dp = False
         if self._use_fused_dp():
             # DDP gradient reduction + AdamW as one NVLink pipeline (reduce-scatter, norm, shard update,
@@ -117,6 +127,8 @@ class PPOTrainer:
         import os
 
         if os.environ.get("MESHY_DP_FUSED", "auto") == "0" or self.device.type != "cuda":
+            return False
+        if self.ep_group is not None:  # expert slices differ per rank: keep the range-aware reducer
             return False
         g = self.loss_group
         if g is None or not dist.is_initialized() or dist.get_world_size(g) < 2:
@@ -269,8 +281,26 @@ class PPOTrainer:
         with timer.timer("train/grad_reduce"):
             self.reducer.finish()
         with timer.timer("train/optim_step"):
-            gn = self.optimizer.step()
+            gn = self.optimizer.step(self._ep_grad_norm() if self.reducer.skip else None)
         return reduce_sums(sums, self.loss_group), gn
+
+    def _ep_grad_norm(self) -> torch.Tensor:
+        """Global gradient norm under expert parallelism: the dense part is replicated (counted once),
+        every rank's experts are its own (their squared norms are summed over the EP group), so all ranks
+        clip with the same coefficient."""
+        g = self.flat.grad
+        exp_sq = torch.zeros((), dtype=torch.float32, device=g.device)
+        for off, n in self.reducer.skip:
+            exp_sq = exp_sq + g[off:off + n].float().pow(2).sum()
+        total_sq = g.float().pow(2).sum()
+        dense_sq = total_sq - exp_sq
+        if dist.is_initialized() and dist.get_world_size(self.ep_group) > 1:
+            t = exp_sq.reshape(1).clone()
+            if dist.get_backend(self.ep_group) != "nccl":
+                t = t.cpu()
+            dist.all_reduce(t, group=self.ep_group)
+            exp_sq = t.to(g.device).reshape(())
+        return (dense_sq + exp_sq).sqrt()
 
     # ------------------------------------------------------------------ weights
     def named_weights(self):

@@ -71,8 +71,14 @@ class TrainerEngine(SpmdEngine):
 
         tc = self.tc
         cp = max(1, int(getattr(tc, "cp_degree", 1)))
+        ep = max(1, int(getattr(tc, "ep_degree", 1)))
         if cp == 1 and int(getattr(tc, "tp_degree", 1)) <= 1:
-            return {"dp_group": self.compute_group}
+            out = {"dp_group": self.compute_group}
+            if ep > 1:
+                if ep != self.world_size:
+                    raise ValueError("ep_degree must equal the replica's DP size (experts split over the DP ranks)")
+                out["ep_group"] = self.compute_group
+            return out
         pd = build_parallel_dims(self.world_size, self.rank, dp_replicate=-1, dp_shard=1, cp=cp,
                                  tp=max(1, int(getattr(tc, "tp_degree", 1))))
         self.parallel_dims = pd

@@ -44,7 +44,7 @@ def _worker(rank, world, port, q):
         g = dist.new_group([0, 1])
         t = _trainer(cp_group=g, loss_group=g)
         m = t.train_step(_samples())
-        q.put((rank, t.flat.grad.clone(), m["pg_loss"]))
+        q.put((rank, t.flat.grad.numpy().copy(), m["pg_loss"]))  # by value: shared tensors die with the worker
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
@@ -71,6 +71,7 @@ def test_context_parallel_step_matches_single_rank():
         p.join(timeout=60)
     for rank, got, loss in res:
         assert not isinstance(got, str), got
+        got = torch.from_numpy(got)
         assert abs(loss - m_ref["pg_loss"]) < 1e-4 * max(1.0, abs(m_ref["pg_loss"])), (loss, m_ref["pg_loss"])
         err = ((got - want).norm() / want.norm()).item()
         assert err < 1e-4, err
