@@ -57,6 +57,7 @@ class PPOTrainer:
         cp_group=None,
         loss_group=None,
         ep_group=None,
+        tp_group=None,
     ):
         self.config = config
         self.params = params or TrainerParamsConfig()
@@ -77,6 +78,11 @@ class PPOTrainer:
             model = build_model(self.model_args, seed=seed, device=self.device, dtype=torch.float32)
         # expert parallelism: this rank keeps 1/ep of every MoE layer's experts (ep_group = the DP ranks
         # that split the experts); their gradients are never summed over that group
+        self.tp_group = tp_group
+        if tp_group is not None and dist.is_initialized() and dist.get_world_size(tp_group) > 1:
+            from ..parallel.tp import shard_model_tp
+
+            shard_model_tp(model, tp_group)
         self.ep_group = ep_group
         if ep_group is not None and dist.is_initialized() and dist.get_world_size(ep_group) > 1:
             from ..parallel.ep import shard_experts
@@ -110,6 +116,11 @@ class PPOTrainer:
         expert_slots = [(sl.offset, sl.numel) for sl in self.flat.slots
                         if ".moe.w13" in sl.name or ".moe.w2" in sl.name] if self.ep_group is not None else []
         self.reducer = GradReducer(self.flat, self.loss_group, skip=expert_slots)
+        # under TP the per-head QK-norm gains are replicated but each rank's gradient covers only its
+        # heads: those slots are summed over the TP group before the DP reduction
+        self.tp_partial = [(sl.offset, sl.numel) for sl in self.flat.slots
+                           if sl.name.endswith(".q_norm") or sl.name.endswith(".k_norm")] \
+            if (self.tp_group is not None and dist.is_initialized() and dist.get_world_size(self.tp_group) > 1) else []
         self.fused_dp = False
         if self._use_fused_dp():
             # DDP gradient reduction + AdamW as one NVLink pipeline (reduce-scatter, norm, shard update,
@@ -279,6 +290,8 @@ class PPOTrainer:
             sums = mb_sums if sums is None else {k: sums[k] + v for k, v in mb_sums.items()}
         self.flat.collect_cpu_grads()
         with timer.timer("train/grad_reduce"):
+            for off, n in self.tp_partial:
+                dist.all_reduce(self.flat.grad[off:off + n], group=self.tp_group)
             self.reducer.finish()
         with timer.timer("train/optim_step"):
             gn = self.optimizer.step(self._ep_grad_norm() if self.reducer.skip else None)

@@ -82,7 +82,8 @@ class TrainerEngine(SpmdEngine):
         pd = build_parallel_dims(self.world_size, self.rank, dp_replicate=-1, dp_shard=1, cp=cp,
                                  tp=max(1, int(getattr(tc, "tp_degree", 1))))
         self.parallel_dims = pd
-        return {"dp_group": pd.batch_group, "cp_group": pd.cp_group, "loss_group": pd.loss_group}
+        return {"dp_group": pd.batch_group, "cp_group": pd.cp_group, "loss_group": pd.loss_group,
+                "tp_group": pd.tp_group}
 
     @property
     def global_step(self) -> int:

@@ -63,7 +63,11 @@ class Block(nn.Module):
         else:
             self.moe.reset_parameters(std, depth_std)
 
+    tp_group = None  # set by parallel.tp.shard_model_tp
+
     def forward(self, x, positions, cu_seqlens, max_seqlen):
+        if self.tp_group is not None:
+            return self._forward_tp(x, positions, cu_seqlens, max_seqlen)
         a = self.args
         T = x.shape[0]
         h = Fx.rmsnorm(x, self.attn_norm, a.norm_eps)
@@ -77,6 +81,22 @@ class Block(nn.Module):
             act = Fx.linear_swiglu(h, self.w13, a.swiglu_block)
             return Fx.linear(act, self.w2, residual=x)
         return x + self.moe(h)
+
+    def _forward_tp(self, x, positions, cu_seqlens, max_seqlen):
+        """Tensor-parallel block: this rank's heads / MLP slice, all-reduce after the row-parallel GEMMs."""
+        from ..parallel.tp import copy_to_tp, reduce_from_tp
+
+        a, g = self.args, self.tp_group
+        T = x.shape[0]
+        h = copy_to_tp(Fx.rmsnorm(x, self.attn_norm, a.norm_eps), g)
+        qkv = Fx.linear(h, self.wqkv, self.bqkv)
+        q, k, v = Fx.qkv_rope(qkv, positions, self.q_norm, self.k_norm, a.n_heads, a.n_kv_heads,
+                              a.head_dim, a.rope_theta, a.norm_eps)
+        o = Fx.flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen)
+        x = x + reduce_from_tp(Fx.linear(o.reshape(T, a.n_heads * a.head_dim), self.wo), g)
+        h = copy_to_tp(Fx.rmsnorm(x, self.mlp_norm, a.norm_eps), g)
+        act = Fx.linear_swiglu(h, self.w13, a.swiglu_block)
+        return x + reduce_from_tp(Fx.linear(act, self.w2), g)
 
 
 class DecoderLM(nn.Module):
