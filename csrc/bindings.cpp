@@ -562,7 +562,12 @@ int64_t launch_count() { return g_launches.load(); }
 
 }  // namespace
 
+namespace meshy {
+void register_vmm(pybind11::module_& m);
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  meshy::register_vmm(m);
   m.doc() = "meshy_b200 sm_100a kernel library";
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues");
   m.def("gemm_norm", &gemm_norm, "decode: fused input RMSNorm + small-M GEMM (returns False if not eligible)");

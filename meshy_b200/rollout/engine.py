@@ -116,6 +116,20 @@ class RolloutEngine:
         for p in self.model.parameters():
             p.requires_grad_(False)
         self.weight_flat, self.weight_slots = flatten_module(self.model, self.dtype, self.device)
+        self._vmm = {}
+        if self.cuda:
+            # weights and KV cache live in virtual-memory regions: releasing them for a colocated trainer
+            # frees the physical pages but keeps the addresses, so captured decode graphs stay valid
+            from ..ops._ext import ext
+
+            n = self.weight_flat.numel()
+            reg = ext().VmmRegion(n * self.weight_flat.element_size(), self.device.index or 0)
+            view = reg.view(0, [n], self.weight_flat.dtype)
+            view.copy_(self.weight_flat)
+            self._vmm["weights"] = reg
+            self.weight_flat = view
+            self._rebind_weights()
+            torch.cuda.empty_cache()
         self.page_size = page_size
         self.max_running = max_running
         self.max_seq_len = min(max_seq_len or args.max_seq_len, args.max_seq_len)
@@ -150,8 +164,21 @@ class RolloutEngine:
     # ------------------------------------------------------------------ memory
     def _alloc_kv(self):
         a = self.args
-        self.kv = torch.zeros(a.n_layers, 2, self.n_pages, a.n_kv_heads, self.page_size, a.head_dim,
-                              dtype=self.dtype, device=self.device)
+        shape = [a.n_layers, 2, self.n_pages, a.n_kv_heads, self.page_size, a.head_dim]
+        if not self.cuda:
+            self.kv = torch.zeros(*shape, dtype=self.dtype, device=self.device)
+            return
+        from ..ops._ext import ext
+
+        nbytes = math.prod(shape) * torch.empty((), dtype=self.dtype).element_size()
+        reg = self._vmm.get("kv_cache") if hasattr(self, "_vmm") else None
+        if reg is None:
+            reg = ext().VmmRegion(nbytes, self.device.index or 0)
+            self._vmm["kv_cache"] = reg
+        elif not reg.mapped:
+            reg.map()
+        self.kv = reg.view(0, shape, self.dtype)
+        self.kv.zero_()
 
     def _init_state(self):
         B, dev = self.max_running, self.device
@@ -178,29 +205,45 @@ class RolloutEngine:
         self._park_rows(0)
 
     def release_memory(self, tags: Sequence[str] = ("kv_cache", "weights")) -> None:
-        """Give GPU memory back for a colocated trainer (graphs are dropped)."""
+        """Give GPU memory back for a colocated trainer.
+
+        On CUDA the physical pages of the tagged regions are released while their virtual addresses stay
+        reserved, so the captured decode graphs remain valid; weights are parked in pinned host memory
+        first (the KV cache is dropped: requests were aborted before a release)."""
         with self.lock:
-            self._graphs.clear()
-            if "kv_cache" in tags and self.kv is not None:
-                self.kv = None
-            if "weights" in tags and self.weight_flat is not None and self.cuda:
+            if not self.cuda:
+                return
+            torch.cuda.synchronize(self.device)
+            if "weights" in tags and self._vmm["weights"].mapped:
                 host = torch.empty(self.weight_flat.shape, dtype=self.weight_flat.dtype, pin_memory=True)
                 host.copy_(self.weight_flat)
                 self._host_weights = host
-                self.weight_flat = None
-                for p in self.model.parameters():
-                    p.data = torch.empty(0, dtype=p.dtype, device=self.device)
-            if self.cuda:
-                torch.cuda.empty_cache()
+                self._vmm["weights"].unmap()
+            if "kv_cache" in tags and "kv_cache" in self._vmm and self._vmm["kv_cache"].mapped:
+                self._vmm["kv_cache"].unmap()
+            torch.cuda.empty_cache()
 
     def resume_memory(self, tags: Sequence[str] = ("kv_cache", "weights")) -> None:
         with self.lock:
-            if "weights" in tags and self.weight_flat is None:
-                self.weight_flat = self._host_weights.to(self.device)
+            if not self.cuda:
+                return
+            if "weights" in tags and not self._vmm["weights"].mapped:
+                self._vmm["weights"].map()
+                self.weight_flat.copy_(self._host_weights)
                 self._host_weights = None
-                self._rebind_weights()
-            if "kv_cache" in tags and self.kv is None:
+            if "kv_cache" in tags and not self._vmm["kv_cache"].mapped:
                 self._alloc_kv()
+
+    def _check_resident(self, tags=("weights", "kv_cache")) -> None:
+        """Touching a released region would fault the GPU: refuse on the host instead."""
+        for t in tags:
+            r = getattr(self, "_vmm", {}).get(t)
+            if r is not None and not r.mapped:
+                raise RuntimeError(f"{t} memory is released; call resume_memory([{t!r}]) first")
+
+    @property
+    def memory_released(self) -> dict:
+        return {k: not r.mapped for k, r in getattr(self, "_vmm", {}).items()}
 
     def _rebind_weights(self):
         for s, p in zip(self.weight_slots, self.model.parameters()):
@@ -210,8 +253,7 @@ class RolloutEngine:
     def update_weights_from_flat(self, src: torch.Tensor, version: int | None = None) -> None:
         """Device weight sync: ``src`` is a flat buffer in the same layout."""
         with self.lock:
-            if self.weight_flat is None:
-                raise RuntimeError("weights are released; resume_memory(['weights']) first")
+            self._check_resident(("weights",))
             if src.numel() != self.weight_flat.numel():
                 raise ValueError("flat weight layout mismatch")
             if src.dtype == self.weight_flat.dtype:
@@ -226,6 +268,7 @@ class RolloutEngine:
 
     def update_weights_from_state_dict(self, sd: dict[str, torch.Tensor], version: int | None = None) -> None:
         with self.lock:
+            self._check_resident(("weights",))
             with torch.no_grad():
                 for s in self.weight_slots:
                     self.weight_flat[s.offset:s.offset + s.numel].copy_(sd[s.name].reshape(-1))
@@ -299,6 +342,8 @@ class RolloutEngine:
     # ------------------------------------------------------------------ scheduling
     def step(self) -> None:
         with self.lock:
+            if self.waiting or self.running:
+                self._check_resident()
             self._admit()
             if not self.running:
                 return

@@ -18,6 +18,7 @@ ARCH = ["-gencode=arch=compute_100a,code=sm_100a"]
 
 cuda_sources = [
     "csrc/bindings.cpp",
+    "csrc/vmm.cpp",
     "csrc/kernels/gemm.cu",
     "csrc/kernels/gemm_small.cu",
     "csrc/kernels/elementwise.cu",

@@ -90,3 +90,32 @@ def test_engine_logprobs_match_trainer():
     m = b.mask > 0
     diff = (lp[m] - b.rollout_logprobs[m]).abs()
     assert diff.mean().item() < 0.05, diff.mean()
+
+
+def test_engine_release_resume_keeps_addresses_and_graphs():
+    """Colocation hand-off through virtual-memory regions: physical pages go back to the driver, the
+    addresses (and so the captured decode graphs) survive, weights come back bit-exact."""
+    from meshy_b200.models import get_model_args
+    from meshy_b200.rollout import RolloutEngine
+
+    args = get_model_args("qwen3", "debugmodel")
+    e = RolloutEngine(args, device="cuda", max_running=8, max_total_tokens=1 << 16, page_size=64, max_seq_len=512,
+                      use_cuda_graph=True, seed=3, sync_every=4)
+    e.generate([[1, 2, 3, 4, 5] * 4], [12], ignore_eos=True)
+    n_graphs = len(e._graphs)
+    w_before = e.weight_flat.clone()
+    kv_ptr, w_ptr = e.kv.data_ptr(), e.weight_flat.data_ptr()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    e.release_memory()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 - free0 >= e.kv.numel() * 2  # at least the KV cache went back
+    assert all(e.memory_released.values())
+    with pytest.raises(RuntimeError, match="released"):
+        e.update_weights_from_flat(w_before)
+    e.resume_memory()
+    assert e.kv.data_ptr() == kv_ptr and e.weight_flat.data_ptr() == w_ptr
+    assert torch.equal(e.weight_flat, w_before)
+    gens = e.generate([[1, 2, 3, 4, 5] * 4, [7, 8, 9]], [12, 9], ignore_eos=True)
+    assert [len(g.output_ids) for g in gens] == [12, 9]
+    assert len(e._graphs) >= n_graphs
