@@ -67,7 +67,7 @@ class TrajectoryLogger:
     async def write(self, group: list, version: int) -> None:
         lines = []
         for s in group:
-            rec = {"weight_version": version, "reward": s.reward, "raw_reward": s.raw_reward,
+            rec = {"timestamp": time.time(), "weight_version": version, "reward": s.reward, "raw_reward": s.raw_reward,
                    "advantage": s.advantage, "finish_reason": s.finish_reason, "truncated": s.truncated,
                    "repetition": s.repetition, "messages": s.messages, "n_tokens": len(s.tokens)}
             if self.verbose:
