@@ -13,10 +13,12 @@ from typing import Any
 
 
 class Dataset:
-    def __init__(self, rows: list[dict], batch_size: int, seed: int | None = None):
+    def __init__(self, rows: list[dict], batch_size: int, seed: int | None = None, limit: int | None = None):
         self.rows = list(rows)
         if seed is not None:
             random.Random(seed).shuffle(self.rows)
+        if limit is not None:  # a bounded run (smoke / fixture recipes): the first ``limit`` prompts only
+            self.rows = self.rows[:int(limit)]
         self.batch_size = int(batch_size)
         self.index = 0
 

@@ -13,9 +13,9 @@ PROMPT_SUFFIX = "\nPlease reason step by step, and put your final answer within 
 class MATH(Dataset):
     """Rows ``{"prompt"|"problem": str, "answer"|"solution": str}`` from a local JSONL."""
 
-    def __init__(self, batch_size: int, seed: int | None = None, path: str | None = None):
+    def __init__(self, batch_size: int, seed: int | None = None, path: str | None = None, limit: int | None = None):
         path = path or os.environ.get("MATH_DATASET_PATH", "")
-        super().__init__(self.read_jsonl(path) if path else [], batch_size, seed)
+        super().__init__(self.read_jsonl(path) if path else [], batch_size, seed, limit)
 
     def apply_chat_template(self, row, builder):
         q = row.get("prompt") or row.get("problem") or row.get("question")
@@ -29,9 +29,9 @@ class MATH(Dataset):
 
 
 class GSM8K(Dataset):
-    def __init__(self, batch_size: int, seed: int | None = None, path: str | None = None):
+    def __init__(self, batch_size: int, seed: int | None = None, path: str | None = None, limit: int | None = None):
         path = path or os.environ.get("GSM8K_DATASET_PATH", "")
-        super().__init__(self.read_jsonl(path) if path else [], batch_size, seed)
+        super().__init__(self.read_jsonl(path) if path else [], batch_size, seed, limit)
 
     def apply_chat_template(self, row, builder):
         s = builder.build_sample([{"role": "user", "content": row["question"] + PROMPT_SUFFIX}])
@@ -44,8 +44,8 @@ class GSM8K(Dataset):
 
 
 class S9Math(MATH):
-    def __init__(self, batch_size: int, seed: int | None = None, path: str | None = None):
-        super().__init__(batch_size, seed, path or os.environ.get("S9_DATASET_PATH", ""))
+    def __init__(self, batch_size: int, seed: int | None = None, path: str | None = None, limit: int | None = None):
+        super().__init__(batch_size, seed, path or os.environ.get("S9_DATASET_PATH", ""), limit)
 
 
 __all__ = ["GSM8K", "MATH", "S9Math"]
