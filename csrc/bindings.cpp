@@ -522,6 +522,8 @@ void symm_dp_adamw_(Tensor grad_ptrs, Tensor master_ptrs, c10::optional<Tensor> 
                     Tensor scalars, int64_t rank, int64_t world, int64_t lo, int64_t hi, int64_t epoch, double max_norm,
                     double lr, double b1, double b2, double eps, double wd, int64_t step, double timeout_s) {
   TORCH_CHECK(scalars.scalar_type() == at::kFloat && scalars.numel() >= 2, "scalars: fp32 [2] (sumsq, norm)");
+  TORCH_CHECK(exp_avg.numel() >= hi - lo && exp_avg_sq.numel() >= hi - lo,
+              "symm_dp_adamw: the moments are this rank's shard [lo, hi)");
   SymmAdamWArgs a;
   auto tab = [](const Tensor& t) { return reinterpret_cast<const unsigned long long*>(t.data_ptr()); };
   a.grad_ptrs = tab(grad_ptrs);

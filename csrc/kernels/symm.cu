@@ -54,9 +54,6 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
 __global__ void symm_barrier_kernel(const unsigned long long* __restrict__ flag_ptrs, int rank, int world,
                                     unsigned int epoch, long long timeout_cycles, int* err) {
   const int p = threadIdx.x;
-  __shared__ int failed;
-  if (p == 0) failed = 0;
-  __syncthreads();
   if (p < world) {
     // flags of rank q: world u32 slots, slot r = last epoch rank r reached
     unsigned int* peer_flags = reinterpret_cast<unsigned int*>(flag_ptrs[p]);
@@ -67,7 +64,6 @@ __global__ void symm_barrier_kernel(const unsigned long long* __restrict__ flag_
     while ((int)(ld_acquire_sys(mine) - epoch) < 0) {
       if (clock64() - t0 > timeout_cycles) {
         atomicCAS(err, 0, (int)kErrTimeoutPeer);
-        failed = 1;
         break;
       }
     }
@@ -155,7 +151,8 @@ __global__ void symm_adamw_push_kernel(const unsigned long long* __restrict__ ma
     const long long e = lo + 4 * i;
     float4 pp = *reinterpret_cast<const float4*>(master_local + e);
     const float4 gg = *reinterpret_cast<const float4*>(g + e);
-    float4 mm = *reinterpret_cast<const float4*>(m + e), vv = *reinterpret_cast<const float4*>(v + e);
+    // moments hold only this rank's shard [lo, hi)
+    float4 mm = *reinterpret_cast<const float4*>(m + 4 * i), vv = *reinterpret_cast<const float4*>(v + 4 * i);
     float* P = &pp.x;
     const float* G = &gg.x;
     float* Mv = &mm.x;
@@ -167,8 +164,8 @@ __global__ void symm_adamw_push_kernel(const unsigned long long* __restrict__ ma
       Vv[k] = b2 * Vv[k] + (1.f - b2) * gk * gk;
       P[k] = P[k] * decay - step * Mv[k] / (sqrtf(Vv[k] * inv_bc2) + eps);
     }
-    *reinterpret_cast<float4*>(m + e) = mm;
-    *reinterpret_cast<float4*>(v + e) = vv;
+    *reinterpret_cast<float4*>(m + 4 * i) = mm;
+    *reinterpret_cast<float4*>(v + 4 * i) = vv;
     const uint2 packed = make_uint2(pack_bf16x2(pp.x, pp.y), pack_bf16x2(pp.z, pp.w));
     for (int q = 0; q < world; ++q) {
       *reinterpret_cast<float4*>(reinterpret_cast<float*>(master_ptrs[q]) + e) = pp;

@@ -26,8 +26,8 @@ struct SymmAdamWArgs {
   const unsigned long long* slot_ptrs = nullptr;     // [world] f32[world] norm slots
   const float* master_local = nullptr;
   float* local_grad = nullptr;
-  float* exp_avg = nullptr;
-  float* exp_avg_sq = nullptr;
+  float* exp_avg = nullptr;     // AdamW moments of this rank's shard only: [hi - lo]
+  float* exp_avg_sq = nullptr;  // (ZeRO-1: every rank keeps 1/world of the optimiser state)
   float* sumsq = nullptr;  // device scratch scalar
   float* norm = nullptr;   // device scalar: global gradient norm (output)
   int* err = nullptr;

@@ -15,12 +15,19 @@ import torch.distributed as dist
 import torch.distributed.checkpoint as dcp
 
 
-def _state(trainer) -> dict:
+def _moments(trainer):
+    """Full-length AdamW moments; an optimiser with sharded moments gathers them (a collective)."""
     f = trainer.flat
-    sd = {f"model.{k}": v for k, v in f.state_dict().items()}
-    sd.update({f"optim.exp_avg.{s.name}": f.exp_avg[s.offset:s.offset + s.numel].view(s.shape) for s in f.slots})
-    sd.update({f"optim.exp_avg_sq.{s.name}": f.exp_avg_sq[s.offset:s.offset + s.numel].view(s.shape)
-               for s in f.slots})
+    full = getattr(trainer.optimizer, "full_moments", None)
+    return full() if full is not None else (f.exp_avg, f.exp_avg_sq)
+
+
+def _state(trainer, moments=None) -> dict:
+    f = trainer.flat
+    m, v = moments if moments is not None else _moments(trainer)
+    sd = {f"model.{k}": t for k, t in f.state_dict().items()}
+    sd.update({f"optim.exp_avg.{s.name}": m[s.offset:s.offset + s.numel].view(s.shape) for s in f.slots})
+    sd.update({f"optim.exp_avg_sq.{s.name}": v[s.offset:s.offset + s.numel].view(s.shape) for s in f.slots})
     sd["train_state"] = torch.tensor([trainer.step, trainer.optimizer.step_count], dtype=torch.int64)
     return sd
 
@@ -38,14 +45,22 @@ def save_trainer_state(trainer, path: str, step: int) -> None:
 
 
 def load_trainer_state(trainer, path: str) -> None:
-    sd = {k: v.cpu().clone() for k, v in _state(trainer).items()}
+    f = trainer.flat
+    sharded = getattr(trainer.optimizer, "set_full_moments", None)
+    # full-length moment buffers to load into (the live ones when the optimiser keeps them whole)
+    moments = ((torch.zeros(f.numel, dtype=torch.float32, device=f.master.device),
+                torch.zeros(f.numel, dtype=torch.float32, device=f.master.device)) if sharded is not None
+               else (f.exp_avg, f.exp_avg_sq))
+    live = _state(trainer, moments)
+    sd = {k: v.cpu().clone() for k, v in live.items()}
     dcp.load(sd, checkpoint_id=path, no_dist=True)
-    live = _state(trainer)
     with torch.no_grad():
         for k, v in live.items():
             if k == "train_state":
                 continue
             v.copy_(sd[k])
+    if sharded is not None:
+        sharded(*moments)
     trainer.step = int(sd["train_state"][0])
     trainer.optimizer.step_count = int(sd["train_state"][1])
     trainer.flat.recast()

@@ -158,6 +158,15 @@ class FusedDPAdamW:
                 p.main_grad = g
             else:
                 p.grad = g
+        # ZeRO-1: each rank keeps the AdamW moments of its shard only (2 x 4 bytes x n / world)
+        shard = self.hi - self.lo
+        for name in ("exp_avg", "exp_avg_sq"):
+            full = getattr(flat, name)
+            part = torch.zeros(shard, dtype=torch.float32, device=dev)
+            if full is not None:
+                part.copy_(full[self.lo:self.hi])
+            setattr(flat, name, part)
+        flat.moment_range = (self.lo, self.hi)
         self.scalars = torch.zeros(2, dtype=torch.float32, device=dev)
         self.epoch = 0
         dist.barrier(group)
@@ -183,26 +192,32 @@ class FusedDPAdamW:
             raise RuntimeError(f"fused DP step failed on rank {self.rank}: device error code {err} "
                                "(a peer did not arrive within the wait limit)")
 
-    def gather_moments(self) -> None:
-        """Moments are sharded (each rank updates only its shard); all-gather them before a checkpoint."""
+    def full_moments(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """All-gather the sharded moments into full-length tensors (collective; checkpoints only)."""
         f = self.flat
+        per = -(-f.numel // self.world)
+        per = -(-per // 4) * 4
+        out = []
         for buf in (f.exp_avg, f.exp_avg_sq):
-            per = self.hi - self.lo
-            full = torch.zeros(per * self.world, dtype=buf.dtype, device=buf.device)
-            full[:f.numel].copy_(buf)
-            out = list(full.chunk(self.world))
-            dist.all_gather(out, out[self.rank].clone(), group=self.group)
-            buf.copy_(torch.cat(out)[:f.numel])
+            mine = torch.zeros(per, dtype=buf.dtype, device=buf.device)
+            mine[:buf.numel()].copy_(buf)
+            parts = [torch.empty_like(mine) for _ in range(self.world)]
+            dist.all_gather(parts, mine, group=self.group)
+            out.append(torch.cat(parts)[:f.numel])
+        return out[0], out[1]
+
+    def set_full_moments(self, exp_avg: torch.Tensor, exp_avg_sq: torch.Tensor) -> None:
+        """Keep this rank's shard of full-length moments (after loading a checkpoint)."""
+        self.flat.exp_avg.copy_(exp_avg.reshape(-1)[self.lo:self.hi])
+        self.flat.exp_avg_sq.copy_(exp_avg_sq.reshape(-1)[self.lo:self.hi])
 
     def state_dict(self) -> dict:
-        self.gather_moments()
-        return {"step": self.step_count, "exp_avg": self.flat.exp_avg, "exp_avg_sq": self.flat.exp_avg_sq,
-                "lr": self.lr}
+        m, v = self.full_moments()
+        return {"step": self.step_count, "exp_avg": m, "exp_avg_sq": v, "lr": self.lr}
 
     def load_state_dict(self, sd: dict) -> None:
         self.step_count = int(sd["step"])
-        self.flat.exp_avg.copy_(sd["exp_avg"])
-        self.flat.exp_avg_sq.copy_(sd["exp_avg_sq"])
+        self.set_full_moments(sd["exp_avg"].to(self.flat.exp_avg.device), sd["exp_avg_sq"].to(self.flat.exp_avg.device))
         self.lr = float(sd.get("lr", self.lr))
 
 

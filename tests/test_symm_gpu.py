@@ -69,6 +69,11 @@ def _numerics(rank, world, port, q):
         other = flat.master.clone()
         dist.broadcast(other, 0)
         assert torch.equal(other, flat.master)
+        # ZeRO-1 moments: each rank keeps its shard; the gathered moments equal the reference's
+        assert flat.exp_avg.numel() == opt.hi - opt.lo
+        fm, fv = opt.full_moments()
+        assert (fm - m).abs().max().item() <= 1e-6 * max(1.0, m.abs().max().item())
+        assert (fv - v).abs().max().item() <= 1e-5 * v.abs().max().item()
         opt.heap.close()
         dist.barrier()
         dist.destroy_process_group()
