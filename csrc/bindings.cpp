@@ -9,11 +9,13 @@
 #include <torch/extension.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
 
 #include "kernels/attention.h"
+#include "kernels/decode_mega.h"
 #include "kernels/elementwise.h"
 #include "kernels/gemm.h"
 #include "kernels/misc.h"
@@ -555,6 +557,89 @@ void symm_dp_adamw_(Tensor grad_ptrs, Tensor master_ptrs, c10::optional<Tensor> 
   count(5);
 }
 
+// Whole-step decode kernel. ``table``: int64 [L, 8] device table of per-layer pointers
+// (attn_norm, bqkv, q_norm, k_norm, mlp_norm, 0, 0, 0); ``w*0``: layer 0's matrices, the other
+// layers at ``layer_stride`` elements; ``ws``: [x, xg, sumsq, acc, q, apart, ao, act, h, ctr];
+// ``gemm``: (T, KB, s) of QKV, o_proj, gate/up, down.
+void mega_decode_(Tensor table, Tensor wqkv0, Tensor wo0, Tensor w130, Tensor w20, int64_t layer_stride, Tensor embed,
+                  Tensor final_norm, Tensor kv, Tensor tok, Tensor pos, Tensor seq_lens, Tensor slot,
+                  Tensor block_table, std::vector<Tensor> ws, int64_t B, int64_t MP, int64_t Hq, int64_t Hkv,
+                  double eps, double scale, double theta, std::vector<int64_t> gemm, int64_t grid,
+                  c10::optional<Tensor> trace) {
+  TORCH_CHECK(ws.size() == 10 && gemm.size() == 12, "mega_decode: 10 workspaces and 4 x (T, KB, s)");
+  TORCH_CHECK(tok.scalar_type() == at::kLong && slot.scalar_type() == at::kLong, "tok / slot must be int64");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  block_table.scalar_type() == at::kInt, "pos / seq_lens / block_table must be int32");
+  TORCH_CHECK(kv.dim() == 6 && kv.size(4) == kMegaPage && kv.size(5) == kMegaHeadDim, "kv: [L, 2, pages, Hkv, 64, 128]");
+  const c10::cuda::CUDAGuard guard(kv.device());
+  const int L = (int)kv.size(0);
+  const int D = (int)embed.size(1);
+  const int qkv_dim = (int)wqkv0.size(0), q_dim = (int)wo0.size(1), F = (int)w20.size(1);
+  TORCH_CHECK(wqkv0.size(1) == D && wo0.size(0) == D && w130.size(0) == 2 * F && w130.size(1) == D && w20.size(0) == D,
+              "mega_decode: weight shapes");
+  TORCH_CHECK(table.size(0) == L && table.size(1) == 8, "mega_decode: layer table [L, 8]");
+  MegaArgs a = {};
+  a.n_layers = L;
+  a.D = D;
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.F = F;
+  a.qkv_dim = qkv_dim;
+  a.q_dim = q_dim;
+  a.B = (int)B;
+  a.MP = (int)MP;
+  a.eps = (float)eps;
+  a.qk_scale_log2 = (float)(scale * 1.4426950408889634);
+  Tensor inv = inv_freq_table(kMegaHeadDim, theta, kv.device());
+  a.inv_freq = ptr<float>(inv);
+  a.layers = reinterpret_cast<const MegaLayer*>(table.data_ptr());
+  a.embed = ptr<bf16>(embed);
+  a.final_norm = ptr<bf16>(final_norm);
+  a.tok = ptr<int64_t>(tok);
+  a.pos = ptr<int>(pos);
+  a.seq_lens = ptr<int>(seq_lens);
+  a.slot = ptr<int64_t>(slot);
+  a.block_table = ptr<int>(block_table);
+  a.max_pages = (int)block_table.size(1);
+  a.n_cache_pages = (int)kv.size(2);
+  a.kv = ptr<bf16>(kv);
+  a.x = ptr<float>(ws[0]);
+  a.xg = ptr<bf16>(ws[1]);
+  a.sumsq = ptr<float>(ws[2]);
+  a.acc = ptr<float>(ws[3]);
+  a.q = ptr<bf16>(ws[4]);
+  a.apart = ptr<float>(ws[5]);
+  a.ao = ptr<bf16>(ws[6]);
+  a.act = ptr<bf16>(ws[7]);
+  a.h = ptr<bf16>(ws[8]);
+  a.ctr = reinterpret_cast<unsigned*>(ws[9].data_ptr());
+  a.err = ptr<int>(scratch(0, 0).err);
+  a.flags = std::getenv("MESHY_MEGA_FLAGS") ? std::atoi(std::getenv("MESHY_MEGA_FLAGS")) : 0;
+  a.trace = trace.has_value() && trace->defined() ? reinterpret_cast<unsigned long long*>(trace->data_ptr()) : nullptr;
+  if (a.trace) TORCH_CHECK(trace->numel() >= (int64_t)(2 + 5 * L) * grid * 8, "mega_decode: trace buffer too small");
+  TORCH_CHECK(ws[9].numel() >= kMegaCtrWords, "mega_decode: counter workspace too small");
+  TORCH_CHECK(ws[5].numel() >= (int64_t)mega_apart_floats((int)grid), "mega_decode: partials workspace too small");
+  MegaGemm* gs[4] = {&a.g_qkv, &a.g_o, &a.g_gu, &a.g_dn};
+  for (int i = 0; i < 4; ++i) *gs[i] = {(int)gemm[3 * i], (int)gemm[3 * i + 1], (int)gemm[3 * i + 2]};
+  const int64_t ls = layer_stride * 2;  // bytes
+  CUtensorMap m_qkv = make_map_bf16_3d(wqkv0.data_ptr(), D, qkv_dim, L, (int64_t)D * 2, ls, 64, 128);
+  CUtensorMap m_o = make_map_bf16_3d(wo0.data_ptr(), q_dim, D, L, (int64_t)q_dim * 2, ls, 64, 128);
+  CUtensorMap m_gu = make_map_bf16_3d(w130.data_ptr(), D, 2 * F, L, (int64_t)D * 2, ls, 64, 128);
+  CUtensorMap m_dn = make_map_bf16_3d(w20.data_ptr(), F, D, L, (int64_t)F * 2, ls, 64, 128);
+  CUtensorMap m_xg = make_map_bf16(ws[1].data_ptr(), MP, D, D, 64, (int)MP);
+  CUtensorMap m_ao = make_map_bf16(ws[6].data_ptr(), MP, q_dim, q_dim, 64, (int)MP);
+  CUtensorMap m_act = make_map_bf16(ws[7].data_ptr(), MP, F, F, 64, (int)MP);
+  const int64_t kv_rows = kv.numel() / kMegaHeadDim;
+  TORCH_CHECK(kv_rows < (int64_t)1 << 31, "mega_decode: KV cache too large for 32-bit TMA row coordinates");
+  CUtensorMap m_kv = make_map_bf16(kv.data_ptr(), kv_rows, kMegaHeadDim, kMegaHeadDim, 64, kMegaPage);
+  mega_decode_launch(a, m_qkv, m_o, m_gu, m_dn, m_xg, m_ao, m_act, m_kv, (int)grid, cur_stream());
+  count();
+}
+
+int64_t mega_grid_() { return mega_grid(); }
+int64_t mega_apart_floats_(int64_t grid) { return (int64_t)mega_apart_floats((int)grid); }
+int64_t mega_ctr_words_() { return kMegaCtrWords; }
+
 int64_t device_error() {
   auto& s = scratch(0, 0);
   return s.err.item<int>();
@@ -572,6 +657,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   meshy::register_vmm(m);
   m.doc() = "meshy_b200 sm_100a kernel library";
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("mega_decode", &mega_decode_, "one decode step of a dense decoder in one persistent cooperative kernel",
+        pybind11::arg("table"), pybind11::arg("wqkv0"), pybind11::arg("wo0"), pybind11::arg("w130"), pybind11::arg("w20"),
+        pybind11::arg("layer_stride"), pybind11::arg("embed"), pybind11::arg("final_norm"), pybind11::arg("kv"),
+        pybind11::arg("tok"), pybind11::arg("pos"), pybind11::arg("seq_lens"), pybind11::arg("slot"),
+        pybind11::arg("block_table"), pybind11::arg("ws"), pybind11::arg("B"), pybind11::arg("MP"), pybind11::arg("Hq"),
+        pybind11::arg("Hkv"), pybind11::arg("eps"), pybind11::arg("scale"), pybind11::arg("theta"), pybind11::arg("gemm"),
+        pybind11::arg("grid"), pybind11::arg("trace") = pybind11::none());
+  m.def("mega_grid", &mega_grid_);
+  m.def("mega_apart_floats", &mega_apart_floats_);
+  m.def("mega_ctr_words", &mega_ctr_words_);
+
   m.def("gemm_norm", &gemm_norm, "decode: fused input RMSNorm + small-M GEMM (returns False if not eligible)");
   m.def("gemm_small_config", [](int64_t enabled, int64_t cluster) { gemm_small_config((int)enabled, (int)cluster); },
         "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");

@@ -590,6 +590,24 @@ CUtensorMap make_map_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t l
   return map;
 }
 
+// 3-D bf16 [d2][d1][d0] (d0 contiguous; strides of d1 and d2 in bytes), box {b0, b1, 1}, 128B swizzle.
+// Used for per-layer weight matrices that sit at a uniform stride in one flat buffer.
+CUtensorMap make_map_bf16_3d(const void* ptr, int64_t d0, int64_t d1, int64_t d2, int64_t stride1_bytes,
+                             int64_t stride2_bytes, int b0, int b1) {
+  MESHY_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base address must be 16-byte aligned");
+  MESHY_CHECK(stride1_bytes % 16 == 0 && stride2_bytes % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)stride1_bytes, (cuuint64_t)stride2_bytes};
+  cuuint32_t box[3] = {(cuuint32_t)b0, (cuuint32_t)b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MESHY_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed (" + std::to_string((int)r) + ")");
+  return map;
+}
+
 static int num_sms() {
   static int n = 0;
   if (!n) {

@@ -93,6 +93,8 @@ def main(argv=None):
     print(json.dumps({
         "bench": "rollout", "model": args.model, "batch": args.batch, "prompt_len": args.prompt_len, "gen": args.gen,
         "impl": "torch-baseline" if args.torch_baseline else "ours", "cuda_graph": not args.no_graph,
+        "decode_path": "whole-step kernel" if eng._mega is not None and args.batch <= 64 else
+        f"per-op kernels ({eng.mega_reason or 'batch > 64'})",
         "prefill_ms": round(prefill_ms, 2), "prefill_tok_s": round(args.batch * args.prompt_len / prefill_ms * 1e3),
         "decode_steps": steps, "decode_ms_per_step": round(step_ms, 4),
         "decode_wall_ms_per_step": round(wall_decode_ms / max(1, steps), 4),

@@ -160,6 +160,16 @@ class RolloutEngine:
         self._graphs: dict[int, Any] = {}
         self.stats = {"decode_steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "graph_replays": 0}
         self._init_state()
+        self._mega = None
+        self._mega_rows = 0
+        self.mega_reason = "not on CUDA"
+        if self.cuda:
+            from .mega import MAX_ROWS, MegaDecoder
+
+            self.mega_reason = MegaDecoder.reason(self.model, self.page_size)
+            if self.mega_reason is None:
+                self._mega = MegaDecoder(self.model, self.kv, self.device)
+                self._mega_rows = MAX_ROWS
 
     # ------------------------------------------------------------------ memory
     def _alloc_kv(self):
@@ -476,7 +486,17 @@ class RolloutEngine:
 
     # ------------------------------------------------------------------ decode
     @torch.no_grad()
-    def _decode_body(self, b: int, eos: torch.Tensor):
+    def _decode_hidden(self, b: int) -> torch.Tensor:
+        """Final normed hidden states ``[b, D]`` of the running rows' next position (writes their K/V).
+
+        Up to 64 rows of an eligible dense model take the whole-step persistent kernel; otherwise one
+        kernel per op."""
+        if self._mega is not None and b <= self._mega_rows:
+            return self._mega(self.st, b)
+        return self._decode_hidden_layers(b)
+
+    @torch.no_grad()
+    def _decode_hidden_layers(self, b: int) -> torch.Tensor:
         a, m, st = self.args, self.model, self.st
         x = Fx.embedding(st["tok_in"][:b], m.embed)
         pos = st["pos"][:b]
@@ -491,7 +511,12 @@ class RolloutEngine:
                 x = Fx.linear(act, layer.w2, residual=x)
             else:
                 x = self._mlp(layer, Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps), x)
-        h = Fx.rmsnorm(x, m.norm, a.norm_eps)
+        return Fx.rmsnorm(x, m.norm, a.norm_eps)
+
+    @torch.no_grad()
+    def _decode_body(self, b: int, eos: torch.Tensor):
+        m, st = self.model, self.st
+        h = self._decode_hidden(b)
         r0 = self.running[0]
         tok, lp = D.sample(h, m.output_weight, r0.temperature, top_k=r0.top_k, top_p=r0.top_p, seed=self.seed,
                            step=st["step"], generator=self._gen if not self.cuda else None)
@@ -549,6 +574,16 @@ class RolloutEngine:
         n = len(self.running)
         if n == 0:
             return
+        if self._mega is not None:
+            # the whole-step kernel reports a timed-out wait through the device error word (this is a
+            # host sync, like the finish-flag read below)
+            from ..ops._ext import ext
+
+            err = int(ext().device_error())
+            if err:
+                ext().clear_device_error()
+                self._mega.reset()
+                raise RuntimeError(f"decode kernel reported device error {err} (a bounded wait timed out)")
         done = self.st["done"][:n].tolist()
         rows = [i for i, d in enumerate(done) if d]
         if rows:

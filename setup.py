@@ -26,6 +26,7 @@ cuda_sources = [
     "csrc/kernels/decode_attn.cu",
     "csrc/kernels/misc.cu",
     "csrc/kernels/decode_noalloc.cu",
+    "csrc/kernels/decode_mega.cu",
 ]
 extra_cuda = [s for s in ("csrc/kernels/symm.cu",) if os.path.exists(os.path.join(ROOT, s))]
 
