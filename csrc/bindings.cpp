@@ -134,6 +134,73 @@ void gemm(Tensor a, Tensor b, Tensor out, bool a_mn, bool b_mn, c10::optional<Te
 
 // Decode-time fused RMSNorm -> linear (optionally SwiGLU): out = epi(rmsnorm(x; w_norm, eps) . W^T (+bias)).
 // Returns false (and does nothing) when the problem is not eligible for the fused small-M path.
+// Decode-time RMSNorm split across two small-M GEMMs (returns false when the problem is not eligible,
+// in which case the caller uses the unfused ops).
+//  * prep:  out = x W^T + residual, xg = bf16(out * g_next), part[t, m] = sum of out^2 over tile t's rows
+//  * scaled: out = epi(rstd[m] * (xg W^T) + bias), rstd from part (part_t tiles, model dim norm_d)
+bool gemm_norm_prep(Tensor x, Tensor w, Tensor residual, Tensor out, Tensor xg, Tensor g_next, Tensor part) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1, "gemm_norm_prep: row-major");
+  TORCH_CHECK(part.scalar_type() == at::kFloat && part.numel() >= (int64_t)((w.size(0) + 127) / 128) * kSmallPartLd,
+              "gemm_norm_prep: part must be fp32 [n_tiles, 256]");
+  TORCH_CHECK(xg.stride(0) == out.stride(0) && residual.size(1) == w.size(0), "gemm_norm_prep: layouts");
+  const c10::cuda::CUDAGuard guard(x.device());
+  GemmProblem g;
+  g.A = x.data_ptr();
+  g.B = w.data_ptr();
+  g.lda = x.stride(0);
+  g.ldb = w.stride(0);
+  g.M = x.size(0);
+  g.K = x.size(1);
+  g.N = w.size(0);
+  g.out = out.data_ptr();
+  g.ldo = out.stride(0);
+  g.epi = EPI_STORE;
+  g.residual = ptr<bf16>(residual);
+  g.ldr = residual.stride(0);
+  g.xg_out = ptr<bf16>(xg);
+  g.g_next = ptr<bf16>(g_next);
+  g.part_out = ptr<float>(part);
+  g.err = ptr<int>(scratch(0, 0).err);
+  if (g.M == 0 || !gemm_small_prep_eligible(g)) return false;
+  gemm_small_launch(g, cur_stream());
+  count();
+  return true;
+}
+
+bool gemm_norm_scaled(Tensor xg, Tensor w, Tensor out, c10::optional<Tensor> bias, Tensor part, int64_t part_t,
+                      double norm_d, double eps, int64_t epi, int64_t block) {
+  CHECK_CUDA(xg);
+  CHECK_BF16(xg);
+  CHECK_BF16(w);
+  TORCH_CHECK(xg.dim() == 2 && w.dim() == 2 && xg.stride(1) == 1 && w.stride(1) == 1, "gemm_norm_scaled: row-major");
+  const c10::cuda::CUDAGuard guard(xg.device());
+  GemmProblem g;
+  g.A = xg.data_ptr();
+  g.B = w.data_ptr();
+  g.lda = xg.stride(0);
+  g.ldb = w.stride(0);
+  g.M = xg.size(0);
+  g.K = xg.size(1);
+  g.N = w.size(0);
+  g.out = out.data_ptr();
+  g.ldo = out.stride(0);
+  g.epi = (int)epi;
+  if (g.epi == EPI_SWIGLU) TORCH_CHECK(block == 64 && out.size(1) * 2 == g.N, "gemm_norm_scaled: swiglu out [M, N/2]");
+  g.bias = optr<bf16>(bias);
+  g.part_in = ptr<float>(part);
+  g.part_t = (int)part_t;
+  g.norm_d = (float)norm_d;
+  g.norm_eps = (float)eps;
+  g.err = ptr<int>(scratch(0, 0).err);
+  if (g.M == 0 || g.M > kSmallPartLd || !gemm_small_eligible(g)) return false;
+  gemm_small_launch(g, cur_stream());
+  count();
+  return true;
+}
+
 bool gemm_norm(Tensor x, Tensor norm_w, double eps, Tensor w, Tensor out, c10::optional<Tensor> bias,
                c10::optional<Tensor> residual, int64_t epi, int64_t block) {
   CHECK_CUDA(x);
@@ -668,6 +735,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mega_apart_floats", &mega_apart_floats_);
   m.def("mega_ctr_words", &mega_ctr_words_);
 
+  m.def("gemm_norm_prep", &gemm_norm_prep, "decode: residual GEMM that also prepares the next RMSNorm");
+  m.def("gemm_norm_scaled", &gemm_norm_scaled, "decode: GEMM on a prepared RMSNorm input, rows scaled by rstd");
   m.def("gemm_norm", &gemm_norm, "decode: fused input RMSNorm + small-M GEMM (returns False if not eligible)");
   m.def("gemm_small_config", [](int64_t enabled, int64_t cluster) { gemm_small_config((int)enabled, (int)cluster); },
         "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");

@@ -43,7 +43,19 @@ struct GemmProblem {
   int force_cs = 0;           // small-M path: cluster split-K size (0 = heuristic)
   const bf16* norm_w = nullptr;  // small-M path: fused input RMSNorm gain (A is the raw stream)
   float norm_eps = 1e-6f;
+  // small-M path, RMSNorm split across two GEMMs (decode). A residual GEMM (out = A W^T + residual)
+  // also writes xg_out = bf16(bf16(out) * g_next) and, per 128-row output tile t and row m, the sum of
+  // squares of the rounded outputs into part_out[t * kSmallPartLd + m]. The next GEMM takes xg as its
+  // A operand and scales output row m by rsqrt(sum_t part_in[t * kSmallPartLd + m] / norm_d + norm_eps):
+  //   W (g * x) * rstd == W RMSNorm(x).
+  bf16* xg_out = nullptr;
+  const bf16* g_next = nullptr;
+  float* part_out = nullptr;
+  const float* part_in = nullptr;
+  int part_t = 0;
+  float norm_d = 0.f;
 };
+constexpr int kSmallPartLd = 256;
 
 void gemm_launch(const GemmProblem& g, cudaStream_t stream);
 
@@ -54,6 +66,8 @@ constexpr int kSmallMaxCluster = 16;  // above 8 the kernel opts in to non-porta
 bool gemm_small_eligible(const GemmProblem& g);
 // Whether the small-M path can also fuse the input RMSNorm for this problem.
 bool gemm_small_norm_eligible(const GemmProblem& g);
+// Whether the small-M path can prepare the next RMSNorm (xg_out / part_out) for this residual GEMM.
+bool gemm_small_prep_eligible(const GemmProblem& g);
 void gemm_small_launch(const GemmProblem& g, cudaStream_t stream);
 // enabled: 1/0 (-1 keeps); force_cs: cluster size override, 0 = heuristic (-1 keeps)
 void gemm_small_config(int enabled, int force_cs);

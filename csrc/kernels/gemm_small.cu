@@ -61,6 +61,13 @@ struct SmallArgs {
   float norm_eps;
   const bf16* x_raw;
   int ldx;
+  // RMSNorm split across GEMMs (see GemmProblem): producer outputs / consumer row scale
+  bf16* xg_out;
+  const bf16* g_next;
+  float* part_out;
+  const float* part_in;
+  int part_t;
+  float norm_d;
 };
 
 template <int MP, bool PERSIST>
@@ -73,7 +80,7 @@ struct SCfg {
   static constexpr int TMEM_COLS = (N_ACC * MP < 32) ? 32 : N_ACC * MP;
   static constexpr int RED_BYTES = 128 * MP * 4;
   static constexpr int BAR_BYTES = 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + MP * 4;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + (MP + 16) * 4;
   static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "reduction buffer must fit in the stage ring");
   static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
 };
@@ -310,6 +317,16 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     // ─────────────────────────────── epilogue ───────────────────────────────────
     pdl_wait();  // bias / residual / output may be touched by the kernels before
     if (!PERSIST && fuse_norm && has_k) norm_stages<MP>(p, smem, full, normed, rstd_s, kb0, kb1, abort_flag);
+    if (p.part_in) {
+      // rows of X were bf16(g * x): their RMSNorm scale from the producer GEMM's per-tile partial sums
+      for (int m = threadIdx.x - 64; m < MP; m += 128) {
+        float ss = 0.f;
+        if (m < p.M)
+          for (int t = 0; t < p.part_t; ++t) ss += p.part_in[(size_t)t * kSmallPartLd + m];
+        rstd_s[m] = m < p.M ? rsqrtf(ss / p.norm_d + p.norm_eps) : 0.f;
+      }
+      named_bar_sync(1, 128);
+    }
     const int q = warp & 3;
     const int f = q * 32 + lane;  // weight row within the tile = TMEM lane
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
@@ -329,7 +346,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
 #pragma unroll
             for (int i = 0; i < CH; ++i) {
               const int m = c * CH + i;
-              if (m < p.M) store_val(p, m, n, v[i]);
+              if (m < p.M) store_val(p, m, n, p.part_in ? v[i] * rstd_s[m] : v[i]);
             }
           }
         }
@@ -402,9 +419,47 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             }
           }
         }
-        const float av[4] = {a.x, a.y, a.z, a.w};
-        const float bv[4] = {b.x, b.y, b.z, b.w};
-        if (!swiglu) {
+        float av[4] = {a.x, a.y, a.z, a.w};
+        float bv[4] = {b.x, b.y, b.z, b.w};
+        if (p.part_in) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float rs = 4 * g + i < p.M ? rstd_s[4 * g + i] : 0.f;
+            av[i] *= rs;
+            bv[i] *= rs;
+          }
+        }
+        if (!swiglu && p.part_out) {
+          // residual GEMM preparing the next RMSNorm (N is a multiple of 128: every lane owns a row)
+          const int n = nt * 128 + f;
+          const float gn = __bfloat162float(p.g_next[n]);
+          float sq[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = 4 * g + i;
+            sq[i] = 0.f;
+            if (m < p.M) {
+              float y = av[i];
+              if (p.bias) y += __bfloat162float(p.bias[n]);
+              if (p.residual) y += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
+              const bf16 yb = __float2bfloat16(y);
+              reinterpret_cast<bf16*>(p.out)[(size_t)m * p.ldo + n] = yb;
+              const float yr = __bfloat162float(yb);
+              p.xg_out[(size_t)m * p.ldo + n] = __float2bfloat16(yr * gn);
+              sq[i] = yr * yr;
+            }
+          }
+          float* red4 = rstd_s + MP;  // [4 warps][4 rows]
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float s4 = warp_sum(sq[i]);
+            if (lane == 0) red4[q * 4 + i] = s4;
+          }
+          named_bar_sync(1, 128);
+          if (f < 4 && 4 * g + f < p.M)
+            p.part_out[(size_t)nt * kSmallPartLd + 4 * g + f] = red4[f] + red4[4 + f] + red4[8 + f] + red4[12 + f];
+          named_bar_sync(1, 128);
+        } else if (!swiglu) {
           const int n = nt * 128 + f;
           if (n < p.N) {
 #pragma unroll
@@ -567,8 +622,18 @@ bool gemm_small_norm_eligible(const GemmProblem& g) {
          (reinterpret_cast<uintptr_t>(g.A) & 15) == 0;
 }
 
+bool gemm_small_prep_eligible(const GemmProblem& g) {
+  if (!gemm_small_eligible(g) || g.epi != EPI_STORE || g.out_f32) return false;
+  const int n_tiles = (g.N + 127) / 128;
+  return g.N % 128 == 0 && n_tiles <= sm_count() && n_tiles <= kSmallPartLd && g.M <= kSmallPartLd;
+}
+
 void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
   MESHY_CHECK(gemm_small_eligible(g), "gemm_small: problem not eligible");
+  MESHY_CHECK(g.part_out == nullptr || (gemm_small_prep_eligible(g) && g.xg_out && g.g_next),
+              "gemm_small: norm preparation needs a STORE epilogue, N a multiple of 128, xg_out and g_next");
+  MESHY_CHECK(g.part_in == nullptr || (g.part_t > 0 && g.norm_d > 0.f && g.norm_w == nullptr),
+              "gemm_small: norm scale needs part_t, norm_d and no fused input norm");
   MESHY_CHECK(g.norm_w == nullptr || gemm_small_norm_eligible(g), "gemm_small: fused RMSNorm not eligible");
   MESHY_CHECK(g.norm_w == nullptr || (reinterpret_cast<uintptr_t>(g.norm_w) & 15) == 0,
               "gemm_small: RMSNorm gain must be 16-byte aligned");
@@ -585,6 +650,12 @@ void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
   a.norm_eps = g.norm_eps;
   a.x_raw = static_cast<const bf16*>(g.A);
   a.ldx = (int)g.lda;
+  a.xg_out = g.xg_out;
+  a.g_next = g.g_next;
+  a.part_out = g.part_out;
+  a.part_in = g.part_in;
+  a.part_t = g.part_t;
+  a.norm_d = g.norm_d;
   const int sms = sm_count();
   CUtensorMap mw = make_map_bf16(g.B, g.N, g.K, g.ldb, SBK, 128);
   CUtensorMap mx = make_map_bf16(g.A, g.M, g.K, g.lda, SBK, MP);

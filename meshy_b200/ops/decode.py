@@ -3,6 +3,10 @@
 * :func:`kv_write` — scatter this step's K/V rows into the paged cache.
 * :func:`qkv_rope_to_cache` — QK-norm + RoPE with the K/V rows written
   straight into the paged cache (one kernel).
+* :func:`linear_norm_prep` / :func:`linear_norm_scaled` — RMSNorm split across
+  the residual GEMM that produces ``x`` (it writes ``bf16(g * x)`` and per-tile
+  sums of squares) and the GEMM that consumes the norm (it scales its output
+  rows by ``rstd``), so decode runs no separate normalisation kernels.
 * :func:`paged_attention` — decode attention over the paged KV cache
   (split-KV flash-decode kernel on CUDA; GQA heads of one KV head share the
   K/V stream).
@@ -63,6 +67,39 @@ def qkv_rope_to_cache(qkv, positions, q_norm, k_norm, n_heads, n_kv, hd, theta, 
     q, k, v = qkv_rope(qkv, positions, q_norm, k_norm, n_heads, n_kv, hd, theta, eps)
     kv_write(k, v, k_cache, v_cache, slot_mapping)
     return (q, k, v) if keep_kv else (q, None, None)
+
+
+def linear_norm_prep(x, w, residual, g_next, xg, part):
+    """``out = x W^T + residual`` that also prepares the next RMSNorm for :func:`linear_norm_scaled`:
+    ``xg = bf16(out * g_next)`` and ``part[t, m]`` = sum of ``out[m]^2`` over output tile ``t``'s 128
+    columns. Returns ``out``, or ``None`` when the fused small-M kernel does not apply (the caller
+    then runs the unfused ops)."""
+    if not native(x):
+        return None
+    from ._ext import ext
+
+    out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    if not ext().gemm_norm_prep(x, w, residual, out, xg[: x.shape[0]], g_next, part):
+        return None
+    return out
+
+
+def linear_norm_scaled(xg, w, bias, part, d: int, eps: float, swiglu_block: int | None = None):
+    """``epi(rstd * (xg W^T) + bias)`` with ``xg = bf16(g * x)`` and the row scale ``rstd`` rebuilt
+    from the partial sums ``part`` written by :func:`linear_norm_prep` -- equal to
+    ``linear(RMSNorm(x; g), W, bias)`` (SwiGLU epilogue with ``swiglu_block``). ``None`` when not
+    applicable."""
+    if not native(xg):
+        return None
+    from ._ext import ext
+
+    n = w.shape[0]
+    out = torch.empty(xg.shape[0], n // 2 if swiglu_block else n, dtype=xg.dtype, device=xg.device)
+    epi = 1 if swiglu_block else 0
+    if not ext().gemm_norm_scaled(xg, w, out, bias, part, (d + 127) // 128, float(d), float(eps), epi,
+                                  int(swiglu_block or 0)):
+        return None
+    return out
 
 
 def paged_attention(q, k_cache, v_cache, block_table, seq_lens, scale=None, workspace=None):
@@ -131,4 +168,5 @@ def decode_advance(state: dict, tok, lp, page_size: int):
     state["slot"][rows] = pg * page_size + p % page_size
 
 
-__all__ = ["decode_advance", "kv_write", "paged_attention", "qkv_rope_to_cache", "sample"]
+__all__ = ["decode_advance", "kv_write", "linear_norm_prep", "linear_norm_scaled", "paged_attention",
+           "qkv_rope_to_cache", "sample"]

@@ -32,6 +32,7 @@ from __future__ import annotations
 
 import itertools
 import math
+import os
 import threading
 import time
 from dataclasses import dataclass, field
@@ -495,21 +496,60 @@ class RolloutEngine:
             return self._mega(self.st, b)
         return self._decode_hidden_layers(b)
 
+    def _norm_ws(self):
+        """Buffers of the split RMSNorm (bf16 g * x and per-tile sums of squares for two norms)."""
+        if getattr(self, "_nws", None) is None:
+            a = self.args
+            tiles = (a.dim + 127) // 128
+            self._nws = (torch.empty(self.max_running, a.dim, dtype=self.dtype, device=self.device),
+                         torch.zeros(2, tiles, 256, dtype=torch.float32, device=self.device))
+        return self._nws
+
     @torch.no_grad()
     def _decode_hidden_layers(self, b: int) -> torch.Tensor:
         a, m, st = self.args, self.model, self.st
         x = Fx.embedding(st["tok_in"][:b], m.embed)
         pos = st["pos"][:b]
+        # RMSNorm split across GEMMs: the residual GEMM producing x writes bf16(g_next * x) and per-tile
+        # sums of squares, the consuming GEMM scales its rows by rstd (no normalisation kernels).
+        # ``prep`` is the part buffer the next norm can use (None: run the unfused norm).
+        split = self.cuda and os.environ.get("MESHY_SPLIT_NORM", "1") != "0"
+        xg, parts = self._norm_ws() if split else (None, None)
+        prep = None
+        L = len(m.layers)
         for li, layer in enumerate(m.layers):
-            qkv = Fx.rmsnorm_linear(x, layer.attn_norm, a.norm_eps, layer.wqkv, layer.bqkv)
+            qkv = None
+            if prep is not None:
+                qkv = D.linear_norm_scaled(xg[:b], layer.wqkv, layer.bqkv, prep, a.dim, a.norm_eps)
+            if qkv is None:
+                qkv = Fx.rmsnorm_linear(x, layer.attn_norm, a.norm_eps, layer.wqkv, layer.bqkv)
             q, _, _ = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
                                           a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1], st["slot"][:b])
             o = D.paged_attention(q, self.kv[li, 0], self.kv[li, 1], st["block_table"][:b], st["seq_lens"][:b])
-            x = Fx.linear(o.reshape(b, a.q_dim), layer.wo, residual=x)
+            o = o.reshape(b, a.q_dim)
+            prep = None
+            if layer.moe is None and split:
+                xn = D.linear_norm_prep(o, layer.wo, x, layer.mlp_norm, xg, parts[1])
+                if xn is not None:
+                    x, prep = xn, parts[1]
+            if prep is None:
+                x = Fx.linear(o, layer.wo, residual=x)
             if layer.moe is None:
-                act = Fx.rmsnorm_linear(x, layer.mlp_norm, a.norm_eps, layer.w13, swiglu_block=a.swiglu_block)
-                x = Fx.linear(act, layer.w2, residual=x)
+                act = None
+                if prep is not None:
+                    act = D.linear_norm_scaled(xg[:b], layer.w13, None, prep, a.dim, a.norm_eps,
+                                               swiglu_block=a.swiglu_block)
+                if act is None:
+                    act = Fx.rmsnorm_linear(x, layer.mlp_norm, a.norm_eps, layer.w13, swiglu_block=a.swiglu_block)
+                prep = None
+                if split and li + 1 < L:
+                    xn = D.linear_norm_prep(act, layer.w2, x, m.layers[li + 1].attn_norm, xg, parts[0])
+                    if xn is not None:
+                        x, prep = xn, parts[0]
+                if prep is None:
+                    x = Fx.linear(act, layer.w2, residual=x)
             else:
+                prep = None
                 x = self._mlp(layer, Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps), x)
         return Fx.rmsnorm(x, m.norm, a.norm_eps)
 
