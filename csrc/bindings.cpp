@@ -201,6 +201,59 @@ bool gemm_norm_scaled(Tensor xg, Tensor w, Tensor out, c10::optional<Tensor> bia
   return true;
 }
 
+Tensor inv_freq_table(int64_t hd, double theta, const torch::Device& dev);
+
+// Decode QKV projection with the rope / KV-cache epilogue: q [M, Hq, 128] out, K and V rows written
+// into the paged caches at ``slots``. With ``part`` the input is a prepared RMSNorm input (see
+// gemm_norm_scaled). Returns false when not eligible.
+bool gemm_qkv_rope(Tensor x, Tensor w, c10::optional<Tensor> bias, c10::optional<Tensor> part, int64_t part_t,
+                   double norm_d, double eps, Tensor pos, c10::optional<Tensor> qn, c10::optional<Tensor> kn,
+                   Tensor q_out, Tensor kc, Tensor vc, Tensor slots, double theta, int64_t Hq, int64_t Hkv) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1, "gemm_qkv_rope: row-major");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && slots.scalar_type() == at::kLong, "gemm_qkv_rope: int32 pos, int64 slots");
+  TORCH_CHECK(kc.dim() == 4 && kc.size(2) == 64 && kc.size(3) == 128 && kc.is_contiguous() && vc.is_contiguous(),
+              "gemm_qkv_rope: caches [pages, Hkv, 64, 128]");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() >= x.size(0) * Hq * 128, "gemm_qkv_rope: q_out [M, Hq, 128]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  GemmProblem g;
+  g.A = x.data_ptr();
+  g.B = w.data_ptr();
+  g.lda = x.stride(0);
+  g.ldb = w.stride(0);
+  g.M = x.size(0);
+  g.K = x.size(1);
+  g.N = w.size(0);
+  g.out = q_out.data_ptr();
+  g.ldo = (int)g.N;
+  g.epi = EPI_STORE;
+  g.bias = optr<bf16>(bias);
+  if (part.has_value() && part->defined()) {
+    g.part_in = ptr<float>(*part);
+    g.part_t = (int)part_t;
+    g.norm_d = (float)norm_d;
+  }
+  g.norm_eps = (float)eps;
+  Tensor inv = inv_freq_table(128, theta, x.device());
+  g.q_out = ptr<bf16>(q_out);
+  g.rope_pos = ptr<int>(pos);
+  g.inv_freq = ptr<float>(inv);
+  g.qn = optr<bf16>(qn);
+  g.kn = optr<bf16>(kn);
+  g.kc = ptr<bf16>(kc);
+  g.vc = ptr<bf16>(vc);
+  g.slots = ptr<int64_t>(slots);
+  g.hq = (int)Hq;
+  g.hkv = (int)Hkv;
+  g.err = ptr<int>(scratch(0, 0).err);
+  if (g.M == 0 || g.M > kSmallPartLd || !gemm_small_rope_eligible(g)) return false;
+  gemm_small_launch(g, cur_stream());
+  count();
+  return true;
+}
+
 bool gemm_norm(Tensor x, Tensor norm_w, double eps, Tensor w, Tensor out, c10::optional<Tensor> bias,
                c10::optional<Tensor> residual, int64_t epi, int64_t block) {
   CHECK_CUDA(x);
@@ -737,6 +790,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 
   m.def("gemm_norm_prep", &gemm_norm_prep, "decode: residual GEMM that also prepares the next RMSNorm");
   m.def("gemm_norm_scaled", &gemm_norm_scaled, "decode: GEMM on a prepared RMSNorm input, rows scaled by rstd");
+  m.def("gemm_qkv_rope", &gemm_qkv_rope, "decode: QKV GEMM with RoPE / QK-norm and the KV-cache write fused");
   m.def("gemm_norm", &gemm_norm, "decode: fused input RMSNorm + small-M GEMM (returns False if not eligible)");
   m.def("gemm_small_config", [](int64_t enabled, int64_t cluster) { gemm_small_config((int)enabled, (int)cluster); },
         "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");

@@ -54,6 +54,19 @@ struct GemmProblem {
   const float* part_in = nullptr;
   int part_t = 0;
   float norm_d = 0.f;
+  // small-M path, fused QKV epilogue (decode): every 128-row tile is one head of head_dim 128 in the
+  // fused [Hq | Hkv | Hkv] layout. Output rows are rounded to bf16 (+bias), q/k heads get the optional
+  // per-head RMSNorm (qn / kn) and rotate-half RoPE at rope_pos, q heads go to q_out [M, Hq, 128],
+  // k / v heads straight into the paged caches kc / vc ([pages, Hkv, 64, 128]) at slots[m].
+  bf16* q_out = nullptr;
+  const int* rope_pos = nullptr;
+  const float* inv_freq = nullptr;
+  const bf16* qn = nullptr;
+  const bf16* kn = nullptr;
+  bf16* kc = nullptr;
+  bf16* vc = nullptr;
+  const int64_t* slots = nullptr;
+  int hq = 0, hkv = 0;
 };
 constexpr int kSmallPartLd = 256;
 
@@ -68,6 +81,8 @@ bool gemm_small_eligible(const GemmProblem& g);
 bool gemm_small_norm_eligible(const GemmProblem& g);
 // Whether the small-M path can prepare the next RMSNorm (xg_out / part_out) for this residual GEMM.
 bool gemm_small_prep_eligible(const GemmProblem& g);
+// Whether the small-M path can run the fused QKV + RoPE + KV-cache epilogue (q_out ...).
+bool gemm_small_rope_eligible(const GemmProblem& g);
 void gemm_small_launch(const GemmProblem& g, cudaStream_t stream);
 // enabled: 1/0 (-1 keeps); force_cs: cluster size override, 0 = heuristic (-1 keeps)
 void gemm_small_config(int enabled, int force_cs);

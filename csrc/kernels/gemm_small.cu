@@ -68,6 +68,16 @@ struct SmallArgs {
   const float* part_in;
   int part_t;
   float norm_d;
+  // fused QKV epilogue (see GemmProblem)
+  bf16* q_out;
+  const int* rope_pos;
+  const float* inv_freq;
+  const bf16* qn;
+  const bf16* kn;
+  bf16* kc;
+  bf16* vc;
+  const int64_t* slots;
+  int hq, hkv;
 };
 
 template <int MP, bool PERSIST>
@@ -80,7 +90,7 @@ struct SCfg {
   static constexpr int TMEM_COLS = (N_ACC * MP < 32) ? 32 : N_ACC * MP;
   static constexpr int RED_BYTES = 128 * MP * 4;
   static constexpr int BAR_BYTES = 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + (MP + 16) * 4;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + (MP + 16 + 4 * 128) * 4;
   static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "reduction buffer must fit in the stage ring");
   static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
 };
@@ -429,7 +439,70 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             bv[i] *= rs;
           }
         }
-        if (!swiglu && p.part_out) {
+        if (p.q_out) {
+          // one head per tile: bias, bf16 rounding, (per-head RMSNorm), RoPE, then q out / K,V to cache
+          const int n = nt * 128 + f;
+          const int hqk = p.hq + p.hkv;
+          float y[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float t = av[i];
+            if (p.bias) t += __bfloat162float(p.bias[n]);
+            y[i] = __bfloat162float(__float2bfloat16(t));
+          }
+          if (nt >= hqk) {  // V head: into the cache as is
+            const int hk = nt - hqk;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int m = 4 * g + i;
+              if (m < p.M) {
+                const int64_t sl = p.slots[m];
+                p.vc[(((size_t)(sl / 64) * p.hkv + hk) * 64 + (size_t)(sl % 64)) * 128 + f] = __float2bfloat16(y[i]);
+              }
+            }
+          } else {
+            float* xch = rstd_s + MP + 16;  // [4 rows][128] pre-rotation values, then [4] head-norm scales
+            const bool is_q = nt < p.hq;
+            const bf16* nw = is_q ? p.qn : p.kn;
+            if (nw) {
+              float* red4 = rstd_s + MP;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float s4 = warp_sum(y[i] * y[i]);
+                if (lane == 0) red4[q * 4 + i] = s4;
+              }
+              named_bar_sync(1, 128);
+              const float w = __bfloat162float(nw[f]);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float ss = red4[i] + red4[4 + i] + red4[8 + i] + red4[12 + i];
+                y[i] = __bfloat162float(__float2bfloat16(y[i] * rsqrtf(ss / 128.f + p.norm_eps) * w));
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xch[i * 128 + f] = y[i];
+            named_bar_sync(1, 128);
+            const float inv = p.inv_freq[f & 63];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int m = 4 * g + i;
+              if (m < p.M) {
+                const float yp = xch[i * 128 + (f ^ 64)];
+                float sn, cs;
+                sincosf((float)p.rope_pos[m] * inv, &sn, &cs);
+                const float o = (f < 64) ? y[i] * cs - yp * sn : y[i] * cs + yp * sn;
+                if (is_q) {
+                  p.q_out[((size_t)m * p.hq + nt) * 128 + f] = __float2bfloat16(o);
+                } else {
+                  const int64_t sl = p.slots[m];
+                  p.kc[(((size_t)(sl / 64) * p.hkv + (nt - p.hq)) * 64 + (size_t)(sl % 64)) * 128 + f] =
+                      __float2bfloat16(o);
+                }
+              }
+            }
+            named_bar_sync(1, 128);  // xch is reused by the next row group
+          }
+        } else if (!swiglu && p.part_out) {
           // residual GEMM preparing the next RMSNorm (N is a multiple of 128: every lane owns a row)
           const int n = nt * 128 + f;
           const float gn = __bfloat162float(p.g_next[n]);
@@ -628,12 +701,21 @@ bool gemm_small_prep_eligible(const GemmProblem& g) {
   return g.N % 128 == 0 && n_tiles <= sm_count() && n_tiles <= kSmallPartLd && g.M <= kSmallPartLd;
 }
 
+bool gemm_small_rope_eligible(const GemmProblem& g) {
+  if (!gemm_small_eligible(g) || g.epi != EPI_STORE || g.out_f32) return false;
+  const int n_tiles = (g.N + 127) / 128;
+  return g.hq > 0 && g.hkv > 0 && g.N == (g.hq + 2 * g.hkv) * 128 && n_tiles <= sm_count();
+}
+
 void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
   MESHY_CHECK(gemm_small_eligible(g), "gemm_small: problem not eligible");
   MESHY_CHECK(g.part_out == nullptr || (gemm_small_prep_eligible(g) && g.xg_out && g.g_next),
               "gemm_small: norm preparation needs a STORE epilogue, N a multiple of 128, xg_out and g_next");
   MESHY_CHECK(g.part_in == nullptr || (g.part_t > 0 && g.norm_d > 0.f && g.norm_w == nullptr),
               "gemm_small: norm scale needs part_t, norm_d and no fused input norm");
+  MESHY_CHECK(g.q_out == nullptr || (gemm_small_rope_eligible(g) && g.part_out == nullptr && g.norm_w == nullptr &&
+                                     g.rope_pos && g.inv_freq && g.kc && g.vc && g.slots),
+              "gemm_small: fused QKV epilogue needs N = (Hq + 2 Hkv) * 128, positions, caches and slots");
   MESHY_CHECK(g.norm_w == nullptr || gemm_small_norm_eligible(g), "gemm_small: fused RMSNorm not eligible");
   MESHY_CHECK(g.norm_w == nullptr || (reinterpret_cast<uintptr_t>(g.norm_w) & 15) == 0,
               "gemm_small: RMSNorm gain must be 16-byte aligned");
@@ -656,6 +738,16 @@ void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
   a.part_in = g.part_in;
   a.part_t = g.part_t;
   a.norm_d = g.norm_d;
+  a.q_out = g.q_out;
+  a.rope_pos = g.rope_pos;
+  a.inv_freq = g.inv_freq;
+  a.qn = g.qn;
+  a.kn = g.kn;
+  a.kc = g.kc;
+  a.vc = g.vc;
+  a.slots = g.slots;
+  a.hq = g.hq;
+  a.hkv = g.hkv;
   const int sms = sm_count();
   CUtensorMap mw = make_map_bf16(g.B, g.N, g.K, g.ldb, SBK, 128);
   CUtensorMap mx = make_map_bf16(g.A, g.M, g.K, g.lda, SBK, MP);

@@ -102,6 +102,23 @@ def linear_norm_scaled(xg, w, bias, part, d: int, eps: float, swiglu_block: int 
     return out
 
 
+def qkv_rope_fused(x, w, bias, positions, q_norm, k_norm, n_heads, n_kv, theta, eps, k_cache, v_cache, slot_mapping,
+                   part=None, d: int = 0):
+    """Decode QKV projection whose epilogue applies bias, (QK-norm), RoPE and writes K/V into the paged
+    cache: returns ``q [T, Hq, 128]``, or ``None`` when the fused kernel does not apply. ``part``:
+    ``x`` is a prepared RMSNorm input (see :func:`linear_norm_prep`) of model dim ``d``."""
+    if not native(x) or w.shape[0] != (n_heads + 2 * n_kv) * 128 or k_cache.shape[-1] != 128:
+        return None
+    from ._ext import ext
+
+    T = x.shape[0]
+    q = torch.empty(T, n_heads, 128, dtype=x.dtype, device=x.device)
+    ok = ext().gemm_qkv_rope(x, w, bias, part, (d + 127) // 128 if part is not None else 0, float(d), float(eps),
+                             positions, q_norm, k_norm, q, k_cache, v_cache, slot_mapping, float(theta), n_heads,
+                             n_kv)
+    return q if ok else None
+
+
 def paged_attention(q, k_cache, v_cache, block_table, seq_lens, scale=None, workspace=None):
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if native(q):
@@ -169,4 +186,4 @@ def decode_advance(state: dict, tok, lp, page_size: int):
 
 
 __all__ = ["decode_advance", "kv_write", "linear_norm_prep", "linear_norm_scaled", "paged_attention",
-           "qkv_rope_to_cache", "sample"]
+           "qkv_rope_fused", "qkv_rope_to_cache", "sample"]

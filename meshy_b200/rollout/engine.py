@@ -514,17 +514,25 @@ class RolloutEngine:
         # sums of squares, the consuming GEMM scales its rows by rstd (no normalisation kernels).
         # ``prep`` is the part buffer the next norm can use (None: run the unfused norm).
         split = self.cuda and os.environ.get("MESHY_SPLIT_NORM", "1") != "0"
+        fuse_rope = os.environ.get("MESHY_FUSED_QKV_ROPE", "1") != "0"
         xg, parts = self._norm_ws() if split else (None, None)
         prep = None
         L = len(m.layers)
         for li, layer in enumerate(m.layers):
-            qkv = None
-            if prep is not None:
-                qkv = D.linear_norm_scaled(xg[:b], layer.wqkv, layer.bqkv, prep, a.dim, a.norm_eps)
-            if qkv is None:
-                qkv = Fx.rmsnorm_linear(x, layer.attn_norm, a.norm_eps, layer.wqkv, layer.bqkv)
-            q, _, _ = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
-                                          a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1], st["slot"][:b])
+            q = None
+            if prep is not None and fuse_rope:
+                q = D.qkv_rope_fused(xg[:b], layer.wqkv, layer.bqkv, pos, layer.q_norm, layer.k_norm, a.n_heads,
+                                     a.n_kv_heads, a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1],
+                                     st["slot"][:b], part=prep, d=a.dim)
+            if q is None:
+                qkv = None
+                if prep is not None:
+                    qkv = D.linear_norm_scaled(xg[:b], layer.wqkv, layer.bqkv, prep, a.dim, a.norm_eps)
+                if qkv is None:
+                    qkv = Fx.rmsnorm_linear(x, layer.attn_norm, a.norm_eps, layer.wqkv, layer.bqkv)
+                q, _, _ = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads,
+                                              a.head_dim, a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1],
+                                              st["slot"][:b])
             o = D.paged_attention(q, self.kv[li, 0], self.kv[li, 1], st["block_table"][:b], st["seq_lens"][:b])
             o = o.reshape(b, a.q_dim)
             prep = None

@@ -1,8 +1,9 @@
 """Decode with RMSNorm split across GEMMs vs the unfused per-op decode, same engine state (GPU).
 
 The residual GEMMs (o_proj, down_proj) also write bf16(g * x) and per-tile sums of squares; the
-consuming GEMMs (QKV, gate/up) scale their rows by rstd. The hidden states of one decode step and
-the K/V rows it writes must match the unfused path to bf16 accuracy.
+consuming GEMMs (QKV, gate/up) scale their rows by rstd; optionally the QKV GEMM's epilogue also
+applies RoPE (+ QK-norm) and writes K/V into the paged cache. The hidden states of one decode step
+and the K/V rows it writes must match the unfused path to bf16 accuracy.
 """
 
 import random
@@ -23,7 +24,8 @@ def _rel(a, b):
     (("qwen3", "1.7B"), [100, 2000]),
     (("minicpm5", "1B"), [33] * 8),
 ])
-def test_split_norm_decode_matches_unfused(model, lens, monkeypatch):
+@pytest.mark.parametrize("fused_rope", [0, 1])
+def test_split_norm_decode_matches_unfused(model, lens, fused_rope, monkeypatch):
     from dataclasses import replace
 
     from meshy_b200.models import get_model_args
@@ -42,6 +44,7 @@ def test_split_norm_decode_matches_unfused(model, lens, monkeypatch):
     from meshy_b200.ops._ext import ext
 
     monkeypatch.setenv("MESHY_SPLIT_NORM", "0")
+    monkeypatch.setenv("MESHY_FUSED_QKV_ROPE", str(fused_rope))
     c0 = ext().launch_count()
     h_ref = e._decode_hidden_layers(n).clone()
     launches_ref = ext().launch_count() - c0
@@ -56,4 +59,5 @@ def test_split_norm_decode_matches_unfused(model, lens, monkeypatch):
     assert _rel(e.kv, kv_ref) < 2e-2
     # every norm between the first and the final one is folded into the GEMMs
     L = len(e.model.layers)
-    assert launches_ref - launches == 2 * L - 1, (launches_ref, launches)
+    # RoPE + KV write ride on the QKV GEMM of every layer after the first
+    assert launches_ref - launches == 2 * L - 1 + (L - 1) * fused_rope, (launches_ref, launches)
