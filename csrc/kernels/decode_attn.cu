@@ -374,9 +374,11 @@ int paged_decode_tma_splits(int B, int Hkv, int max_pages) {
   const int slots = 2 * 148;
   const int ctas = std::max(1, B * Hkv);
   int want = std::max(1, slots / ctas);
-  // a merge kernel costs more than the idle SMs of a cluster-capped grid unless fewer than half
-  // of the SMs would get a CTA
-  if (want > kMaxClusterSplits && ctas * kMaxClusterSplits >= 74) want = kMaxClusterSplits;
+  // A separate merge kernel costs more than the SMs a cluster-capped grid leaves idle, unless every
+  // split would still walk many pages (measured on B200, 1-8 rows: 8 cluster splits beat 16-64 split
+  // + merge up to ~8k-token contexts, e.g. 1 row x 2k: 14.3 us vs 19.5 us).
+  if (want > kMaxClusterSplits && (max_pages + kMaxClusterSplits - 1) / kMaxClusterSplits <= 48)
+    want = kMaxClusterSplits;
   return std::max(1, std::min({want, max_pages, 64}));
 }
 
