@@ -383,7 +383,7 @@ void flash_attn_fwd_(Tensor q, Tensor k, Tensor v, Tensor cu, Tensor out, Tensor
   const c10::cuda::CUDAGuard guard(q.device());
   flash_attn_fwd(ptr<bf16>(q), ptr<bf16>(k), ptr<bf16>(v), ptr<int>(cu), (int)cu.numel() - 1, ptr<bf16>(out),
                  ptr<float>(lse), (int)q.size(0), (int)max_seqlen, (int)q.size(1), (int)k.size(1), (int)q.size(2),
-                 (float)scale, cur_stream());
+                 (float)scale, cur_stream(), nullptr, nullptr, (int)k.size(0), ptr<int>(scratch(0, 0).err));
   count();
 }
 
@@ -411,7 +411,8 @@ void flash_attn_fwd_kv_(Tensor q, Tensor k, Tensor v, Tensor cu_q, Tensor cu_k, 
   const c10::cuda::CUDAGuard guard(q.device());
   flash_attn_fwd(ptr<bf16>(q), ptr<bf16>(k), ptr<bf16>(v), ptr<int>(cu_q), (int)cu_q.numel() - 1, ptr<bf16>(out),
                  ptr<float>(lse), (int)q.size(0), (int)max_seqlen_q, (int)q.size(1), (int)k.size(1), (int)q.size(2),
-                 (float)scale, cur_stream(), ptr<int>(cu_k), ptr<int>(q_off));
+                 (float)scale, cur_stream(), ptr<int>(cu_k), ptr<int>(q_off), (int)k.size(0),
+                 ptr<int>(scratch(0, 0).err));
   count();
 }
 

@@ -759,9 +759,14 @@ static void set_smem(F f, int bytes) {
 
 void flash_attn_fwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, bf16* o, float* lse, int T,
                     int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st, const int* cu_k,
-                    const int* q_off) {
+                    const int* q_off, int Tk, int* err) {
   MESHY_CHECK(hd == 64 || hd == 128, "flash_attn: head_dim must be 64 or 128");
   MESHY_CHECK(Hq % Hkv == 0, "flash_attn: Hq must be a multiple of Hkv");
+  if (hd == 128 && flash_attn_tc_enabled()) {
+    flash_attn_fwd_tc(q, k, v, cu, n_docs, o, lse, T, Tk < 0 ? T : Tk, max_seqlen, Hq, Hkv, scale, st, cu_k, q_off,
+                      err);
+    return;
+  }
   int mb = (max_seqlen + BQ - 1) / BQ;
   dim3 grid(n_docs * mb, Hq);
   if (n_docs * mb == 0) return;

@@ -7,7 +7,13 @@ namespace meshy {
 // form is what context parallelism uses: local query chunks against the gathered sequence.
 void flash_attn_fwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, bf16* o, float* lse, int T,
                     int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st,
-                    const int* cu_k = nullptr, const int* q_off = nullptr);
+                    const int* cu_k = nullptr, const int* q_off = nullptr, int Tk = -1, int* err = nullptr);
+// head_dim 128 on the tcgen05 tensor cores (attention_tc.cu); Tk = rows of k / v. flash_attn_fwd
+// dispatches here unless MESHY_FA_TC=0.
+void flash_attn_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, bf16* o, float* lse,
+                       int T, int Tk, int max_seqlen, int Hq, int Hkv, float scale, cudaStream_t st, const int* cu_k,
+                       const int* q_off, int* err);
+bool flash_attn_tc_enabled();
 // dk / dv are written for every key row of every key document (zero where no query attends).
 void flash_attn_bwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, const bf16* o,
                     const bf16* dout, const float* lse, float* dvec, bf16* dq, bf16* dk, bf16* dv, int T,

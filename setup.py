@@ -23,6 +23,7 @@ cuda_sources = [
     "csrc/kernels/gemm_small.cu",
     "csrc/kernels/elementwise.cu",
     "csrc/kernels/attention.cu",
+    "csrc/kernels/attention_tc.cu",
     "csrc/kernels/decode_attn.cu",
     "csrc/kernels/misc.cu",
     "csrc/kernels/decode_noalloc.cu",
