@@ -394,7 +394,7 @@ void flash_attn_bwd_(Tensor q, Tensor k, Tensor v, Tensor cu, Tensor out, Tensor
   flash_attn_bwd(ptr<bf16>(q), ptr<bf16>(k), ptr<bf16>(v), ptr<int>(cu), (int)cu.numel() - 1, ptr<bf16>(out),
                  ptr<bf16>(gout), ptr<float>(lse), ptr<float>(dvec), ptr<bf16>(gq), ptr<bf16>(gk), ptr<bf16>(gv),
                  (int)q.size(0), (int)max_seqlen, (int)q.size(1), (int)k.size(1), (int)q.size(2), (float)scale,
-                 cur_stream());
+                 cur_stream(), nullptr, nullptr, 0, (int)k.size(0), ptr<int>(scratch(0, 0).err));
   count(3);
 }
 
@@ -424,7 +424,8 @@ void flash_attn_bwd_kv_(Tensor q, Tensor k, Tensor v, Tensor cu_q, Tensor cu_k, 
   flash_attn_bwd(ptr<bf16>(q), ptr<bf16>(k), ptr<bf16>(v), ptr<int>(cu_q), (int)cu_q.numel() - 1, ptr<bf16>(out),
                  ptr<bf16>(gout), ptr<float>(lse), ptr<float>(dvec), ptr<bf16>(gq), ptr<bf16>(gk), ptr<bf16>(gv),
                  (int)q.size(0), (int)max_seqlen_q, (int)q.size(1), (int)k.size(1), (int)q.size(2), (float)scale,
-                 cur_stream(), ptr<int>(cu_k), ptr<int>(q_off), (int)max_seqlen_k);
+                 cur_stream(), ptr<int>(cu_k), ptr<int>(q_off), (int)max_seqlen_k, (int)k.size(0),
+                 ptr<int>(scratch(0, 0).err));
   count(3);
 }
 

@@ -785,11 +785,16 @@ void flash_attn_fwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, 
 void flash_attn_bwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, const bf16* o,
                     const bf16* dout, const float* lse, float* dvec, bf16* dq, bf16* dk, bf16* dv, int T,
                     int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st, const int* cu_k,
-                    const int* q_off, int max_seqlen_k) {
+                    const int* q_off, int max_seqlen_k, int Tk, int* err) {
   MESHY_CHECK(hd == 64 || hd == 128, "flash_attn: head_dim must be 64 or 128");
   long long warps = (long long)T * Hq;
   if (warps == 0) return;
   fa_bwd_prep_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(o, dout, dvec, T, Hq, hd);
+  if (hd == 128 && flash_attn_tc_enabled()) {
+    flash_attn_bwd_tc(q, k, v, dout, lse, dvec, cu, n_docs, dq, dk, dv, T, Tk < 0 ? T : Tk, max_seqlen,
+                      cu_k ? max_seqlen_k : max_seqlen, Hq, Hkv, scale, st, cu_k, q_off, err);
+    return;
+  }
   int mb = (max_seqlen + BQ - 1) / BQ;
   int mbk = ((cu_k ? max_seqlen_k : max_seqlen) + BKV - 1) / BKV;
   dim3 g_kv(n_docs * mbk, Hkv), g_q(n_docs * mb, Hq);

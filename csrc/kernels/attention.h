@@ -18,7 +18,13 @@ bool flash_attn_tc_enabled();
 void flash_attn_bwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, const bf16* o,
                     const bf16* dout, const float* lse, float* dvec, bf16* dq, bf16* dk, bf16* dv, int T,
                     int max_seqlen, int Hq, int Hkv, int hd, float scale, cudaStream_t st,
-                    const int* cu_k = nullptr, const int* q_off = nullptr, int max_seqlen_k = 0);
+                    const int* cu_k = nullptr, const int* q_off = nullptr, int max_seqlen_k = 0, int Tk = -1,
+                    int* err = nullptr);
+// head_dim 128 on tcgen05 (attention_tc.cu): dK/dV and dQ kernels after the D = rowsum(dO * O) prep.
+void flash_attn_bwd_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* dout, const float* lse,
+                       const float* dvec, const int* cu, int n_docs, bf16* dq, bf16* dk, bf16* dv, int T, int Tk,
+                       int max_seqlen, int max_seqlen_k, int Hq, int Hkv, float scale, cudaStream_t st,
+                       const int* cu_k, const int* q_off, int* err);
 int paged_decode_splits(int B, int Hkv, int max_pages);
 void paged_decode(const bf16* q, const bf16* kc, const bf16* vc, const int* bt, const int* seq_lens, bf16* o,
                   float* part, int B, int Hq, int Hkv, int hd, int page, int max_pages, int n_split, float scale,

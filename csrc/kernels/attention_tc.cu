@@ -55,6 +55,21 @@ constexpr float kL2e = 1.4426950408889634f;
 constexpr float kLn2f = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
+// Named barrier with an AND-reduction: every participating thread gets the same answer, so a
+// decision to stop is taken by all of them together.
+__device__ __forceinline__ bool bar_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // 2^x on the special-function unit (the hardware instruction; inputs here are <= 0 or -inf).
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -310,6 +325,473 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ═════════════════════════════ backward ═════════════════════════════════════
+//
+// dK / dV: one CTA per 128-key block of one KV head, sweeping the GQA query heads and the causal
+// 64-query blocks. Transposed products keep the key rows on the TMEM lanes:
+//   S^T = K Q_i^T, dP^T = V dO_i^T            (M=128 keys, N=64 queries, K=128 dims)
+//   P^T = 2^(S^T scale log2e - LSE log2e), dS^T = P^T (dP^T - D)   (thread = key row)
+//   dV += P^T dO_i, dK += dS^T Q_i           (M=128 keys, N=128 dims, K=64 queries)
+// Q_i and dO_i are loaded once in the K-major layout and read as the MN-major B operand of the
+// accumulating products through a descriptor with the other leading-dimension stride.
+// TMEM: S^T[2] (64 cols each), dP^T[2], dV (128), dK (128).
+constexpr int kBQ = 64;                   // query block of the dK/dV kernel
+constexpr int kQdoBytes = 64 * 128 * 2;   // one 64-row Q or dO tile
+constexpr int kPdsBytes = 128 * 64 * 2;   // one 128 x 64 P^T or dS^T tile
+// shared memory: K, V, {Q, dO}[2], {P^T, dS^T}[2], LSE/D [2][2][64], barriers
+constexpr int kBK_K = 0, kBK_V = kTileBytes, kBK_QDO = 2 * kTileBytes;
+constexpr int kBK_PDS = kBK_QDO + 2 * 2 * kQdoBytes;
+constexpr int kBK_LD = kBK_PDS + 2 * 2 * kPdsBytes;
+constexpr int kBK_BAR = kBK_LD + 2 * 2 * 64 * 4;
+constexpr int kBKSmem = 1024 + kBK_BAR + 256;
+
+__global__ void __launch_bounds__(kFaThreads, 1)
+    fa_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapDO,
+                          const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV,
+                          const float* __restrict__ LSE, const float* __restrict__ Dv, const int* __restrict__ cu,
+                          const int* __restrict__ cu_k, const int* __restrict__ q_off, bf16* __restrict__ dK,
+                          bf16* __restrict__ dV, int T, int max_blocks, int Hq, int Hkv, float scale, int* err) {
+  extern __shared__ __align__(1024) uint8_t smraw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kBK_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;     // [2] S^T and dP^T of a block
+  uint64_t* s_free = bars + 7;     // [2]
+  uint64_t* p_full = bars + 9;     // [2] P^T and dS^T of a block in shared memory
+  uint64_t* p_free = bars + 11;    // [2]
+  uint64_t* acc_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* ld_s = reinterpret_cast<float*>(sm + kBK_LD);  // [buf][LSE | D][64]
+
+  const int doc = blockIdx.x / max_blocks;
+  const int kb = blockIdx.x % max_blocks;
+  const int hk = blockIdx.y, rep = Hq / Hkv;
+  const int s = cu[doc], e = cu[doc + 1], L = e - s;
+  const int ks = cu_k ? cu_k[doc] : s, ke = cu_k ? cu_k[doc + 1] : e, Lk = ke - ks;
+  const int qo = q_off ? q_off[doc] : 0;
+  const int k0 = kb * TBK;
+  if (k0 >= Lk) return;
+  // query blocks that see any key of this block: query q sees key k iff k <= qo + q
+  const int n_qb = (L + kBQ - 1) / kBQ;
+  const int qb0 = min(n_qb, max(0, k0 - qo) / kBQ);
+  const int per_head = n_qb - qb0;
+  const int n_blk = rep * per_head;  // (head, query block) pairs, head-major
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_free[i], 1);
+    }
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mapQ);
+    tma_prefetch_desc(&mapDO);
+    tma_prefetch_desc(&mapK);
+    tma_prefetch_desc(&mapV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S^T[b] at 64 b, dP^T[b] at 128 + 64 b, dV at 256, dK at 384
+
+  if (warp == 0) {
+    // ───────────────────────────── TMA producer ─────────────────────────────
+    if (lane == 0 && n_blk > 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_2d(sm + kBK_K + c * 16384, &mapK, kv_full, hk * THD + c * 64, ks + k0);
+        tma_load_2d(sm + kBK_V + c * 16384, &mapV, kv_full, hk * THD + c * 64, ks + k0);
+      }
+      for (int n = 0; n < n_blk; ++n) {
+        const int st = n & 1;
+        const int h = hk * rep + n / per_head, qb = qb0 + n % per_head;
+        if (!mbar_wait(&qdo_empty[st], ((n >> 1) & 1) ^ 1, abort_flag, err, 101)) break;
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * kQdoBytes);
+        uint8_t* dst = sm + kBK_QDO + st * 2 * kQdoBytes;
+        for (int c = 0; c < 2; ++c) {
+          tma_load_2d(dst + c * 8192, &mapQ, &qdo_full[st], h * THD + c * 64, s + qb * kBQ);
+          tma_load_2d(dst + kQdoBytes + c * 8192, &mapDO, &qdo_full[st], h * THD + c * 64, s + qb * kBQ);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ───────────────────────────── MMA issuer ───────────────────────────────
+    if (lane == 0 && n_blk > 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(128, 64, false, false);   // K-major Q / dO as B
+      constexpr uint32_t id_a = idesc_bf16_f32(128, 128, false, true);   // MN-major Q / dO as B
+      const uint32_t sk = smem_u32(sm + kBK_K), sv = smem_u32(sm + kBK_V);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, err, 103);
+      auto issue_s = [&](int n) -> bool {
+        const int st = n & 1;
+        if (!mbar_wait(&qdo_full[st], (n >> 1) & 1, abort_flag, err, 104)) return false;
+        if (!mbar_wait(&s_free[st], ((n >> 1) & 1) ^ 1, abort_flag, err, 105)) return false;
+        tc_fence_after();
+        const uint32_t sq = smem_u32(sm + kBK_QDO + st * 2 * kQdoBytes), sdo = sq + kQdoBytes;
+#pragma unroll
+        for (int k = 0; k < THD / 16; ++k) {
+          const uint32_t a_off = (k >> 2) * 16384 + (k & 3) * 32;
+          const uint32_t b_off = (k >> 2) * 8192 + (k & 3) * 32;
+          mma_bf16(tmem + st * 64, smem_desc_sw128(sk + a_off, 16, 1024), smem_desc_sw128(sq + b_off, 16, 1024), id_s,
+                   k > 0 ? 1u : 0u);
+          mma_bf16(tmem + 128 + st * 64, smem_desc_sw128(sv + a_off, 16, 1024), smem_desc_sw128(sdo + b_off, 16, 1024),
+                   id_s, k > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n_blk > 1) ok = issue_s(1);
+      for (int n = 0; n < n_blk && ok; ++n) {
+        const int st = n & 1;
+        if (!mbar_wait(&p_full[st], (n >> 1) & 1, abort_flag, err, 106)) break;
+        tc_fence_after();
+        const uint32_t sq = smem_u32(sm + kBK_QDO + st * 2 * kQdoBytes), sdo = sq + kQdoBytes;
+        const uint32_t spt = smem_u32(sm + kBK_PDS + st * 2 * kPdsBytes), sdst = spt + kPdsBytes;
+#pragma unroll
+        for (int k = 0; k < kBQ / 16; ++k) {
+          const uint32_t a_off = (k & 3) * 32;    // K-major P^T / dS^T: 64 queries = one 128-byte row
+          const uint32_t b_off = (k & 3) * 2048;  // MN-major dO / Q: 16 query rows
+          const uint32_t acc = (n > 0 || k > 0) ? 1u : 0u;
+          mma_bf16(tmem + 256, smem_desc_sw128(spt + a_off, 16, 1024), smem_desc_sw128(sdo + b_off, 8192, 1024), id_a,
+                   acc);
+          mma_bf16(tmem + 384, smem_desc_sw128(sdst + a_off, 16, 1024), smem_desc_sw128(sq + b_off, 8192, 1024), id_a,
+                   acc);
+        }
+        mma_commit(&p_free[st]);
+        mma_commit(&qdo_empty[st]);
+        if (n + 2 < n_blk) ok = issue_s(n + 2);
+      }
+      if (ok) mma_commit(acc_done);
+    }
+  } else {
+    // ───────────────────────────── compute warps ────────────────────────────
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;  // key row of this thread = TMEM lane
+    const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const float sl2 = scale * kL2e;
+    const int key = k0 + r;
+    const int ept = threadIdx.x - 64;  // 0..127
+    bool ok = true;
+    for (int n = 0; n < n_blk && ok; ++n) {
+      const int st = n & 1;
+      const int h = hk * rep + n / per_head, qb = qb0 + n % per_head;
+      const int qrow0 = qb * kBQ;
+      // LSE and D of the block's 64 queries (buffer st; the block two back has finished with it)
+      float* lse_b = ld_s + st * 128;
+      float* d_b = lse_b + 64;
+      if (ept < 64) {
+        const int q = qrow0 + ept;
+        lse_b[ept] = q < L ? LSE[(size_t)h * T + s + q] * kL2e : INFINITY;
+        d_b[ept] = q < L ? Dv[(size_t)h * T + s + q] : 0.f;
+      }
+      named_bar_sync(1, 128);
+      ok = bar_and(1, 128, mbar_wait(&s_full[st], (n >> 1) & 1, abort_flag, err, 107));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[64], dp[64];
+      tmem_ld32(t_lane + st * 64, sv);
+      tmem_ld32(t_lane + st * 64 + 32, sv + 32);
+      tmem_ld32(t_lane + 128 + st * 64, dp);
+      tmem_ld32(t_lane + 128 + st * 64 + 32, dp + 32);
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);
+      // the products of the block two back must be done with this P^T / dS^T buffer
+      if (n >= 2) {
+        ok = bar_and(1, 128, mbar_wait(&p_free[st], ((n >> 1) & 1) ^ 1, abort_flag, err, 108));
+        if (!ok) break;
+      }
+      // visible: key <= qo + q, key < Lk, q < L (q = qrow0 + c)
+      const bool full = key < Lk && key <= qo + qrow0 && qrow0 + kBQ <= L;
+      const int cmin = key - qo - qrow0;  // first visible column
+      uint8_t* ptrow = sm + kBK_PDS + st * 2 * kPdsBytes + r * 128;
+      uint8_t* dsrow = ptrow + kPdsBytes;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        uint32_t pk[4], dk4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c0 = c + 2 * i;
+          float p0 = ex2(fmaf(sv[c0], sl2, -lse_b[c0]));
+          float p1 = ex2(fmaf(sv[c0 + 1], sl2, -lse_b[c0 + 1]));
+          if (!full) {
+            if (key >= Lk || c0 < cmin) p0 = 0.f;
+            if (key >= Lk || c0 + 1 < cmin) p1 = 0.f;
+          }
+          pk[i] = pack_bf16x2(p0, p1);
+          dk4[i] = pack_bf16x2(p0 * (dp[c0] - d_b[c0]), p1 * (dp[c0 + 1] - d_b[c0 + 1]));
+        }
+        const int chunk = c >> 3;
+        const int off = (chunk ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(ptrow + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(dsrow + off) = make_uint4(dk4[0], dk4[1], dk4[2], dk4[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&p_full[st]);
+    }
+    // epilogue: dV and scale * dK rows of this key
+    if (ok && n_blk > 0) ok = bar_and(1, 128, mbar_wait(acc_done, 0, abort_flag, err, 109));
+    if (ok) {
+      // tcgen05.ld is warp-collective: every lane loads, only rows of real keys are stored
+      tc_fence_after();
+      const bool key_ok = key < Lk;
+      bf16* dvrow = dV + ((size_t)(ks + key) * Hkv + hk) * THD;
+      bf16* dkrow = dK + ((size_t)(ks + key) * Hkv + hk) * THD;
+      for (int which = 0; which < 2; ++which) {
+        bf16* dst = which ? dkrow : dvrow;
+        const float mul = which ? scale : 1.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          if (n_blk > 0) {
+            tmem_ld32(t_lane + 256 + which * 128 + c * 32, ov);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = 0.f;
+          }
+          if (key_ok) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(dst + c * 32 + i) = make_uint4(
+                  pack_bf16x2(ov[i] * mul, ov[i + 1] * mul), pack_bf16x2(ov[i + 2] * mul, ov[i + 3] * mul),
+                  pack_bf16x2(ov[i + 4] * mul, ov[i + 5] * mul), pack_bf16x2(ov[i + 6] * mul, ov[i + 7] * mul));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// dQ: one CTA per 128-query block of one head, sweeping the causal 64-key blocks:
+//   S = Q K_j^T, dP = dO V_j^T                (M=128 queries, N=64 keys, K=128 dims)
+//   dS = P (dP - D), P = 2^(S scale log2e - LSE log2e)            (thread = query row)
+//   dQ += dS K_j                              (M=128 queries, N=128 dims, K=64 keys)
+// TMEM: S[2] (64 cols), dP[2], dQ (128).
+constexpr int kBKq = 64;                  // key block of the dQ kernel
+constexpr int kKvBytes = 64 * 128 * 2;    // one 64-row K or V tile
+constexpr int kDsBytes = 128 * 64 * 2;    // one 128 x 64 dS tile
+constexpr int kDQ_Q = 0, kDQ_DO = kTileBytes, kDQ_KV = 2 * kTileBytes;
+constexpr int kDQ_DS = kDQ_KV + 2 * 2 * kKvBytes;
+constexpr int kDQ_BAR = kDQ_DS + 2 * kDsBytes;
+constexpr int kDQSmem = 1024 + kDQ_BAR + 256;
+
+__global__ void __launch_bounds__(kFaThreads, 1)
+    fa_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapDO,
+                        const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV,
+                        const float* __restrict__ LSE, const float* __restrict__ Dv, const int* __restrict__ cu,
+                        const int* __restrict__ cu_k, const int* __restrict__ q_off, bf16* __restrict__ dQ, int T,
+                        int max_blocks, int Hq, int Hkv, float scale, int* err) {
+  extern __shared__ __align__(1024) uint8_t smraw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kDQ_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;    // [2] dS in shared memory
+  uint64_t* p_free = bars + 11;   // [2]
+  uint64_t* acc_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int doc = blockIdx.x / max_blocks;
+  const int qb = max_blocks - 1 - blockIdx.x % max_blocks;
+  const int h = blockIdx.y, hk = h / (Hq / Hkv);
+  const int s = cu[doc], e = cu[doc + 1], L = e - s;
+  const int ks = cu_k ? cu_k[doc] : s, ke = cu_k ? cu_k[doc + 1] : e, Lk = ke - ks;
+  const int qo = q_off ? q_off[doc] : 0;
+  const int q0 = qb * TBQ;
+  if (q0 >= L) return;
+  const int n_kb = max(0, min((Lk + kBKq - 1) / kBKq, (qo + q0 + TBQ - 1) / kBKq + 1));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_free[i], 1);
+    }
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mapQ);
+    tma_prefetch_desc(&mapDO);
+    tma_prefetch_desc(&mapK);
+    tma_prefetch_desc(&mapV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S[b] at 64 b, dP[b] at 128 + 64 b, dQ at 256
+
+  if (warp == 0) {
+    if (lane == 0 && n_kb > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_2d(sm + kDQ_Q + c * 16384, &mapQ, q_full, h * THD + c * 64, s + q0);
+        tma_load_2d(sm + kDQ_DO + c * 16384, &mapDO, q_full, h * THD + c * 64, s + q0);
+      }
+      for (int j = 0; j < n_kb; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, abort_flag, err, 111)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kKvBytes);
+        uint8_t* dst = sm + kDQ_KV + st * 2 * kKvBytes;
+        for (int c = 0; c < 2; ++c) {
+          tma_load_2d(dst + c * 8192, &mapK, &kv_full[st], hk * THD + c * 64, ks + j * kBKq);
+          tma_load_2d(dst + kKvBytes + c * 8192, &mapV, &kv_full[st], hk * THD + c * 64, ks + j * kBKq);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_kb > 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(128, 64, false, false);
+      constexpr uint32_t id_a = idesc_bf16_f32(128, 128, false, true);
+      const uint32_t sq = smem_u32(sm + kDQ_Q), sdo = smem_u32(sm + kDQ_DO);
+      bool ok = mbar_wait(q_full, 0, abort_flag, err, 113);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, err, 114)) return false;
+        if (!mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, abort_flag, err, 115)) return false;
+        tc_fence_after();
+        const uint32_t skk = smem_u32(sm + kDQ_KV + st * 2 * kKvBytes), svv = skk + kKvBytes;
+#pragma unroll
+        for (int k = 0; k < THD / 16; ++k) {
+          const uint32_t a_off = (k >> 2) * 16384 + (k & 3) * 32;
+          const uint32_t b_off = (k >> 2) * 8192 + (k & 3) * 32;
+          mma_bf16(tmem + st * 64, smem_desc_sw128(sq + a_off, 16, 1024), smem_desc_sw128(skk + b_off, 16, 1024), id_s,
+                   k > 0 ? 1u : 0u);
+          mma_bf16(tmem + 128 + st * 64, smem_desc_sw128(sdo + a_off, 16, 1024), smem_desc_sw128(svv + b_off, 16, 1024),
+                   id_s, k > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n_kb > 1) ok = issue_s(1);
+      for (int j = 0; j < n_kb && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&p_full[st], (j >> 1) & 1, abort_flag, err, 116)) break;
+        tc_fence_after();
+        const uint32_t skk = smem_u32(sm + kDQ_KV + st * 2 * kKvBytes);
+        const uint32_t sds = smem_u32(sm + kDQ_DS + st * kDsBytes);
+#pragma unroll
+        for (int k = 0; k < kBKq / 16; ++k)
+          mma_bf16(tmem + 256, smem_desc_sw128(sds + (k & 3) * 32, 16, 1024),
+                   smem_desc_sw128(skk + (k & 3) * 2048, 8192, 1024), id_a, (j > 0 || k > 0) ? 1u : 0u);
+        mma_commit(&p_free[st]);
+        mma_commit(&kv_empty[st]);
+        if (j + 2 < n_kb) ok = issue_s(j + 2);
+      }
+      if (ok) mma_commit(acc_done);
+    }
+  } else {
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;  // query row = TMEM lane
+    const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const float sl2 = scale * kL2e;
+    const int row = q0 + r;
+    const bool row_ok = row < L;
+    const int qpos = qo + row;
+    const float lse2 = row_ok ? LSE[(size_t)h * T + s + row] * kL2e : INFINITY;
+    const float dval = row_ok ? Dv[(size_t)h * T + s + row] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kb && ok; ++j) {
+      const int st = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1, abort_flag, err, 117));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[64], dp[64];
+      tmem_ld32(t_lane + st * 64, sv);
+      tmem_ld32(t_lane + st * 64 + 32, sv + 32);
+      tmem_ld32(t_lane + 128 + st * 64, dp);
+      tmem_ld32(t_lane + 128 + st * 64 + 32, dp + 32);
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&p_free[st], ((j >> 1) & 1) ^ 1, abort_flag, err, 118));
+        if (!ok) break;
+      }
+      const int key0 = j * kBKq;
+      const bool full = row_ok && key0 + kBKq - 1 <= qpos && key0 + kBKq <= Lk;
+      const int lim = min(qpos + 1, Lk) - key0;  // visible keys [0, lim) of this block
+      uint8_t* dsrow = sm + kDQ_DS + st * kDsBytes + r * 128;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        uint32_t d4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c0 = c + 2 * i;
+          float p0 = ex2(fmaf(sv[c0], sl2, -lse2));
+          float p1 = ex2(fmaf(sv[c0 + 1], sl2, -lse2));
+          if (!full) {
+            if (!row_ok || c0 >= lim) p0 = 0.f;
+            if (!row_ok || c0 + 1 >= lim) p1 = 0.f;
+          }
+          d4[i] = pack_bf16x2(p0 * (dp[c0] - dval), p1 * (dp[c0 + 1] - dval));
+        }
+        *reinterpret_cast<uint4*>(dsrow + (((c >> 3) ^ (r & 7)) << 4)) = make_uint4(d4[0], d4[1], d4[2], d4[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&p_full[st]);
+    }
+    if (ok && n_kb > 0) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, abort_flag, err, 119));
+    if (ok) {
+      // tcgen05.ld is warp-collective: every lane loads, only rows of real queries are stored
+      tc_fence_after();
+      bf16* dqrow = dQ + ((size_t)(s + row) * Hq + h) * THD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        if (n_kb > 0) {
+          tmem_ld32(t_lane + 256 + c * 32, ov);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] = 0.f;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8)
+            *reinterpret_cast<uint4*>(dqrow + c * 32 + i) = make_uint4(
+                pack_bf16x2(ov[i] * scale, ov[i + 1] * scale), pack_bf16x2(ov[i + 2] * scale, ov[i + 3] * scale),
+                pack_bf16x2(ov[i + 4] * scale, ov[i + 5] * scale), pack_bf16x2(ov[i + 6] * scale, ov[i + 7] * scale));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 }  // namespace
 
 bool flash_attn_tc_enabled() {
@@ -338,6 +820,39 @@ void flash_attn_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const int* c
   }
   dim3 grid(n_docs * mb, Hq);
   fa_fwd_tc_kernel<<<grid, kFaThreads, kFaSmem, st>>>(mq, mk, mv, cu, cu_k, q_off, o, lse, T, mb, Hq, Hkv, scale, err);
+  MESHY_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace meshy
+
+namespace meshy {
+
+void flash_attn_bwd_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* dout, const float* lse,
+                       const float* dvec, const int* cu, int n_docs, bf16* dq, bf16* dk, bf16* dv, int T, int Tk,
+                       int max_seqlen, int max_seqlen_k, int Hq, int Hkv, float scale, cudaStream_t st,
+                       const int* cu_k, const int* q_off, int* err) {
+  if (T == 0 || Tk == 0 || n_docs == 0) return;
+  CUtensorMap mq128 = make_map_bf16(q, T, (int64_t)Hq * THD, (int64_t)Hq * THD, 64, 128);
+  CUtensorMap mdo128 = make_map_bf16(dout, T, (int64_t)Hq * THD, (int64_t)Hq * THD, 64, 128);
+  CUtensorMap mq64 = make_map_bf16(q, T, (int64_t)Hq * THD, (int64_t)Hq * THD, 64, 64);
+  CUtensorMap mdo64 = make_map_bf16(dout, T, (int64_t)Hq * THD, (int64_t)Hq * THD, 64, 64);
+  CUtensorMap mk128 = make_map_bf16(k, Tk, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 128);
+  CUtensorMap mv128 = make_map_bf16(v, Tk, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 128);
+  CUtensorMap mk64 = make_map_bf16(k, Tk, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 64);
+  CUtensorMap mv64 = make_map_bf16(v, Tk, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 64);
+  static bool attr = false;
+  if (!attr) {
+    MESHY_CUDA_CHECK(cudaFuncSetAttribute(fa_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBKSmem));
+    MESHY_CUDA_CHECK(cudaFuncSetAttribute(fa_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDQSmem));
+    attr = true;
+  }
+  const int mbk = ((cu_k ? max_seqlen_k : max_seqlen) + TBK - 1) / TBK;
+  const int mbq = (max_seqlen + TBQ - 1) / TBQ;
+  fa_bwd_dkdv_tc_kernel<<<dim3(n_docs * mbk, Hkv), kFaThreads, kBKSmem, st>>>(
+      mq64, mdo64, mk128, mv128, lse, dvec, cu, cu_k, q_off, dk, dv, T, mbk, Hq, Hkv, scale, err);
+  MESHY_CUDA_CHECK(cudaGetLastError());
+  fa_bwd_dq_tc_kernel<<<dim3(n_docs * mbq, Hq), kFaThreads, kDQSmem, st>>>(
+      mq128, mdo128, mk64, mv64, lse, dvec, cu, cu_k, q_off, dq, T, mbq, Hq, Hkv, scale, err);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 
