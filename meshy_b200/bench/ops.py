@@ -141,6 +141,28 @@ def main(argv=None):
             fl = 2.0 * T * n * kk
             emit(dict(op=f"gemm_{k}", M=T, N=n, K=kk, us=round(us, 2), tflops=round(fl / us / 1e6, 1),
                       frac_of_bf16=round(fl / us / 1e6 / tflops, 3), impl="cublas" if args.torch_baseline else "ours"))
+        if only and "flash_attn" not in only:
+            return
+        # packed causal attention, forward and backward (MESHY_FA_TC=0: the mma.sync kernels)
+        hq, hkv, hd = a.n_heads, a.n_kv_heads, a.head_dim
+        for lens in ([2048] * 8, [4096] * 4, [1300] * 8, [16384]):
+            Tt = sum(lens)
+            q = torch.randn(Tt, hq, hd, device=dev).to(torch.bfloat16)
+            kx = torch.randn(Tt, hkv, hd, device=dev).to(torch.bfloat16)
+            vx = torch.randn(Tt, hkv, hd, device=dev).to(torch.bfloat16)
+            cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=dev)
+            o = torch.empty_like(q)
+            lse = torch.empty(hq, Tt, device=dev)
+            sc = 1 / math.sqrt(hd)
+            us_f = time_op(lambda: C.flash_attn_fwd(q, kx, vx, cu, o, lse, max(lens), sc), iters=10)
+            go = torch.randn_like(q)
+            gq, gk, gv = torch.empty_like(q), torch.empty_like(kx), torch.empty_like(vx)
+            us_b = time_op(lambda: C.flash_attn_bwd(q, kx, vx, cu, o, go, lse, gq, gk, gv, max(lens), sc), iters=10)
+            fl = sum(2.0 * L * L * hq * hd for L in lens)
+            emit(dict(op="flash_attn", docs=f"{len(lens)}x{lens[0]}", fwd_us=round(us_f, 1),
+                      fwd_tflops=round(fl / us_f / 1e6, 1), bwd_us=round(us_b, 1),
+                      bwd_tflops=round(2.5 * fl / us_b / 1e6, 1),
+                      impl="mma.sync" if os.environ.get("MESHY_FA_TC", "1") == "0" else "tcgen05"))
 
 
 if __name__ == "__main__":
