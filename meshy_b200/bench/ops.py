@@ -130,6 +130,8 @@ def main(argv=None):
     else:
         T = args.tokens
         for k, w in W.items():
+            if only and k not in only:
+                continue
             n, kk = w.shape
             x = torch.randn(T, kk, device=dev).to(torch.bfloat16)
             out = torch.empty(T, n, device=dev, dtype=torch.bfloat16)
