@@ -515,6 +515,95 @@ void lmhead_sample(Tensor h, Tensor w, Tensor tok, Tensor lp, double temperature
   count(2);
 }
 
+// One decode step's sampling and bookkeeping in two kernels: the LM head with the Gumbel-max sampler
+// in its epilogue on the small-M path (optionally on a prepared RMSNorm input: h = bf16(g * x) with
+// the per-tile sums of squares ``part``), then the partial merge fused with the row advance (and
+// step += 1). Returns false when the small-M sampler cannot take the problem.
+bool decode_sample_advance(Tensor h, Tensor w, c10::optional<Tensor> part, int64_t part_t, double norm_d, double eps,
+                           double temperature, int64_t seed, Tensor step, Tensor tok_in, Tensor pos, Tensor seq_lens,
+                           Tensor gen, Tensor max_new, Tensor done, Tensor slot, Tensor bt, Tensor req,
+                           Tensor out_tok, Tensor out_lp, Tensor eos, int64_t page) {
+  CHECK_CUDA(h);
+  CHECK_BF16(h);
+  CHECK_BF16(w);
+  TORCH_CHECK(h.dim() == 2 && w.dim() == 2 && h.stride(1) == 1 && w.stride(1) == 1, "decode_sample_advance: row-major");
+  TORCH_CHECK(step.scalar_type() == at::kLong, "decode_sample_advance: int64 step");
+  if (!(temperature > 0.0)) return false;
+  const c10::cuda::CUDAGuard guard(h.device());
+  GemmProblem g;
+  g.A = h.data_ptr();
+  g.B = w.data_ptr();
+  g.lda = h.stride(0);
+  g.ldb = w.stride(0);
+  g.M = h.size(0);
+  g.K = h.size(1);
+  g.N = w.size(0);
+  g.epi = EPI_LSE;
+  g.gumbel = 1;
+  g.inv_temp = (float)(1.0 / temperature);
+  g.seed = (uint64_t)seed;
+  g.step_ptr = ptr<int64_t>(step);
+  if (part.has_value() && part->defined()) {
+    g.part_in = ptr<float>(*part);
+    g.part_t = (int)part_t;
+    g.norm_d = (float)norm_d;
+    g.norm_eps = (float)eps;
+  }
+  g.err = ptr<int>(scratch(0, 0).err);
+  if (g.M == 0 || !gemm_small_lse_eligible(g)) return false;
+  const int parts = gemm_small_lse_parts(g.N);
+  Tensor pbuf = torch::empty({g.M, parts, 8}, h.options().dtype(torch::kFloat));
+  g.partial = ptr<float>(pbuf);
+  gemm_small_launch(g, cur_stream());
+  sample_advance(ptr<float>(pbuf), parts, ptr<int64_t>(tok_in), ptr<int>(pos), ptr<int>(seq_lens), ptr<int>(gen),
+                 ptr<int>(max_new), ptr<int>(done), ptr<int64_t>(slot), ptr<int>(bt), ptr<int>(req),
+                 ptr<int64_t>(out_tok), ptr<float>(out_lp), eos.numel() ? ptr<int64_t>(eos) : nullptr,
+                 (int)eos.numel(), g.M, (int)bt.size(1), (int)out_tok.size(1), (int)page, ptr<int64_t>(step),
+                 cur_stream());
+  count(2);
+  return true;
+}
+
+// The small-M sampler alone (tokens and log-probs out), for tests and benchmarks of the kernel.
+bool lmhead_sample_small(Tensor h, Tensor w, c10::optional<Tensor> part, int64_t part_t, double norm_d, double eps,
+                         Tensor tok, Tensor lp, double temperature, int64_t seed, c10::optional<Tensor> step) {
+  CHECK_CUDA(h);
+  CHECK_BF16(h);
+  CHECK_BF16(w);
+  TORCH_CHECK(h.dim() == 2 && w.dim() == 2 && h.stride(1) == 1 && w.stride(1) == 1, "lmhead_sample_small: row-major");
+  if (!(temperature > 0.0)) return false;
+  const c10::cuda::CUDAGuard guard(h.device());
+  GemmProblem g;
+  g.A = h.data_ptr();
+  g.B = w.data_ptr();
+  g.lda = h.stride(0);
+  g.ldb = w.stride(0);
+  g.M = h.size(0);
+  g.K = h.size(1);
+  g.N = w.size(0);
+  g.epi = EPI_LSE;
+  g.gumbel = 1;
+  g.inv_temp = (float)(1.0 / temperature);
+  g.seed = (uint64_t)seed;
+  g.step_ptr = optr<int64_t>(step);
+  if (part.has_value() && part->defined()) {
+    g.part_in = ptr<float>(*part);
+    g.part_t = (int)part_t;
+    g.norm_d = (float)norm_d;
+    g.norm_eps = (float)eps;
+  }
+  g.err = ptr<int>(scratch(0, 0).err);
+  if (g.M == 0 || !gemm_small_lse_eligible(g)) return false;
+  const int parts = gemm_small_lse_parts(g.N);
+  Tensor pbuf = torch::empty({g.M, parts, 8}, h.options().dtype(torch::kFloat));
+  g.partial = ptr<float>(pbuf);
+  gemm_small_launch(g, cur_stream());
+  lse_merge(ptr<float>(pbuf), parts, 128, nullptr, nullptr, nullptr, nullptr, ptr<int64_t>(tok), ptr<float>(lp), g.M,
+            cur_stream());
+  count(2);
+  return true;
+}
+
 void embedding_fwd_(Tensor ids, Tensor w, Tensor out) {
   const c10::cuda::CUDAGuard guard(w.device());
   TORCH_CHECK(ids.scalar_type() == at::kLong, "ids must be int64");
@@ -575,7 +664,7 @@ void kv_write_(Tensor k, Tensor v, Tensor kc, Tensor vc, Tensor slots) {
 }
 
 void paged_attention_(Tensor q, Tensor kc, Tensor vc, Tensor bt, Tensor seq_lens, Tensor out, double scale,
-                      c10::optional<Tensor> workspace) {
+                      c10::optional<Tensor> workspace, bool decode_step) {
   const c10::cuda::CUDAGuard guard(q.device());
   CHECK_CONTIG(q);
   CHECK_CONTIG(kc);
@@ -592,7 +681,7 @@ void paged_attention_(Tensor q, Tensor kc, Tensor vc, Tensor bt, Tensor seq_lens
   }
   paged_decode_tma(ptr<bf16>(q), ptr<bf16>(kc), ptr<bf16>(vc), (int)kc.size(0), ptr<int>(bt), ptr<int>(seq_lens),
                    ptr<bf16>(out), part.defined() ? ptr<float>(part) : nullptr, B, Hq, Hkv, hd, page, max_pages,
-                   n_split, (float)scale, ptr<int>(scratch(0, 0).err), cur_stream());
+                   n_split, (float)scale, ptr<int>(scratch(0, 0).err), cur_stream(), decode_step);
   count(n_split > kMaxClusterSplits ? 2 : 1);
 }
 
@@ -809,6 +898,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lmhead_logprob_fwd", &lmhead_logprob_fwd);
   m.def("lmhead_dlogits", &lmhead_dlogits);
   m.def("lmhead_sample", &lmhead_sample);
+  m.def("lmhead_sample_small", &lmhead_sample_small,
+        "small-M LM-head sampler (<= 64 rows); returns false when not eligible");
+  m.def("decode_sample_advance", &decode_sample_advance,
+        "decode step tail: small-M LM-head sampler + merge fused with the row advance; false when not eligible");
   m.def("embedding_fwd", &embedding_fwd_);
   m.def("embedding_bwd", &embedding_bwd_);
   m.def("sq_norm", &sq_norm_);
@@ -816,7 +909,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ppo_loss_fused", &ppo_loss_fused_);
   m.def("gae_scan", &gae_scan_);
   m.def("kv_write", &kv_write_);
-  m.def("paged_attention", &paged_attention_);
+  m.def("paged_attention", &paged_attention_, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_table"), py::arg("seq_lens"), py::arg("out"), py::arg("scale"), py::arg("workspace"),
+        py::arg("decode_step") = false,
+        "paged decode attention; decode_step: the kernel before wrote only each sequence's newest K/V row");
   m.def("paged_decode_force_splits", [](int64_t n) { paged_decode_force_splits((int)n); },
         "decode attention split count override (0 = heuristic); for tests and benchmarks");
   m.def("decode_advance", &decode_advance_);

@@ -98,8 +98,22 @@ struct Philox {
   }
 };
 
-// Uniform in (0, 1): 24 random bits, offset by half an ulp so 0 and 1 never occur.
-__device__ __forceinline__ float u01(uint32_t x) { return ((x >> 8) + 0.5f) * (1.0f / 16777216.0f); }
+// Uniform in (0, 1): 23 random bits, offset by half a step so 0 and 1 never occur. (With 24 bits the
+// top value 2^24 - 0.5 is not a float and rounds to 2^24, i.e. u = 1 exactly and log(u) = 0.)
+__device__ __forceinline__ float u01(uint32_t x) { return ((x >> 9) + 0.5f) * (1.0f / 8388608.0f); }
+
+// Standard Gumbel variate -log(-log(u)) from 32 random bits. The inner -log(u) must be accurate relative
+// to its value: u can lie within 2^-24 of 1, where -log(u) is ~6e-8 and the fast __logf's absolute error
+// (~1e-7) could make it zero or negative -- an infinite or NaN perturbation that hands the draw to an
+// arbitrary token (a few draws in 10^7, a few percent of the rows of a 152k-entry vocabulary). Near 1 it
+// is the Taylor series -log(1 - v) = v + v^2/2 + v^3/3 + v^4/4 (v = 1 - u is exact, truncation < v^5/5);
+// elsewhere |log u| > 0.01 and the fast log's relative error stays below 2e-5.
+__device__ __forceinline__ float gumbel(uint32_t bits) {
+  const float u = u01(bits);
+  const float v = 1.0f - u;
+  const float e = v < 0.01f ? v * (1.0f + v * (0.5f + v * (1.0f / 3.0f + v * 0.25f))) : -__logf(u);
+  return -__logf(e);
+}
 #endif  // __CUDACC__
 
 }  // namespace meshy

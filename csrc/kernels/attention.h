@@ -34,9 +34,12 @@ void paged_decode(const bf16* q, const bf16* kc, const bf16* vc, const int* bt, 
 constexpr int kMaxClusterSplits = 8;
 int paged_decode_tma_splits(int B, int Hkv, int max_pages);
 void paged_decode_force_splits(int n);  // tests: 0 restores the heuristic
+// ``decode_step``: the kernel before this one in the stream wrote, of this cache, at most the row of each
+// sequence's last position (seq_lens[b] - 1) and nothing of bt / seq_lens. Pages before a sequence's last
+// one are then loaded before the programmatic-dependent-launch wait, under that kernel's tail.
 void paged_decode_tma(const bf16* q, const bf16* kc, const bf16* vc, int n_cache_pages, const int* bt,
                       const int* seq_lens, bf16* o, float* part, int B, int Hq, int Hkv, int hd, int page,
-                      int max_pages, int n_split, float scale, int* err, cudaStream_t st);
+                      int max_pages, int n_split, float scale, int* err, cudaStream_t st, bool decode_step = false);
 void paged_decode_combine(const float* part, bf16* o, int B, int Hq, int hd, int n_split, cudaStream_t st);
 void kv_write(const bf16* k, const bf16* v, bf16* kc, bf16* vc, const int64_t* slots, int n, int Hkv, int hd, int page,
               cudaStream_t st);

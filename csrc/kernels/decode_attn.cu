@@ -81,7 +81,7 @@ template <int HD, bool CLUSTER>
 __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
     const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV, const bf16* __restrict__ Q,
     const int* __restrict__ bt, const int* __restrict__ seq_lens, bf16* __restrict__ O, float* __restrict__ part,
-    int Hq, int Hkv, int max_pages, int n_split, float scale, int* err) {
+    int Hq, int Hkv, int max_pages, int n_split, float scale, int* err, int early) {
   using C = DCfg<HD>;
   extern __shared__ __align__(1024) uint8_t smraw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
@@ -92,12 +92,6 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
 
   const int b = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
   const int rep = Hq / Hkv;
-  pdl_wait();  // Q, the cache rows of this step and the lengths come from the kernels before
-  pdl_trigger();
-  const int L = seq_lens[b];
-  const int n_pages = (L + kPage - 1) / kPage;
-  const int per = (n_pages + n_split - 1) / n_split;
-  const int p0 = min(n_pages, sp * per), p1 = min(n_pages, p0 + per);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const float sl2 = scale * kLog2eD;
 
@@ -111,6 +105,33 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
     tma_prefetch_desc(&mapK);
     tma_prefetch_desc(&mapV);
   }
+  // Decode step (``early``): the kernel before wrote only each sequence's newest K/V row, and the lengths
+  // and block table are older, so everything but the Q rows and the last page may be read before the
+  // wait; the producer starts the ring on the split's complete pages under that kernel's tail.
+  if (!early) pdl_wait();
+  const int L = seq_lens[b];
+  const int n_pages = (L + kPage - 1) / kPage;
+  const int per = (n_pages + n_split - 1) / n_split;
+  const int p0 = min(n_pages, sp * per), p1 = min(n_pages, p0 + per);
+  int npre = 0;
+  if (early) {
+    __syncthreads();  // barriers initialised
+    npre = max(0, min(min(p1, n_pages - 1) - p0, C::STAGES));
+    if (warp == 4 && lane == 0) {
+      for (int j = 0; j < npre; ++j) {
+        const int row = (bt[(size_t)b * max_pages + p0 + j] * Hkv + hk) * kPage;
+        uint8_t* sk = ring + j * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[j], C::STAGE_BYTES);
+#pragma unroll
+        for (int h = 0; h < HD / 64; ++h) {
+          tma_load_2d(sk + h * 8192, &mapK, &full[j], h * 64, row);
+          tma_load_2d(sk + C::TILE_BYTES + h * 8192, &mapV, &full[j], h * 64, row);
+        }
+      }
+    }
+    pdl_wait();  // Q and the newest K/V rows come from the kernel before
+  }
+  pdl_trigger();
   // query rows of this GQA group → Qs[16][HD] (XOR swizzle of 16-byte chunks), rows >= rep zero
   for (int i = threadIdx.x; i < 16 * HD / 8; i += kThreadsDec) {
     int r = i / (HD / 8), c = (i % (HD / 8)) * 8;
@@ -129,11 +150,11 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
   if (warp == 4) {
     // ───────────────────────────── producer ─────────────────────────────
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0, last_stage = 0;
+      int stage = npre % C::STAGES;
+      uint32_t phase = npre == C::STAGES ? 1u : 0u;
+      int issued = npre, last_stage = npre > 0 ? npre - 1 : 0;
       uint32_t last_phase = 0;
-      for (int pi = p0; pi < p1; ++pi) {
+      for (int pi = p0 + npre; pi < p1; ++pi) {
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
         const int pg = bt[(size_t)b * max_pages + pi];
         const int row = (pg * Hkv + hk) * kPage;
@@ -335,7 +356,7 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
 template <int HD, bool CLUSTER>
 void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, const int* bt, const int* seq_lens,
                 bf16* o, float* part, int B, int Hq, int Hkv, int max_pages, int n_split, float scale, int* err,
-                cudaStream_t st) {
+                bool early, cudaStream_t st) {
   using C = DCfg<HD>;
   auto k = paged_decode_tma_kernel<HD, CLUSTER>;
   static bool attr_set = false;
@@ -358,7 +379,7 @@ void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, con
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   MESHY_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, mk, mv, q, bt, seq_lens, o, part, Hq, Hkv, max_pages, n_split, scale,
-                                      err));
+                                      err, early ? 1 : 0));
 }
 
 }  // namespace
@@ -384,7 +405,7 @@ int paged_decode_tma_splits(int B, int Hkv, int max_pages) {
 
 void paged_decode_tma(const bf16* q, const bf16* kc, const bf16* vc, int n_cache_pages, const int* bt,
                       const int* seq_lens, bf16* o, float* part, int B, int Hq, int Hkv, int hd, int page,
-                      int max_pages, int n_split, float scale, int* err, cudaStream_t st) {
+                      int max_pages, int n_split, float scale, int* err, cudaStream_t st, bool decode_step) {
   MESHY_CHECK(hd == 64 || hd == 128, "paged_decode: head_dim must be 64 or 128");
   MESHY_CHECK(page == kPage, "paged_decode: page size must be 64");
   MESHY_CHECK(Hq % Hkv == 0 && Hq / Hkv <= 16, "paged_decode: at most 16 query heads per KV head");
@@ -395,12 +416,17 @@ void paged_decode_tma(const bf16* q, const bf16* kc, const bf16* vc, int n_cache
   const int64_t rows = (int64_t)n_cache_pages * Hkv * kPage;
   CUtensorMap mk = make_map_bf16(kc, rows, hd, hd, 64, kPage);
   CUtensorMap mv = make_map_bf16(vc, rows, hd, hd, 64, kPage);
+  const bool early = decode_step && pdl_enabled();
   if (hd == 128) {
-    if (cluster) launch_dec<128, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, st);
-    else launch_dec<128, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, st);
+    if (cluster)
+      launch_dec<128, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, st);
+    else
+      launch_dec<128, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, st);
   } else {
-    if (cluster) launch_dec<64, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, st);
-    else launch_dec<64, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, st);
+    if (cluster)
+      launch_dec<64, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, st);
+    else
+      launch_dec<64, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, st);
   }
   if (!cluster) paged_decode_combine(part, o, B, Hq, hd, n_split, st);
 }

@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int t = 0; t < 4; ++t) {
                 float z = v[i + t];
                 if (z == -INFINITY) continue;
-                float gsc = z - __logf(-__logf(u01(rr[t])));
+                float gsc = z + gumbel(rr[t]);
                 if (gsc > best) {
                   best = gsc;
                   besti = col0 + i + t;

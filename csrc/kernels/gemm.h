@@ -83,6 +83,11 @@ bool gemm_small_norm_eligible(const GemmProblem& g);
 bool gemm_small_prep_eligible(const GemmProblem& g);
 // Whether the small-M path can run the fused QKV + RoPE + KV-cache epilogue (q_out ...).
 bool gemm_small_rope_eligible(const GemmProblem& g);
+// Fused LM-head sampler on the small-M path: EPI_LSE with Gumbel noise (no labels), M <= 64, any
+// vocabulary size; writes gemm_small_lse_parts(N) partials per token row ([M][parts][8], the layout
+// lse_merge reads). With part_in the rows of A are prepared RMSNorm inputs (see above).
+bool gemm_small_lse_eligible(const GemmProblem& g);
+int gemm_small_lse_parts(int N);
 void gemm_small_launch(const GemmProblem& g, cudaStream_t stream);
 // enabled: 1/0 (-1 keeps); force_cs: cluster size override, 0 = heuristic (-1 keeps)
 void gemm_small_config(int enabled, int force_cs);

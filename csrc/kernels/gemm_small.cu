@@ -78,6 +78,12 @@ struct SmallArgs {
   bf16* vc;
   const int64_t* slots;
   int hq, hkv;
+  // fused LM-head sampler (EPI_LSE, persistent schedule): per CTA and token row, the log-sum-exp
+  // partial and the Gumbel-max winner of the CTA's vocabulary tiles -> partial[m][gridDim.x][8]
+  float* partial;
+  float inv_temp;
+  uint64_t seed;
+  const int64_t* step_ptr;
 };
 
 template <int MP, bool PERSIST>
@@ -90,7 +96,10 @@ struct SCfg {
   static constexpr int TMEM_COLS = (N_ACC * MP < 32) ? 32 : N_ACC * MP;
   static constexpr int RED_BYTES = 128 * MP * 4;
   static constexpr int BAR_BYTES = 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + (MP + 16 + 4 * 128) * 4;
+  // after the barriers: rstd [MP], 16 floats of cross-warp sums, then the QKV epilogue's row exchange
+  // [4][128] or the sampler's cross-warp statistics [4][MP][5]
+  static constexpr int XCH_FLOATS = (MP <= 64 && 20 * MP > 4 * 128) ? 20 * MP : 4 * 128;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + (MP + 16 + XCH_FLOATS) * 4;
   static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "reduction buffer must fit in the stage ring");
   static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
 };
@@ -177,6 +186,162 @@ __device__ __forceinline__ void norm_stages(const SmallArgs& p, uint8_t* smem, u
   }
 }
 
+// ─── fused LM-head sampler (EPI_LSE) ─────────────────────────────────────────
+// Statistics of a set of logits z_n (one token row): max, sum exp(z - max), and the Gumbel-max winner
+// (largest z_n + g_n, its z_n and its vocabulary index n). Two sets combine exactly, in any order.
+struct LseSt {
+  float mx, s, best, bz;
+  int bi;
+};
+
+__device__ __forceinline__ LseSt lse_comb(const LseSt& a, const LseSt& b) {
+  LseSt r;
+  const float hi = fmaxf(a.mx, b.mx), lo = fminf(a.mx, b.mx);
+  const float e = (hi == -INFINITY) ? 0.f : __expf(lo - hi);
+  r.mx = hi;
+  r.s = (a.mx >= b.mx) ? a.s + b.s * e : a.s * e + b.s;
+  // ties go to the smaller index; -1 (no winner) compares as the largest unsigned index
+  const bool tb = b.best > a.best || (b.best == a.best && (unsigned)b.bi < (unsigned)a.bi);
+  r.best = tb ? b.best : a.best;
+  r.bz = tb ? b.bz : a.bz;
+  r.bi = tb ? b.bi : a.bi;
+  return r;
+}
+
+__device__ __forceinline__ LseSt lse_shfl(const LseSt& a, int o) {
+  LseSt r;
+  r.mx = __shfl_xor_sync(0xffffffffu, a.mx, o);
+  r.s = __shfl_xor_sync(0xffffffffu, a.s, o);
+  r.best = __shfl_xor_sync(0xffffffffu, a.best, o);
+  r.bz = __shfl_xor_sync(0xffffffffu, a.bz, o);
+  r.bi = __shfl_xor_sync(0xffffffffu, a.bi, o);
+  return r;
+}
+
+// One halving step of the warp reduce-scatter: the lane keeps the upper or lower half of its C
+// statistics (by lane bit C/2) and folds in the partner's copy of the same half.
+template <int C>
+__device__ __forceinline__ void lse_halve(LseSt* S, int lane) {
+  if constexpr (C > 1) {
+    constexpr int h = C / 2;
+    const bool up = (lane & h) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const LseSt keep = up ? S[i + h] : S[i];
+      const LseSt send = up ? S[i] : S[i + h];
+      S[i] = lse_comb(keep, lse_shfl(send, h));
+    }
+    lse_halve<h>(S, lane);
+  }
+}
+
+// Reduce-scatter over the warp: lane l holds logits z[0..CH) and perturbed logits zg of its vocabulary
+// row n for CH token columns; afterwards it holds the warp's statistics (32 vocabulary rows) of token
+// column l % CH. 31 combines and ~80 shuffles per lane instead of a full reduction per column.
+template <int CH>
+__device__ __forceinline__ LseSt lse_warp_scatter(const float* z, const float* zg, int n, int lane) {
+  constexpr int H = CH / 2;
+  LseSt S[H];
+  const bool up = (lane & H) != 0;
+#pragma unroll
+  for (int i = 0; i < H; ++i) {
+    // first step on single logits: only z and z + g cross lanes (the partner's row is n ^ H)
+    const float kz = up ? z[i + H] : z[i], kg = up ? zg[i + H] : zg[i];
+    const float sz = up ? z[i] : z[i + H], sg = up ? zg[i] : zg[i + H];
+    const float rz = __shfl_xor_sync(0xffffffffu, sz, H), rg = __shfl_xor_sync(0xffffffffu, sg, H);
+    const LseSt a{kz, kz == -INFINITY ? 0.f : 1.f, kg, kz, n};
+    const LseSt b{rz, rz == -INFINITY ? 0.f : 1.f, rg, rz, n ^ H};
+    S[i] = lse_comb(a, b);
+  }
+  lse_halve<H>(S, lane);
+  LseSt r = S[0];
+  if constexpr (CH < 32) r = lse_comb(r, lse_shfl(r, CH));  // lanes l and l + CH hold the same column
+  return r;
+}
+
+// Persistent-schedule epilogue of the sampler. Every tile: logits z = acc * rstd[m] / T of the tile's
+// 128 vocabulary rows (TMEM lanes) for each token column m, Gumbel noise from Philox-4x32-10 keyed by
+// (seed, step) with counter (n, m & ~3, step >> 32, tag) -- one call covers four token columns of a
+// row -- and the warp reduce-scatter above; each lane folds its column into running statistics. At
+// the end the four warps combine through shared memory and thread m writes the CTA's partial
+// (max, sum, 0, 0, best, z of best, index, 0) of row m, the layout lse_merge reads.
+template <int MP>
+__device__ __forceinline__ void lse_epilogue(const SmallArgs& p, uint32_t t_lane, uint64_t* tfull, uint64_t* tempty,
+                                             volatile int* abort_flag, const float* sc, float* red, int first,
+                                             int stride) {
+  constexpr int CH = MP < 32 ? MP : 32;
+  constexpr int NC = MP / CH;
+  const int lane = threadIdx.x % 32, q = (threadIdx.x / 32) & 3, f = q * 32 + lane;
+  const uint64_t step = p.step_ptr ? (uint64_t)*p.step_ptr : 0ull;
+  const uint2 key = make_uint2((uint32_t)p.seed, (uint32_t)(p.seed >> 32) ^ (uint32_t)step);
+  LseSt run[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) run[c] = LseSt{-INFINITY, 0.f, -INFINITY, 0.f, -1};
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  for (int nt = first; nt < p.n_tiles; nt += stride) {
+    if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+    tc_fence_after();
+    const int n = nt * 128 + f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float v[32];
+      ld_cols<MP>(t_lane + acc * MP + c * CH, v);
+      if (c == NC - 1) {  // the accumulator is in registers: hand it back to the MMA warp
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      }
+      if (c * CH >= p.M) continue;  // warp-uniform
+      float z[CH], zg[CH];
+#pragma unroll
+      for (int i = 0; i < CH; i += 4) {
+        const int m0 = c * CH + i;
+        uint4 r = make_uint4(0u, 0u, 0u, 0u);
+        if (m0 < p.M)  // warp-uniform: no noise for padding columns
+          r = Philox::gen(make_uint4((uint32_t)n, (uint32_t)m0, (uint32_t)(step >> 32), 0x6B1Fu), key);
+        const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int m = m0 + t;
+          const float zz = (n < p.N && m < p.M) ? v[i + t] * sc[m] : -INFINITY;
+          z[i + t] = zz;
+          zg[i + t] = zz == -INFINITY ? -INFINITY : zz + gumbel(rr[t]);
+        }
+      }
+      run[c] = lse_comb(run[c], lse_warp_scatter<CH>(z, zg, n, lane));
+    }
+    if (++acc == 2) {
+      acc = 0;
+      acc_phase ^= 1;
+    }
+  }
+  // combine the four warps: red[w][MP][5]
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    if (lane < CH) {
+      float* o = red + ((size_t)q * MP + c * CH + lane) * 5;
+      o[0] = run[c].mx;
+      o[1] = run[c].s;
+      o[2] = run[c].best;
+      o[3] = run[c].bz;
+      o[4] = __int_as_float(run[c].bi);
+    }
+  }
+  named_bar_sync(1, 128);
+  const int m = threadIdx.x - 64;
+  if (m < p.M) {
+    LseSt t{-INFINITY, 0.f, -INFINITY, 0.f, -1};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float* o = red + ((size_t)w * MP + m) * 5;
+      t = lse_comb(t, LseSt{o[0], o[1], o[2], o[3], __float_as_int(o[4])});
+    }
+    float* o = p.partial + ((size_t)m * gridDim.x + blockIdx.x) * 8;
+    *reinterpret_cast<float4*>(o) = make_float4(t.mx, t.s, 0.f, 0.f);
+    *reinterpret_cast<float4*>(o + 4) = make_float4(t.best, t.bz, __int_as_float(t.bi), 0.f);
+  }
+}
+
 template <int MP, bool PERSIST>
 __global__ void __launch_bounds__(kSmallThreads, 1)
     gemm_small_kernel(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapX,
@@ -237,7 +402,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       // The weights do not depend on the kernel before this one: under programmatic dependent
       // launch the first STAGES weight tiles stream in while that kernel finishes; the activation
       // tiles of those stages follow once it has completed.
-      const int npre = PERSIST ? 0 : min(kb1 - kb0, C::STAGES);
+      const int npre = first < p.n_tiles ? min(kb1 - kb0, C::STAGES) : 0;
       for (int j = 0; j < npre; ++j) {
         mbar_arrive_expect_tx(&full[j], C::STAGE_BYTES);
         tma_load_2d(smem + j * C::STAGE_BYTES, &mapW, &full[j], (kb0 + j) * SBK, first * 128);
@@ -327,13 +492,19 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     // ─────────────────────────────── epilogue ───────────────────────────────────
     pdl_wait();  // bias / residual / output may be touched by the kernels before
     if (!PERSIST && fuse_norm && has_k) norm_stages<MP>(p, smem, full, normed, rstd_s, kb0, kb1, abort_flag);
-    if (p.part_in) {
+    const bool lse = PERSIST && p.epi == EPI_LSE;
+    if (p.part_in || lse) {
       // rows of X were bf16(g * x): their RMSNorm scale from the producer GEMM's per-tile partial sums
+      // (the sampler also folds in 1 / temperature)
       for (int m = threadIdx.x - 64; m < MP; m += 128) {
-        float ss = 0.f;
-        if (m < p.M)
-          for (int t = 0; t < p.part_t; ++t) ss += p.part_in[(size_t)t * kSmallPartLd + m];
-        rstd_s[m] = m < p.M ? rsqrtf(ss / p.norm_d + p.norm_eps) : 0.f;
+        float r = 1.f;
+        if (p.part_in) {
+          float ss = 0.f;
+          if (m < p.M)
+            for (int t = 0; t < p.part_t; ++t) ss += p.part_in[(size_t)t * kSmallPartLd + m];
+          r = m < p.M ? rsqrtf(ss / p.norm_d + p.norm_eps) : 0.f;
+        }
+        rstd_s[m] = lse ? r * p.inv_temp : r;
       }
       named_bar_sync(1, 128);
     }
@@ -342,29 +513,34 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
     constexpr int CH = MP < 32 ? MP : 32;
     if constexpr (PERSIST) {
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      for (int nt = first; nt < p.n_tiles; nt += stride) {
-        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
-        tc_fence_after();
-        const int n = nt * 128 + f;
-        float v[32];
+      if (lse) {
+        if constexpr (MP <= 64)
+          lse_epilogue<MP>(p, t_lane, tfull, tempty, abort_flag, rstd_s, rstd_s + MP + 16, first, stride);
+      } else {
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int nt = first; nt < p.n_tiles; nt += stride) {
+          if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+          tc_fence_after();
+          const int n = nt * 128 + f;
+          float v[32];
 #pragma unroll 1
-        for (int c = 0; c < MP / CH; ++c) {
-          ld_cols<MP>(t_lane + acc * MP + c * CH, v);
-          if (n < p.N) {
+          for (int c = 0; c < MP / CH; ++c) {
+            ld_cols<MP>(t_lane + acc * MP + c * CH, v);
+            if (n < p.N) {
 #pragma unroll
-            for (int i = 0; i < CH; ++i) {
-              const int m = c * CH + i;
-              if (m < p.M) store_val(p, m, n, p.part_in ? v[i] * rstd_s[m] : v[i]);
+              for (int i = 0; i < CH; ++i) {
+                const int m = c * CH + i;
+                if (m < p.M) store_val(p, m, n, p.part_in ? v[i] * rstd_s[m] : v[i]);
+              }
             }
           }
-        }
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
-        if (++acc == C::N_ACC) {
-          acc = 0;
-          acc_phase ^= 1;
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+          if (++acc == C::N_ACC) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
         }
       }
     } else {
@@ -707,8 +883,18 @@ bool gemm_small_rope_eligible(const GemmProblem& g) {
   return g.hq > 0 && g.hkv > 0 && g.N == (g.hq + 2 * g.hkv) * 128 && n_tiles <= sm_count();
 }
 
+bool gemm_small_lse_eligible(const GemmProblem& g) {
+  return small_enabled() && g.epi == EPI_LSE && g.gumbel && g.labels == nullptr &&
+         !g.a_mn && !g.b_mn && g.M >= 1 && g.M <= 64 && g.K % 8 == 0 && g.lda % 8 == 0 && g.ldb % 8 == 0 &&
+         g.norm_w == nullptr && g.part_out == nullptr && g.q_out == nullptr;
+}
+
+int gemm_small_lse_parts(int N) { return std::max(1, std::min(sm_count(), (N + 127) / 128)); }
+
 void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
-  MESHY_CHECK(gemm_small_eligible(g), "gemm_small: problem not eligible");
+  const bool lse = g.epi == EPI_LSE;
+  MESHY_CHECK(lse ? gemm_small_lse_eligible(g) : gemm_small_eligible(g), "gemm_small: problem not eligible");
+  MESHY_CHECK(!lse || g.partial != nullptr, "gemm_small: the sampler needs a partial buffer");
   MESHY_CHECK(g.part_out == nullptr || (gemm_small_prep_eligible(g) && g.xg_out && g.g_next),
               "gemm_small: norm preparation needs a STORE epilogue, N a multiple of 128, xg_out and g_next");
   MESHY_CHECK(g.part_in == nullptr || (g.part_t > 0 && g.norm_d > 0.f && g.norm_w == nullptr),
@@ -748,10 +934,19 @@ void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
   a.slots = g.slots;
   a.hq = g.hq;
   a.hkv = g.hkv;
+  a.partial = g.partial;
+  a.inv_temp = g.inv_temp;
+  a.seed = g.seed;
+  a.step_ptr = g.step_ptr;
   const int sms = sm_count();
   CUtensorMap mw = make_map_bf16(g.B, g.N, g.K, g.ldb, SBK, 128);
   CUtensorMap mx = make_map_bf16(g.A, g.M, g.K, g.lda, SBK, MP);
-  if (a.n_tiles <= sms) {
+  if (lse) {
+    // persistent: every CTA walks its vocabulary tiles and writes one partial per token row
+    a.cs = 1;
+    a.kb_per = a.k_blocks;
+    launch_mp<true>(MP, mw, mx, a, gemm_small_lse_parts(g.N), 1, st);
+  } else if (a.n_tiles <= sms) {
     // largest split whose clusters all fit in one wave (clusters are placed per GPC, so fewer
     // than sms / cs of them may be resident)
     int cs = 1;

@@ -239,15 +239,14 @@ void gae_scan(const float* x, const float* d, const float* valid, float* out, in
 }
 
 // ─── LM-head partial merge ─────────────────────────────────────────────────
-__global__ void lse_merge_kernel(const float* __restrict__ part, int n_tiles, int bn, const int64_t* __restrict__ labels,
-                                 float* __restrict__ lp, float* __restrict__ lse, float* __restrict__ ent,
-                                 int64_t* __restrict__ tok, float* __restrict__ tok_lp, int rows) {
-  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  pdl_wait();
-  pdl_trigger();
-  if (row >= rows) return;
-  const float* pr = part + (size_t)row * n_tiles * 8;
+// One warp merges the n_tiles partials (max, sum, sum p*z, target z, best, z of best, index) of a row:
+// log-sum-exp l, sum p*z / sum p (for the entropy) and the Gumbel-max winner over all tiles.
+struct RowMerge {
+  float l, pz_s, bestz;
+  int besti;
+};
+
+__device__ __forceinline__ RowMerge merge_row(const float* __restrict__ pr, int n_tiles, int lane) {
   float M = -INFINITY;
   for (int t = lane; t < n_tiles; t += 32) M = fmaxf(M, pr[t * 8]);
   M = warp_max(M);
@@ -277,10 +276,23 @@ __global__ void lse_merge_kernel(const float* __restrict__ part, int n_tiles, in
       bestz = oz;
     }
   }
+  return RowMerge{M + logf(S), PZ / S, bestz, besti};
+}
+
+__global__ void lse_merge_kernel(const float* __restrict__ part, int n_tiles, int bn, const int64_t* __restrict__ labels,
+                                 float* __restrict__ lp, float* __restrict__ lse, float* __restrict__ ent,
+                                 int64_t* __restrict__ tok, float* __restrict__ tok_lp, int rows) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  pdl_wait();
+  pdl_trigger();
+  if (row >= rows) return;
+  const float* pr = part + (size_t)row * n_tiles * 8;
+  const RowMerge r = merge_row(pr, n_tiles, lane);
   if (lane == 0) {
-    float l = M + logf(S);
+    const float l = r.l;
     if (lse) lse[row] = l;
-    if (ent) ent[row] = l - PZ / S;
+    if (ent) ent[row] = l - r.pz_s;
     if (lp && labels) {
       int64_t y = labels[row];
       int t = (int)(y / bn);
@@ -288,8 +300,8 @@ __global__ void lse_merge_kernel(const float* __restrict__ part, int n_tiles, in
       lp[row] = tgt - l;
     }
     if (tok) {
-      tok[row] = besti;
-      tok_lp[row] = bestz - l;
+      tok[row] = r.besti;
+      tok_lp[row] = r.bestz - l;
     }
   }
 }
@@ -340,6 +352,55 @@ void decode_advance(const int64_t* tok, const float* lp, int64_t* tok_in, int* p
   if (B == 0) return;
   launch_pdl(decode_advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, tok, lp, tok_in, pos, seq_lens, gen,
              max_new, done, slot, bt, req, out_tok, out_lp, eos, n_eos, B, max_pages, cap, page);
+  MESHY_CUDA_CHECK(cudaGetLastError());
+}
+
+// ─── sampler merge + decode row advance (one kernel) ───────────────────────
+// One warp per running row: merges the LM-head sampler partials into the sampled token and its
+// log-probability, then advances the row exactly as decode_advance_kernel does. Thread 0 of block 0
+// bumps the step counter that keys the sampler's noise (the sampler kernel has completed: pdl_wait).
+__global__ void sample_advance_kernel(const float* __restrict__ part, int n_parts, int64_t* __restrict__ tok_in,
+                                      int* __restrict__ pos, int* __restrict__ seq_lens, int* __restrict__ gen,
+                                      const int* __restrict__ max_new, int* __restrict__ done,
+                                      int64_t* __restrict__ slot, const int* __restrict__ bt,
+                                      const int* __restrict__ req, int64_t* __restrict__ out_tok,
+                                      float* __restrict__ out_lp, const int64_t* __restrict__ eos, int n_eos, int B,
+                                      int max_pages, int cap, int page, int64_t* __restrict__ step) {
+  const int i = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  pdl_wait();
+  pdl_trigger();
+  if (step && blockIdx.x == 0 && threadIdx.x == 0) *step += 1;
+  if (i >= B || done[i]) return;
+  const RowMerge r = merge_row(part + (size_t)i * n_parts * 8, n_parts, lane);
+  if (lane != 0) return;
+  const int q = req[i];
+  int g = gen[i];
+  const int64_t t = r.besti;
+  if (g < cap) {
+    out_tok[(size_t)q * cap + g] = t;
+    out_lp[(size_t)q * cap + g] = r.bestz - r.l;
+  }
+  g += 1;
+  gen[i] = g;
+  tok_in[i] = t;
+  bool fin = g >= max_new[i];
+  for (int e = 0; e < n_eos; ++e) fin |= (t == eos[e]);
+  done[i] = fin ? 1 : 0;
+  const int p = pos[i] + 1;
+  pos[i] = p;
+  seq_lens[i] = seq_lens[i] + 1;
+  const int pi = p / page;
+  slot[i] = (pi < max_pages) ? (int64_t)bt[(size_t)i * max_pages + pi] * page + p % page : 0;
+}
+
+void sample_advance(const float* part, int n_parts, int64_t* tok_in, int* pos, int* seq_lens, int* gen,
+                    const int* max_new, int* done, int64_t* slot, const int* bt, const int* req, int64_t* out_tok,
+                    float* out_lp, const int64_t* eos, int n_eos, int B, int max_pages, int cap, int page,
+                    int64_t* step, cudaStream_t st) {
+  if (B == 0) return;
+  launch_pdl(sample_advance_kernel, dim3((B + 7) / 8), dim3(256), 0, st, part, n_parts, tok_in, pos, seq_lens, gen,
+             max_new, done, slot, bt, req, out_tok, out_lp, eos, n_eos, B, max_pages, cap, page, step);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 

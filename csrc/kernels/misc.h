@@ -15,4 +15,10 @@ void decode_advance(const int64_t* tok, const float* lp, int64_t* tok_in, int* p
                     const int* max_new, int* done, int64_t* slot, const int* bt, const int* req, int64_t* out_tok,
                     float* out_lp, const int64_t* eos, int n_eos, int B, int max_pages, int cap, int page,
                     cudaStream_t st);
+// Merge of the small-M sampler's partials ([B][n_parts][8]) fused with decode_advance; also adds 1 to
+// ``step`` (the sampler's noise key) when given.
+void sample_advance(const float* part, int n_parts, int64_t* tok_in, int* pos, int* seq_lens, int* gen,
+                    const int* max_new, int* done, int64_t* slot, const int* bt, const int* req, int64_t* out_tok,
+                    float* out_lp, const int64_t* eos, int n_eos, int B, int max_pages, int cap, int page,
+                    int64_t* step, cudaStream_t st);
 }  // namespace meshy

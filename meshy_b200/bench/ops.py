@@ -110,6 +110,22 @@ def main(argv=None):
                 emit(dict(op=f"gemm_{k}", M=M, N=n, K=kk, us=round(us, 2), bytes=byts,
                           gbs=round(byts / us / 1e3, 1), frac_of_hbm=round(byts / us / 1e3 / hbm, 3),
                           impl="cublas" if args.torch_baseline else "ours"))
+            if not only or "lm_sample" in only:
+                # LM head + sampler: the regular 128-row tiling vs the small-M path (M <= 64)
+                n, kk = W["lm_head"].shape
+                h = torch.randn(M, kk, device=dev).to(torch.bfloat16)
+                tok = torch.empty(M, dtype=torch.int64, device=dev)
+                lp = torch.empty(M, device=dev)
+                step = torch.zeros(1, dtype=torch.int64, device=dev)
+                byts = W["lm_head"].numel() * 2
+                impls = [("regular", lambda: C.lmhead_sample(h, W["lm_head"], tok, lp, 1.0, 0, step))]
+                if M <= 64:
+                    impls.append(("small_m", lambda: C.lmhead_sample_small(h, W["lm_head"], None, 0, 0.0, 0.0, tok,
+                                                                           lp, 1.0, 0, step)))
+                for impl, fn in impls:
+                    us = time_op(fn)
+                    emit(dict(op="lm_sample", M=M, N=n, K=kk, us=round(us, 2), bytes=byts,
+                              gbs=round(byts / us / 1e3, 1), frac_of_hbm=round(byts / us / 1e3 / hbm, 3), impl=impl))
             if only and "paged_decode" not in only:
                 continue
             # paged decode attention

@@ -19,6 +19,11 @@
 * :func:`decode_advance` — per-row bookkeeping after sampling (append token,
   bump lengths, recompute the next cache slot, finish flags), so a whole
   decode step can be replayed from a CUDA graph with no host work.
+* :func:`sample_advance` — the decode step's tail in two kernels for up to 64
+  rows: the LM head with the sampler in the epilogue of the small-M GEMM
+  (vocabulary rows on the MMA's 128 lanes, tokens as its N; optionally on a
+  prepared RMSNorm input, so the final norm runs no kernel of its own), then
+  the partial merge fused with :func:`decode_advance` and ``step += 1``.
 """
 
 from __future__ import annotations
@@ -119,13 +124,17 @@ def qkv_rope_fused(x, w, bias, positions, q_norm, k_norm, n_heads, n_kv, theta, 
     return q if ok else None
 
 
-def paged_attention(q, k_cache, v_cache, block_table, seq_lens, scale=None, workspace=None):
+def paged_attention(q, k_cache, v_cache, block_table, seq_lens, scale=None, workspace=None, decode_step=False):
+    """Decode attention of ``q [B, Hq, hd]`` over each row's paged K/V. ``decode_step``: the op just
+    before wrote only each row's newest K/V row (its position ``seq_lens - 1``) and neither the block
+    table nor the lengths, so the kernel may load the older pages before that op has finished."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if native(q):
         from ._ext import ext
 
         out = torch.empty_like(q)
-        ext().paged_attention(q, k_cache, v_cache, block_table, seq_lens, out, float(scale), workspace)
+        ext().paged_attention(q, k_cache, v_cache, block_table, seq_lens, out, float(scale), workspace,
+                              bool(decode_step))
         return out
     return ref.attention_decode_paged(q, k_cache, v_cache, block_table, seq_lens, scale)
 
@@ -147,6 +156,23 @@ def sample(h, w, temperature: float, *, top_k: int = -1, top_p: float = 1.0, see
         return tok, lp
     logits = h.float() @ w.float().t() if not h.is_cuda else torch.nn.functional.linear(h, w).float()
     return ref.sample_with_logprob(logits, temperature, generator=generator, top_k=top_k, top_p=top_p)
+
+
+def sample_advance(state: dict, h, w, temperature: float, *, seed: int, page_size: int, part=None, d: int = 0,
+                   eps: float = 0.0) -> bool:
+    """Sample the next token of every row from ``h [B, D]`` (temperature-only Gumbel-max sampling) and
+    advance the rows (see :func:`decode_advance`), bumping ``state["step"]``. With ``part``, ``h`` is
+    a prepared RMSNorm input ``bf16(g * x)`` of model dim ``d`` (see :func:`linear_norm_prep`). Returns
+    False, having done nothing, when the fused kernels do not apply (no CUDA, > 64 rows, T <= 0)."""
+    if not native(h) or not temperature > 0 or h.shape[0] > 64:
+        return False
+    from ._ext import ext
+
+    st = state
+    return bool(ext().decode_sample_advance(
+        h, w, part, (d + 127) // 128 if part is not None else 0, float(d), float(eps), float(temperature), int(seed),
+        st["step"], st["tok_in"], st["pos"], st["seq_lens"], st["gen"], st["max_new"], st["done"], st["slot"],
+        st["block_table"], st["req"], st["out_tok"], st["out_lp"], st["eos"], int(page_size)))
 
 
 def decode_advance(state: dict, tok, lp, page_size: int):
@@ -186,4 +212,4 @@ def decode_advance(state: dict, tok, lp, page_size: int):
 
 
 __all__ = ["decode_advance", "kv_write", "linear_norm_prep", "linear_norm_scaled", "paged_attention",
-           "qkv_rope_fused", "qkv_rope_to_cache", "sample"]
+           "qkv_rope_fused", "qkv_rope_to_cache", "sample", "sample_advance"]

@@ -487,14 +487,15 @@ class RolloutEngine:
 
     # ------------------------------------------------------------------ decode
     @torch.no_grad()
-    def _decode_hidden(self, b: int) -> torch.Tensor:
+    def _decode_hidden(self, b: int, final_split: bool = False):
         """Final normed hidden states ``[b, D]`` of the running rows' next position (writes their K/V).
 
         Up to 64 rows of an eligible dense model take the whole-step persistent kernel; otherwise one
-        kernel per op."""
+        kernel per op. ``final_split``: the per-op path may instead return ``(xg, part)``, the final
+        RMSNorm's prepared input (see :meth:`_decode_hidden_layers`)."""
         if self._mega is not None and b <= self._mega_rows:
             return self._mega(self.st, b)
-        return self._decode_hidden_layers(b)
+        return self._decode_hidden_layers(b, final_split=final_split)
 
     def _norm_ws(self):
         """Buffers of the split RMSNorm (bf16 g * x and per-tile sums of squares for two norms)."""
@@ -506,7 +507,11 @@ class RolloutEngine:
         return self._nws
 
     @torch.no_grad()
-    def _decode_hidden_layers(self, b: int) -> torch.Tensor:
+    def _decode_hidden_layers(self, b: int, final_split: bool = False):
+        """Per-op decode of all layers. With ``final_split`` the last down_proj prepares the final
+        RMSNorm like the others (``bf16(g * x)`` and per-tile sums of squares) and, when it could, the
+        result is ``(xg [b, D], part)`` for a consumer that applies ``rstd`` itself (the LM-head
+        sampler) instead of the normed hidden states."""
         a, m, st = self.args, self.model, self.st
         x = Fx.embedding(st["tok_in"][:b], m.embed)
         pos = st["pos"][:b]
@@ -533,7 +538,8 @@ class RolloutEngine:
                 q, _, _ = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads,
                                               a.head_dim, a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1],
                                               st["slot"][:b])
-            o = D.paged_attention(q, self.kv[li, 0], self.kv[li, 1], st["block_table"][:b], st["seq_lens"][:b])
+            o = D.paged_attention(q, self.kv[li, 0], self.kv[li, 1], st["block_table"][:b], st["seq_lens"][:b],
+                                  decode_step=True)
             o = o.reshape(b, a.q_dim)
             prep = None
             if layer.moe is None and split:
@@ -550,8 +556,9 @@ class RolloutEngine:
                 if act is None:
                     act = Fx.rmsnorm_linear(x, layer.mlp_norm, a.norm_eps, layer.w13, swiglu_block=a.swiglu_block)
                 prep = None
-                if split and li + 1 < L:
-                    xn = D.linear_norm_prep(act, layer.w2, x, m.layers[li + 1].attn_norm, xg, parts[0])
+                if split and (li + 1 < L or final_split):
+                    g_next = m.layers[li + 1].attn_norm if li + 1 < L else m.norm
+                    xn = D.linear_norm_prep(act, layer.w2, x, g_next, xg, parts[0])
                     if xn is not None:
                         x, prep = xn, parts[0]
                 if prep is None:
@@ -559,17 +566,31 @@ class RolloutEngine:
             else:
                 prep = None
                 x = self._mlp(layer, Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps), x)
+        if final_split and prep is not None:
+            return xg[:b], prep
         return Fx.rmsnorm(x, m.norm, a.norm_eps)
 
     @torch.no_grad()
     def _decode_body(self, b: int, eos: torch.Tensor):
-        m, st = self.model, self.st
-        h = self._decode_hidden(b)
+        m, st, a = self.model, self.st, self.args
         r0 = self.running[0]
-        tok, lp = D.sample(h, m.output_weight, r0.temperature, top_k=r0.top_k, top_p=r0.top_p, seed=self.seed,
-                           step=st["step"], generator=self._gen if not self.cuda else None)
         sub = {k: (v[:b] if k not in ("out_tok", "out_lp", "eos", "noeos", "step") else v) for k, v in st.items()}
         sub["eos"] = eos
+        # temperature-only sampling of <= 64 rows: LM head + sampler, then merge + row advance (2 kernels)
+        fused = (self.cuda and b <= 64 and r0.temperature > 0 and r0.top_k <= 0 and r0.top_p >= 1.0
+                 and os.environ.get("MESHY_FUSED_SAMPLER", "1") != "0")
+        h = self._decode_hidden(b, final_split=fused)
+        part = None
+        if isinstance(h, tuple):
+            h, part = h
+        if fused and D.sample_advance(sub, h, m.output_weight, r0.temperature, seed=self.seed,
+                                      page_size=self.page_size, part=part, d=a.dim, eps=a.norm_eps):
+            return
+        if part is not None:  # undo the split: h = RMSNorm(x) from bf16(g * x) and the row sums of squares
+            rstd = torch.rsqrt(part.sum(0)[:b] / a.dim + a.norm_eps)
+            h = (h.float() * rstd[:, None]).to(h.dtype)
+        tok, lp = D.sample(h, m.output_weight, r0.temperature, top_k=r0.top_k, top_p=r0.top_p, seed=self.seed,
+                           step=st["step"], generator=self._gen if not self.cuda else None)
         D.decode_advance(sub, tok, lp, self.page_size)
         st["step"] += 1
 

@@ -189,6 +189,12 @@ def test_paged_decode_and_kv_write():
     C().paged_attention(q, kc, vc, bt, seq, out, 1 / math.sqrt(hd), None)
     o_ref = ref.attention_decode_paged(q.float(), kc.float(), vc.float(), bt, seq, 1 / math.sqrt(hd))
     assert rel_err(out, o_ref) < 1e-2
+    # decode-step mode (older pages loaded before the dependency wait): same result
+    out2 = torch.empty_like(q)
+    C().paged_attention(q, kc, vc, bt, seq, out2, 1 / math.sqrt(hd), None, True)
+    torch.cuda.synchronize()
+    assert C().device_error() == 0
+    assert torch.equal(out2, out)
 
 
 def test_lmhead_logprob_fwd_bwd():
@@ -239,6 +245,79 @@ def test_lmhead_sample_distribution():
     # total-variation distance of the empirical distribution
     tv = 0.5 * (emp - p).abs().sum(-1)
     assert (tv < 0.08).all(), tv
+
+
+def test_lmhead_sample_small_distribution():
+    """The small-M sampler (LM head on the swapped-operand GEMM, sampler in its epilogue) draws from
+    softmax(z / T): empirical distribution and log-probs of the drawn tokens."""
+    torch.manual_seed(9)
+    B, D, V = 5, 64, 300
+    h, w = bf(B, D), bf(V, D, scale=0.3)
+    for T in (1.0, 0.7):
+        z = (h.float() @ w.float().t()) / T
+        p = torch.softmax(z, -1)
+        counts = torch.zeros(B, V, device=DEV)
+        step = torch.zeros(1, dtype=torch.int64, device=DEV)
+        tok = torch.empty(B, dtype=torch.int64, device=DEV)
+        lp = torch.empty(B, device=DEV)
+        n = 4000
+        for _ in range(n):
+            assert C().lmhead_sample_small(h, w, None, 0, 0.0, 0.0, tok, lp, T, 1234, step)
+            step += 1
+            counts[torch.arange(B, device=DEV), tok] += 1
+        torch.cuda.synchronize()
+        assert C().device_error() == 0
+        assert torch.allclose(lp, torch.log(p.gather(1, tok[:, None]).squeeze(1)), atol=2e-2)
+        tv = 0.5 * (counts / n - p).abs().sum(-1)
+        assert (tv < 0.08).all(), tv
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 33, 64])
+@pytest.mark.parametrize("prepared", [False, True])
+def test_lmhead_sample_small_large_vocab(M, prepared):
+    """Qwen2.5 vocabulary (151936 rows, 1187 tiles over the persistent grid): the drawn token's log-prob
+    equals z / T - logsumexp(z / T), and at a temperature of 1e-3 the drawn token is the argmax up to
+    bf16 rounding. With ``prepared`` the input is bf16(g * x) plus per-128-column sums of squares of x
+    (the split RMSNorm)."""
+    torch.manual_seed(M)
+    D, V, eps = 1536, 151936, 1e-6
+    w = bf(V, D, scale=0.05)
+    x = bf(M, D)
+    g = (1.0 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    xf = x.float()
+    hn = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * g.float()).to(torch.bfloat16)
+    if prepared:
+        h = (xf * g.float()).to(torch.bfloat16)
+        part = torch.zeros(D // 128, 256, device=DEV)
+        part[:, :M] = xf.pow(2).view(M, D // 128, 128).sum(-1).t()
+        args = (h, w, part, D // 128, float(D), eps)
+    else:
+        args = (hn, w, None, 0, 0.0, 0.0)
+    z = hn.float() @ w.float().t()
+    step = torch.full((1,), 7, dtype=torch.int64, device=DEV)
+    tok = torch.empty(M, dtype=torch.int64, device=DEV)
+    lp = torch.empty(M, device=DEV)
+    for T in (1.0, 1e-3):
+        assert C().lmhead_sample_small(*args, tok, lp, T, 99, step)
+        torch.cuda.synchronize()
+        if not prepared:  # the regular 128-row tiling draws with the same rules
+            tok2, lp2 = torch.empty_like(tok), torch.empty_like(lp)
+            C().lmhead_sample(hn, w, tok2, lp2, T, 99, step)
+            torch.cuda.synchronize()
+            zt = z / T
+            if T == 1.0:
+                want2 = zt.gather(1, tok2[:, None]).squeeze(1) - torch.logsumexp(zt, -1)
+                assert torch.allclose(lp2, want2, atol=0.05), (lp2, want2)
+            else:
+                assert (z.gather(1, tok2[:, None]).squeeze(1) >= z.max(-1).values - 0.06).all()
+        assert C().device_error() == 0
+        zt = z / T
+        if T == 1.0:
+            want_lp = zt.gather(1, tok[:, None]).squeeze(1) - torch.logsumexp(zt, -1)
+            assert torch.allclose(lp, want_lp, atol=0.05), (lp, want_lp)
+        else:
+            # Gumbel noise spans ~20 units of z / T = 0.02 of z: the winner is the argmax up to rounding
+            assert (z.gather(1, tok[:, None]).squeeze(1) >= z.max(-1).values - 0.06).all()
 
 
 def test_ppo_loss_matches_torch():
