@@ -674,15 +674,26 @@ void paged_attention_(Tensor q, Tensor kc, Tensor vc, Tensor bt, Tensor seq_lens
   const int max_pages = bt.size(1);
   const int n_split = paged_decode_tma_splits(B, Hkv, max_pages);
   Tensor part;
-  if (n_split > kMaxClusterSplits) {
+  const int max_cluster = paged_decode_max_cluster();
+  if (n_split > max_cluster) {
     int64_t need = (int64_t)B * Hq * n_split * (hd + 2);
     if (workspace.has_value() && workspace->defined() && workspace->numel() >= need) part = *workspace;
     else part = torch::empty({need}, q.options().dtype(torch::kFloat));
   }
+  // split counters of the in-kernel merge: zeroed once per device, left zero by every launch
+  static Tensor ctrs[64];
+  Tensor ctr;
+  {
+    std::lock_guard<std::mutex> g(g_mu);
+    Tensor& c = ctrs[q.get_device()];
+    if (!c.defined()) c = torch::zeros({kDecodeCtrs}, q.options().dtype(torch::kInt32));
+    ctr = c;
+  }
   paged_decode_tma(ptr<bf16>(q), ptr<bf16>(kc), ptr<bf16>(vc), (int)kc.size(0), ptr<int>(bt), ptr<int>(seq_lens),
                    ptr<bf16>(out), part.defined() ? ptr<float>(part) : nullptr, B, Hq, Hkv, hd, page, max_pages,
-                   n_split, (float)scale, ptr<int>(scratch(0, 0).err), cur_stream(), decode_step);
-  count(n_split > kMaxClusterSplits ? 2 : 1);
+                   n_split, (float)scale, ptr<int>(scratch(0, 0).err), cur_stream(), decode_step,
+                   reinterpret_cast<unsigned*>(ctr.data_ptr<int>()));
+  count(n_split > max_cluster && (int64_t)B * Hkv > kDecodeCtrs ? 2 : 1);
 }
 
 void decode_advance_(Tensor tok, Tensor lp, Tensor tok_in, Tensor pos, Tensor seq_lens, Tensor gen, Tensor max_new,
@@ -883,6 +894,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_norm_scaled", &gemm_norm_scaled, "decode: GEMM on a prepared RMSNorm input, rows scaled by rstd");
   m.def("gemm_qkv_rope", &gemm_qkv_rope, "decode: QKV GEMM with RoPE / QK-norm and the KV-cache write fused");
   m.def("gemm_norm", &gemm_norm, "decode: fused input RMSNorm + small-M GEMM (returns False if not eligible)");
+  m.def("gemm_small_trace",
+        [](c10::optional<Tensor> buf) {
+          if (buf.has_value() && buf->defined()) {
+            TORCH_CHECK(buf->scalar_type() == at::kLong && buf->is_contiguous() && buf->size(-1) == 8 &&
+                            buf->size(-2) == 160, "gemm_small_trace: int64 [slots, 160, 8]");
+            gemm_small_trace(reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>()), (int)buf->size(0));
+          } else {
+            gemm_small_trace(nullptr, 0);
+          }
+        },
+        "record the timelines of the next small-M GEMM launches into int64 [slots, 160, 8] (None: stop)");
   m.def("gemm_small_config", [](int64_t enabled, int64_t cluster) { gemm_small_config((int)enabled, (int)cluster); },
         "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");
   m.def("swiglu_bwd", &swiglu_bwd_);

@@ -30,16 +30,23 @@ void paged_decode(const bf16* q, const bf16* kc, const bf16* vc, const int* bt, 
                   float* part, int B, int Hq, int Hkv, int hd, int page, int max_pages, int n_split, float scale,
                   cudaStream_t st);
 // TMA-pipelined split-KV decode (decode_attn.cu). Up to kMaxClusterSplits splits reduce
-// through distributed shared memory; more splits need ``part`` [B, Hq, n_split, hd + 2] fp32.
-constexpr int kMaxClusterSplits = 8;
+// through distributed shared memory (above 8 a non-portable cluster size); more splits need
+// ``part`` [B, Hq, n_split, hd + 2] fp32.
+constexpr int kMaxClusterSplits = 16;
 int paged_decode_tma_splits(int B, int Hkv, int max_pages);
+int paged_decode_max_cluster();  // kMaxClusterSplits, or 8 where the device cannot place 16-CTA clusters
 void paged_decode_force_splits(int n);  // tests: 0 restores the heuristic
 // ``decode_step``: the kernel before this one in the stream wrote, of this cache, at most the row of each
 // sequence's last position (seq_lens[b] - 1) and nothing of bt / seq_lens. Pages before a sequence's last
 // one are then loaded before the programmatic-dependent-launch wait, under that kernel's tail.
+// ``ctr``: with more splits than one cluster holds, [kDecodeCtrs] zeroed counters let the last split of each
+// (sequence, KV head) merge the partials in the same kernel (and leave the counter zero again); null runs
+// paged_decode_combine after the kernel instead.
+constexpr int kDecodeCtrs = 1 << 16;
 void paged_decode_tma(const bf16* q, const bf16* kc, const bf16* vc, int n_cache_pages, const int* bt,
                       const int* seq_lens, bf16* o, float* part, int B, int Hq, int Hkv, int hd, int page,
-                      int max_pages, int n_split, float scale, int* err, cudaStream_t st, bool decode_step = false);
+                      int max_pages, int n_split, float scale, int* err, cudaStream_t st, bool decode_step = false,
+                      unsigned* ctr = nullptr);
 void paged_decode_combine(const float* part, bf16* o, int B, int Hq, int hd, int n_split, cudaStream_t st);
 void kv_write(const bf16* k, const bf16* v, bf16* kc, bf16* vc, const int64_t* slots, int n, int Hkv, int hd, int page,
               cudaStream_t st);

@@ -81,7 +81,7 @@ template <int HD, bool CLUSTER>
 __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
     const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV, const bf16* __restrict__ Q,
     const int* __restrict__ bt, const int* __restrict__ seq_lens, bf16* __restrict__ O, float* __restrict__ part,
-    int Hq, int Hkv, int max_pages, int n_split, float scale, int* err, int early) {
+    int Hq, int Hkv, int max_pages, int n_split, float scale, int* err, int early, unsigned* __restrict__ ctr) {
   using C = DCfg<HD>;
   extern __shared__ __align__(1024) uint8_t smraw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
@@ -318,6 +318,51 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
       }
     }
   }
+  if constexpr (!CLUSTER) {
+    if (n_split > 1 && ctr != nullptr) {
+      // the last split of (b, hk) to finish merges all splits' partials (no second kernel); it resets
+      // the counter for the next launch
+      volatile int* last_s = reinterpret_cast<volatile int*>(abort_flag) + 1;
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) *last_s = atomicAdd(&ctr[b * Hkv + hk], 1u) == (unsigned)(n_split - 1);
+      __syncthreads();
+      if (*last_s) {
+        __threadfence();
+        float* fm = reinterpret_cast<float*>(ring);  // [16][64]: split maxima, then their weights
+        float* fl = fm + 16 * 64;                    // [16]: merged sums
+        for (int i = threadIdx.x; i < rep * n_split; i += kThreadsDec) {
+          const int row = i / n_split, sp2 = i % n_split;
+          fm[row * 64 + sp2] = __ldcg(part + (((size_t)b * Hq + hk * rep + row) * n_split + sp2) * (HD + 2) + HD);
+        }
+        __syncthreads();
+        if (threadIdx.x < rep) {
+          const int row = threadIdx.x;
+          const float* pr = part + ((size_t)b * Hq + hk * rep + row) * n_split * (HD + 2);
+          float M = -INFINITY;
+          for (int t = 0; t < n_split; ++t) M = fmaxf(M, fm[row * 64 + t]);
+          float Ls = 0.f;
+          for (int t = 0; t < n_split; ++t) {
+            const float ms = fm[row * 64 + t];
+            const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+            Ls += __ldcg(pr + t * (HD + 2) + HD + 1) * f;
+            fm[row * 64 + t] = f;
+          }
+          fl[row] = Ls;
+        }
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < rep * HD; idx += kThreadsDec) {
+          const int row = idx / HD, c = idx % HD;
+          const float* pr = part + ((size_t)b * Hq + hk * rep + row) * n_split * (HD + 2);
+          float acc = 0.f;
+          for (int t = 0; t < n_split; ++t) acc += __ldcg(pr + t * (HD + 2) + c) * fm[row * 64 + t];
+          const float Ls = fl[row];
+          O[((size_t)b * Hq + hk * rep + row) * HD + c] = __float2bfloat16(Ls > 0.f ? acc / Ls : 0.f);
+        }
+        if (threadIdx.x == 0) ctr[b * Hkv + hk] = 0u;
+      }
+    }
+  }
   if constexpr (CLUSTER) {
     if (n_split > 1) {
       __syncwarp();
@@ -325,7 +370,7 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
       const uint32_t base_m = smem_u32(cm), base_l = smem_u32(cl), base_o = smem_u32(co);
       for (int idx = sp * kThreadsDec + threadIdx.x; idx < rep * HD; idx += n_split * kThreadsDec) {
         int row = idx / HD, c = idx % HD;
-        float ms[8];
+        float ms[kMaxClusterSplits];
         float M = -INFINITY;
         for (int r = 0; r < n_split; ++r) {
           float v;
@@ -356,12 +401,13 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
 template <int HD, bool CLUSTER>
 void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, const int* bt, const int* seq_lens,
                 bf16* o, float* part, int B, int Hq, int Hkv, int max_pages, int n_split, float scale, int* err,
-                bool early, cudaStream_t st) {
+                bool early, unsigned* ctr, cudaStream_t st) {
   using C = DCfg<HD>;
   auto k = paged_decode_tma_kernel<HD, CLUSTER>;
   static bool attr_set = false;
   if (!attr_set) {
     MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    if (CLUSTER) MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -379,10 +425,42 @@ void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, con
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   MESHY_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, mk, mv, q, bt, seq_lens, o, part, Hq, Hkv, max_pages, n_split, scale,
-                                      err, early ? 1 : 0));
+                                      err, early ? 1 : 0, ctr));
 }
 
 }  // namespace
+
+// Largest cluster of decode CTAs the device can place (16 needs a non-portable cluster size; if the
+// occupancy query finds no room for one, stay at the portable 8).
+static int dec_max_cluster() {
+  static int n = 0;
+  if (!n) {
+    auto k = paged_decode_tma_kernel<128, true>;
+    using C = DCfg<128>;
+    MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, kMaxClusterSplits);
+    cfg.blockDim = dim3(kThreadsDec, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = kMaxClusterSplits;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, k, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      c = 0;
+    }
+    n = c > 0 ? kMaxClusterSplits : 8;
+  }
+  return n;
+}
+
+int paged_decode_max_cluster() { return dec_max_cluster(); }
 
 static int g_force_splits = 0;
 void paged_decode_force_splits(int n) { g_force_splits = n < 0 ? 0 : n; }
@@ -395,40 +473,50 @@ int paged_decode_tma_splits(int B, int Hkv, int max_pages) {
   const int slots = 2 * 148;
   const int ctas = std::max(1, B * Hkv);
   int want = std::max(1, slots / ctas);
-  // A separate merge kernel costs more than the SMs a cluster-capped grid leaves idle, unless every
-  // split would still walk many pages (measured on B200, 1-8 rows: 8 cluster splits beat 16-64 split
-  // + merge up to ~8k-token contexts, e.g. 1 row x 2k: 14.3 us vs 19.5 us).
-  if (want > kMaxClusterSplits && (max_pages + kMaxClusterSplits - 1) / kMaxClusterSplits <= 48)
-    want = kMaxClusterSplits;
+  // Merging more splits than one cluster holds (partials through global memory) costs more than the SMs a
+  // cluster-capped grid leaves idle, unless every split would still walk many pages (measured on B200,
+  // 1-16 rows, 2k-8k tokens: 8 cluster splits beat 16-64 global splits in every case). 16-CTA clusters
+  // pay off only for a tiny grid over long contexts (1 row x 8k: 12.0 us vs 14.6 us per layer); with
+  // 8 or more rows they place poorly (8 rows x 4k: 28 us vs 15 us), so the cap stays at 8 there.
+  int cap = 8;
+  const int cl = dec_max_cluster();
+  if (cl > 8 && ctas * cl <= 64 && max_pages >= 4 * cl) cap = cl;
+  if (want > cap && (max_pages + cap - 1) / cap <= 48) want = cap;
   return std::max(1, std::min({want, max_pages, 64}));
 }
 
 void paged_decode_tma(const bf16* q, const bf16* kc, const bf16* vc, int n_cache_pages, const int* bt,
                       const int* seq_lens, bf16* o, float* part, int B, int Hq, int Hkv, int hd, int page,
-                      int max_pages, int n_split, float scale, int* err, cudaStream_t st, bool decode_step) {
+                      int max_pages, int n_split, float scale, int* err, cudaStream_t st, bool decode_step,
+                      unsigned* ctr) {
   MESHY_CHECK(hd == 64 || hd == 128, "paged_decode: head_dim must be 64 or 128");
   MESHY_CHECK(page == kPage, "paged_decode: page size must be 64");
   MESHY_CHECK(Hq % Hkv == 0 && Hq / Hkv <= 16, "paged_decode: at most 16 query heads per KV head");
   MESHY_CHECK(n_split >= 1, "paged_decode: n_split must be >= 1");
-  const bool cluster = n_split <= kMaxClusterSplits;
+  const bool cluster = n_split <= dec_max_cluster();
   MESHY_CHECK(cluster || part != nullptr, "paged_decode: more than 8 splits need a partial buffer");
   if (B == 0) return;
   const int64_t rows = (int64_t)n_cache_pages * Hkv * kPage;
   CUtensorMap mk = make_map_bf16(kc, rows, hd, hd, 64, kPage);
   CUtensorMap mv = make_map_bf16(vc, rows, hd, hd, 64, kPage);
   const bool early = decode_step && pdl_enabled();
+  if (cluster || (int64_t)B * Hkv > kDecodeCtrs) ctr = nullptr;
   if (hd == 128) {
     if (cluster)
-      launch_dec<128, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, st);
+      launch_dec<128, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, ctr,
+                            st);
     else
-      launch_dec<128, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, st);
+      launch_dec<128, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, ctr,
+                             st);
   } else {
     if (cluster)
-      launch_dec<64, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, st);
+      launch_dec<64, true>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, ctr,
+                           st);
     else
-      launch_dec<64, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, st);
+      launch_dec<64, false>(mk, mv, q, bt, seq_lens, o, part, B, Hq, Hkv, max_pages, n_split, scale, err, early, ctr,
+                            st);
   }
-  if (!cluster) paged_decode_combine(part, o, B, Hq, hd, n_split, st);
+  if (!cluster && ctr == nullptr) paged_decode_combine(part, o, B, Hq, hd, n_split, st);
 }
 
 }  // namespace meshy

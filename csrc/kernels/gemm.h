@@ -91,6 +91,9 @@ int gemm_small_lse_parts(int N);
 void gemm_small_launch(const GemmProblem& g, cudaStream_t stream);
 // enabled: 1/0 (-1 keeps); force_cs: cluster size override, 0 = heuristic (-1 keeps)
 void gemm_small_config(int enabled, int force_cs);
+// Diagnostics: while ``buf`` is set, the next ``slots`` small-M launches record their timelines into
+// buf[slot][160][8] (global-timer ns per CTA, see SmallArgs::trace); null stops recording.
+void gemm_small_trace(unsigned long long* buf, int slots);
 CUtensorMap make_map_bf16(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int bi, int bo);
 CUtensorMap make_map_bf16_3d(const void* ptr, int64_t d0, int64_t d1, int64_t d2, int64_t stride1_bytes,
                              int64_t stride2_bytes, int b0, int b1);

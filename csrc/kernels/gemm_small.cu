@@ -84,7 +84,16 @@ struct SmallArgs {
   float inv_temp;
   uint64_t seed;
   const int64_t* step_ptr;
+  // optional timeline of this launch, [gridDim.x][8] global-timer ns: entry, producer past the dependency
+  // wait, first stage landed at the MMA, last MMA committed, accumulator ready at the epilogue, partials
+  // exchanged (first cluster barrier), epilogue done, exit
+  unsigned long long* trace;
 };
+
+#define SMALL_TRACE(k)                                                   \
+  do {                                                                   \
+    if (p.trace) p.trace[(size_t)blockIdx.x * 8 + (k)] = globaltimer_ns(); \
+  } while (0)
 
 template <int MP, bool PERSIST>
 struct SCfg {
@@ -368,6 +377,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   const bool has_k = kb1 > kb0;
 
   if (threadIdx.x == 0) {
+    SMALL_TRACE(0);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -391,6 +401,13 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Epilogue operands of the first row group this CTA reduces (group ``rank``: rows 4 rank .. 4 rank + 3),
+  // loaded by the epilogue warps while the MMAs run so the epilogue after the reduction issues no
+  // dependent global loads: bias / gain of the output row, residual rows, RoPE position and cache slot.
+  float pre_bias = 0.f, pre_gain = 0.f, pre_freq = 0.f;
+  float pre_res[4] = {0.f, 0.f, 0.f, 0.f};
+  int pre_pos[4] = {0, 0, 0, 0};
+  int64_t pre_slot[4] = {0, 0, 0, 0};
 
   if (warp == 0) {
     // ─────────────────────────────── TMA producer ───────────────────────────────
@@ -408,6 +425,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         tma_load_2d(smem + j * C::STAGE_BYTES, &mapW, &full[j], (kb0 + j) * SBK, first * 128);
       }
       pdl_wait();
+      SMALL_TRACE(1);
       for (int j = 0; j < npre; ++j)
         tma_load_2d(smem + j * C::STAGE_BYTES + W_TILE_BYTES, &mapX, &full[j], (kb0 + j) * SBK, 0);
       if (npre > 0) {
@@ -459,6 +477,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             ok = false;
             break;
           }
+          if (!any) SMALL_TRACE(2);
           tc_fence_after();
           const uint32_t sw = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t sx = sw + W_TILE_BYTES;
@@ -482,6 +501,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         }
       }
       if (any) {
+        SMALL_TRACE(3);
         mma_commit(drain);
         long long t0 = clock64();
         while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
@@ -544,6 +564,30 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         }
       }
     } else {
+      if (p.epi != EPI_SWIGLU && 4 * (int)rank < p.M) {
+        const int n = first * 128 + f;
+        if (n < p.N) {
+          if (p.bias) pre_bias = __bfloat162float(p.bias[n]);
+          if (p.q_out) {
+            const bf16* nw = first < p.hq ? p.qn : (first < p.hq + p.hkv ? p.kn : nullptr);
+            pre_gain = nw ? __bfloat162float(nw[f]) : 0.f;
+            pre_freq = p.inv_freq[f & 63];
+          } else if (p.part_out) {
+            pre_gain = __bfloat162float(p.g_next[n]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = 4 * (int)rank + i;
+            if (m < p.M) {
+              if (p.residual) pre_res[i] = __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
+              if (p.q_out) {
+                pre_pos[i] = p.rope_pos[m];
+                pre_slot[i] = p.slots[m];
+              }
+            }
+          }
+        }
+      }
       // drain this CTA's partial into the (now idle) stage ring: layout [MP/4][128][4] fp32
       float* red = reinterpret_cast<float*>(smem);
       bool ok = true;
@@ -551,6 +595,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         ok = mbar_wait(&tfull[0], 0, abort_flag, p.err, kErrTimeoutEpilogue);
         tc_fence_after();
       }
+      if (threadIdx.x == 64) SMALL_TRACE(4);
       float v[32];
 #pragma unroll 1
       for (int c = 0; c < MP / CH; ++c) {
@@ -573,6 +618,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   if constexpr (!PERSIST) {
     __syncwarp();
     cluster_sync_all();  // every partial of the cluster is in shared memory
+    if (threadIdx.x == 64) SMALL_TRACE(5);
     if (warp >= 2) {
       const int q = warp & 3;
       const int f = q * 32 + lane;
@@ -583,12 +629,25 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       for (int g = (int)rank; g < G; g += p.cs) {
         if (4 * g >= p.M) break;
         if (swiglu && f >= 64) break;
+        const bool pf = g == (int)rank;  // operands prefetched for this group
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
         const uint32_t off_a = red_addr + (uint32_t)((g * 128 + f) * 16);
         const uint32_t off_b = red_addr + (uint32_t)((g * 128 + f + 64) * 16);
-        // issue the peers' loads in batches before summing, so the DSMEM latency is paid once
-        // per batch instead of once per peer
-        for (int r0 = 0; r0 < p.cs; r0 += 4) {
+        // issue the peers' loads before summing, so the DSMEM latency is paid once (all peers at once
+        // for a plain output, in batches of four when SwiGLU pairs two rows)
+        if (!swiglu) {
+          float4 xa[kSmallMaxCluster];
+#pragma unroll
+          for (int j = 0; j < kSmallMaxCluster; ++j)
+            if (j < p.cs) xa[j] = ld_dsmem_f4(mapa_shared(off_a, (uint32_t)j));
+#pragma unroll
+          for (int j = 0; j < kSmallMaxCluster; ++j) {
+            if (j < p.cs) {
+              a.x += xa[j].x; a.y += xa[j].y; a.z += xa[j].z; a.w += xa[j].w;
+            }
+          }
+        }
+        for (int r0 = 0; swiglu && r0 < p.cs; r0 += 4) {
           float4 xa[4], xb[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -623,7 +682,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             float t = av[i];
-            if (p.bias) t += __bfloat162float(p.bias[n]);
+            if (p.bias) t += pf ? pre_bias : __bfloat162float(p.bias[n]);
             y[i] = __bfloat162float(__float2bfloat16(t));
           }
           if (nt >= hqk) {  // V head: into the cache as is
@@ -632,7 +691,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             for (int i = 0; i < 4; ++i) {
               const int m = 4 * g + i;
               if (m < p.M) {
-                const int64_t sl = p.slots[m];
+                const int64_t sl = pf ? pre_slot[i] : p.slots[m];
                 p.vc[(((size_t)(sl / 64) * p.hkv + hk) * 64 + (size_t)(sl % 64)) * 128 + f] = __float2bfloat16(y[i]);
               }
             }
@@ -648,7 +707,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
                 if (lane == 0) red4[q * 4 + i] = s4;
               }
               named_bar_sync(1, 128);
-              const float w = __bfloat162float(nw[f]);
+              const float w = pf ? pre_gain : __bfloat162float(nw[f]);
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const float ss = red4[i] + red4[4 + i] + red4[8 + i] + red4[12 + i];
@@ -658,19 +717,19 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
 #pragma unroll
             for (int i = 0; i < 4; ++i) xch[i * 128 + f] = y[i];
             named_bar_sync(1, 128);
-            const float inv = p.inv_freq[f & 63];
+            const float inv = pf ? pre_freq : p.inv_freq[f & 63];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int m = 4 * g + i;
               if (m < p.M) {
                 const float yp = xch[i * 128 + (f ^ 64)];
                 float sn, cs;
-                sincosf((float)p.rope_pos[m] * inv, &sn, &cs);
+                sincosf((float)(pf ? pre_pos[i] : p.rope_pos[m]) * inv, &sn, &cs);
                 const float o = (f < 64) ? y[i] * cs - yp * sn : y[i] * cs + yp * sn;
                 if (is_q) {
                   p.q_out[((size_t)m * p.hq + nt) * 128 + f] = __float2bfloat16(o);
                 } else {
-                  const int64_t sl = p.slots[m];
+                  const int64_t sl = pf ? pre_slot[i] : p.slots[m];
                   p.kc[(((size_t)(sl / 64) * p.hkv + (nt - p.hq)) * 64 + (size_t)(sl % 64)) * 128 + f] =
                       __float2bfloat16(o);
                 }
@@ -681,7 +740,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         } else if (!swiglu && p.part_out) {
           // residual GEMM preparing the next RMSNorm (N is a multiple of 128: every lane owns a row)
           const int n = nt * 128 + f;
-          const float gn = __bfloat162float(p.g_next[n]);
+          const float gn = pf ? pre_gain : __bfloat162float(p.g_next[n]);
           float sq[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -689,8 +748,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             sq[i] = 0.f;
             if (m < p.M) {
               float y = av[i];
-              if (p.bias) y += __bfloat162float(p.bias[n]);
-              if (p.residual) y += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
+              if (p.bias) y += pf ? pre_bias : __bfloat162float(p.bias[n]);
+              if (p.residual) y += pf ? pre_res[i] : __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
               const bf16 yb = __float2bfloat16(y);
               reinterpret_cast<bf16*>(p.out)[(size_t)m * p.ldo + n] = yb;
               const float yr = __bfloat162float(yb);
@@ -712,8 +771,19 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
           const int n = nt * 128 + f;
           if (n < p.N) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              if (4 * g + i < p.M) store_val(p, 4 * g + i, n, av[i]);
+            for (int i = 0; i < 4; ++i) {
+              const int m = 4 * g + i;
+              if (m >= p.M) continue;
+              if (!pf) {
+                store_val(p, m, n, av[i]);
+                continue;
+              }
+              float x = av[i];
+              if (p.bias) x += pre_bias;
+              if (p.residual) x += pre_res[i];
+              if (p.out_f32) reinterpret_cast<float*>(p.out)[(size_t)m * p.ldo + n] = x;
+              else reinterpret_cast<bf16*>(p.out)[(size_t)m * p.ldo + n] = __float2bfloat16(x);
+            }
           }
         } else {
           // rows [128 nt, 128 nt + 64) are gate, the next 64 the matching up rows
@@ -731,8 +801,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         }
       }
     }
+    if (threadIdx.x == 64) SMALL_TRACE(6);
     __syncwarp();
     cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
+    if (threadIdx.x == 64) SMALL_TRACE(7);
   }
 
   tc_fence_before();
@@ -833,6 +905,10 @@ void launch_mp(int MP, const CUtensorMap& mw, const CUtensorMap& mx, const Small
 // Process-wide switches (tests and the op benchmark compare schedules with them).
 int g_small_enabled = -1;  // -1: from MESHY_GEMM_SMALL_M (default on)
 int g_small_force_cs = 0;
+// Timeline capture: launch i writes trace slot i of [slots][kSmallTraceCtas][8] until the slots run out.
+constexpr int kSmallTraceCtas = 160;
+unsigned long long* g_trace = nullptr;
+int g_trace_slots = 0, g_trace_next = 0;
 
 bool small_enabled() {
   if (g_small_enabled < 0) {
@@ -843,6 +919,12 @@ bool small_enabled() {
 }
 
 }  // namespace
+
+void gemm_small_trace(unsigned long long* buf, int slots) {
+  g_trace = buf;
+  g_trace_slots = buf ? slots : 0;
+  g_trace_next = 0;
+}
 
 void gemm_small_config(int enabled, int force_cs) {
   if (enabled >= 0) g_small_enabled = enabled ? 1 : 0;
@@ -938,6 +1020,8 @@ void gemm_small_launch(const GemmProblem& g, cudaStream_t st) {
   a.inv_temp = g.inv_temp;
   a.seed = g.seed;
   a.step_ptr = g.step_ptr;
+  a.trace = nullptr;
+  if (g_trace && g_trace_next < g_trace_slots) a.trace = g_trace + (size_t)(g_trace_next++) * kSmallTraceCtas * 8;
   const int sms = sm_count();
   CUtensorMap mw = make_map_bf16(g.B, g.N, g.K, g.ldb, SBK, 128);
   CUtensorMap mx = make_map_bf16(g.A, g.M, g.K, g.lda, SBK, MP);
