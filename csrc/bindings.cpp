@@ -416,6 +416,32 @@ void flash_attn_fwd_kv_(Tensor q, Tensor k, Tensor v, Tensor cu_q, Tensor cu_k, 
   count();
 }
 
+// Context-parallel attention forward that reads every CP rank's K / V in place (no all-gather):
+// ``k_ptrs`` / ``v_ptrs`` are the device addresses, in this process, of each rank's local [rows * 2 chunk,
+// Hkv, 128] K / V buffers (peer mappings of symmetric memory; this rank's own at index rank).
+void flash_attn_fwd_cp_peer(Tensor q, std::vector<int64_t> k_ptrs, std::vector<int64_t> v_ptrs, int64_t rows,
+                            int64_t chunk, int64_t hkv, Tensor cu_q, Tensor q_off, int64_t docs_per_row, Tensor out,
+                            Tensor lse, int64_t max_seqlen_q, double scale) {
+  CHECK_CONTIG(q);
+  TORCH_CHECK(q.size(2) == 128, "flash_attn_fwd_cp_peer: head_dim 128");
+  TORCH_CHECK(k_ptrs.size() == v_ptrs.size() && !k_ptrs.empty() && (int)k_ptrs.size() <= kFaMaxCp,
+              "flash_attn_fwd_cp_peer: 1 to 8 ranks");
+  TORCH_CHECK(cu_q.scalar_type() == at::kInt && q_off.scalar_type() == at::kInt && q_off.numel() == cu_q.numel() - 1,
+              "cu_q / q_off: int32, one offset per query document");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const bf16* kr[kFaMaxCp];
+  const bf16* vr[kFaMaxCp];
+  for (size_t r = 0; r < k_ptrs.size(); ++r) {
+    kr[r] = reinterpret_cast<const bf16*>(k_ptrs[r]);
+    vr[r] = reinterpret_cast<const bf16*>(v_ptrs[r]);
+  }
+  flash_attn_fwd_tc_cp(ptr<bf16>(q), kr, vr, (int)k_ptrs.size(), (int)rows, (int)chunk, ptr<int>(cu_q),
+                       (int)cu_q.numel() - 1, (int)docs_per_row, ptr<int>(q_off), ptr<bf16>(out), ptr<float>(lse),
+                       (int)q.size(0), (int)max_seqlen_q, (int)q.size(1), (int)hkv, (float)scale, cur_stream(),
+                       ptr<int>(scratch(0, 0).err));
+  count();
+}
+
 void flash_attn_bwd_kv_(Tensor q, Tensor k, Tensor v, Tensor cu_q, Tensor cu_k, Tensor q_off, Tensor out, Tensor gout,
                         Tensor lse, Tensor gq, Tensor gk, Tensor gv, int64_t max_seqlen_q, int64_t max_seqlen_k,
                         double scale) {
@@ -917,6 +943,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_bwd", &flash_attn_bwd_);
   m.def("flash_attn_fwd_kv", &flash_attn_fwd_kv_, "causal attention of query chunks against a separate key stream");
   m.def("flash_attn_bwd_kv", &flash_attn_bwd_kv_);
+  m.def("flash_attn_fwd_cp_peer", &flash_attn_fwd_cp_peer,
+        "context-parallel attention forward reading every rank's K/V in place over NVLink (no all-gather)");
   m.def("lmhead_logprob_fwd", &lmhead_logprob_fwd);
   m.def("lmhead_dlogits", &lmhead_dlogits);
   m.def("lmhead_sample", &lmhead_sample);

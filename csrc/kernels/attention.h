@@ -13,6 +13,15 @@ void flash_attn_fwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, 
 void flash_attn_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, bf16* o, float* lse,
                        int T, int Tk, int max_seqlen, int Hq, int Hkv, float scale, cudaStream_t st, const int* cu_k,
                        const int* q_off, int* err);
+// Context-parallel forward without an all-gather (tcgen05, head_dim 128): query chunks ``q`` of this rank
+// (documents ``cu``, ``docs_per_row`` of them per sequence row, causal offsets ``q_off``) against the
+// whole rows, whose K / V are read in place from every CP rank's local buffer (``k_ranks[r]`` /
+// ``v_ranks[r]``: rank r's [rows * 2 chunk, Hkv * 128] head and tail chunks, mapped into this process).
+// The buffers must stay unchanged until the kernel has finished on every rank.
+constexpr int kFaMaxCp = 8;
+void flash_attn_fwd_tc_cp(const bf16* q, const bf16* const* k_ranks, const bf16* const* v_ranks, int cp, int rows,
+                          int chunk, const int* cu, int n_docs, int docs_per_row, const int* q_off, bf16* o, float* lse,
+                          int T, int max_seqlen, int Hq, int Hkv, float scale, cudaStream_t st, int* err);
 bool flash_attn_tc_enabled();
 // dk / dv are written for every key row of every key document (zero where no query attends).
 void flash_attn_bwd(const bf16* q, const bf16* k, const bf16* v, const int* cu, int n_docs, const bf16* o,

@@ -77,11 +77,23 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Key / value streams of the forward kernel. NP == 1: one local [Tk, Hkv * 128] stream. NP > 1:
+// context parallelism over ``cp`` ranks without an all-gather: every rank's local K / V ([rows * 2c, Hkv
+// * 128], its head chunk r then its tail chunk 2 cp - 1 - r of every row) is read in place, through the
+// rank's peer mapping, by plain (non-multicast) TMA loads; key position p of row ``doc / docs_per_row``
+// lives in chunk p / c on rank (chunk < cp ? chunk : 2 cp - 1 - chunk).
+template <int NP>
+struct FaKV {
+  CUtensorMap k[NP], v[NP];
+  int cp, chunk, seq, docs_per_row;
+};
+
+template <int NP>
 __global__ void __launch_bounds__(kFaThreads, 1)
-    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
-                     const __grid_constant__ CUtensorMap mapV, const int* __restrict__ cu,
-                     const int* __restrict__ cu_k, const int* __restrict__ q_off, bf16* __restrict__ O,
-                     float* __restrict__ LSE, int T, int max_blocks, int Hq, int Hkv, float scale, int* err) {
+    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ FaKV<NP> kv,
+                     const int* __restrict__ cu, const int* __restrict__ cu_k, const int* __restrict__ q_off,
+                     bf16* __restrict__ O, float* __restrict__ LSE, int T, int max_blocks, int Hq, int Hkv,
+                     float scale, int* err) {
   extern __shared__ __align__(1024) uint8_t smraw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kBarOff);
@@ -101,7 +113,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const int qb = max_blocks - 1 - blockIdx.x % max_blocks;  // longest causal rows first
   const int h = blockIdx.y, hk = h / (Hq / Hkv);
   const int s = cu[doc], e = cu[doc + 1], L = e - s;
-  const int ks = cu_k ? cu_k[doc] : s, ke = cu_k ? cu_k[doc + 1] : e, Lk = ke - ks;
+  const int ks = NP > 1 ? 0 : (cu_k ? cu_k[doc] : s);
+  const int Lk = NP > 1 ? kv.seq : (cu_k ? cu_k[doc + 1] : e) - ks;
   const int qo = q_off ? q_off[doc] : 0;
   const int q0 = qb * TBQ;
   if (q0 >= L) return;
@@ -123,8 +136,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&mapQ);
-    tma_prefetch_desc(&mapK);
-    tma_prefetch_desc(&mapV);
+    tma_prefetch_desc(&kv.k[0]);
+    tma_prefetch_desc(&kv.v[0]);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -145,17 +158,26 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       for (int j = 0; j < n_kb; ++j) {
         const int st = j & 1;
         const uint32_t par = (j >> 1) & 1;
-        const int row = ks + j * TBK;
+        int row = ks + j * TBK;
+        const CUtensorMap* mapK = &kv.k[0];
+        const CUtensorMap* mapV = &kv.v[0];
+        if constexpr (NP > 1) {
+          const int pos = j * TBK, ci = pos / kv.chunk;  // a key tile never straddles two chunks
+          const int owner = ci < kv.cp ? ci : 2 * kv.cp - 1 - ci;
+          row = (doc / kv.docs_per_row) * 2 * kv.chunk + (ci < kv.cp ? 0 : kv.chunk) + pos % kv.chunk;
+          mapK = &kv.k[owner];
+          mapV = &kv.v[owner];
+        }
         if (!mbar_wait(&k_empty[st], par ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
         mbar_arrive_expect_tx(&k_full[st], kTileBytes);
         for (int c = 0; c < 2; ++c)
-          tma_load_2d(sm + kKOff + st * kTileBytes + c * 16384, &mapK, &k_full[st], hk * THD + c * 64, row);
+          tma_load_2d(sm + kKOff + st * kTileBytes + c * 16384, mapK, &k_full[st], hk * THD + c * 64, row);
         if (!mbar_wait(&v_empty[st], par ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
         mbar_arrive_expect_tx(&v_full[st], kTileBytes);
         // MN-major B operand: [key block of 64][dim block of 64][64 keys][64 dims]
         for (int kb2 = 0; kb2 < 2; ++kb2)
           for (int c = 0; c < 2; ++c)
-            tma_load_2d(sm + kVOff + st * kTileBytes + kb2 * 16384 + c * 8192, &mapV, &v_full[st], hk * THD + c * 64,
+            tma_load_2d(sm + kVOff + st * kTileBytes + kb2 * 16384 + c * 8192, mapV, &v_full[st], hk * THD + c * 64,
                         row + kb2 * 64);
         last = st;
         last_par = par;
@@ -811,15 +833,47 @@ void flash_attn_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const int* c
   if (n_docs * mb == 0 || T == 0 || Tk == 0) return;
   // [T, H * 128] views; K-major tiles: box {64 dims, 128 rows}; V (MN-major operand): box {64, 64}
   CUtensorMap mq = make_map_bf16(q, T, (int64_t)Hq * THD, (int64_t)Hq * THD, 64, 128);
-  CUtensorMap mk = make_map_bf16(k, Tk, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 128);
-  CUtensorMap mv = make_map_bf16(v, Tk, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 64);
+  FaKV<1> kv{};
+  kv.k[0] = make_map_bf16(k, Tk, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 128);
+  kv.v[0] = make_map_bf16(v, Tk, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 64);
   static bool attr = false;
   if (!attr) {
-    MESHY_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFaSmem));
+    MESHY_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFaSmem));
     attr = true;
   }
   dim3 grid(n_docs * mb, Hq);
-  fa_fwd_tc_kernel<<<grid, kFaThreads, kFaSmem, st>>>(mq, mk, mv, cu, cu_k, q_off, o, lse, T, mb, Hq, Hkv, scale, err);
+  fa_fwd_tc_kernel<1><<<grid, kFaThreads, kFaSmem, st>>>(mq, kv, cu, cu_k, q_off, o, lse, T, mb, Hq, Hkv, scale, err);
+  MESHY_CUDA_CHECK(cudaGetLastError());
+}
+
+void flash_attn_fwd_tc_cp(const bf16* q, const bf16* const* k_ranks, const bf16* const* v_ranks, int cp, int rows,
+                          int chunk, const int* cu, int n_docs, int docs_per_row, const int* q_off, bf16* o, float* lse,
+                          int T, int max_seqlen, int Hq, int Hkv, float scale, cudaStream_t st, int* err) {
+  MESHY_CHECK(Hq % Hkv == 0, "flash_attn_cp: Hq must be a multiple of Hkv");
+  MESHY_CHECK(cp >= 1 && cp <= kFaMaxCp, "flash_attn_cp: 1 to 8 context-parallel ranks");
+  MESHY_CHECK(chunk % TBK == 0, "flash_attn_cp: the chunk length must be a multiple of 128 tokens");
+  const int mb = (max_seqlen + TBQ - 1) / TBQ;
+  if (n_docs * mb == 0 || T == 0) return;
+  CUtensorMap mq = make_map_bf16(q, T, (int64_t)Hq * THD, (int64_t)Hq * THD, 64, 128);
+  FaKV<kFaMaxCp> kv{};
+  const int64_t local = (int64_t)rows * 2 * chunk;
+  for (int r = 0; r < cp; ++r) {
+    kv.k[r] = make_map_bf16(k_ranks[r], local, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 128);
+    kv.v[r] = make_map_bf16(v_ranks[r], local, (int64_t)Hkv * THD, (int64_t)Hkv * THD, 64, 64);
+  }
+  kv.cp = cp;
+  kv.chunk = chunk;
+  kv.seq = 2 * cp * chunk;
+  kv.docs_per_row = docs_per_row;
+  static bool attr = false;
+  if (!attr) {
+    MESHY_CUDA_CHECK(
+        cudaFuncSetAttribute(fa_fwd_tc_kernel<kFaMaxCp>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFaSmem));
+    attr = true;
+  }
+  dim3 grid(n_docs * mb, Hq);
+  fa_fwd_tc_kernel<kFaMaxCp>
+      <<<grid, kFaThreads, kFaSmem, st>>>(mq, kv, cu, nullptr, q_off, o, lse, T, mb, Hq, Hkv, scale, err);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -12,13 +12,23 @@ and torch's CP SDPA dispatcher with its default all-gather rotation):
   so the reference's CP all-reduce of those counts is not needed
   (:meth:`CpSharder.all_reduce_sum` remains for callers that have sharded sums).
 
-Attention: each layer all-gathers K and V over the CP group (the reference's
-rotation), reorders them into sequence order, and runs the chunked causal
-kernel: the two local query chunks of a row are two query documents at key
-positions ``r c`` and ``(2 cp - 1 - r) c`` of the gathered row
+Attention, gathered path: each layer all-gathers K and V over the CP group
+(the reference's rotation), reorders them into sequence order, and runs the
+chunked causal kernel: the two local query chunks of a row are two query
+documents at key positions ``r c`` and ``(2 cp - 1 - r) c`` of the gathered row
 (:func:`meshy_b200.ops.functional.flash_attn_chunks`).  Backward reduce-scatters
-dK / dV back to their owners.  The collectives go through NCCL (gloo on CPU);
-the in-kernel NVLink ring of KV chunks is the planned replacement.
+dK / dV back to their owners.  The collectives go through NCCL (gloo on CPU).
+
+Attention, peer path (one node, NCCL, head_dim 128, chunks a multiple of 128
+tokens; ``MESHY_CP_PEER=0`` turns it off): the forward runs no all-gather.
+Every rank copies its local K / V into a symmetric-memory buffer that every
+rank maps, and the tcgen05 attention kernel reads each key tile straight from
+its owner's buffer over NVLink with plain TMA loads, so the transfer of a tile
+overlaps the tensor-core work on the previous one
+(``_C.flash_attn_fwd_cp_peer``). Two device barriers over the CP group bracket
+the copy (previous readers done; every rank's K / V in place). The backward
+gathers K / V (NCCL), runs the chunked backward kernels and reduce-scatters
+dK / dV, as the gathered path does.
 """
 
 from __future__ import annotations
@@ -30,6 +40,12 @@ import torch
 import torch.distributed as dist
 
 from ..ops import functional as Fx
+
+
+def _peer_enabled() -> bool:
+    import os
+
+    return os.environ.get("MESHY_CP_PEER", "1") != "0" and os.environ.get("MESHY_FA_TC", "1") != "0"
 
 
 def _nccl(group) -> bool:
@@ -75,11 +91,30 @@ class CpLayout:
     chunk: int     # c = S / (2 cp)
 
 
+class _CpPeerAttn(torch.autograd.Function):
+    """Forward: K / V read in place on every CP rank (no all-gather). Backward: the gathered path."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, sharder, layout, scale):
+        out, lse = sharder._peer_forward(q, k, v, layout, scale)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.sharder, ctx.layout, ctx.scale = sharder, layout, scale
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        q, k, v, out, lse = ctx.saved_tensors
+        gq, gk, gv = ctx.sharder._gathered_backward(q, k, v, out, lse, g.contiguous(), ctx.layout, ctx.scale)
+        return gq, gk, gv, None, None, None
+
+
 class CpSharder:
     def __init__(self, group):
         self.group = group
         self.size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self._heap = None       # symmetric K / V buffers of the peer path
+        self._epoch = 0
 
     # ------------------------------------------------------------------ index maps
     def chunk_ids(self, rank: int | None = None) -> tuple[int, int]:
@@ -153,20 +188,120 @@ class CpSharder:
         return b
 
     # ------------------------------------------------------------------ attention
-    def attention(self, q, k, v, layout: CpLayout, scale: float | None = None):
-        """Local ``q/k/v [rows * 2c, H, hd]`` → local attention output, exact causal over full rows."""
-        rows, S, c = layout.rows, layout.seq_len, layout.chunk
+    def peer_ok(self, q, layout: CpLayout) -> bool:
+        """Whether the no-all-gather peer path applies to this call."""
+        if not (q.is_cuda and _peer_enabled() and _nccl(self.group) and self.size <= 8):
+            return False
+        from .symm import SymmetricHeap
+
+        return q.shape[-1] == 128 and layout.chunk % 128 == 0 and SymmetricHeap.supported(self.group)
+
+    def _barrier(self) -> None:
+        from ..ops._ext import ext
+
+        self._epoch += 1
+        ext().symm_barrier(self._flags, self.rank, self.size, self._epoch, 30.0)
+
+    def _peer_buffers(self, numel: int):
+        """Symmetric K and V buffers of at least ``numel`` bf16 elements (collective on first use / growth)."""
+        from .symm import SymmetricHeap
+
+        if self._heap is None or self._cap < numel:
+            if self._heap is not None:
+                torch.cuda.synchronize()
+                dist.barrier(self.group)
+                self._heap.close()
+            cap = max(numel, 1 << 20)
+            self._heap = SymmetricHeap(2 * cap * 2 + 4096, self.group)
+            self._kbuf, ktab = self._heap.alloc(cap, torch.bfloat16)
+            self._vbuf, vtab = self._heap.alloc(cap, torch.bfloat16)
+            _, self._flags = self._heap.alloc(self.size, torch.int32)
+            self._kptrs, self._vptrs = ktab.tolist(), vtab.tolist()
+            self._cap, self._epoch = cap, 0
+            dist.barrier(self.group)
+        return self._kbuf, self._vbuf
+
+    def close(self) -> None:
+        if self._heap is not None:
+            torch.cuda.synchronize()
+            dist.barrier(self.group)
+            self._heap.close()
+            self._heap = None
+
+    def _peer_forward(self, q, k, v, layout: CpLayout, scale: float):
+        from ..ops._ext import ext
+
+        rows, c = layout.rows, layout.chunk
+        n = k.numel()
+        kb, vb = self._peer_buffers(n)
+        self._barrier()  # every rank has finished reading the previous contents
+        kb[:n].copy_(k.reshape(-1))
+        vb[:n].copy_(v.reshape(-1))
+        self._barrier()  # every rank's K / V are in place
         dev = q.device
+        a, b = self.chunk_ids()
+        cu_q = torch.arange(0, rows * 2 * c + 1, c, dtype=torch.int32, device=dev)
+        q_off = torch.tensor([a * c, b * c], dtype=torch.int32, device=dev).repeat(rows)
+        out = torch.empty_like(q)
+        lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=dev)
+        ext().flash_attn_fwd_cp_peer(q.contiguous(), self._kptrs, self._vptrs, rows, c, k.shape[1], cu_q, q_off, 2,
+                                     out, lse, c, float(scale))
+        return out, lse
+
+    def _gathered_kv(self, k, v, layout: CpLayout):
+        """K / V of the whole rows in sequence order (differentiable: backward reduce-scatters)."""
+        rows, S, c = layout.rows, layout.seq_len, layout.chunk
+        dev = k.device
         kf = _AllGather.apply(k, self.group)  # [cp * rows * 2c, Hkv, hd], rank-major
         vf = _AllGather.apply(v, self.group)
         # rank-major [cp, rows, 2c] → [rows, S] in sequence order
-        order = self.gather_order(S, dev)                       # within a row: rank-major position per token
+        order = self.gather_order(S, dev)
         rank_of = order // (2 * c)
         within = order % (2 * c)
         src = (rank_of.unsqueeze(0) * rows * 2 * c + torch.arange(rows, device=dev).unsqueeze(1) * 2 * c
                + within.unsqueeze(0)).reshape(-1)
-        kf = kf.index_select(0, src)
-        vf = vf.index_select(0, src)
+        return kf.index_select(0, src), vf.index_select(0, src)
+
+    def _gathered_backward(self, q, k, v, out, lse, g, layout: CpLayout, scale: float):
+        from ..ops._ext import ext
+
+        rows, S, c = layout.rows, layout.seq_len, layout.chunk
+        dev = q.device
+        with torch.enable_grad():
+            kd = k.detach().requires_grad_(True)
+            vd = v.detach().requires_grad_(True)
+            kf, vf = self._gathered_kv(kd, vd, layout)
+        H, hd = q.shape[1], q.shape[2]
+        qv, ov, gvw = q.view(rows, 2, c, H, hd), out.view(rows, 2, c, H, hd), g.view(rows, 2, c, H, hd)
+        lv = lse.view(H, rows, 2, c)
+        gq = torch.empty_like(q).view(rows, 2, c, H, hd)
+        cu_q = torch.arange(0, rows * c + 1, c, dtype=torch.int32, device=dev)
+        cu_k = torch.arange(0, rows * S + 1, S, dtype=torch.int32, device=dev)
+        gkf = gvf = None
+        kfd, vfd = kf.detach(), vf.detach()
+        for j, chunk in enumerate(self.chunk_ids()):
+            qj = qv[:, j].reshape(rows * c, H, hd).contiguous()
+            oj = ov[:, j].reshape(rows * c, H, hd).contiguous()
+            gj = gvw[:, j].reshape(rows * c, H, hd).contiguous()
+            lj = lv[:, :, j].reshape(H, rows * c).contiguous()
+            off = torch.full((rows,), chunk * c, dtype=torch.int32, device=dev)
+            gqj, gkj, gvj = torch.empty_like(qj), torch.zeros_like(kfd), torch.zeros_like(vfd)
+            ext().flash_attn_bwd_kv(qj, kfd, vfd, cu_q, cu_k, off, oj, gj, lj, gqj, gkj, gvj, c, S, float(scale))
+            gq[:, j] = gqj.view(rows, c, H, hd)
+            gkf = gkj if gkf is None else gkf + gkj
+            gvf = gvj if gvf is None else gvf + gvj
+        gk, gv = torch.autograd.grad((kf, vf), (kd, vd), (gkf, gvf))
+        return gq.view_as(q), gk, gv
+
+    def attention(self, q, k, v, layout: CpLayout, scale: float | None = None):
+        """Local ``q/k/v [rows * 2c, H, hd]`` → local attention output, exact causal over full rows."""
+        if scale is None:
+            scale = 1.0 / (q.shape[-1] ** 0.5)
+        if self.peer_ok(q, layout):
+            return _CpPeerAttn.apply(q, k.contiguous(), v.contiguous(), self, layout, float(scale))
+        rows, S, c = layout.rows, layout.seq_len, layout.chunk
+        dev = q.device
+        kf, vf = self._gathered_kv(k, v, layout)
         a, b = self.chunk_ids()
         H, hd = q.shape[1], q.shape[2]
         qv = q.view(rows, 2, c, H, hd)
