@@ -19,16 +19,18 @@ documents at key positions ``r c`` and ``(2 cp - 1 - r) c`` of the gathered row
 (:func:`meshy_b200.ops.functional.flash_attn_chunks`).  Backward reduce-scatters
 dK / dV back to their owners.  The collectives go through NCCL (gloo on CPU).
 
-Attention, peer path (one node, NCCL, head_dim 128, chunks a multiple of 128
-tokens; ``MESHY_CP_PEER=0`` turns it off): the forward runs no all-gather.
-Every rank copies its local K / V into a symmetric-memory buffer that every
-rank maps, and the tcgen05 attention kernel reads each key tile straight from
-its owner's buffer over NVLink with plain TMA loads, so the transfer of a tile
-overlaps the tensor-core work on the previous one
-(``_C.flash_attn_fwd_cp_peer``). Two device barriers over the CP group bracket
-the copy (previous readers done; every rank's K / V in place). The backward
-gathers K / V (NCCL), runs the chunked backward kernels and reduce-scatters
-dK / dV, as the gathered path does.
+Attention, peer path (opt-in, ``MESHY_CP_PEER=1``; one node, NCCL, head_dim
+128, chunks a multiple of 128 tokens): the forward runs no all-gather. Every
+rank copies its local K / V into a symmetric-memory buffer that every rank
+maps, and the tcgen05 attention kernel reads each key tile straight from its
+owner's buffer over NVLink with plain TMA loads (``_C.flash_attn_fwd_cp_peer``).
+Two device barriers over the CP group bracket the copy (previous readers done;
+every rank's K / V in place). The backward gathers K / V (NCCL), runs the
+chunked backward kernels and reduce-scatters dK / dV, as the gathered path
+does. It is off by default because it measured slower (B200, 2 ranks, 1 row,
+12 query / 2 KV heads: forward 3.7 ms vs 0.8 ms at 16k tokens, 40.6 ms vs
+7.7 ms at 64k): every (query block, head) CTA re-reads its key tiles, which a
+local gathered buffer serves from L2, while peer reads cross NVLink each time.
 """
 
 from __future__ import annotations
@@ -45,7 +47,7 @@ from ..ops import functional as Fx
 def _peer_enabled() -> bool:
     import os
 
-    return os.environ.get("MESHY_CP_PEER", "1") != "0" and os.environ.get("MESHY_FA_TC", "1") != "0"
+    return os.environ.get("MESHY_CP_PEER", "0") == "1" and os.environ.get("MESHY_FA_TC", "1") != "0"
 
 
 def _nccl(group) -> bool:
