@@ -72,6 +72,10 @@ struct GemmArgs {
   const int64_t* step_ptr;
   int gumbel;
   int* err;
+  // 1: the epilogue stages each 128-row x 128-byte slice of the tile in shared memory and writes it with one
+  // TMA store (bf16 output; SwiGLU output and pre-activations) or TMA reduce-add (fp32 accumulation), so
+  // the global writes are whole lines instead of one 16-byte piece per row and lane
+  int tma_out;
 };
 
 template <int BN>
@@ -80,7 +84,65 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STG_BYTES = BM * 128;  // one epilogue staging buffer: 128 rows x 128 bytes
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES + 1024;  // after the barriers, 1024-aligned for the swizzle
+  static constexpr int SMEM_BYTES = 1024 /*align*/ + STG_OFF + 2 * STG_BYTES;
+};
+
+// Named barrier 1 over the four epilogue warps with an AND of ``v``: every thread gets the same answer.
+__device__ __forceinline__ bool epi_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, 1, 128, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+// ─── epilogue through shared memory + TMA store ─────────────────────────────
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               :
+               : "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];"
+               :
+               : "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+
+// The four epilogue warps write one 128 x 128-byte slice (row r = TMEM lane, 128-byte swizzle) into staging
+// buffer ``sb`` and one thread sends it with a TMA store (or reduce-add) at (c0, r0). A buffer is reused two
+// slices later, after the store that read it has finished reading.
+struct Stager {
+  uint8_t* stg;
+  int sb;
+  template <bool REDUCE>
+  __device__ __forceinline__ void put(const uint4* row16, int r, const CUtensorMap* map, int c0, int r0, int et) {
+    if (et == 0) bulk_wait_read1();
+    named_bar_sync(1, 128);
+    uint8_t* buf = stg + sb * (BM * 128);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(buf + r * 128 + ((j ^ (r & 7)) << 4)) = row16[j];
+    fence_async_smem();
+    named_bar_sync(1, 128);
+    if (et == 0) {
+      if (REDUCE) tma_reduce_add_2d(map, buf, c0, r0);
+      else tma_store_2d(map, buf, c0, r0);
+      bulk_commit();
+    }
+    sb ^= 1;
+  }
 };
 
 __device__ __forceinline__ void unit_coords(const GemmArgs& p, int u, int& mt, int& nt, int& ks) {
@@ -100,7 +162,8 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x));
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmArgs p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapAux, GemmArgs p) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -248,12 +311,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const int et = threadIdx.x - 64;  // 0..127
+    Stager stager{smem + C::STG_OFF, 0};
     pdl_wait();  // residual / labels / workspace may come from the kernels before
     pdl_trigger();
     for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
       int mt, nt, ks;
       unit_coords(p, u, mt, nt, ks);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      if (!epi_all(mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue))) break;
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
@@ -261,7 +325,92 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = nt * BN;
       float v[32];
 
-      if (p.epi == EPI_STORE || p.epi == EPI_ACC_F32) {
+      if (p.tma_out && p.epi == EPI_ACC_F32) {
+        // fp32 accumulation: 32-column slices, reduce-added by TMA
+        for (int c = 0; c < BN / 32; ++c) {
+          tmem_ld32(t_row + c * 32, v);
+          if (n0 + c * 32 >= p.N) break;  // uniform over the warps
+          uint4 r16[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            r16[j] = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
+                                __float_as_uint(v[4 * j + 3]));
+          stager.put<true>(r16, q * 32 + lane, &mapC, n0 + c * 32, mt * BM, et);
+        }
+      } else if (p.tma_out && p.epi == EPI_STORE) {
+        // bf16 output: 64-column slices (+bias, +residual), stored by TMA (rows >= M / columns >= N clipped)
+        for (int c = 0; c < BN / 64; ++c) {
+          float w[64];
+          tmem_ld32(t_row + c * 64, w);
+          tmem_ld32(t_row + c * 64 + 32, w + 32);
+          const int col0 = n0 + c * 64;
+          if (col0 >= p.N) break;  // uniform over the warps
+          const int ncol = min(64, p.N - col0);
+          if (p.bias) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) w[i] += (i < ncol) ? __bfloat162float(p.bias[col0 + i]) : 0.f;
+          }
+          if (p.residual && row_ok) {
+            const bf16* rr = p.residual + (size_t)row * p.ldr + col0;
+            if (ncol == 64) {
+#pragma unroll
+              for (int i = 0; i < 64; i += 8) {
+                uint4 x = *reinterpret_cast<const uint4*>(rr + i);
+                float2 a0 = unpack_bf16x2(x.x), a1 = unpack_bf16x2(x.y), a2 = unpack_bf16x2(x.z),
+                       a3 = unpack_bf16x2(x.w);
+                w[i] += a0.x; w[i + 1] += a0.y; w[i + 2] += a1.x; w[i + 3] += a1.y;
+                w[i + 4] += a2.x; w[i + 5] += a2.y; w[i + 6] += a3.x; w[i + 7] += a3.y;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 64; ++i)
+                if (i < ncol) w[i] += __bfloat162float(rr[i]);
+            }
+          }
+          uint4 r16[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            r16[j] = make_uint4(pack_bf16x2(w[8 * j], w[8 * j + 1]), pack_bf16x2(w[8 * j + 2], w[8 * j + 3]),
+                                pack_bf16x2(w[8 * j + 4], w[8 * j + 5]), pack_bf16x2(w[8 * j + 6], w[8 * j + 7]));
+          stager.put<false>(r16, q * 32 + lane, &mapC, col0, mt * BM, et);
+        }
+      } else if (p.tma_out && p.epi == EPI_SWIGLU) {
+        // columns [128j, 128j+64) are gate, [128j+64, 128j+128) the matching up rows -> 64 SwiGLU columns
+        for (int j = 0; j < BN / 128; ++j) {
+          const int gcol = n0 + j * 128;
+          if (gcol >= p.N) break;  // uniform over the warps
+          uint4 act[8], hg[8], hu[8];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float g[32];
+            tmem_ld32(t_row + j * 128 + h * 32, g);
+            tmem_ld32(t_row + j * 128 + 64 + h * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              float a[8];
+#pragma unroll
+              for (int t = 0; t < 8; ++t) {
+                // round the pre-activations to bf16 first so forward and the
+                // backward recompute (from the stored bf16 h) agree exactly
+                float gg = __bfloat162float(__float2bfloat16(g[i + t]));
+                float uu = __bfloat162float(__float2bfloat16(v[i + t]));
+                a[t] = silu(gg) * uu;
+              }
+              act[h * 4 + i / 8] = make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]),
+                                              pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+              hg[h * 4 + i / 8] = make_uint4(pack_bf16x2(g[i], g[i + 1]), pack_bf16x2(g[i + 2], g[i + 3]),
+                                             pack_bf16x2(g[i + 4], g[i + 5]), pack_bf16x2(g[i + 6], g[i + 7]));
+              hu[h * 4 + i / 8] = make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                                             pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+            }
+          }
+          stager.put<false>(act, q * 32 + lane, &mapC, n0 / 2 + j * 64, mt * BM, et);
+          if (p.aux) {
+            stager.put<false>(hg, q * 32 + lane, &mapAux, gcol, mt * BM, et);
+            stager.put<false>(hu, q * 32 + lane, &mapAux, gcol + 64, mt * BM, et);
+          }
+        }
+      } else if (p.epi == EPI_STORE || p.epi == EPI_ACC_F32) {
         for (int c = 0; c < BN / 32; ++c) {
           tmem_ld32(t_row + c * 32, v);
           const int col0 = n0 + c * 32;
@@ -517,6 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_sync(1, 128);
       }
     }
+    if (p.tma_out && et == 0) bulk_wait_all();  // staged stores complete before the CTA leaves
   }
 
   tc_fence_before();
@@ -619,7 +769,8 @@ static int num_sms() {
 }
 
 template <int BN, bool A_MN, bool B_MN>
-static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, int grid, cudaStream_t st) {
+static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mx,
+                     const GemmArgs& a, int grid, cudaStream_t st) {
   using C = Cfg<BN>;
   auto k = gemm_kernel<BN, A_MN, B_MN>;
   static bool attr_set = false;
@@ -627,16 +778,40 @@ static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
     MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_set = true;
   }
-  launch_pdl(k, dim3(grid), dim3(kThreads), C::SMEM_BYTES, st, ma, mb, a);
+  launch_pdl(k, dim3(grid), dim3(kThreads), C::SMEM_BYTES, st, ma, mb, mc, mx, a);
 }
 
 template <int BN>
-static void launch_bn(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, int grid,
-                      cudaStream_t st) {
-  if (!a_mn && !b_mn) launch_t<BN, false, false>(ma, mb, a, grid, st);
-  else if (!a_mn && b_mn) launch_t<BN, false, true>(ma, mb, a, grid, st);
-  else if (a_mn && !b_mn) launch_t<BN, true, false>(ma, mb, a, grid, st);
-  else launch_t<BN, true, true>(ma, mb, a, grid, st);
+static void launch_bn(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                      const CUtensorMap& mx, const GemmArgs& a, int grid, cudaStream_t st) {
+  if (!a_mn && !b_mn) launch_t<BN, false, false>(ma, mb, mc, mx, a, grid, st);
+  else if (!a_mn && b_mn) launch_t<BN, false, true>(ma, mb, mc, mx, a, grid, st);
+  else if (a_mn && !b_mn) launch_t<BN, true, false>(ma, mb, mc, mx, a, grid, st);
+  else launch_t<BN, true, true>(ma, mb, mc, mx, a, grid, st);
+}
+
+// fp32 [rows, cols] (row stride ld elements), box {bi, bo}, 128-byte swizzle: TMA reduce-add target.
+static CUtensorMap make_map_f32(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int bi, int bo) {
+  MESHY_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * 4) % 16 == 0, "TMA: 16-byte aligned rows");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {(cuuint32_t)bi, (cuuint32_t)bo};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MESHY_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp32) failed (" + std::to_string((int)r) + ")");
+  return map;
+}
+
+static bool gemm_tma_out_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MESHY_GEMM_TMA_OUT");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
 }
 
 void gemm_launch(const GemmProblem& g, cudaStream_t stream) {
@@ -692,11 +867,28 @@ void gemm_launch(const GemmProblem& g, cudaStream_t stream) {
   // tensor maps: K-major operand [rows, K] box {64, rows_box}; MN-major [K, mn] box {64, 64}
   CUtensorMap ma = g.a_mn ? make_map_bf16(g.A, g.K, g.M, g.lda, 64, 64) : make_map_bf16(g.A, g.M, g.K, g.lda, 64, BM);
   CUtensorMap mb = g.b_mn ? make_map_bf16(g.B, g.K, g.N, g.ldb, 64, 64) : make_map_bf16(g.B, g.N, g.K, g.ldb, 64, BN);
+  // TMA-store epilogue: 128-row x 128-byte slices of the output (and of the SwiGLU pre-activations)
+  CUtensorMap mc = ma, mx = ma;
+  a.tma_out = 0;
+  if (gemm_tma_out_enabled() && a.split_k == 1) {
+    const bool aux_ok = g.aux == nullptr || ((reinterpret_cast<uintptr_t>(g.aux) & 15) == 0 && (g.ld_aux * 2) % 16 == 0);
+    if (g.epi == EPI_STORE && !g.out_f32 && g.aux == nullptr) {
+      mc = make_map_bf16(g.out, g.M, g.N, g.ldo, 64, BM);
+      a.tma_out = 1;
+    } else if (g.epi == EPI_ACC_F32) {
+      mc = make_map_f32(g.out, g.M, g.N, g.ldo, 32, BM);
+      a.tma_out = 1;
+    } else if (g.epi == EPI_SWIGLU && !g.out_f32 && aux_ok) {
+      mc = make_map_bf16(g.out, g.M, g.N / 2, g.ldo, 64, BM);
+      if (g.aux) mx = make_map_bf16(g.aux, g.M, g.N, g.ld_aux, 64, BM);
+      a.tma_out = 1;
+    }
+  }
   int grid = std::min(a.total_units, sms);
   switch (BN) {
-    case 256: launch_bn<256>(g.a_mn, g.b_mn, ma, mb, a, grid, stream); break;
-    case 128: launch_bn<128>(g.a_mn, g.b_mn, ma, mb, a, grid, stream); break;
-    default: launch_bn<64>(g.a_mn, g.b_mn, ma, mb, a, grid, stream); break;
+    case 256: launch_bn<256>(g.a_mn, g.b_mn, ma, mb, mc, mx, a, grid, stream); break;
+    case 128: launch_bn<128>(g.a_mn, g.b_mn, ma, mb, mc, mx, a, grid, stream); break;
+    default: launch_bn<64>(g.a_mn, g.b_mn, ma, mb, mc, mx, a, grid, stream); break;
   }
 }
 
