@@ -374,6 +374,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 pack_bf16x2(w[8 * j + 4], w[8 * j + 5]), pack_bf16x2(w[8 * j + 6], w[8 * j + 7]));
           stager.put<false>(r16, q * 32 + lane, &mapC, col0, mt * BM, et);
         }
+      } else if (p.tma_out && p.epi == EPI_DLOGITS) {
+        // d logits = g * (onehot(label) - softmax), 64-column slices stored by TMA
+        const float lse = row_ok ? p.row_lse[row] : 0.f;
+        const float gr = row_ok ? p.row_g[row] : 0.f;
+        const int64_t label = row_ok ? p.labels[row] : -1;
+        for (int c = 0; c < BN / 64; ++c) {
+          float w[64];
+          tmem_ld32(t_row + c * 64, w);
+          tmem_ld32(t_row + c * 64 + 32, w + 32);
+          const int col0 = n0 + c * 64;
+          if (col0 >= p.N) break;  // uniform over the warps
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float pr = __expf(w[i] - lse);
+            w[i] = gr * (((int64_t)(col0 + i) == label ? 1.f : 0.f) - pr);
+          }
+          uint4 r16[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            r16[j] = make_uint4(pack_bf16x2(w[8 * j], w[8 * j + 1]), pack_bf16x2(w[8 * j + 2], w[8 * j + 3]),
+                                pack_bf16x2(w[8 * j + 4], w[8 * j + 5]), pack_bf16x2(w[8 * j + 6], w[8 * j + 7]));
+          stager.put<false>(r16, q * 32 + lane, &mapC, col0, mt * BM, et);
+        }
       } else if (p.tma_out && p.epi == EPI_SWIGLU) {
         // columns [128j, 128j+64) are gate, [128j+64, 128j+128) the matching up rows -> 64 SwiGLU columns
         for (int j = 0; j < BN / 128; ++j) {
@@ -877,6 +900,9 @@ void gemm_launch(const GemmProblem& g, cudaStream_t stream) {
       a.tma_out = 1;
     } else if (g.epi == EPI_ACC_F32) {
       mc = make_map_f32(g.out, g.M, g.N, g.ldo, 32, BM);
+      a.tma_out = 1;
+    } else if (g.epi == EPI_DLOGITS && !g.out_f32) {
+      mc = make_map_bf16(g.out, g.M, g.N, g.ldo, 64, BM);
       a.tma_out = 1;
     } else if (g.epi == EPI_SWIGLU && !g.out_f32 && aux_ok) {
       mc = make_map_bf16(g.out, g.M, g.N / 2, g.ldo, 64, BM);
