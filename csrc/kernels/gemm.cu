@@ -866,6 +866,8 @@ void gemm_launch(const GemmProblem& g, cudaStream_t stream) {
   int split = 1;
   const int tiles = a.m_tiles * a.n_tiles;
   if ((g.epi == EPI_STORE && g.ws != nullptr) || g.epi == EPI_ACC_F32) {
+    // (splitting weight-gradient GEMMs further, to fill whole waves of the persistent grid, measured no
+    // faster on the 1.5B training step: 3086 vs 3083 ms)
     if (tiles * 2 <= sms && a.k_blocks >= 4) {
       split = std::min(a.k_blocks / 2, (sms + tiles - 1) / tiles);
       split = std::max(1, std::min(split, 32));
@@ -893,7 +895,7 @@ void gemm_launch(const GemmProblem& g, cudaStream_t stream) {
   // TMA-store epilogue: 128-row x 128-byte slices of the output (and of the SwiGLU pre-activations)
   CUtensorMap mc = ma, mx = ma;
   a.tma_out = 0;
-  if (gemm_tma_out_enabled() && a.split_k == 1) {
+  if (gemm_tma_out_enabled() && (a.split_k == 1 || g.epi == EPI_ACC_F32)) {
     const bool aux_ok = g.aux == nullptr || ((reinterpret_cast<uintptr_t>(g.aux) & 15) == 0 && (g.ld_aux * 2) % 16 == 0);
     if (g.epi == EPI_STORE && !g.out_f32 && g.aux == nullptr) {
       mc = make_map_bf16(g.out, g.M, g.N, g.ldo, 64, BM);

@@ -53,7 +53,7 @@ def test_gemm_bias_residual_f32(M, N, K):
     assert rel_err(out32, a.float() @ b.float().t()) < 5e-3
 
 
-@pytest.mark.parametrize("T,N,K", [(512, 256, 384), (300, 1536, 1536), (4096, 1024, 2048)])
+@pytest.mark.parametrize("T,N,K", [(512, 256, 384), (300, 1536, 1536), (4096, 1024, 2048), (4096, 2048, 1536)])
 def test_gemm_dgrad_wgrad(T, N, K):
     torch.manual_seed(2)
     gy, w, x = bf(T, N), bf(N, K), bf(T, K)
