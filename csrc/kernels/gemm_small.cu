@@ -634,8 +634,13 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         const uint32_t off_a = red_addr + (uint32_t)((g * 128 + f) * 16);
         const uint32_t off_b = red_addr + (uint32_t)((g * 128 + f + 64) * 16);
         // issue the peers' loads before summing, so the DSMEM latency is paid once (all peers at once
-        // for a plain output, in batches of four when SwiGLU pairs two rows)
-        if (!swiglu) {
+        // for a plain output, in batches of four when SwiGLU pairs two rows); a CTA alone on its tile reads
+        // its partial straight from its own shared memory
+        if (p.cs == 1) {
+          const float4* red = reinterpret_cast<const float4*>(smem);
+          a = red[g * 128 + f];
+          if (swiglu) b = red[g * 128 + f + 64];
+        } else if (!swiglu) {
           float4 xa[kSmallMaxCluster];
 #pragma unroll
           for (int j = 0; j < kSmallMaxCluster; ++j)
@@ -647,7 +652,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             }
           }
         }
-        for (int r0 = 0; swiglu && r0 < p.cs; r0 += 4) {
+        for (int r0 = 0; swiglu && p.cs > 1 && r0 < p.cs; r0 += 4) {
           float4 xa[4], xb[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
