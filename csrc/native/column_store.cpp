@@ -32,6 +32,8 @@ int64_t ColumnStore::put_columns(const std::string& part, const std::vector<int6
                                  const std::vector<std::string>& fields,
                                  const std::vector<std::vector<std::string>>& values) {
   if (values.size() != fields.size()) throw std::invalid_argument("put_columns: one value list per field");
+  for (auto& v : values)  // validate before writing anything
+    if (v.size() != idx.size()) throw std::invalid_argument("put_columns: length mismatch");
   int64_t written = 0;
   {
     std::lock_guard<std::mutex> g(mu_);
@@ -41,10 +43,7 @@ int64_t ColumnStore::put_columns(const std::string& part, const std::vector<int6
     for (size_t r = 0; r < idx.size(); ++r) {
       auto rit = p.rows.find(idx[r]);
       if (rit == p.rows.end()) continue;
-      for (size_t f = 0; f < fields.size(); ++f) {
-        if (values[f].size() != idx.size()) throw std::invalid_argument("put_columns: length mismatch");
-        rit->second.cols[fields[f]] = values[f][r];
-      }
+      for (size_t f = 0; f < fields.size(); ++f) rit->second.cols[fields[f]] = values[f][r];
       ++written;
     }
   }
