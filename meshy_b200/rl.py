@@ -139,16 +139,21 @@ class ColocatedGRPO:
 
     def step(self, prompts: Sequence[Sequence[int]], max_new_tokens: Sequence[int] | int) -> StepReport:
         """One lock-step GRPO iteration on this rank (collective across the DP group)."""
+        from .utils.timer import nvtx_range
+
         times = {}
         t0 = time.perf_counter()
-        samples = self.rollout(prompts, max_new_tokens)
+        with nvtx_range("rl/rollout"):
+            samples = self.rollout(prompts, max_new_tokens)
         times["rollout_s"] = time.perf_counter() - t0
         t1 = time.perf_counter()
-        local, minis = self.plan_local(samples)
-        metrics = self.trainer.train_step(local, plan=minis)
+        with nvtx_range("rl/train"):
+            local, minis = self.plan_local(samples)
+            metrics = self.trainer.train_step(local, plan=minis)
         times["train_s"] = time.perf_counter() - t1
         self.version += 1
-        times["weight_sync_ms"] = self.sync_weights()
+        with nvtx_range("rl/weight_sync"):
+            times["weight_sync_ms"] = self.sync_weights()
         n_tok = sum(len(s["tokens"]) for s in samples)
         n_resp = sum(int(s["mask_assistant"].sum()) for s in samples)
         metrics["rollout/raw_reward_mean"] = sum(float(s["reward"]) for s in samples) / max(1, len(samples))

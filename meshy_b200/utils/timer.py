@@ -5,11 +5,14 @@
 ``torch.cuda.synchronize`` so the number covers device work.
 :class:`DeviceTimer` times a region with CUDA events instead (no host sync
 inside the region); :func:`max_over_ranks` turns a per-rank time into the
-job time.
+job time. Every timed region, and every :func:`nvtx_range`, is also an NVTX
+range on a CUDA machine (``MESHY_NVTX=0`` turns them off), so a profiler
+timeline (or ``ncu --nvtx --nvtx-include``) shows the RL step's phases.
 """
 
 from __future__ import annotations
 
+import os
 import time
 from collections import defaultdict
 from contextlib import contextmanager
@@ -17,6 +20,32 @@ from contextlib import contextmanager
 import torch
 
 _GLOBAL_ENABLED = True
+
+
+_NVTX_BROKEN = False
+
+
+def _nvtx_on() -> bool:
+    return (not _NVTX_BROKEN and os.environ.get("MESHY_NVTX", "1") != "0" and torch.cuda.is_available()
+            and torch.cuda.is_initialized())
+
+
+@contextmanager
+def nvtx_range(name: str):
+    """An NVTX range around the block on a CUDA machine (a no-op otherwise, or if NVTX is unavailable)."""
+    global _NVTX_BROKEN
+    pushed = False
+    if _nvtx_on():
+        try:
+            torch.cuda.nvtx.range_push(name)
+            pushed = True
+        except Exception:  # profiling annotations must never fail the step
+            _NVTX_BROKEN = True
+    try:
+        yield
+    finally:
+        if pushed:
+            torch.cuda.nvtx.range_pop()
 
 
 def set_timers_enabled(flag: bool) -> None:
@@ -33,14 +62,16 @@ class TimerStats:
     @contextmanager
     def timer(self, name: str, sync: bool = False):
         if not (self.enabled and _GLOBAL_ENABLED):
-            yield
+            with nvtx_range(name):
+                yield
             return
         cuda = sync and torch.cuda.is_available() and torch.cuda.is_initialized()
         if cuda:
             torch.cuda.synchronize()
         t0 = time.perf_counter()
         try:
-            yield
+            with nvtx_range(name):
+                yield
         finally:
             if cuda:
                 torch.cuda.synchronize()
@@ -87,4 +118,4 @@ def max_over_ranks(value: float, group=None, device=None) -> float:
     return float(t.item())
 
 
-__all__ = ["DeviceTimer", "TimerStats", "max_over_ranks", "set_timers_enabled"]
+__all__ = ["DeviceTimer", "TimerStats", "max_over_ranks", "nvtx_range", "set_timers_enabled"]
