@@ -87,3 +87,38 @@ def test_launcher_runs_topk_distillation_on_cpu(tmp_path):
     assert r.returncode == 0, detail
     rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
     assert len(rows) == 2 and all("train/distill_loss" in x and x["train/teacher_topk_mass"] > 0 for x in rows), detail
+
+
+def _launch(rt, steps, *extra):
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS=str(steps), XRL_SMOKE_CKPT="1", PYTHONPATH=ROOT)
+    return subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
+                           "--runtime-dir", str(rt), "--master-port", str(_free_port()), *extra], cwd=ROOT, env=env,
+                          capture_output=True, text=True, timeout=540)
+
+
+@pytest.mark.timeout(900)
+def test_kill_and_resume_on_cpu(tmp_path):
+    """A run that stopped after two steps resumes from the newest step every participant committed: shards
+    newer than that are dropped, the step counter continues from there, and reusing the directory without
+    ``--resume`` is refused."""
+    rt = tmp_path / "rt"
+    r = _launch(rt, 2)
+    assert r.returncode == 0, r.stderr[-3000:]
+    state = rt / "state"
+    trainer_done = sorted(int(f.split("-")[1].split(".")[0]) for f in os.listdir(state / "actor_train-0")
+                          if f.endswith(".complete"))
+    rollout_done = sorted(int(f.split("-")[1].split(".")[0]) for f in os.listdir(state / "rollout-0")
+                          if f.endswith(".complete"))
+    resume_at = max(set(trainer_done) & set(rollout_done))
+    # a fresh start over a directory with checkpoints is an error
+    r = _launch(rt, 3)
+    text = r.stdout + r.stderr + "".join(f.read_text(errors="replace") for f in (rt / "logs").glob("ignitor-*.log"))
+    assert r.returncode != 0 and "--resume was not passed" in text, text[-3000:]
+    r = _launch(rt, 3, "--resume")
+    ign = (rt / "logs" / "ignitor-0.log").read_text()
+    assert r.returncode == 0, r.stderr[-3000:] + ign[-2000:]
+    if max(trainer_done) > resume_at:
+        assert f"past step {resume_at}" in ign, ign[-2000:]
+    rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
+    # the resumed run's first step follows the resume point
+    assert rows[-1]["step"] > resume_at and rows[len(rows) - 1]["step"] <= 3, rows
