@@ -34,7 +34,7 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "RL step time & trained tokens/s (JustRL 1.5B, 8 GPU); weight-sync latency"
-BASELINE_VALUE = None  # the reference publishes no number
+BASELINE_VALUE = None  # the reference publishes no number for this metric
 
 
 def parse():
@@ -58,14 +58,15 @@ def reference_arm(args):
     ref = os.path.join(ROOT, "baseline", "_ref")
     why = None
     if not os.path.isdir(ref):
-        why = "baseline/_ref not installed (reference install failed offline: see DESIGN.md)"
+        why = ("baseline/_ref not installed; the reference's rollout also needs SGLang 0.5.18, which is not "
+               "installable offline in this image")
     else:
         sys.path.insert(0, ref)
         try:
             import sglang  # noqa: F401
         except Exception:
             why = ("reference needs SGLang 0.5.18 + torch 2.13 + TransferQueue/tensordict, none installable offline "
-                   "in this image (see DESIGN.md)")
+                   "in this image")
     if why is None:
         why = "reference path not runnable on this box"
     print(json.dumps({"impl": "reference", "unavailable": why}))
