@@ -68,8 +68,25 @@ def is_equiv(pred: str | None, truth: str | None) -> bool:
     return x is not None and y is not None and x == y
 
 
+def _truth(truth) -> str | None:
+    """The ground truth as an answer string: a boxed ground truth is unwrapped."""
+    if truth is None:
+        return None
+    t = str(truth)
+    return last_boxed(t) if "\\boxed" in t or "\\fbox" in t else t
+
+
 def boxed_reward(response: str, truth: str) -> float:
-    return 1.0 if is_equiv(last_boxed(response), truth) else 0.0
+    """1 when the response's last boxed answer equals the ground truth (strict form: ``2+2`` is not ``4``)."""
+    return 1.0 if is_equiv(last_boxed(response), _truth(truth)) else 0.0
+
+
+# names of the reference's math reward entry points (``meshy/dataset/math_reward.py``)
+math_reward = boxed_reward
+
+
+def grade_answer_verl(response: str, truth: str) -> bool:
+    return boxed_reward(response, truth) == 1.0
 
 
 def gsm8k_reward(response: str, truth: str) -> float:
@@ -79,4 +96,4 @@ def gsm8k_reward(response: str, truth: str) -> float:
     return 1.0 if is_equiv(pred, t) else 0.0
 
 
-__all__ = ["boxed_reward", "gsm8k_reward", "is_equiv", "last_boxed", "normalize"]
+__all__ = ["boxed_reward", "grade_answer_verl", "gsm8k_reward", "is_equiv", "last_boxed", "math_reward", "normalize"]
