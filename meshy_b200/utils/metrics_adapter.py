@@ -123,6 +123,30 @@ def rollout_metrics(samples: Sequence[Any], seq_len: int | None = None,
         hist["response_length"] = resp_lens
     if seq_lens:
         out["rollout/seq_len/mean"] = sum(seq_lens) / len(seq_lens)
+        if seq_len:
+            out["rollout/seq_len_truncated_ratio"] = sum(1.0 for L in seq_lens if L >= seq_len) / len(seq_lens)
+    # the reference's tag names for the same quantities (meshy/backend/titan/metrics.py), so dashboards carry over
+    if "rollout/repetition_ratio" in out:
+        out["rollout/repetition_frac"] = out["rollout/repetition_ratio"]
+    if "rollout/mixed_version_ratio" in out:
+        out["rollout/weight_version/mixed_version_ratio"] = out["rollout/mixed_version_ratio"]
+    if versions and current_version is not None:
+        stale = [current_version - v for v in versions]
+        out["rollout/weight_version/stale_ratio"] = sum(1.0 for x in stale if x > 0) / len(stale)
+        out["rollout/weight_version/staleness_mean"] = sum(stale) / len(stale)
+        out["rollout/weight_version/staleness_max"] = float(max(stale))
+    if rewards:
+        out["rollout/raw_reward_mean"] = sum(rewards) / len(rewards)
+        out["rollout/rewards"] = out["rollout/raw_reward_mean"]
+    lps = []
+    for s in samples:
+        lp = _as_list(_field(s, "logprobs"))
+        mask = _as_list(_field(s, "mask_assistant")) or _as_list(_field(s, "masks"))
+        if lp and mask and len(lp) == len(mask):
+            lps.extend(float(x) for x, m in zip(lp, mask) if m)  # sampled tokens only, prompt placeholders out
+    if lps:
+        out["rollout/log_probs"] = sum(lps) / len(lps)
+        hist["rollout/log_probs"] = lps
     if rewards:
         hist["reward"] = rewards
     if adv:
