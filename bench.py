@@ -33,6 +33,7 @@ import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+PHASES = ("rollout_s", "wait_s", "train_compute_s", "optim_s")
 METRIC = "RL step time & trained tokens/s (JustRL 1.5B, 8 GPU); weight-sync latency"
 BASELINE_VALUE = None  # the reference publishes no number for this metric
 
@@ -49,34 +50,52 @@ def parse():
     p.add_argument("--resp-cap", type=int, default=8192)
     p.add_argument("--sigma", type=float, default=0.6)
     p.add_argument("--model", default="qwen2_5_math:R1-Distill-1.5B")
-    p.add_argument("--max-tokens-per-micro", type=int, default=32768)
+    p.add_argument("--max-tokens-per-micro", type=int, default=None,
+                   help="packed micro-batch token budget (default 32768; 16384 for --impl torch, whose eager "
+                        "autograd keeps every activation: 16384 is the reference recipe's seq_len with one "
+                        "sample per micro)")
     p.add_argument("--no-clocks", action="store_true")
     return p.parse_args()
 
 
 def reference_arm(args):
+    """Run the unmodified reference (``baseline/_ref``) through its public API, or say exactly why not.
+
+    The reference's headline run is ``scripts/launch.py --recipe recipe.justrl``: the Meshy control plane
+    (``meshy.service.ignite``) drives SGLang inference servers (``sglang.launch_server``) and a torchtitan
+    trainer through TransferQueue. Each module that path imports is tried in turn and the first errors are
+    reported verbatim."""
     ref = os.path.join(ROOT, "baseline", "_ref")
-    why = None
-    if not os.path.isdir(ref):
-        why = ("baseline/_ref not installed; the reference's rollout also needs SGLang 0.5.18, which is not "
-               "installable offline in this image")
-    else:
-        sys.path.insert(0, ref)
+    if not os.path.isdir(os.path.join(ref, "meshy")):
+        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed (no meshy package)"}))
+        return
+    sys.path.insert(0, ref)
+    import importlib
+
+    needed = ["meshy.config", "meshy.service.ignite", "meshy.engine.sglang", "meshy.backend.titan.trainer",
+              "meshy.transferqueue", "sglang", "sglang.srt.entrypoints.http_server", "sgl_kernel",
+              "transfer_queue", "tensordict"]
+    errors = []
+    for mod in needed:
         try:
-            import sglang  # noqa: F401
-        except Exception:
-            why = ("reference needs SGLang 0.5.18 + torch 2.13 + TransferQueue/tensordict, none installable offline "
-                   "in this image")
-    if why is None:
-        why = "reference path not runnable on this box"
-    print(json.dumps({"impl": "reference", "unavailable": why}))
+            importlib.import_module(mod)
+        except BaseException as e:  # noqa: BLE001 - report whatever the import raised
+            errors.append(f"{mod}: {type(e).__name__}: {str(e).splitlines()[0] if str(e) else ''}"[:200])
+    if errors:
+        print(json.dumps({"impl": "reference", "unavailable": "import failed -- " + "; ".join(errors)}))
+        return
+    # not reached in this image: SGLang and TransferQueue are missing, so the recipe cannot start
+    print(json.dumps({"impl": "reference", "unavailable": "every reference import succeeded, but the package install "
+                      "does not ship the reference's scripts/launch.py that starts recipe.justrl"}))
 
 
 class ClockSampler:
     def __init__(self, enabled: bool, index: int):
         self.enabled = enabled
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+        import tempfile
+
+        self.path = os.path.join(tempfile.gettempdir(), f"meshy_bench_clocks_{os.getpid()}_rank{index}.csv")
         self.index = index
 
     def __enter__(self):
@@ -140,6 +159,10 @@ def main():
     if args.impl == "reference":
         reference_arm(args)
         return
+    if args.max_tokens_per_micro is None:
+        args.max_tokens_per_micro = 16384 if args.impl == "torch" else 32768
+    if args.impl == "torch":
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     import torch
     import torch.distributed as dist
 
@@ -170,7 +193,9 @@ def main():
                              ppo_clip_eps_low=0.2, ppo_clip_eps_high=0.28, old_logprobs_source="train",
                              log_entropy=True)
     rl = ColocatedGRPO(tc, tp, device=dev, group_size=args.group, dp_group=group, seed=0,
-                       engine_kwargs=dict(max_running=args.prompts_per_gpu * args.group, page_size=64,
+                       engine_kwargs=dict(max_running=args.prompts_per_gpu * args.group,
+                                          # FlashAttention-2's paged decode (the baseline's) wants 256-token pages
+                                          page_size=256 if args.impl == "torch" else 64,
                                           max_seq_len=max_len, mem_fraction=0.25, sync_every=16))
     try:
         C = __import__("meshy_b200._C", fromlist=["_C"])
@@ -191,6 +216,7 @@ def main():
     tokens = 0
     resp_tokens = 0
     sync_ms = []
+    phases = []
     times = []
     e2e_ms = []
     h2d = d2h = 0
@@ -226,6 +252,7 @@ def main():
             tokens += rep.n_tokens
             resp_tokens += rep.n_response_tokens
             sync_ms.append(rep.times["weight_sync_ms"])
+            phases.append([rep.times.get(k, 0.0) for k in PHASES])
             del loss
         end.record()
         barrier()
@@ -235,6 +262,25 @@ def main():
         launches = C.launch_count() - launches0 + (rl.engine.stats.get("graph_kernels", 0) - graph0)
 
     from meshy_b200.utils.timer import max_over_ranks
+
+    # per-rank phase times of every timed step, gathered after the timed region: rollout (ends with the
+    # host reading the generations), wait at the step's first collective, the rest of the train phase,
+    # and the gradient reduction + optimiser buckets (CUDA-event device time)
+    ph = torch.tensor(phases, dtype=torch.float64, device=dev)
+    if world > 1:
+        allph = [torch.empty_like(ph) for _ in range(world)]
+        dist.all_gather(allph, ph)
+        ph = torch.stack(allph)  # [rank, step, phase]
+    else:
+        ph = ph[None]
+    phase_summary = {k: {"max_over_ranks_s": round(float(ph[:, :, i].max(0).values.mean()), 3),
+                         "min_over_ranks_s": round(float(ph[:, :, i].min(0).values.mean()), 3)}
+                     for i, k in enumerate(PHASES)}
+    if rank == 0:
+        for s_i in range(ph.shape[1]):
+            print(f"[bench] phases step {s_i}: " + " ".join(
+                f"{k}=[{float(ph[:, s_i, i].min()):.3f}..{float(ph[:, s_i, i].max()):.3f}]"
+                for i, k in enumerate(PHASES)), file=sys.stderr, flush=True)
 
     ms_max = max_over_ranks(ms, group, dev)
     e2e_max = max_over_ranks(sum(e2e_ms), group, dev)
@@ -285,6 +331,7 @@ def main():
             "e2e": {"value": round(e2e_value, 1), "unit": "trained tokens/s (all GPUs)",
                     "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
             "gpu_launches": launches,
+            "phases_per_step": phase_summary,
         }
         cs = clocks.summary()
         if cs is not None:

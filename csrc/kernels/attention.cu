@@ -563,7 +563,8 @@ __global__ void __launch_bounds__(NT) paged_decode_kernel(const bf16* __restrict
   const int b = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
   const int rep = Hq / Hkv;
   const int L = seq_lens[b];
-  const int n_pages = (L + page - 1) / page;
+  // never read past the row's block table, whatever seq_lens says
+  const int n_pages = min((L + page - 1) / page, max_pages);
   const int per = (n_pages + n_split - 1) / n_split;
   const int p0 = sp * per, p1 = min(n_pages, p0 + per);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;

@@ -79,6 +79,10 @@ extern "C" int meshy_paged_decode_noalloc(const void* q, const void* k_cache, co
   if (batch < 0 || n_q_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || max_pages <= 0 || n_split < 0)
     return fail("invalid size argument", 1);
   if (n_q_heads % n_kv_heads != 0) return fail("n_q_heads must be a multiple of n_kv_heads", 1);
+  if (page_size != 64) return fail("page_size must be 64 (got " + std::to_string(page_size) + ")", 1);
+  if (head_dim != 64 && head_dim != 128)
+    return fail("head_dim must be 64 or 128 (got " + std::to_string(head_dim) + ")", 1);
+  if (n_q_heads / n_kv_heads > 16) return fail("at most 16 query heads per KV head", 1);
   if (batch == 0) return 0;
   if (!q || !k_cache || !v_cache || !block_table || !seq_lens || !out) return fail("null pointer argument", 1);
   int splits = n_split;

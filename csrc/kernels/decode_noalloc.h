@@ -21,6 +21,15 @@
 //  * q [batch, n_q_heads, head_dim] bf16; k_cache / v_cache
 //    [n_pages, n_kv_heads, page_size, head_dim] bf16; block_table
 //    [batch, max_pages] int32; seq_lens [batch] int32; out like q.
+//  * Layout preconditions, checked before anything is launched (return code
+//    1 and a message otherwise): page_size == 64, head_dim 64 or 128,
+//    n_q_heads a multiple of n_kv_heads with at most 16 query heads per KV
+//    head.
+//  * Each row reads at most max_pages block-table entries, however large its
+//    seq_lens value.  The kernel does not know the cache's page count, so the
+//    caller guarantees that every block-table entry a row reads (the first
+//    ceil(seq_lens[b] / page_size) of row b, capped at max_pages) is a valid
+//    page index of k_cache / v_cache.
 //  * n_split = 0 picks the split count automatically (capped so the partials
 //    fit the array); n_split > 0 is used as given and a request whose
 //    partials do not fit is rejected with an error.

@@ -26,6 +26,7 @@ import torch
 import torch.nn as nn
 
 from ..ops._ext import ext
+from ..ops.functional import native
 
 ALIGN = 64  # elements; 128 B for bf16, 256 B for fp32
 
@@ -108,8 +109,18 @@ class FlatParams:
                     p.grad = self.grad[s.offset:s.offset + s.numel].view(s.shape)
 
     def collect_cpu_grads(self) -> None:
-        """CPU path: autograd may have replaced ``.grad``; fold it back in."""
+        """Fold gradients that autograd left in ``.grad`` into the flat fp32 buffer.
+
+        The native GEMMs accumulate straight into ``main_grad`` and leave ``.grad`` empty. The PyTorch
+        paths (the CPU oracle, and the library comparison baseline on CUDA) produce ordinary ``.grad``
+        tensors: with a separate compute dtype they are added to ``main_grad`` in fp32 and dropped, so
+        call this after every backward; without one ``.grad`` is re-pointed at the flat buffer."""
         if self.separate_compute:
+            with torch.no_grad():
+                for s, p in zip(self.slots, self.params):
+                    if p.grad is not None:
+                        p.main_grad.add_(p.grad)
+                        p.grad = None
             return
         for s, p in zip(self.slots, self.params):
             view = self.grad[s.offset:s.offset + s.numel].view(s.shape)
@@ -139,7 +150,7 @@ class FlatParams:
     # ------------------------------------------------------------------
     def grad_norm(self) -> torch.Tensor:
         """Global L2 norm of ``grad`` (device scalar, no host sync)."""
-        if self.grad.is_cuda:
+        if self.grad.is_cuda and native(self.grad):
             out = torch.zeros(1, dtype=torch.float32, device=self.device)
             ext().sq_norm(self.grad, out)
             return out.sqrt().reshape(())
@@ -173,7 +184,9 @@ class FlatAdamW:
             grad_norm = f.grad_norm()
         self.step_count += 1
         b1, b2 = self.betas
-        if f.grad.is_cuda:
+        if f.grad.is_cuda and not native(f.grad):
+            self._library_step(grad_norm)
+        elif f.grad.is_cuda:
             ext().adamw_flat(f.master, f.grad, f.exp_avg, f.exp_avg_sq,
                              f.compute if f.separate_compute else None, self.mirror, grad_norm.reshape(1),
                              float(self.max_norm), float(self.lr), float(b1), float(b2), float(self.eps),
@@ -193,6 +206,26 @@ class FlatAdamW:
                 if self.mirror is not None:
                     self.mirror.copy_(f.master)
         return grad_norm
+
+    def _library_step(self, grad_norm: torch.Tensor) -> None:
+        """Comparison baseline only: ``clip_grad_norm_``-style scaling and PyTorch's fused AdamW kernel over
+        the flat fp32 buffers, then a cast copy into the compute weights."""
+        f = self.flat
+        b1, b2 = self.betas
+        with torch.no_grad():
+            if self.max_norm and self.max_norm > 0:
+                coef = (self.max_norm / (grad_norm.float() + 1e-6)).clamp(max=1.0)
+                f.grad.mul_(coef)
+            if not hasattr(self, "_step_t"):
+                self._step_t = torch.zeros((), dtype=torch.float32, device=f.grad.device)
+            self._step_t.fill_(float(self.step_count))  # the fused kernel reads the already-advanced step
+            torch._fused_adamw_([f.master], [f.grad], [f.exp_avg], [f.exp_avg_sq], [], [self._step_t],
+                                lr=self.lr, beta1=b1, beta2=b2, weight_decay=self.weight_decay, eps=self.eps,
+                                amsgrad=False, maximize=False)
+            if f.separate_compute:
+                f.compute.copy_(f.master)
+            if self.mirror is not None:
+                self.mirror.copy_(f.master)
 
     def state_dict(self) -> dict:
         return {"step": self.step_count, "exp_avg": self.flat.exp_avg, "exp_avg_sq": self.flat.exp_avg_sq,

@@ -78,9 +78,27 @@ class _FusedPPO(torch.autograd.Function):
         return grad * gloss, None, None, None, None, None, None, None, None, None, None
 
 
+def _ess_sums(seg_w, seg_w2, cnt, cp):
+    """Effective-sample-size sums of one micro-batch.
+
+    ``seg_w`` / ``seg_w2`` are this rank's per-sequence sums of the ratio and its square. Under context
+    parallelism a sequence's tokens are spread over the ``cp`` ranks, so both are summed over the CP group
+    first; every CP rank then holds the same per-sequence ESS, and the loss group's sum (DP x CP) counts each
+    sequence ``cp`` times, which the division by the CP degree undoes (reference
+    ``meshy/backend/titan/trainer.py:826-835``)."""
+    deg = 1
+    if cp is not None and cp.size > 1:
+        both = cp.all_reduce_sum(torch.stack([seg_w, seg_w2]))
+        seg_w, seg_w2, deg = both[0], both[1], cp.size
+    ess = (seg_w * seg_w) / (cnt.clamp(min=1) * seg_w2.clamp(min=1e-8))
+    live = (cnt > 0).to(ess.dtype)
+    return (ess * live).sum() / deg, live.sum() / deg
+
+
 def ppo_clip_loss(new_lp, old_lp, batch, n_docs_global: int, n_tokens_global: int, cfg: LossConfig,
-                  entropy: torch.Tensor | None = None):
-    """Returns ``(loss, sums)``; ``sums`` is a dict of detached scalar tensors."""
+                  entropy: torch.Tensor | None = None, cp=None):
+    """Returns ``(loss, sums)``; ``sums`` is a dict of detached scalar tensors. ``cp`` is the context-parallel
+    sharder (:class:`~meshy_b200.parallel.cp.CpSharder`) when sequences are split over a CP group."""
     mask = batch.mask
     adv = batch.advantages
     if batch.adv_per_token:
@@ -100,13 +118,9 @@ def ppo_clip_loss(new_lp, old_lp, batch, n_docs_global: int, n_tokens_global: in
         loss, sums_t, seg = _FusedPPO.apply(new_lp, old_lp, adv_tok, mask, batch.rollout_logprobs, inv,
                                             pos_w_tok, entropy, batch.doc_ids, batch.n_slots, cfg)
         # ESS needs the per-sequence sums of w and w^2 (seg[:, 0:2]) and counts
-        seg_w, seg_w2 = seg[: batch.n_docs, 0], seg[: batch.n_docs, 1]
-        cnt = batch.seg_count[: batch.n_docs]
-        ess = (seg_w * seg_w) / (cnt.clamp(min=1) * seg_w2.clamp(min=1e-8))
-        live = (cnt > 0).float()
         sums = {k: sums_t[i] for i, k in enumerate(SUM_KEYS)}
-        sums["ess_sum"] = (ess * live).sum()
-        sums["doc_count"] = live.sum()
+        sums["ess_sum"], sums["doc_count"] = _ess_sums(seg[: batch.n_docs, 0], seg[: batch.n_docs, 1],
+                                                       batch.seg_count[: batch.n_docs], cp)
         if batch.rollout_logprobs is None:
             sums.pop("train_rollout_kl_sum")
             sums.pop("train_rollout_logdiff_abs_sum")
@@ -139,8 +153,7 @@ def ppo_clip_loss(new_lp, old_lp, batch, n_docs_global: int, n_tokens_global: in
         seg_w = torch.zeros(batch.n_slots, dtype=r.dtype, device=r.device).index_add_(0, flat, r * mask)
         seg_w2 = torch.zeros(batch.n_slots, dtype=r.dtype, device=r.device).index_add_(0, flat, r * r * mask)
         n = batch.n_docs
-        cnt = batch.seg_count[:n]
-        ess = (seg_w[:n] ** 2) / (cnt.clamp(min=1) * seg_w2[:n].clamp(min=1e-8))
+        ess_sum, doc_count = _ess_sums(seg_w[:n], seg_w2[:n], batch.seg_count[:n], cp)
         sums = {
             "loss": pg_loss.detach(),
             "total_loss": loss.detach(),
@@ -152,8 +165,8 @@ def ppo_clip_loss(new_lp, old_lp, batch, n_docs_global: int, n_tokens_global: in
             "token_count": mask.sum(),
             "ppo_kl_sum": (-lr_ * mask).sum(),
             "log_ratio_abs_sum": (lr_.abs() * mask).sum(),
-            "ess_sum": ess[cnt > 0].sum(),
-            "doc_count": (cnt > 0).float().sum(),
+            "ess_sum": ess_sum,
+            "doc_count": doc_count,
         }
         if batch.rollout_logprobs is not None:
             train_lp = old_lp if cfg.train_old else new_lp.detach()

@@ -139,6 +139,10 @@ class PPOTrainer:
 
         if os.environ.get("MESHY_DP_FUSED", "auto") == "0" or self.device.type != "cuda":
             return False
+        from ..ops.functional import native
+
+        if not native(self.flat.grad):  # library comparison baseline: NCCL all-reduce + PyTorch AdamW
+            return False
         if self.ep_group is not None:  # expert slices differ per rank: keep the range-aware reducer
             return False
         g = self.loss_group
@@ -279,7 +283,7 @@ class PPOTrainer:
             with timer.timer("train/forward"):
                 new_lp, ent = self.forward_batch(b, with_entropy=self.params.log_entropy)
                 loss, mb_sums = ppo_clip_loss(new_lp, old_lp, b, mini.n_docs_global, mini.n_tokens_global,
-                                              self.loss_cfg, entropy=ent)
+                                              self.loss_cfg, entropy=ent, cp=self.cp)
             with timer.timer("train/backward"):
                 if micro.is_filler:
                     loss = loss * 0.0
@@ -287,8 +291,8 @@ class PPOTrainer:
                 if last:
                     self.reducer.arm()
                 loss.backward()
+                self.flat.collect_cpu_grads()  # PyTorch paths only: fold .grad into the fp32 buffer
             sums = mb_sums if sums is None else {k: sums[k] + v for k, v in mb_sums.items()}
-        self.flat.collect_cpu_grads()
         with timer.timer("train/grad_reduce"):
             for off, n in self.tp_partial:
                 dist.all_reduce(self.flat.grad[off:off + n], group=self.tp_group)

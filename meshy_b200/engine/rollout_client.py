@@ -184,6 +184,14 @@ class EngineClient(_Base):
         self._mgmt("POST", "/update_weights_from_ipc", json={"handle": handle, "weight_version": version},
                    timeout=1800.0)
 
+    def load_weights_ipc_set(self, ref: str) -> None:
+        """Every engine maps the trainer snapshot exported on its own GPU (``ipc-set:`` reference)."""
+        from ..rollout.weight_sync import decode_handle_set
+
+        doc = decode_handle_set(ref)
+        self._mgmt("POST", "/update_weights_from_ipc", json={"handles": doc["handles"],
+                                                              "weight_version": doc["version"]}, timeout=1800.0)
+
     def release_for_colocate(self) -> None:
         self.pause_generation()
         self.wait_until_idle()
@@ -192,7 +200,9 @@ class EngineClient(_Base):
     def restore_for_colocate(self, payload_ref: str | None) -> None:
         self.resume_memory(("weights",))
         if payload_ref:
-            if payload_ref.startswith("ipc:"):
+            if payload_ref.startswith("ipc-set:"):
+                self.load_weights_ipc_set(payload_ref)
+            elif payload_ref.startswith("ipc:"):
                 self.load_weights_ipc(payload_ref[4:])
             else:
                 self.load_weights(payload_ref)

@@ -134,11 +134,26 @@ class TrainerEngine(SpmdEngine):
 
     # ------------------------------------------------------------------ weights
     def publish_weights(self) -> str | None:
-        mode = self.weight_sync_mode
-        if mode in ("auto", "device") and self.device.type == "cuda" and self.world_size == 1:
-            from ..rollout.weight_sync import export_ipc_flat
+        """Make this step's weights available to the inference engines; returns the reference that travels
+        through the colocation ring as ``payload_ref`` (rank 0; other ranks return ``None``).
 
-            return "ipc:" + export_ipc_flat(self.trainer.flat.master)
+        Device path (``weight_sync_mode`` ``device``, or ``auto`` when every trainer rank and the engines
+        share one node): every rank casts its fp32 master weights into a bf16 snapshot in the engines'
+        flat layout (:class:`~meshy_b200.rollout.weight_sync.DevicePublisher`) and exports a CUDA IPC handle
+        of it; rank 0 gathers the handles keyed by GPU UUID into one ``ipc-set:`` reference, and each
+        engine copies the snapshot of the trainer rank on its own GPU. No disk, no gather of weights.
+        Disk path: an HF safetensors export (also the checkpoint format), as the reference does for
+        every sync (``meshy/engine/titan.py:80-123``)."""
+        mode = self.weight_sync_mode
+        if mode in ("auto", "device") and self.device.type == "cuda" and self._replicated_weights() and (
+                mode == "device" or self._single_node()):
+            from ..rollout.weight_sync import DevicePublisher, encode_handle_set
+
+            if getattr(self, "_publisher", None) is None:
+                self._publisher = DevicePublisher(self.trainer.flat, self.device)
+            entry = self._publisher.publish(self.version)
+            entries = self.gather_objects(entry)
+            return encode_handle_set(entries) if self.rank == 0 else None
         if self.runtime is None:
             return None
         path = self.runtime.checkpoint_path(self.service_name, self.version)
@@ -147,6 +162,35 @@ class TrainerEngine(SpmdEngine):
             self.prune_weights()
         self.barrier()
         return path
+
+    def _replicated_weights(self) -> bool:
+        """Whether every rank holds the whole model (DP / CP): expert- or tensor-parallel ranks hold parts."""
+        t = self.trainer
+        sharded = [g for g in (t.ep_group, t.tp_group) if g is not None and torch.distributed.is_initialized()
+                   and torch.distributed.get_world_size(g) > 1]
+        return not sharded
+
+    def _single_node(self) -> bool:
+        """Whether every rank of this replica runs on this host (the IPC handles only open there)."""
+        if self.world_size == 1:
+            return True
+        if getattr(self, "_hosts_same", None) is None:
+            import socket
+
+            hosts = self.gather_objects(socket.gethostname())
+            same = None
+            if self.rank == 0:
+                same = len(set(hosts)) == 1
+            self._hosts_same = bool(self.broadcast_object(same))
+        return self._hosts_same
+
+    def gather_objects(self, obj) -> list | None:
+        """Every rank's ``obj`` on rank 0 (``None`` elsewhere), over the gloo control group."""
+        if self.world_size == 1 or not torch.distributed.is_initialized():
+            return [obj]
+        out = [None] * self.world_size if self.rank == 0 else None
+        torch.distributed.gather_object(obj, out, dst=0, group=self.control_group)
+        return out
 
     def prune_weights(self) -> list[int]:
         if self.runtime is None or self.weights_keep_latest_k <= 0:
@@ -170,6 +214,12 @@ class TrainerEngine(SpmdEngine):
     # ------------------------------------------------------------------ checkpoints
     def save_global_checkpoint(self, step: int) -> None:
         store = self.runtime.state_store()
+        # a resumed run boots its engines from the HF export of the checkpointed weight version; with
+        # device weight sync no per-step export exists, so the checkpoint writes that one
+        path = self.runtime.checkpoint_path(self.service_name, self.version)
+        if self.rank == 0 and not os.path.isdir(path):
+            self.trainer.export_hf(path)
+            self.prune_weights()
         self.trainer.save_checkpoint(store.shard_dir(self.service_name, step), step)
         if self.rank == 0:
             store.write_meta(self.service_name, step, {"step_index": self.step_index, "weight_version": self.version,

@@ -136,7 +136,24 @@ def paged_attention(q, k_cache, v_cache, block_table, seq_lens, scale=None, work
         ext().paged_attention(q, k_cache, v_cache, block_table, seq_lens, out, float(scale), workspace,
                               bool(decode_step))
         return out
+    if q.is_cuda:
+        return _library_paged_decode(q, k_cache, v_cache, block_table, seq_lens, scale)
     return ref.attention_decode_paged(q, k_cache, v_cache, block_table, seq_lens, scale)
+
+
+def _library_paged_decode(q, k_cache, v_cache, block_table, seq_lens, scale):
+    """Comparison baseline only: FlashAttention-2's paged KV-cache kernel (``flash_attn_with_kvcache``),
+    the library kernel an SGLang/vLLM-class engine runs. It reads the cache through the block table with
+    device-side lengths, so a decode step stays graph-capturable. It needs pages of a multiple of 256
+    tokens; the cache ``[n_pages, Hkv, page, hd]`` is handed over as the strided view
+    ``[n_pages, page, Hkv, hd]``."""
+    from flash_attn import flash_attn_with_kvcache
+
+    kc = k_cache.permute(0, 2, 1, 3)
+    vc = v_cache.permute(0, 2, 1, 3)
+    out = flash_attn_with_kvcache(q.unsqueeze(1), kc, vc, cache_seqlens=seq_lens, block_table=block_table,
+                                  softmax_scale=scale, causal=True)
+    return out.squeeze(1)
 
 
 def sample(h, w, temperature: float, *, top_k: int = -1, top_p: float = 1.0, seed: int = 0,
@@ -154,8 +171,19 @@ def sample(h, w, temperature: float, *, top_k: int = -1, top_p: float = 1.0, see
         lp = torch.empty(B, dtype=torch.float32, device=h.device)
         ext().lmhead_sample(h, w, tok, lp, float(temperature), int(seed), step)
         return tok, lp
+    if h.is_cuda and temperature > 0 and top_k <= 0 and top_p >= 1.0:
+        return _library_sample(h, w, temperature)
     logits = h.float() @ w.float().t() if not h.is_cuda else torch.nn.functional.linear(h, w).float()
     return ref.sample_with_logprob(logits, temperature, generator=generator, top_k=top_k, top_p=top_p)
+
+
+def _library_sample(h, w, temperature: float):
+    """Comparison baseline only: cuBLAS logits, log-softmax, and an exponential-race draw
+    (``argmax p / E`` with ``E ~ Exp(1)`` samples from ``p``), which stays graph-capturable."""
+    logp = torch.log_softmax(torch.nn.functional.linear(h, w).float() / temperature, dim=-1)
+    e = torch.empty_like(logp).exponential_()
+    tok = (logp - e.log()).argmax(-1)
+    return tok, logp.gather(-1, tok.unsqueeze(-1)).squeeze(-1)
 
 
 def sample_advance(state: dict, h, w, temperature: float, *, seed: int, page_size: int, part=None, d: int = 0,
@@ -190,6 +218,9 @@ def decode_advance(state: dict, tok, lp, page_size: int):
                              state["max_new"], state["done"], state["slot"], state["block_table"],
                              state["req"], state["out_tok"], state["out_lp"], state["eos"], int(page_size))
         return
+    if tok.is_cuda:
+        _advance_masked(state, tok, lp, page_size)
+        return
     live = state["done"] == 0
     rows = torch.nonzero(live).flatten()
     if rows.numel() == 0:
@@ -209,6 +240,32 @@ def decode_advance(state: dict, tok, lp, page_size: int):
     p = state["pos"][rows].long()
     pg = state["block_table"][rows, p // page_size].long()
     state["slot"][rows] = pg * page_size + p % page_size
+
+
+def _advance_masked(st: dict, tok, lp, page_size: int) -> None:
+    """:func:`decode_advance` in torch ops with no host synchronisation (comparison baseline on CUDA, so
+    its decode step can be graph-captured): every row is updated and finished rows keep their values."""
+    B = tok.shape[0]
+    live = st["done"][:B] == 0
+    # rows that are not live write into the spare last output row, so they never collide with a live row
+    trash = st["out_tok"].shape[0] - 1
+    r = torch.where(live, st["req"][:B].long(), trash)
+    g = torch.where(live, st["gen"][:B].long().clamp(max=st["out_tok"].shape[1] - 1), 0)
+    st["out_tok"][r, g] = tok
+    st["out_lp"][r, g] = lp.to(st["out_lp"].dtype)
+    inc = live.to(st["gen"].dtype)
+    st["gen"][:B] += inc
+    st["tok_in"][:B] = torch.where(live, tok.to(st["tok_in"].dtype), st["tok_in"][:B])
+    fin = st["gen"][:B] >= st["max_new"][:B]
+    if st["eos"].numel():
+        fin |= (tok.unsqueeze(-1) == st["eos"].unsqueeze(0)).any(-1)
+    st["done"][:B] = torch.where(live, fin.to(st["done"].dtype), st["done"][:B])
+    st["pos"][:B] += inc.to(st["pos"].dtype)
+    st["seq_lens"][:B] += inc.to(st["seq_lens"].dtype)
+    p = st["pos"][:B].long()
+    pi = (p // page_size).clamp(max=st["block_table"].shape[1] - 1)
+    pg = st["block_table"][:B].gather(1, pi.unsqueeze(1)).squeeze(1).long()
+    st["slot"][:B] = torch.where(live, (pg * page_size + p % page_size).to(st["slot"].dtype), st["slot"][:B])
 
 
 __all__ = ["decode_advance", "kv_write", "linear_norm_prep", "linear_norm_scaled", "paged_attention",

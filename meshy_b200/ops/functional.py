@@ -312,9 +312,20 @@ def flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen: int, scale: float | None 
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if native(q):
         return _FlashAttnVarlen.apply(q, k, v, cu_seqlens, max_seqlen, scale)
-    if q.is_cuda:  # torch baseline: SDPA per document batch
-        return _sdpa_varlen(q, k, v, cu_seqlens, scale)
+    if q.is_cuda:  # torch baseline: PyTorch's FlashAttention varlen kernel
+        return _torch_varlen(q, k, v, cu_seqlens, max_seqlen, scale)
     return _RefAttn.apply(q, k, v, cu_seqlens, scale)
+
+
+def _torch_varlen(q, k, v, cu, max_seqlen, scale):
+    """Comparison baseline: causal varlen attention through ``torch.nn.attention.varlen`` (FlashAttention
+    inside PyTorch, differentiable, GQA by head count), else SDPA per document."""
+    try:
+        from torch.nn.attention.varlen import varlen_attn
+    except ImportError:  # older PyTorch
+        return _sdpa_varlen(q, k, v, cu, scale)
+    cu32 = cu.to(torch.int32)
+    return varlen_attn(q, k, v, cu32, cu32, int(max_seqlen), int(max_seqlen), scale=scale, window_size=(-1, 0))
 
 
 class _FlashAttnKV(torch.autograd.Function):

@@ -128,12 +128,17 @@ class ColocatedGRPO:
         lengths, loss_tokens = t.sample_lengths(samples, t.config.seq_len)
         plan: Plan = build_plan(lengths, loss_tokens, 1, t.planner_config)
         minis = list(plan.per_rank[0])
+        self.last_wait_s = 0.0
         if self.dp_group is not None and dist.is_initialized() and dist.get_world_size(self.dp_group) > 1:
             dev = self.device if dist.get_backend(self.dp_group) == "nccl" else torch.device("cpu")
             cnt = torch.tensor([[m.n_docs_global, m.n_tokens_global] for m in minis], dtype=torch.float64,
                                device=dev)
+            # the step's first cross-rank collective: a rank whose rollout finished early waits here for the
+            # slowest one (the all-reduce plus the read-back is host-synchronous, so this is device time)
+            t_wait = time.perf_counter()
             dist.all_reduce(cnt, group=self.dp_group)
             cnt = cnt.cpu().long().tolist()
+            self.last_wait_s = time.perf_counter() - t_wait
             minis = [MiniPlan(m.micros, c[0], c[1], m.tokens_per_rank) for m, c in zip(minis, cnt)]
         return plan.local_samples(samples, 0), minis
 
@@ -151,6 +156,10 @@ class ColocatedGRPO:
             local, minis = self.plan_local(samples)
             metrics = self.trainer.train_step(local, plan=minis)
         times["train_s"] = time.perf_counter() - t1
+        times["wait_s"] = getattr(self, "last_wait_s", 0.0)
+        times["optim_s"] = float(metrics.get("time/train/optim_step", 0.0)) + float(
+            metrics.get("time/train/grad_reduce", 0.0))
+        times["train_compute_s"] = times["train_s"] - times["wait_s"]
         self.version += 1
         with nvtx_range("rl/weight_sync"):
             times["weight_sync_ms"] = self.sync_weights()

@@ -206,8 +206,9 @@ class RolloutEngine:
             "slot": torch.zeros(B, dtype=i64, device=dev),
             "block_table": torch.zeros(B, self.max_pages_per_seq, dtype=i32, device=dev),
             "req": torch.arange(B, dtype=i32, device=dev),
-            "out_tok": torch.zeros(R, self.max_new_cap, dtype=i64, device=dev),
-            "out_lp": torch.zeros(R, self.max_new_cap, dtype=torch.float32, device=dev),
+            # one spare row past the R output slots: a write that must land nowhere goes there
+            "out_tok": torch.zeros(R + 1, self.max_new_cap, dtype=i64, device=dev),
+            "out_lp": torch.zeros(R + 1, self.max_new_cap, dtype=torch.float32, device=dev),
             "eos": torch.tensor(self.eos, dtype=i64, device=dev),
             "noeos": torch.zeros(0, dtype=i64, device=dev),
             "step": torch.zeros(1, dtype=i64, device=dev),
@@ -269,7 +270,7 @@ class RolloutEngine:
                 raise ValueError("flat weight layout mismatch")
             if src.dtype == self.weight_flat.dtype:
                 self.weight_flat.copy_(src, non_blocking=True)
-            elif src.is_cuda:
+            elif src.is_cuda and Fx.native(src):
                 from ..ops._ext import ext
 
                 ext().cast_copy(src, self.weight_flat)

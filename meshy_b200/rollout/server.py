@@ -139,8 +139,12 @@ def build_app(runner: EngineRunner, model_name: str = ""):
         return web.json_response({"loads": [eng.loads()]})
 
     async def info(req):
-        return web.json_response({"model_path": model_name, "weight_version": eng.weight_version,
-                                  "max_running": eng.max_running})
+        out = {"model_path": model_name, "weight_version": eng.weight_version, "max_running": eng.max_running}
+        if eng.cuda:
+            from .weight_sync import device_uuid
+
+            out["gpu_uuid"] = device_uuid(eng.device)
+        return web.json_response(out)
 
     async def pause(req):
         body = await req.json() if req.can_read_body else {}
@@ -169,21 +173,31 @@ def build_app(runner: EngineRunner, model_name: str = ""):
         return web.json_response({"ok": True, "seconds": time.perf_counter() - t0})
 
     async def load_ipc(req):
+        """``{handle}``: one exported buffer; ``{handles: {gpu_uuid: handle}}``: one per trainer rank, of
+        which this server maps the one exported on its own GPU (see ``weight_sync.pick_handle``)."""
         body = await req.json()
-        from .weight_sync import open_ipc_flat
+        from .weight_sync import device_uuid, open_ipc_flat, pick_handle
 
         t0 = time.perf_counter()
+        local = True
 
         def do():
-            src = open_ipc_flat(body["handle"])
+            nonlocal local
+            handle = body.get("handle")
+            if handle is None:
+                handle, local = pick_handle(body["handles"], device_uuid(eng.device))
+            src = open_ipc_flat(handle)
             eng.update_weights_from_flat(src, body.get("weight_version"))
             if eng.cuda:
                 import torch
 
                 torch.cuda.synchronize(eng.device)
+            del src
 
         await asyncio.to_thread(do)
-        return web.json_response({"ok": True, "seconds": time.perf_counter() - t0})
+        dt = time.perf_counter() - t0
+        print(f"[weight-sync] ipc version {body.get('weight_version')} local={local} {dt * 1e3:.2f} ms", flush=True)
+        return web.json_response({"ok": True, "seconds": dt, "local": local})
 
     app = web.Application(client_max_size=1 << 30)
     app.add_routes([

@@ -1,24 +1,32 @@
-"""Trainer → rollout-engine weight synchronisation paths.
+"""Trainer → rollout-engine weight synchronisation.
 
-Both sides lay parameters out identically in one flat buffer
+Trainer and engines lay parameters out identically in one flat buffer
 (:func:`meshy_b200.backend.flat.flatten_module`), so a sync never re-keys or
-re-shapes anything:
+re-shapes anything. Three routes, fastest first:
 
-* same process (colocated :class:`~meshy_b200.rl.ColocatedGRPO`): one cast
-  kernel from the fp32 master buffer into the engine's bf16 buffer, or the
-  AdamW kernel writes the engine buffer directly (``FlatAdamW.mirror``);
-* same node, different process: the trainer exports its buffer as a CUDA IPC
-  handle (:func:`export_ipc_flat`); the engine maps it (:func:`open_ipc_flat`)
-  and copies device-to-device;
-* different node / resharding (FSDP shards → full replicas): the NVLink
-  reshard kernel in :mod:`meshy_b200.parallel.reshard`;
-* disk: HF safetensors export + ``/update_weights_from_disk`` (checkpoint
-  format, and the fallback the reference uses for every sync).
+* same process (:class:`~meshy_b200.rl.ColocatedGRPO`): one cast kernel from
+  the fp32 master buffer into the engine's bf16 buffer;
+* same node, other processes (the launcher's services, any DP size): every
+  trainer rank keeps a bf16 snapshot of its weights in the engines' layout
+  (:class:`DevicePublisher`; one cast kernel per publish) and exports a CUDA
+  IPC handle of it. Rank 0 gathers the handles, keyed by GPU UUID, into one
+  ``ipc-set:`` reference (:func:`encode_handle_set`) that travels through the
+  colocation ring as ``payload_ref``. Each engine server maps the handle of
+  the trainer rank on its own GPU (:func:`pick_handle`) and copies the
+  snapshot into its weight buffer: one device-to-device copy, no disk. DDP
+  ranks hold identical weights, so any rank's snapshot is a full replica;
+* disk: HF safetensors export + ``/update_weights_from_disk`` (the checkpoint
+  format, and what the reference does for every sync,
+  ``meshy/engine/titan.py:80-123`` / ``meshy/engine/sglang.py:289-300``).
+
+The reference has no device route; it gathers the full state dict to rank 0
+and writes safetensors every step.
 """
 
 from __future__ import annotations
 
 import base64
+import json
 import pickle
 
 import torch
@@ -38,4 +46,69 @@ def open_ipc_flat(handle: str) -> torch.Tensor:
     return fn(*args)
 
 
-__all__ = ["export_ipc_flat", "open_ipc_flat"]
+def device_uuid(device: torch.device | int | None = None) -> str:
+    """Stable identity of a GPU across processes (CUDA_VISIBLE_DEVICES renumbers ordinals, UUIDs stay)."""
+    return str(torch.cuda.get_device_properties(device if device is not None else torch.cuda.current_device()).uuid)
+
+
+class DevicePublisher:
+    """One trainer rank's published weights: two bf16 snapshots used alternately.
+
+    ``publish(version)`` casts the fp32 master weights into the snapshot of
+    ``version % 2`` and returns ``(gpu_uuid, version, handle)``. Two buffers let
+    an engine still copying version ``v`` overlap the trainer publishing
+    ``v + 1``. The snapshots stay on the GPU while the trainer is offloaded
+    (2 bytes per parameter each)."""
+
+    def __init__(self, flat, device):
+        self.flat = flat
+        self.device = torch.device(device)
+        self.uuid = device_uuid(self.device)
+        self._bufs: list[torch.Tensor | None] = [None, None]
+        self._handles: list[str | None] = [None, None]
+
+    def publish(self, version: int) -> tuple[str, int, str]:
+        i = version % 2
+        if self._bufs[i] is None:
+            self._bufs[i] = torch.empty(self.flat.numel, dtype=torch.bfloat16, device=self.device)
+            self._handles[i] = export_ipc_flat(self._bufs[i])
+        src = self.flat.master
+        from ..ops.functional import native
+
+        if native(src):
+            from ..ops._ext import ext
+
+            ext().cast_copy(src, self._bufs[i])
+        else:
+            self._bufs[i].copy_(src)
+        torch.cuda.current_stream(self.device).synchronize()  # the snapshot is complete before it is announced
+        return self.uuid, int(version), self._handles[i]
+
+
+def encode_handle_set(entries) -> str:
+    """``[(gpu_uuid, version, handle), ...]`` of every trainer rank → one ``ipc-set:`` reference."""
+    versions = {int(v) for _, v, _ in entries}
+    if len(versions) != 1:
+        raise ValueError(f"trainer ranks published different weight versions: {sorted(versions)}")
+    doc = {"version": versions.pop(), "handles": {u: h for u, _, h in entries}}
+    return "ipc-set:" + json.dumps(doc, separators=(",", ":"))
+
+
+def decode_handle_set(ref: str) -> dict:
+    if not ref.startswith("ipc-set:"):
+        raise ValueError("not an ipc-set reference")
+    return json.loads(ref[len("ipc-set:"):])
+
+
+def pick_handle(handles: dict[str, str], my_uuid: str) -> tuple[str, bool]:
+    """The handle exported on this engine's GPU if there is one (``local=True``), else a peer GPU's (read
+    over NVLink; any DDP rank's snapshot holds the same weights)."""
+    if my_uuid in handles:
+        return handles[my_uuid], True
+    if not handles:
+        raise ValueError("empty handle set")
+    return handles[sorted(handles)[0]], False
+
+
+__all__ = ["DevicePublisher", "decode_handle_set", "device_uuid", "encode_handle_set", "export_ipc_flat",
+           "open_ipc_flat", "pick_handle"]

@@ -1,140 +1,176 @@
-"""Global checkpoint shards and resume-point derivation.
+"""Global checkpoints of a run: per-service shards with a commit protocol, and the resume point.
 
-Layout per service: ``state/{svc}/step-N/`` (the shard: DCP directory or role
-files), ``step-N.json`` (sidecar: counters, weight version ...) and
-``step-N.complete`` (commit marker, written last, fsync'd and renamed into
-place).  The resume point is the newest step at which every participant
-committed — an intersection, so nobody has to coordinate (reference
-``meshy/service/checkpoint.py:1-246``).
+On-disk format (kept from the reference, ``meshy/service/checkpoint.py``, so
+a run directory reads the same under both)::
+
+    state/<service>/step-<n>/           the shard (a DCP directory or role files)
+    state/<service>/step-<n>.json       sidecar {service, global_step, created_at, payload}
+    state/<service>/step-<n>.complete   commit marker
+
+Commit protocol: a writer fills the shard, writes the sidecar, and writes the
+marker last; each file goes to a temporary name, is fsync'd and renamed, so a
+crash leaves either a committed step or an uncommitted one, never a torn
+marker. Removal inverts the order (marker first), so a half-removed step is
+never mistaken for a committed one.
+
+Resume point: the newest step that *every* service taking part at that step
+committed. Each service commits on its own schedule, so this is an
+intersection computed from one directory scan per service; nobody
+coordinates at save time.
 """
 
 from __future__ import annotations
 
 import json
 import os
-import re
 import shutil
 import time
 from typing import Any, Callable, Iterable, Sequence
 
 RESUME_ENV = "XRL_RESUME"
 RESUME_STEP_ENV = "XRL_RESUME_STEP"
-_COMPLETE_RE = re.compile(r"^step-(\d+)\.complete$")
+
+_MARK = ".complete"
+_SIDECAR = ".json"
+_PREFIX = "step-"
 
 
 def resume_requested() -> bool:
-    return os.environ.get(RESUME_ENV, "").strip().lower() not in ("", "0", "false", "no")
+    """``XRL_RESUME`` set to anything but empty / 0 / false / no."""
+    return os.environ.get(RESUME_ENV, "").strip().lower() not in {"", "0", "false", "no"}
 
 
-def _atomic_write(path: str, text: str) -> None:
-    os.makedirs(os.path.dirname(path), exist_ok=True)
-    tmp = f"{path}.tmp"
-    with open(tmp, "w", encoding="utf-8") as f:
-        f.write(text)
-        f.flush()
-        os.fsync(f.fileno())
-    os.replace(tmp, path)
+def run_resume_step() -> int:
+    """The resume step the ignitor published for this run (0 = fresh start)."""
+    raw = os.environ.get(RESUME_STEP_ENV) or "0"
+    return int(raw)
+
+
+def _durable_write(path: str, text: str) -> None:
+    parent = os.path.dirname(path)
+    os.makedirs(parent, exist_ok=True)
+    staging = path + ".partial"
+    fd = os.open(staging, os.O_WRONLY | os.O_CREAT | os.O_TRUNC, 0o644)
+    try:
+        os.write(fd, text.encode("utf-8"))
+        os.fsync(fd)
+    finally:
+        os.close(fd)
+    os.rename(staging, path)
+
+
+def _step_of(entry: str, suffix: str) -> int | None:
+    """``step-<n><suffix>`` -> n, anything else -> None."""
+    if not (entry.startswith(_PREFIX) and entry.endswith(suffix)):
+        return None
+    digits = entry[len(_PREFIX):len(entry) - len(suffix)]
+    return int(digits) if digits.isdigit() else None
 
 
 class StateStore:
+    """The ``state/`` directory of a run."""
+
     def __init__(self, state_dir: str):
         self.root = os.path.abspath(state_dir)
 
+    # ------------------------------------------------------------------ paths
     def service_dir(self, service: str) -> str:
         return os.path.join(self.root, service)
 
+    def _base(self, service: str, step: int) -> str:
+        return os.path.join(self.service_dir(service), "%s%d" % (_PREFIX, int(step)))
+
     def shard_dir(self, service: str, step: int) -> str:
-        return os.path.join(self.service_dir(service), f"step-{int(step)}")
+        return self._base(service, step)
 
     def meta_path(self, service: str, step: int) -> str:
-        return os.path.join(self.service_dir(service), f"step-{int(step)}.json")
+        return self._base(service, step) + _SIDECAR
 
-    def _complete_path(self, service: str, step: int) -> str:
-        return os.path.join(self.service_dir(service), f"step-{int(step)}.complete")
+    def marker_path(self, service: str, step: int) -> str:
+        return self._base(service, step) + _MARK
 
+    # ------------------------------------------------------------------ commit
     def write_meta(self, service: str, step: int, payload: dict[str, Any]) -> str:
-        doc = {"service": service, "global_step": int(step), "created_at": time.time(), "payload": payload}
         path = self.meta_path(service, step)
-        _atomic_write(path, json.dumps(doc, indent=2, sort_keys=True))
+        doc = {"created_at": time.time(), "global_step": int(step), "payload": payload, "service": service}
+        _durable_write(path, json.dumps(doc, indent=2, sort_keys=True))
         return path
 
     def mark_complete(self, service: str, step: int) -> None:
-        _atomic_write(self._complete_path(service, step), str(int(step)))
+        _durable_write(self.marker_path(service, step), str(int(step)))
 
+    # ------------------------------------------------------------------ queries
     def read_meta(self, service: str, step: int) -> dict | None:
         try:
             with open(self.meta_path(service, step), encoding="utf-8") as f:
                 return json.load(f)
-        except (FileNotFoundError, NotADirectoryError, json.JSONDecodeError):
+        except (OSError, ValueError):
             return None
 
     def payload(self, service: str, step: int) -> dict:
-        return dict((self.read_meta(service, step) or {}).get("payload") or {})
+        doc = self.read_meta(service, step) or {}
+        return dict(doc.get("payload") or {})
+
+    def _entries(self, path: str) -> list[str]:
+        try:
+            return os.listdir(path)
+        except (FileNotFoundError, NotADirectoryError):
+            return []
 
     def complete_steps(self, service: str) -> list[int]:
-        try:
-            entries = os.listdir(self.service_dir(service))
-        except (FileNotFoundError, NotADirectoryError):
-            return []
-        return sorted(int(m.group(1)) for m in map(_COMPLETE_RE.match, entries) if m)
+        found = (_step_of(e, _MARK) for e in self._entries(self.service_dir(service)))
+        return sorted(s for s in found if s is not None)
 
     def is_complete(self, service: str, step: int) -> bool:
-        return os.path.exists(self._complete_path(service, step))
+        return os.path.isfile(self.marker_path(service, step))
 
     def known_services(self) -> list[str]:
-        try:
-            return sorted(n for n in os.listdir(self.root) if os.path.isdir(os.path.join(self.root, n)))
-        except (FileNotFoundError, NotADirectoryError):
-            return []
+        return sorted(e for e in self._entries(self.root) if os.path.isdir(os.path.join(self.root, e)))
 
     def has_any_shard(self) -> bool:
-        return any(self.complete_steps(s) for s in self.known_services())
+        return any(self.complete_steps(svc) for svc in self.known_services())
+
+    # ------------------------------------------------------------------ removal
+    def drop(self, service: str, step: int) -> None:
+        """Uncommit first (marker), then the sidecar and the shard."""
+        for path in (self.marker_path(service, step), self.meta_path(service, step)):
+            if os.path.lexists(path):
+                os.remove(path)
+        shutil.rmtree(self.shard_dir(service, step), ignore_errors=True)
 
     def prune(self, service: str, keep_latest_k: int) -> list[int]:
+        """Drop all but the newest ``keep_latest_k`` committed steps of ``service`` (k <= 0 keeps all)."""
         if keep_latest_k <= 0:
             return []
-        stale = self.complete_steps(service)[:-keep_latest_k]
-        for s in stale:
+        steps = self.complete_steps(service)
+        old = steps[:max(0, len(steps) - keep_latest_k)]
+        for s in old:
             self.drop(service, s)
-        return stale
+        return old
 
     def drop_newer_than(self, step: int) -> dict[str, list[int]]:
-        dropped = {}
+        """Remove every service's commits past ``step`` (a resumed run rewrites them)."""
+        removed: dict[str, list[int]] = {}
         for svc in self.known_services():
-            stale = [s for s in self.complete_steps(svc) if s > step]
-            for s in stale:
+            newer = [s for s in self.complete_steps(svc) if s > step]
+            for s in newer:
                 self.drop(svc, s)
-            if stale:
-                dropped[svc] = stale
-        return dropped
-
-    def drop(self, service: str, step: int) -> None:
-        for p in (self._complete_path(service, step), self.meta_path(service, step)):
-            try:
-                os.remove(p)
-            except FileNotFoundError:
-                pass
-        shutil.rmtree(self.shard_dir(service, step), ignore_errors=True)
+            if newer:
+                removed[svc] = newer
+        return removed
 
 
 def resolve_resume_step(store: StateStore, participants_at: Callable[[int], Sequence[str]], *,
                         candidates: Iterable[int] | None = None) -> int:
-    """Newest step every participant completed; 0 when none (fresh start)."""
-    if candidates is None:
-        seen: set[int] = set()
-        for svc in store.known_services():
-            seen.update(store.complete_steps(svc))
-        candidates = seen
-    for step in sorted(candidates, reverse=True):
-        who = participants_at(step)
-        if who and all(store.is_complete(s, step) for s in who):
+    """Newest step at which every participant (``participants_at(step)``) committed; 0 if none."""
+    committed = {svc: set(store.complete_steps(svc)) for svc in store.known_services()}
+    pool = set(candidates) if candidates is not None else set().union(*committed.values()) if committed else set()
+    for step in sorted(pool, reverse=True):
+        who = list(participants_at(step))
+        if who and all(step in committed.get(svc, ()) for svc in who):
             return int(step)
     return 0
 
 
-def run_resume_step() -> int:
-    """The resume step the ignitor published for this run (0 = fresh)."""
-    return int(os.environ.get(RESUME_STEP_ENV, "0") or 0)
-
-
-__all__ = ["RESUME_ENV", "RESUME_STEP_ENV", "StateStore", "resolve_resume_step", "resume_requested", "run_resume_step"]
+__all__ = ["RESUME_ENV", "RESUME_STEP_ENV", "StateStore", "resolve_resume_step", "resume_requested",
+           "run_resume_step"]

@@ -1,17 +1,29 @@
-"""Topology: a pure function of (recipe service groups, all-gathered GPU list).
+"""Service placement: a pure function from (recipe service groups, all GPUs of the job) to services.
 
-Cards are assigned in declaration order; ``colocate_with=X`` reuses X's exact
-card block; ports are ``<role base> + master rank``; colocation rings are
-attached and validated; checkpoint policies and critic/trainer column wiring
-are checked before any process starts.  Semantics follow the reference
-(``meshy/service/topology.py:233-526``) because every rank must derive the
-same answer from the same inputs.
+Every rank evaluates :func:`build_topology` on the same inputs and so agrees
+on the placement without talking to the others. The rules are the
+reference's contract (``meshy/service/topology.py``), since recipes written
+for it must land on the same cards and ports:
+
+* GPU groups take consecutive blocks of cards in declaration order; a group
+  with ``colocate_with=X`` takes X's block again (and must be the same size);
+* replica ``r`` of a group owns the ``r``-th ``n_gpus_per_replica`` cards of
+  its block; its ports are the config class's port bases plus the global rank
+  of its first card (plus ``XRL_PORT_OFFSET``, default 0, which lets two runs
+  share a host);
+* CPU groups get no cards and no ports.
+
+Then colocation rings are attached to their member services, and the whole
+placement is checked (ports, ring membership, critic-to-trainer columns,
+checkpoint policy) before any process starts; every problem found is
+reported at once.
 """
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
-from typing import Any
+from typing import Any, Callable
 
 from ..config import CRITIC_OUTPUT_FIELDS_BY_MODE, ServiceConfig
 from .base import GPU, ServiceGroup
@@ -44,30 +56,38 @@ class ServiceInfo:
         return self.replica_gpus[0].global_rank
 
     def contains_rank(self, rank: int) -> bool:
-        return any(g.global_rank == rank for g in self.replica_gpus)
+        return rank in {g.global_rank for g in self.replica_gpus}
+
+    @property
+    def checkpoint_policy(self):
+        ck = getattr(self.config, "checkpoint", None)
+        return ck if ck is not None and ck.enabled else None
 
 
 @dataclass
 class Topology:
     services: list[ServiceInfo]
 
+    def _where(self, pred: Callable[[ServiceInfo], bool]) -> list[ServiceInfo]:
+        return [s for s in self.services if pred(s)]
+
     def group(self, gid: str) -> list[ServiceInfo]:
-        return [s for s in self.services if s.group_id == gid]
+        return self._where(lambda s: s.group_id == gid)
 
     def by_name(self, name: str) -> ServiceInfo:
-        for s in self.services:
-            if s.name == name:
-                return s
-        raise KeyError(f"no service named {name!r}")
+        hit = self._where(lambda s: s.name == name)
+        if not hit:
+            raise KeyError(f"topology has no service {name!r}")
+        return hit[0]
 
     def gpu_services(self):
-        return [s for s in self.services if s.uses_gpu]
+        return self._where(lambda s: s.uses_gpu)
 
     def cpu_services(self):
-        return [s for s in self.services if not s.uses_gpu]
+        return self._where(lambda s: not s.uses_gpu)
 
     def services_by_role(self, role: str):
-        return [s for s in self.services if s.role == role]
+        return self._where(lambda s: s.role == role)
 
     def inference_services(self):
         return self.services_by_role("inference")
@@ -85,182 +105,195 @@ class Topology:
         return [{"name": s.name, "endpoint": s.endpoint} for s in self.inference_services()]
 
     def trainer_endpoint(self) -> str | None:
-        t = self.training_services()
-        return t[0].endpoint if t else None
+        trainers = self.training_services()
+        return trainers[0].endpoint if trainers else None
 
     def checkpointing_services(self):
-        return [s for s in self.services
-                if getattr(getattr(s, "config", None), "checkpoint", None) is not None and s.config.checkpoint.enabled]
+        return self._where(lambda s: s.checkpoint_policy is not None)
 
     def checkpoint_config(self):
-        e = self.checkpointing_services()
-        return e[0].config.checkpoint if e else None
+        ck = self.checkpointing_services()
+        return ck[0].checkpoint_policy if ck else None
 
     def cold_start_windows(self) -> int:
-        for s in self.services_by_role("critic"):
-            return int(getattr(s.config, "cold_start_windows", 0))
-        return 0
+        critics = self.services_by_role("critic")
+        return int(getattr(critics[0].config, "cold_start_windows", 0)) if critics else 0
 
     def checkpoint_participants(self, step: int) -> tuple[str, ...]:
-        """Services that must hold a shard for ``step``; the trainer is exempt during the critic cold start."""
+        """Services whose shard a resume at ``step`` needs. The trainer has none while the critic cold-starts
+        (windows ``1..cold_start_windows``; a negative count means it never stops)."""
         cold = self.cold_start_windows()
-        return tuple(s.name for s in self.checkpointing_services()
-                     if not (s.role == "training" and (cold < 0 or int(step) <= cold)))
+        trainer_idle = cold < 0 or int(step) <= cold
+        return tuple(s.name for s in self.checkpointing_services() if not (s.role == "training" and trainer_idle))
 
     def dependency_names(self, s: ServiceInfo) -> list[str]:
-        return [x.name for gid in s.wait_until for x in self.group(gid)]
+        return [dep.name for gid in s.wait_until for dep in self.group(gid)]
 
     def local_services(self, rank: int) -> list[ServiceInfo]:
         return [s for s in self.gpu_services() if s.contains_rank(rank)]
 
     def colocated_inference_for(self, trainer: ServiceInfo):
+        """Inference replicas sharing the trainer's cards: names, {rank: name}, endpoints."""
         if trainer.colocate_with is None:
             return [], {}, []
         mine = {g.global_rank for g in trainer.replica_gpus}
-        names, by_rank, eps = [], {}, []
+        names, by_rank, endpoints = [], {}, []
         for inf in self.group(trainer.colocate_with):
             shared = [g.global_rank for g in inf.replica_gpus if g.global_rank in mine]
-            if not shared:
-                continue
-            for r in shared:
-                by_rank[r] = inf.name
-            names.append(inf.name)
-            eps.append(inf.endpoint)
-        return names, by_rank, eps
+            if shared:
+                names.append(inf.name)
+                endpoints.append(inf.endpoint)
+                by_rank.update({r: inf.name for r in shared})
+        return names, by_rank, endpoints
+
+
+def _port_offset() -> int:
+    return int(os.environ.get("XRL_PORT_OFFSET", "0") or 0)
+
+
+class _CardBlocks:
+    """Hands out consecutive card blocks and remembers each group's block for its colocated followers."""
+
+    def __init__(self, gpus: list[GPU]):
+        self.free = sorted(gpus, key=lambda g: g.global_rank)
+        self.next = 0
+        self.of_group: dict[str, list[GPU]] = {}
+
+    def block_for(self, sg: ServiceGroup) -> list[GPU]:
+        want = sg.n_replicas * sg.n_gpus_per_replica
+        if sg.colocate_with is not None:
+            host = self.of_group.get(sg.colocate_with)
+            if host is None:
+                raise ValueError(f"{sg.id!r} colocates with {sg.colocate_with!r}, which is not a GPU group declared "
+                                 "before it")
+            if len(host) != want:
+                raise ValueError(f"{sg.id!r} needs {want} cards but its colocation target {sg.colocate_with!r} "
+                                 f"holds {len(host)}; colocated groups must be the same size")
+            return host
+        block = self.free[self.next:self.next + want]
+        if len(block) < want:
+            raise ValueError(f"{sg.id!r} needs {want} cards; only {len(block)} are left")
+        self.next += want
+        self.of_group[sg.id] = block
+        return block
 
 
 def build_topology(service_groups: list[ServiceGroup], gpus: list[GPU], colocations: list | None = None) -> Topology:
-    gpus = sorted(gpus, key=lambda g: g.global_rank)
-    targets = {sg.colocate_with for sg in service_groups if sg.colocate_with}
-    blocks: dict[str, list[GPU]] = {}
+    cards = _CardBlocks(gpus)
+    hosts_of_colocation = {sg.colocate_with for sg in service_groups if sg.colocate_with}
+    offset = _port_offset()
     services: list[ServiceInfo] = []
-    cursor = 0
     for sg in service_groups:
-        ctype = type(sg.config)
+        cfg_type = type(sg.config)
         if not sg.role or sg.role == "?":
-            raise ValueError(f"ServiceConfig {ctype.__name__} must declare a role")
+            raise ValueError(f"{cfg_type.__name__} declares no role")
+        waits = list(sg.wait_until)
         if not sg.uses_gpu:
-            for r in range(sg.n_replicas):
-                services.append(ServiceInfo(f"{sg.id}-{r}", sg.id, sg.role, False, r, "127.0.0.1", 0, 0, [], False,
-                                            None, list(sg.wait_until), sg.config))
+            services += [ServiceInfo(f"{sg.id}-{r}", sg.id, sg.role, False, r, "127.0.0.1", 0, 0, [], False, None,
+                                     list(waits), sg.config) for r in range(sg.n_replicas)]
             continue
-        total = sg.n_replicas * sg.n_gpus_per_replica
-        if sg.colocate_with is not None:
-            if sg.colocate_with not in blocks:
-                raise ValueError(f"group {sg.id!r} colocate_with={sg.colocate_with!r} which is not a GPU group "
-                                 "declared earlier")
-            block = blocks[sg.colocate_with]
-            if len(block) != total:
-                raise ValueError(f"colocate group {sg.id!r} occupies {total} cards but {sg.colocate_with!r} "
-                                 f"occupies {len(block)}; they must match")
-        else:
-            block = gpus[cursor:cursor + total]
-            if len(block) != total:
-                raise ValueError(f"group {sg.id!r} needs {total} cards but only {len(block)} remain")
-            cursor += total
-            blocks[sg.id] = block
-        colo = sg.colocate_with is not None or sg.id in targets
-        if ctype.endpoint_port_base is None or ctype.dist_port_base is None:
-            raise ValueError(f"GPU ServiceConfig {ctype.__name__} must declare endpoint_port_base and dist_port_base")
+        if cfg_type.endpoint_port_base is None or cfg_type.dist_port_base is None:
+            raise ValueError(f"{cfg_type.__name__} runs on GPUs, so it must declare endpoint_port_base and "
+                             "dist_port_base")
+        block = cards.block_for(sg)
+        shared = sg.colocate_with is not None or sg.id in hosts_of_colocation
+        per = sg.n_gpus_per_replica
         for r in range(sg.n_replicas):
-            rg = block[r * sg.n_gpus_per_replica:(r + 1) * sg.n_gpus_per_replica]
-            m = rg[0].global_rank
-            services.append(ServiceInfo(f"{sg.id}-{r}", sg.id, sg.role, True, r, rg[0].host,
-                                        ctype.endpoint_port_base + m, ctype.dist_port_base + m, list(rg), colo,
-                                        sg.colocate_with, list(sg.wait_until), sg.config))
-    _attach_colocations(services, colocations or [])
-    _validate_ports(services)
-    _validate_critic_columns(services)
-    _validate_checkpoint(services)
+            own = list(block[r * per:(r + 1) * per])
+            first = own[0].global_rank
+            services.append(ServiceInfo(
+                f"{sg.id}-{r}", sg.id, sg.role, True, r, own[0].host, cfg_type.endpoint_port_base + first + offset,
+                cfg_type.dist_port_base + first + offset, own, shared, sg.colocate_with, list(waits), sg.config))
+    _attach_rings(services, colocations or [])
+    problems = [p for check in (_port_problems, _critic_column_problems, _checkpoint_problems)
+                for p in check(services)]
+    if problems:
+        raise ValueError("invalid service topology:\n  " + "\n  ".join(problems))
     return Topology(services)
 
 
-def _validate_checkpoint(services: list[ServiceInfo]) -> None:
-    enabled = [s for s in services
-               if getattr(getattr(s, "config", None), "checkpoint", None) is not None and s.config.checkpoint.enabled]
-    if not enabled:
-        return
-    policies = {s.name: s.config.checkpoint for s in enabled}
-    if len(set(policies.values())) != 1:
-        raise ValueError("every checkpointing service must share one GlobalCheckpointConfig (the resume point is an "
-                         "intersection over shards), got: " + ", ".join(f"{k}={v}" for k, v in sorted(policies.items())))
-    roles = {s.role for s in enabled}
-    present = {s.role for s in services}
-    for role in ("training", "critic", "rollout"):
-        if role in present and role not in roles:
-            raise ValueError(f"checkpointing is enabled but the {role!r} service does not carry the shared "
-                             "GlobalCheckpointConfig; a resume would reset it")
-    for c in [s for s in services if s.role == "critic"]:
-        cold = int(getattr(c.config, "cold_start_windows", 0))
-        for t in [s for s in services if s.role == "training"]:
-            off = int(getattr(t.config, "critic_cold_start_windows", 0))
-            if off != cold:
-                raise ValueError(f"critic {c.name!r} cold_start_windows={cold} but trainer {t.name!r} "
-                                 f"critic_cold_start_windows={off}; they number one gate stream and must match")
-
-
-def _validate_critic_columns(services: list[ServiceInfo]) -> None:
-    critics = [s for s in services if s.role == "critic"]
-    trainers = [s for s in services if s.role == "training"]
-    for c in critics:
-        mode = getattr(c.config, "publish_mode", "advantage")
-        published = set(CRITIC_OUTPUT_FIELDS_BY_MODE[mode])
-        for t in trainers:
-            fetched = set(getattr(t.config, "tq_fields", ()))
-            if not published <= fetched:
-                raise ValueError(f"critic {c.name!r} publishes {sorted(published)} (publish_mode={mode!r}) but trainer "
-                                 f"{t.name!r} fetches {sorted(fetched)}; the trainer would never see a scored row")
-            gae = bool(getattr(getattr(t.config, "trainer_params", None), "enable_gae", False))
-            if mode == "values" and not gae:
-                raise ValueError(f"critic {c.name!r} publishes per-token values but trainer {t.name!r} has "
-                                 "enable_gae=False")
-            if mode != "values" and gae:
-                raise ValueError(f"trainer {t.name!r} has enable_gae=True but critic {c.name!r} does not publish values")
-
-
-def _attach_colocations(services: list[ServiceInfo], rings: list) -> None:
-    if not rings:
-        return
-    ids = [r.group_id for r in rings]
-    if len(set(ids)) != len(ids):
-        raise ValueError(f"duplicate colocation group ids: {ids}")
-    known = {s.group_id for s in services}
-    assigned: set[str] = set()
+def _attach_rings(services: list[ServiceInfo], rings: list) -> None:
+    """Give each member service its ring (replica 0 of a group leads); rings must be disjoint and cover
+    exactly one shared card block."""
+    seen_ids: set[str] = set()
+    taken: set[str] = set()
+    groups = {s.group_id for s in services}
     for ring in rings:
-        members = {n.service_id for n in ring.ring}
-        if members - known:
-            raise ValueError(f"colocation {ring.group_id!r} references unknown groups: {sorted(members - known)}")
-        if members & assigned:
-            raise ValueError(f"ServiceGroups can belong to only one colocation ring: {sorted(members & assigned)}")
-        assigned |= members
-        cards = {g: frozenset(x.global_rank for s in services if s.group_id == g for x in s.replica_gpus)
-                 for g in members}
-        if len(set(cards.values())) != 1:
-            raise ValueError(f"colocation ring {ring.group_id!r} members do not share the same GPU block: "
-                             f"{ {k: sorted(v) for k, v in cards.items()} }")
+        if ring.group_id in seen_ids:
+            raise ValueError(f"colocation id {ring.group_id!r} is used twice")
+        seen_ids.add(ring.group_id)
+        members = {m.service_id for m in ring.ring}
+        if not members <= groups:
+            raise ValueError(f"colocation {ring.group_id!r} names groups that do not exist: {sorted(members - groups)}")
+        if members & taken:
+            raise ValueError(f"groups {sorted(members & taken)} appear in more than one colocation ring")
+        taken |= members
+        blocks = {g: frozenset(c.global_rank for s in services if s.group_id == g for c in s.replica_gpus)
+                  for g in members}
+        if len(set(blocks.values())) > 1:
+            raise ValueError(f"members of colocation {ring.group_id!r} sit on different cards: "
+                             f"{ {g: sorted(b) for g, b in blocks.items()} }")
         for g in members:
-            ms = [s for s in services if s.group_id == g]
-            if not ms or not all(s.is_colocate for s in ms):
-                raise ValueError(f"colocation ring member {g!r} is not placed on colocated GPUs")
-            for s in ms:
-                s.colocation = ring
-                s.is_colocation_leader = s.replica_idx == 0
+            mine = [s for s in services if s.group_id == g]
+            if not mine or any(not s.is_colocate for s in mine):
+                raise ValueError(f"{g!r} is in colocation {ring.group_id!r} but is not placed on shared cards")
+            for s in mine:
+                s.colocation, s.is_colocation_leader = ring, s.replica_idx == 0
 
 
-def _validate_ports(services: list[ServiceInfo]) -> None:
-    for attr in ("endpoint_port", "dist_port"):
-        owners: dict = {}
-        for s in services:
-            if not s.uses_gpu:
+def _port_problems(services: list[ServiceInfo]) -> list[str]:
+    out = []
+    for kind in ("endpoint_port", "dist_port"):
+        claimed: dict[tuple[str, int], str] = {}
+        for s in (x for x in services if x.uses_gpu):
+            port = getattr(s, kind)
+            if not 0 < port < 65536:
+                out.append(f"{s.name}: {kind} {port} is outside 1..65535")
                 continue
-            port = getattr(s, attr)
-            if not 1 <= port <= 65535:
-                raise ValueError(f"service {s.name!r} has invalid {attr} {port}")
-            key = (s.host, port)
-            if key in owners:
-                raise ValueError(f"{attr} collision on {s.host}:{port} between services {owners[key]!r} and "
-                                 f"{s.name!r}; choose distinct port bases")
-            owners[key] = s.name
+            other = claimed.setdefault((s.host, port), s.name)
+            if other != s.name:
+                out.append(f"{kind} collision: {other} and {s.name} both want {s.host}:{port} (give their configs "
+                           "different port bases)")
+    return out
+
+
+def _critic_column_problems(services: list[ServiceInfo]) -> list[str]:
+    out = []
+    trainers = [s for s in services if s.role == "training"]
+    for critic in (s for s in services if s.role == "critic"):
+        mode = getattr(critic.config, "publish_mode", "advantage")
+        produced = set(CRITIC_OUTPUT_FIELDS_BY_MODE[mode])
+        for t in trainers:
+            consumed = set(getattr(t.config, "tq_fields", ()))
+            if not produced <= consumed:
+                out.append(f"{t.name} never reads the critic's columns {sorted(produced - consumed)} "
+                           f"(critic {critic.name}, publish_mode {mode!r})")
+            wants_values = bool(getattr(getattr(t.config, "trainer_params", None), "enable_gae", False))
+            if wants_values != (mode == "values"):
+                out.append(f"{t.name} has enable_gae={wants_values} but critic {critic.name} publishes "
+                           f"{'values' if mode == 'values' else 'advantages'}; GAE needs per-token values")
+    return out
+
+
+def _checkpoint_problems(services: list[ServiceInfo]) -> list[str]:
+    on = [s for s in services if s.checkpoint_policy is not None]
+    if not on:
+        return []
+    out = []
+    if len({s.checkpoint_policy for s in on}) > 1:
+        out.append("checkpointing services disagree on the GlobalCheckpointConfig (the resume point is the "
+                   "newest step all of them saved): " + ", ".join(f"{s.name}={s.checkpoint_policy}" for s in on))
+    missing = {s.role for s in services} - {s.role for s in on}
+    for role in sorted(missing & {"training", "critic", "rollout"}):
+        out.append(f"checkpointing is on but the {role} service has it off; a resume would restart that service "
+                   "from scratch")
+    for critic in (s for s in services if s.role == "critic"):
+        cold = int(getattr(critic.config, "cold_start_windows", 0))
+        for t in (s for s in services if s.role == "training"):
+            if int(getattr(t.config, "critic_cold_start_windows", 0)) != cold:
+                out.append(f"{t.name} critic_cold_start_windows differs from {critic.name} cold_start_windows "
+                           f"({cold}); both count windows of one gate stream")
+    return out
 
 
 __all__ = ["ServiceInfo", "Topology", "build_topology"]

@@ -130,14 +130,25 @@ def rollout_metrics(samples: Sequence[Any], seq_len: int | None = None,
         out["rollout/repetition_frac"] = out["rollout/repetition_ratio"]
     if "rollout/mixed_version_ratio" in out:
         out["rollout/weight_version/mixed_version_ratio"] = out["rollout/mixed_version_ratio"]
+    if versions:
+        # version spread inside the batch: "stale" means older than the newest version present in the batch
+        newest = max(versions)
+        out["rollout/weight_version/mean"] = sum(versions) / len(versions)
+        out["rollout/weight_version/min"] = float(min(versions))
+        out["rollout/weight_version/max"] = float(newest)
+        out["rollout/weight_version/median"] = _percentile(sorted(float(v) for v in versions), 0.5)
+        out["rollout/weight_version/num_versions"] = float(len(set(versions)))
+        out["rollout/weight_version/stale_ratio"] = sum(1.0 for v in versions if v < newest) / len(versions)
     if versions and current_version is not None:
+        # lag behind the weights the trainer is about to update
         stale = [current_version - v for v in versions]
-        out["rollout/weight_version/stale_ratio"] = sum(1.0 for x in stale if x > 0) / len(stale)
         out["rollout/weight_version/staleness_mean"] = sum(stale) / len(stale)
         out["rollout/weight_version/staleness_max"] = float(max(stale))
     if rewards:
-        out["rollout/raw_reward_mean"] = sum(rewards) / len(rewards)
-        out["rollout/rewards"] = out["rollout/raw_reward_mean"]
+        # raw_reward is the unshaped reward when the rollout published one; reward is the shaped value
+        out["rollout/raw_reward_mean"] = sum(solve) / len(solve)
+        out["rollout/raw_reward"] = out["rollout/raw_reward_mean"]
+        out["rollout/rewards"] = sum(rewards) / len(rewards)
     lps = []
     for s in samples:
         lp = _as_list(_field(s, "logprobs"))

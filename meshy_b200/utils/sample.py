@@ -1,17 +1,27 @@
-"""Rollout samples and the chat-template-aware builder.
+"""Rollout samples, and turning chat messages into token spans with loss masks.
 
-``SampleBuilder`` renders messages to token spans by prefix diffing (each
-message's ids are the difference between successive renders without the
-generation prompt), so masks mark exactly the assistant tokens (reference
-``meshy/utils/sample.py:8-122``).
+A :class:`Sample` is one trajectory: its messages, the token ids the policy
+saw, a per-token behaviour log-prob, and a per-token mask that is 1 exactly on
+assistant tokens (the tokens the loss trains). Its field names are the
+column names the rollout publishes, as in the reference
+(``meshy/utils/sample.py``).
+
+Chat templates are not compositional token by token, so the token ids of
+message ``i`` are found by rendering the conversation up to and including
+``i`` and keeping what that render adds to the render up to ``i - 1``. The
+trailing generation prompt (``<|im_start|>assistant`` and the like) is the
+part that the final render *with* ``add_generation_prompt`` adds, and it
+belongs to the prompt (mask 0).
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import Any, Iterable
+from typing import Any, Iterable, Iterator
 
 from .tokenizer import load_tokenizer
+
+ASSISTANT = "assistant"
 
 
 @dataclass
@@ -31,60 +41,74 @@ class Sample:
     positive_lm_weight: float = 0.0
     prompt_id: int = -1
 
+    def extend(self, ids: list[int], *, trained: bool, logprobs: Iterable[float] | float = 0.0) -> None:
+        """Append ``ids`` with their behaviour log-probs (one per id, or one value for all) and mask."""
+        lps = [float(logprobs)] * len(ids) if isinstance(logprobs, (int, float)) else [float(x) for x in logprobs]
+        if len(lps) != len(ids):
+            raise ValueError(f"{len(ids)} tokens but {len(lps)} log-probs")
+        self.tokens += ids
+        self.logprobs += lps
+        self.masks += [int(trained)] * len(ids)
+
+
+def _ids(rendered) -> list[int]:
+    """Token ids of a ``apply_chat_template(tokenize=True)`` result (a list, or a BatchEncoding)."""
+    if isinstance(rendered, (list, tuple)):
+        return list(rendered)
+    ids = rendered["input_ids"] if "input_ids" in rendered else rendered
+    return list(ids)
+
 
 class SampleBuilder:
     def __init__(self, model_path: str | None = None, tokenizer=None):
-        self.tokenizer = tokenizer or load_tokenizer(model_path)
+        self.tokenizer = tokenizer if tokenizer is not None else load_tokenizer(model_path)
 
-    def _render(self, messages, *, add_generation_prompt: bool) -> list[int]:
+    def render(self, messages: list[dict], generation_prompt: bool) -> list[int]:
         if not messages:
             return []
-        out = self.tokenizer.apply_chat_template(messages, tokenize=True, add_generation_prompt=add_generation_prompt)
-        return list(out["input_ids"] if hasattr(out, "keys") else out)
+        return _ids(self.tokenizer.apply_chat_template(messages, tokenize=True,
+                                                       add_generation_prompt=generation_prompt))
 
-    def _spans(self, messages):
-        spans, prev = [], []
-        for i, m in enumerate(messages):
-            full = self._render(messages[: i + 1], add_generation_prompt=False)
-            spans.append((m["role"], full[len(prev):]))
-            prev = full
-        spans.append((None, self._render(messages, add_generation_prompt=True)[len(prev):]))
-        return spans
+    def segments(self, messages: list[dict]) -> Iterator[tuple[str | None, list[int]]]:
+        """``(role, ids)`` of every message, then ``(None, generation-prompt ids)``."""
+        done: list[int] = []
+        for k in range(len(messages)):
+            upto = self.render(messages[:k + 1], False)
+            yield messages[k]["role"], upto[len(done):]
+            done = upto
+        yield None, self.render(messages, True)[len(done):]
 
     def build_sample(self, messages: Iterable[dict], logprob: float = 0.0) -> Sample:
-        messages = [{"role": m["role"], "content": m["content"]} for m in messages]
-        s = Sample(messages=messages)
-        for role, ids in self._spans(messages):
-            s.tokens.extend(ids)
-            s.logprobs.extend([logprob] * len(ids))
-            s.masks.extend([1 if role == "assistant" else 0] * len(ids))
-        return s
+        msgs = [{"role": m["role"], "content": m["content"]} for m in messages]
+        sample = Sample(messages=msgs)
+        for role, ids in self.segments(msgs):
+            sample.extend(ids, trained=role == ASSISTANT, logprobs=logprob)
+        return sample
 
     def from_tokens(self, prompt_ids: Iterable[int], ground_truth: Any = None) -> Sample:
-        ids = list(prompt_ids)
-        return Sample(messages=[{"role": "user", "content": ""}], tokens=ids, logprobs=[0.0] * len(ids),
-                      masks=[0] * len(ids), ground_truth=ground_truth)
+        """A prompt given as token ids (no chat template; one empty user message stands for it)."""
+        sample = Sample(messages=[{"role": "user", "content": ""}], ground_truth=ground_truth)
+        sample.extend(list(prompt_ids), trained=False)
+        return sample
 
     def append_text(self, sample: Sample, role: str, content: str, logprob: float = 0.0, *,
                     add_generation_prompt: bool = True) -> Sample:
-        old = self._render(list(sample.messages), add_generation_prompt=False)
-        new_msgs = [*sample.messages, {"role": role, "content": content}]
-        new = self._render(new_msgs, add_generation_prompt=add_generation_prompt)
-        if new[: len(old)] != old:
-            raise ValueError("chat template changed the existing message prefix")
-        sample.messages.append({"role": role, "content": content})
-        ids = new[len(old):]
-        sample.tokens.extend(ids)
-        sample.logprobs.extend([logprob] * len(ids))
-        sample.masks.extend([1 if role == "assistant" else 0] * len(ids))
+        """Add one message rendered through the template; the existing render must stay a prefix."""
+        before = self.render(list(sample.messages), False)
+        msg = {"role": role, "content": content}
+        after = self.render([*sample.messages, msg], add_generation_prompt)
+        if after[:len(before)] != before:
+            raise ValueError("the chat template re-rendered earlier messages differently; cannot append")
+        sample.messages.append(msg)
+        sample.extend(after[len(before):], trained=role == ASSISTANT, logprobs=logprob)
         return sample
 
     def append_tokens(self, sample: Sample, role: str, tokens: Iterable[int], logprobs: Iterable[float]) -> Sample:
-        tokens = list(tokens)
-        sample.messages.append({"role": role, "content": self.tokenizer.decode(tokens, skip_special_tokens=True)})
-        sample.tokens.extend(tokens)
-        sample.logprobs.extend(list(logprobs))
-        sample.masks.extend([1 if role == "assistant" else 0] * len(tokens))
+        """Add generated tokens verbatim (the engine's ids and log-probs); the message text is their decode."""
+        ids = list(tokens)
+        text = self.tokenizer.decode(ids, skip_special_tokens=True)
+        sample.messages.append({"role": role, "content": text})
+        sample.extend(ids, trained=role == ASSISTANT, logprobs=list(logprobs))
         return sample
 
 

@@ -1,8 +1,12 @@
 """Accumulating named stopwatches (reference ``meshy/utils/timer.py:53-178``).
 
-``TimerStats.timer(name, sync=...)`` accumulates wall time per bucket; with
-``sync=True`` on a CUDA machine the block is bracketed by
-``torch.cuda.synchronize`` so the number covers device work.
+``TimerStats.timer(name, sync=...)`` accumulates time per bucket.  On a CUDA
+machine every bucket is device time: a pair of CUDA events on the current
+stream brackets the block, and :meth:`TimerStats.pop_metrics` waits for the
+last event once and sums the elapsed times, so timing adds no host sync inside
+the step.  ``sync=True`` additionally brackets the block with
+``torch.cuda.synchronize`` (the bucket then also covers host work that kept
+the device idle).  On CPU the buckets are wall time.
 :class:`DeviceTimer` times a region with CUDA events instead (no host sync
 inside the region); :func:`max_over_ranks` turns a per-rank time into the
 job time. Every timed region, and every :func:`nvtx_range`, is also an NVTX
@@ -53,11 +57,17 @@ def set_timers_enabled(flag: bool) -> None:
     _GLOBAL_ENABLED = bool(flag)
 
 
+def _cuda_live() -> bool:
+    return torch.cuda.is_available() and torch.cuda.is_initialized()
+
+
 class TimerStats:
-    def __init__(self, enabled: bool = True):
+    def __init__(self, enabled: bool = True, device: bool | None = None):
         self.enabled = enabled
+        self.device = device
         self.totals: dict[str, float] = defaultdict(float)
         self.counts: dict[str, int] = defaultdict(int)
+        self._events: list[tuple[str, object, object]] = []
 
     @contextmanager
     def timer(self, name: str, sync: bool = False):
@@ -65,24 +75,44 @@ class TimerStats:
             with nvtx_range(name):
                 yield
             return
-        cuda = sync and torch.cuda.is_available() and torch.cuda.is_initialized()
-        if cuda:
+        cuda = _cuda_live() and (self.device is None or self.device)
+        if cuda and torch.cuda.is_current_stream_capturing():
+            cuda = sync = False  # events cannot be timed inside a graph capture
+        if cuda and sync:
             torch.cuda.synchronize()
         t0 = time.perf_counter()
+        ev = None
+        if cuda:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
         try:
             with nvtx_range(name):
                 yield
         finally:
-            if cuda:
-                torch.cuda.synchronize()
-            self.totals[name] += time.perf_counter() - t0
+            if ev is not None:
+                ev[1].record()
+                if sync:
+                    torch.cuda.synchronize()
+                self._events.append((name, ev[0], ev[1]))
+            else:
+                self.totals[name] += time.perf_counter() - t0
             self.counts[name] += 1
 
     def add(self, name: str, seconds: float) -> None:
         self.totals[name] += seconds
         self.counts[name] += 1
 
+    def _drain(self) -> None:
+        if not self._events:
+            return
+        self._events[-1][2].synchronize()
+        for name, s, e in self._events:
+            e.synchronize()
+            self.totals[name] += s.elapsed_time(e) / 1e3
+        self._events.clear()
+
     def pop_metrics(self, prefix: str = "") -> dict[str, float]:
+        self._drain()
         out = {f"{prefix}{k}": v for k, v in self.totals.items()}
         self.totals.clear()
         self.counts.clear()

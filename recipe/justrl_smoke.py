@@ -23,6 +23,8 @@ CARDS = int(os.environ.get("XRL_SMOKE_CARDS", "2"))
 PROMPTS = int(os.environ.get("XRL_SMOKE_PROMPTS", "4"))
 GROUP = 2
 STEPS = int(os.environ.get("XRL_SMOKE_STEPS", "3"))
+# "auto": CUDA IPC snapshots on a GPU node, the HF safetensors export on CPU
+SYNC = os.environ.get("XRL_SMOKE_WEIGHT_SYNC", "auto")
 CKPT = GlobalCheckpointConfig(enabled=os.environ.get("XRL_SMOKE_CKPT", "0") == "1", interval=1, keep_latest_k=2)
 
 
@@ -41,7 +43,7 @@ SERVICE_GROUPS = [
                      model_path=None, trainer_config=_trainer_config(),
                      trainer_params=TrainerParamsConfig(mini_batch_size=PROMPTS * GROUP, batch_layout="packed",
                                                         max_tokens_per_micro=2048, old_logprobs_source="train"),
-                     batch_size=PROMPTS * GROUP, weight_sync_mode="disk", checkpoint=CKPT)),
+                     batch_size=PROMPTS * GROUP, weight_sync_mode=SYNC, checkpoint=CKPT)),
     ServiceGroup(id="rollout", n_replicas=1, n_gpus_per_replica=0, wait_until=["actor_train", "actor_infer"],
                  config=RolloutServiceConfig(
                      model_path=None, dataset="meshy_b200.dataset.synthetic:SyntheticPrompts",

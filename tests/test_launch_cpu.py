@@ -22,9 +22,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _port_offset() -> str:
+    """Shift every service port of this run so launcher tests running side by side do not collide."""
+    return str(100 + (_free_port() % 400) * 10)
+
+
 @pytest.mark.timeout(600)
 def test_launcher_runs_colocated_grpo_on_cpu(tmp_path):
-    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="3", XRL_SMOKE_CKPT="1", PYTHONPATH=ROOT)
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="3", XRL_SMOKE_CKPT="1", PYTHONPATH=ROOT, XRL_PORT_OFFSET=_port_offset())
     port = _free_port()
     rt = tmp_path / "rt"
     r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
@@ -53,7 +58,7 @@ def test_launcher_runs_colocated_grpo_on_cpu(tmp_path):
 def test_launcher_runs_critic_ppo_on_cpu(tmp_path):
     """Ring of inference → critic → trainer on one card: the critic cold-starts for one window (it raises
     the gate itself), then publishes values that the trainer turns into VAPO-GAE advantages."""
-    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", XRL_SMOKE_COLD="1", PYTHONPATH=ROOT)
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", XRL_SMOKE_COLD="1", PYTHONPATH=ROOT, XRL_PORT_OFFSET=_port_offset())
     rt = tmp_path / "rt"
     r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_ii_smoke",
                         "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
@@ -74,7 +79,7 @@ def test_launcher_runs_critic_ppo_on_cpu(tmp_path):
 def test_launcher_runs_topk_distillation_on_cpu(tmp_path):
     """Inference → teacher (Top-K columns appended in place) → student trainer (forward KL over the teacher's
     Top-K), all ring members of one card."""
-    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", PYTHONPATH=ROOT)
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", PYTHONPATH=ROOT, XRL_PORT_OFFSET=_port_offset())
     rt = tmp_path / "rt"
     r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.student_topk_opd_smoke",
                         "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
@@ -90,7 +95,7 @@ def test_launcher_runs_topk_distillation_on_cpu(tmp_path):
 
 
 def _launch(rt, steps, *extra):
-    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS=str(steps), XRL_SMOKE_CKPT="1", PYTHONPATH=ROOT)
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS=str(steps), XRL_SMOKE_CKPT="1", PYTHONPATH=ROOT, XRL_PORT_OFFSET=_port_offset())
     return subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
                            "--runtime-dir", str(rt), "--master-port", str(_free_port()), *extra], cwd=ROOT, env=env,
                           capture_output=True, text=True, timeout=540)

@@ -36,7 +36,12 @@ def test_rollout_metrics_use_stamps_and_rewards():
     assert m["rollout/truncated_ratio"] == pytest.approx(0.5)
     assert m["rollout/repetition_frac"] == pytest.approx(0.25)
     assert m["rollout/weight_version/mixed_version_ratio"] == pytest.approx(0.5)
-    assert m["rollout/weight_version/stale_ratio"] == pytest.approx(1.0)  # every sample is behind version 4
+    # two of the four samples are older than the newest version in the batch (3)
+    assert m["rollout/weight_version/stale_ratio"] == pytest.approx(0.5)
+    assert m["rollout/weight_version/max"] == 3 and m["rollout/weight_version/min"] == 1
+    assert m["rollout/weight_version/num_versions"] == 3
+    assert m["rollout/weight_version/mean"] == pytest.approx(9 / 4)
+    assert m["rollout/weight_version/median"] == pytest.approx(2.5)
     assert m["rollout/weight_version/staleness_mean"] == pytest.approx((1 + 1 + 2 + 3) / 4)
     assert m["rollout/weight_version/staleness_max"] == 3
     assert m["rollout/raw_reward_mean"] == pytest.approx(0.5)
@@ -57,3 +62,17 @@ def test_rollout_metrics_without_stamps_omit_the_tags():
         assert tag not in m
     assert m["rollout/seq_len_truncated_ratio"] == 1.0
     assert m["rollout/log_probs"] == pytest.approx(-1.0)
+
+
+def test_raw_reward_tags_read_the_unshaped_reward():
+    """With shaping on, ``reward`` is shaped and ``raw_reward`` is not: the raw tags and the pass rate follow
+    ``raw_reward``, ``rollout/rewards`` follows the shaped value."""
+    samples = [_sample(reward=0.8, seed=5), _sample(reward=-0.3, seed=6)]
+    samples[0]["raw_reward"] = torch.tensor(1.0)
+    samples[1]["raw_reward"] = torch.tensor(0.0)
+    m, _ = rollout_metrics(samples, current_version=3)
+    assert m["rollout/raw_reward_mean"] == pytest.approx(0.5)
+    assert m["rollout/raw_reward"] == pytest.approx(0.5)
+    assert m["rollout/rewards"] == pytest.approx(0.25)
+    assert m["rollout/pass_rate"] == pytest.approx(0.5)
+    assert m["rollout/weight_version/stale_ratio"] == 0.0

@@ -106,3 +106,16 @@ def test_noalloc_decode_explicit_splits_and_rejects_oversize():
     assert "scratch" in lib.meshy_noalloc_last_error().decode()
     torch.cuda.synchronize()
     assert int(out.float().abs().sum().item()) == 0  # nothing was launched
+
+
+def test_noalloc_decode_rejects_unsupported_layout():
+    """A page size other than 64 (or an unsupported head size) returns a non-zero code and a message, and
+    launches nothing."""
+    C, lib, fn = _lib()
+    q, kc, vc, bt, seq = _case(14, [100, 40], page=32, n_pages=16, max_pages=8)
+    out = torch.zeros_like(q)
+    rc = _call(fn, q, kc, vc, bt, seq, out, 1.0 / math.sqrt(q.shape[-1]))
+    assert rc != 0
+    assert "page_size" in lib.meshy_noalloc_last_error().decode()
+    torch.cuda.synchronize()
+    assert int(out.float().abs().sum().item()) == 0
