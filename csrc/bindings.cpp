@@ -19,6 +19,7 @@
 #include "kernels/elementwise.h"
 #include "kernels/gemm.h"
 #include "kernels/misc.h"
+#include "kernels/moe.h"
 #include "kernels/symm.h"
 
 using torch::Tensor;
@@ -745,6 +746,167 @@ void cast_copy(Tensor src, Tensor dst) {
 }
 
 // ─── symmetric peer memory ────────────────────────────────────────────────────
+// ─── mixture of experts ─────────────────────────────────────────────────────
+void moe_route_(Tensor logits, int64_t k, bool norm, Tensor probs, Tensor weights, Tensor experts) {
+  CHECK_CUDA(logits);
+  CHECK_BF16(logits);
+  CHECK_CONTIG(logits);
+  CHECK_F32(probs);
+  CHECK_F32(weights);
+  TORCH_CHECK(experts.scalar_type() == at::kInt, "experts must be int32");
+  const int T = logits.size(0), E = logits.size(1);
+  TORCH_CHECK(probs.numel() == (int64_t)T * E && weights.numel() == (int64_t)T * k && experts.numel() == (int64_t)T * k,
+              "moe_route: shape mismatch");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  moe_route(ptr<bf16>(logits), T, E, (int)k, norm, ptr<float>(probs), ptr<float>(weights), ptr<int>(experts),
+            cur_stream());
+  count();
+}
+
+void moe_route_bwd_(Tensor dw, Tensor probs, Tensor weights, Tensor experts, bool norm, Tensor dlogits) {
+  CHECK_CUDA(dw);
+  CHECK_F32(dw);
+  CHECK_CONTIG(dw);
+  CHECK_BF16(dlogits);
+  const int T = probs.size(0), E = probs.size(1), k = weights.size(1);
+  TORCH_CHECK(dlogits.numel() == (int64_t)T * E && dw.numel() == (int64_t)T * k, "moe_route_bwd: shape mismatch");
+  const c10::cuda::CUDAGuard guard(dw.device());
+  moe_route_bwd(ptr<float>(dw), ptr<float>(probs), ptr<float>(weights), ptr<int>(experts), T, E, k, norm,
+                ptr<bf16>(dlogits), cur_stream());
+  count();
+}
+
+void moe_plan_(Tensor experts, Tensor cnt, Tensor off, Tensor slot_of, Tensor row_src, c10::optional<Tensor> x,
+               c10::optional<Tensor> xp) {
+  CHECK_CUDA(experts);
+  CHECK_CONTIG(experts);
+  TORCH_CHECK(experts.scalar_type() == at::kInt && cnt.scalar_type() == at::kInt && off.scalar_type() == at::kInt &&
+                  slot_of.scalar_type() == at::kInt && row_src.scalar_type() == at::kInt,
+              "moe_plan: int32 index tensors");
+  const int E = cnt.numel();
+  TORCH_CHECK(off.numel() == E + 1, "moe_plan: off must have E + 1 entries");
+  const int n = experts.numel(), k = experts.size(-1);
+  TORCH_CHECK(slot_of.numel() == n, "moe_plan: slot_of must have one entry per assignment");
+  const int rows_cap = row_src.numel();
+  int D = 0;
+  if (xp.has_value() && xp->defined()) {
+    TORCH_CHECK(x.has_value() && x->defined(), "moe_plan: xp needs x");
+    CHECK_BF16(*x);
+    CHECK_BF16(*xp);
+    CHECK_CONTIG(*x);
+    CHECK_CONTIG(*xp);
+    D = x->size(1);
+    TORCH_CHECK(xp->size(0) == rows_cap && xp->size(1) == D && x->size(0) * k == n, "moe_plan: x / xp shapes");
+  }
+  const c10::cuda::CUDAGuard guard(experts.device());
+  moe_plan(ptr<int>(experts), n, k, E, ptr<int>(cnt), ptr<int>(off), ptr<int>(slot_of), ptr<int>(row_src),
+           D ? ptr<bf16>(*x) : nullptr, D ? D : 8, D ? ptr<bf16>(*xp) : nullptr, rows_cap, ptr<int>(scratch(0, 0).err),
+           cur_stream());
+  count(2);
+}
+
+void moe_zero_pad_(Tensor off, Tensor cnt, Tensor buf) {
+  CHECK_CUDA(buf);
+  CHECK_BF16(buf);
+  CHECK_CONTIG(buf);
+  const c10::cuda::CUDAGuard guard(buf.device());
+  moe_zero_pad(ptr<int>(off), ptr<int>(cnt), cnt.numel(), ptr<bf16>(buf), buf.size(1), cur_stream());
+  count();
+}
+
+void moe_combine_(Tensor y, Tensor slot_of, c10::optional<Tensor> w, Tensor out) {
+  CHECK_CUDA(y);
+  CHECK_BF16(y);
+  CHECK_BF16(out);
+  CHECK_CONTIG(y);
+  CHECK_CONTIG(out);
+  const int T = out.size(0), D = out.size(1);
+  const int k = slot_of.numel() / std::max(T, 1);
+  TORCH_CHECK(y.size(1) == D && slot_of.numel() == (int64_t)T * k, "moe_combine: shapes");
+  const c10::cuda::CUDAGuard guard(y.device());
+  moe_combine(ptr<bf16>(y), y.size(0), ptr<int>(slot_of), optr<float>(w), T, k, D, ptr<bf16>(out), cur_stream());
+  count();
+}
+
+void moe_combine_bwd_(Tensor dout, Tensor y, Tensor slot_of, Tensor w, Tensor dy, Tensor dw) {
+  CHECK_CUDA(dout);
+  CHECK_BF16(dout);
+  CHECK_CONTIG(dout);
+  CHECK_BF16(dy);
+  CHECK_F32(dw);
+  const int T = dout.size(0), D = dout.size(1), k = w.size(1);
+  TORCH_CHECK(dy.size(1) == D && y.size(1) == D && slot_of.numel() == (int64_t)T * k, "moe_combine_bwd: shapes");
+  const c10::cuda::CUDAGuard guard(dout.device());
+  moe_combine_bwd(ptr<bf16>(dout), ptr<bf16>(y), y.size(0), ptr<int>(slot_of), ptr<float>(w), T, k, D,
+                  ptr<bf16>(dy), ptr<float>(dw), cur_stream());
+  count();
+}
+
+// Grouped GEMM over 128-aligned token segments (off [G + 1] on the device):
+//   mode 1 (GRP_M): out[seg_g] = a[seg_g] . op(b[g])^T, a [rows, K], b [G, N, K] (or [G, K, N] with b_mn),
+//                   epilogue store or SwiGLU (out [rows, N / 2], optional pre-activation aux [rows, N]);
+//   mode 2 (GRP_K): out[g] += a[seg_g]^T . b[seg_g], a [rows, M], b [rows, N], out [G * M, N] fp32.
+void gemm_grouped(Tensor a, Tensor b, Tensor out, Tensor off, int64_t mode, bool b_mn, int64_t epi,
+                  c10::optional<Tensor> aux) {
+  CHECK_CUDA(a);
+  CHECK_BF16(a);
+  CHECK_BF16(b);
+  CHECK_CONTIG(a);
+  CHECK_CONTIG(b);
+  CHECK_CONTIG(out);
+  TORCH_CHECK(off.scalar_type() == at::kInt, "gemm_grouped: int32 offsets");
+  const c10::cuda::CUDAGuard guard(a.device());
+  GemmProblem g;
+  g.grp_mode = (int)mode;
+  g.grp_off = ptr<int>(off);
+  g.grp_n = off.numel() - 1;
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.out = out.data_ptr();
+  g.ldo = out.stride(0);
+  g.out_f32 = out.scalar_type() == at::kFloat;
+  g.err = ptr<int>(scratch(0, 0).err);
+  if (mode == GRP_M) {
+    TORCH_CHECK(b.dim() == 3 && b.size(0) == g.grp_n, "GRP_M: b must be [G, N, K] / [G, K, N]");
+    g.a_mn = false;
+    g.b_mn = b_mn;
+    g.M = a.size(0);
+    g.K = a.size(1);
+    g.lda = a.stride(0);
+    g.N = b_mn ? b.size(2) : b.size(1);
+    TORCH_CHECK((b_mn ? b.size(1) : b.size(2)) == g.K, "GRP_M: K mismatch");
+    g.ldb = b.stride(1);
+    g.grp_stride = b.stride(0);
+    g.epi = (int)epi;
+    if (epi == EPI_SWIGLU) {
+      TORCH_CHECK(out.size(0) == g.M && out.size(1) * 2 == g.N, "GRP_M SwiGLU: out [rows, N / 2]");
+      if (aux.has_value() && aux->defined()) {
+        CHECK_BF16(*aux);
+        TORCH_CHECK(aux->size(0) == g.M && aux->size(1) == g.N, "GRP_M SwiGLU: aux [rows, N]");
+        g.aux = ptr<bf16>(*aux);
+        g.ld_aux = aux->stride(0);
+      }
+    } else {
+      TORCH_CHECK(epi == EPI_STORE && out.size(0) == g.M && out.size(1) == g.N, "GRP_M: out [rows, N]");
+    }
+  } else {
+    TORCH_CHECK(mode == GRP_K, "gemm_grouped: mode 1 (GRP_M) or 2 (GRP_K)");
+    TORCH_CHECK(b.dim() == 2 && a.size(0) == b.size(0), "GRP_K: a [rows, M], b [rows, N]");
+    g.a_mn = true;
+    g.b_mn = true;
+    g.K = a.size(0);
+    g.M = a.size(1);
+    g.N = b.size(1);
+    g.lda = a.stride(0);
+    g.ldb = b.stride(0);
+    g.epi = EPI_ACC_F32;
+    TORCH_CHECK(g.out_f32 && out.size(0) == (int64_t)g.M * g.grp_n && out.size(1) == g.N, "GRP_K: out [G * M, N] fp32");
+  }
+  if (g.M == 0 || g.N == 0 || g.K == 0) return;
+  gemm_launch(g, cur_stream());
+  count();
+}
+
 int64_t symm_alloc_(int64_t nbytes) {
   const c10::cuda::CUDAGuard guard(at::cuda::current_device());
   return reinterpret_cast<int64_t>(symm_malloc((size_t)nbytes));
@@ -934,6 +1096,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_small_config", [](int64_t enabled, int64_t cluster) { gemm_small_config((int)enabled, (int)cluster); },
         "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");
   m.def("swiglu_bwd", &swiglu_bwd_);
+  m.def("moe_route", &moe_route_, "router softmax + top-k (+ renormalisation)");
+  m.def("moe_route_bwd", &moe_route_bwd_, "router backward: d logits from d weights");
+  m.def("moe_plan", &moe_plan_, "device-side expert plan: counts, 128-aligned offsets, slots, gather");
+  m.def("moe_zero_pad", &moe_zero_pad_, "zero the padding rows of every expert segment");
+  m.def("moe_combine", &moe_combine_, "weighted gather-sum of expert outputs per token");
+  m.def("moe_combine_bwd", &moe_combine_bwd_, "combine backward: expert-row gradients and routing-weight gradients");
+  m.def("gemm_grouped", &gemm_grouped, "grouped tcgen05 GEMM over 128-aligned expert segments");
   m.def("rmsnorm_fwd", &rmsnorm_fwd_);
   m.def("rmsnorm_bwd", &rmsnorm_bwd_);
   m.def("qkv_rope_fwd", &qkv_rope_fwd_);

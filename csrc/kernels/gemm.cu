@@ -76,6 +76,15 @@ struct GemmArgs {
   // TMA store (bf16 output; SwiGLU output and pre-activations) or TMA reduce-add (fp32 accumulation), so
   // the global writes are whole lines instead of one 16-byte piece per row and lane
   int tma_out;
+  // grouped problems (mixture-of-experts): grp_off[0..grp_n] are device row offsets, multiples of 128, of
+  // each group's segment of the token rows. GRP_M: the segment rows of A are multiplied by the group's own
+  // B (a 3-D tensor map, group = outermost coordinate); units past grp_off[grp_n] are skipped. GRP_K: the
+  // contraction runs over the group's segment rows (A and B MN-major) into output rows
+  // [g * grp_rows, (g + 1) * grp_rows); empty groups are skipped.
+  const int* grp_off;
+  int grp_n;
+  int grp_mode;
+  int grp_rows;
 };
 
 template <int BN>
@@ -158,6 +167,46 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& p, int u, int& mt, i
   nt = r / gm;
 }
 
+// One work unit of a CTA: its tile, its k-block range, the first output row, and (grouped) its group.
+struct Unit {
+  int mt, nt, ks, kb0, kb1, row0, grp;
+};
+
+// Every role of the CTA resolves units the same way and skips the same ones (no work: a grouped problem
+// is launched for its largest possible size).
+__device__ __forceinline__ bool resolve_unit(const GemmArgs& p, int u, Unit& w) {
+  if (p.grp_mode == GRP_K) {
+    const int per = p.m_tiles * p.n_tiles;
+    w.grp = u / per;
+    const int r = u - w.grp * per;
+    w.mt = r % p.m_tiles;
+    w.nt = r / p.m_tiles;
+    w.ks = 0;
+    w.kb0 = p.grp_off[w.grp] / BK;
+    w.kb1 = p.grp_off[w.grp + 1] / BK;
+    w.row0 = w.grp * p.grp_rows + w.mt * BM;
+    return w.kb1 > w.kb0;
+  }
+  unit_coords(p, u, w.mt, w.nt, w.ks);
+  w.kb0 = w.ks * p.kb_per_split;
+  w.kb1 = min(p.k_blocks, w.kb0 + p.kb_per_split);
+  w.row0 = w.mt * BM;
+  w.grp = 0;
+  if (p.grp_mode == GRP_M) {
+    if (w.row0 >= p.grp_off[p.grp_n]) return false;
+    // owner of rows [row0, row0 + 128): the last group whose segment starts at or before row0 (segments are
+    // 128-aligned, so a tile never spans two groups; empty groups before it share its start)
+    int lo = 0, hi = p.grp_n - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.grp_off[mid] <= w.row0) lo = mid;
+      else hi = mid - 1;
+    }
+    w.grp = lo;
+  }
+  return true;
+}
+
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -213,10 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0, last_stage = 0;
       uint32_t last_phase = 0;
       for (int u = blockIdx.x; u < p.total_units && !*abort_flag; u += gridDim.x) {
-        int mt, nt, ks;
-        unit_coords(p, u, mt, nt, ks);
-        int kb0 = ks * p.kb_per_split, kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        Unit w;
+        if (!resolve_unit(p, u, w)) continue;
+        const int mt = w.mt, nt = w.nt;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
@@ -227,7 +276,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j) tma_load_2d(sa + j * 8192, &mapA, &full[stage], mt * BM + 64 * j, kb * BK);
           }
-          if (!B_MN) {
+          if (p.grp_mode == GRP_M) {
+            if (!B_MN) {
+              tma_load_3d(sb, &mapB, &full[stage], kb * BK, nt * BN, w.grp);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_3d(sb + j * 8192, &mapB, &full[stage], nt * BN + 64 * j, kb * BK, w.grp);
+            }
+          } else if (!B_MN) {
             tma_load_2d(sb, &mapB, &full[stage], kb * BK, nt * BN);
           } else {
 #pragma unroll
@@ -253,15 +310,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ───────────────────────────── MMA issuer ───────────────────────────────
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      if (p.grp_mode) pdl_wait();  // the group offsets come from the kernel before
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool any = false;
       for (int u = blockIdx.x; u < p.total_units && !*abort_flag; u += gridDim.x) {
-        int mt, nt, ks;
-        unit_coords(p, u, mt, nt, ks);
-        int kb0 = ks * p.kb_per_split, kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        Unit w;
+        if (!resolve_unit(p, u, w)) continue;
+        const int kb0 = w.kb0, kb1 = w.kb1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -315,11 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();  // residual / labels / workspace may come from the kernels before
     pdl_trigger();
     for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
-      int mt, nt, ks;
-      unit_coords(p, u, mt, nt, ks);
+      Unit w_;
+      if (!resolve_unit(p, u, w_)) continue;
+      const int mt = w_.mt, nt = w_.nt;
+      const int r0 = w_.row0;  // first output row of the tile
       if (!epi_all(mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue))) break;
       tc_fence_after();
-      const int row = mt * BM + q * 32 + lane;
+      const int row = r0 + q * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       const int n0 = nt * BN;
@@ -335,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 8; ++j)
             r16[j] = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
                                 __float_as_uint(v[4 * j + 3]));
-          stager.put<true>(r16, q * 32 + lane, &mapC, n0 + c * 32, mt * BM, et);
+          stager.put<true>(r16, q * 32 + lane, &mapC, n0 + c * 32, r0, et);
         }
       } else if (p.tma_out && p.epi == EPI_STORE) {
         // bf16 output: 64-column slices (+bias, +residual), stored by TMA (rows >= M / columns >= N clipped)
@@ -372,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 8; ++j)
             r16[j] = make_uint4(pack_bf16x2(w[8 * j], w[8 * j + 1]), pack_bf16x2(w[8 * j + 2], w[8 * j + 3]),
                                 pack_bf16x2(w[8 * j + 4], w[8 * j + 5]), pack_bf16x2(w[8 * j + 6], w[8 * j + 7]));
-          stager.put<false>(r16, q * 32 + lane, &mapC, col0, mt * BM, et);
+          stager.put<false>(r16, q * 32 + lane, &mapC, col0, r0, et);
         }
       } else if (p.tma_out && p.epi == EPI_DLOGITS) {
         // d logits = g * (onehot(label) - softmax), 64-column slices stored by TMA
@@ -395,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 8; ++j)
             r16[j] = make_uint4(pack_bf16x2(w[8 * j], w[8 * j + 1]), pack_bf16x2(w[8 * j + 2], w[8 * j + 3]),
                                 pack_bf16x2(w[8 * j + 4], w[8 * j + 5]), pack_bf16x2(w[8 * j + 6], w[8 * j + 7]));
-          stager.put<false>(r16, q * 32 + lane, &mapC, col0, mt * BM, et);
+          stager.put<false>(r16, q * 32 + lane, &mapC, col0, r0, et);
         }
       } else if (p.tma_out && p.epi == EPI_SWIGLU) {
         // columns [128j, 128j+64) are gate, [128j+64, 128j+128) the matching up rows -> 64 SwiGLU columns
@@ -427,10 +487,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
             }
           }
-          stager.put<false>(act, q * 32 + lane, &mapC, n0 / 2 + j * 64, mt * BM, et);
+          stager.put<false>(act, q * 32 + lane, &mapC, n0 / 2 + j * 64, r0, et);
           if (p.aux) {
-            stager.put<false>(hg, q * 32 + lane, &mapAux, gcol, mt * BM, et);
-            stager.put<false>(hu, q * 32 + lane, &mapAux, gcol + 64, mt * BM, et);
+            stager.put<false>(hg, q * 32 + lane, &mapAux, gcol, r0, et);
+            stager.put<false>(hu, q * 32 + lane, &mapAux, gcol + 64, r0, et);
           }
         }
       } else if (p.epi == EPI_STORE || p.epi == EPI_ACC_F32) {
@@ -837,8 +897,14 @@ static bool gemm_tma_out_enabled() {
   return v == 1;
 }
 
+static void gemm_grouped_launch(const GemmProblem& g, cudaStream_t stream);
+
 void gemm_launch(const GemmProblem& g, cudaStream_t stream) {
   MESHY_CHECK(g.M > 0 && g.N > 0 && g.K > 0, "empty GEMM");
+  if (g.grp_mode != GRP_NONE) {
+    gemm_grouped_launch(g, stream);
+    return;
+  }
   if (g.force_bn == 0 && gemm_small_eligible(g)) {
     gemm_small_launch(g, stream);
     return;
@@ -913,6 +979,85 @@ void gemm_launch(const GemmProblem& g, cudaStream_t stream) {
     }
   }
   int grid = std::min(a.total_units, sms);
+  switch (BN) {
+    case 256: launch_bn<256>(g.a_mn, g.b_mn, ma, mb, mc, mx, a, grid, stream); break;
+    case 128: launch_bn<128>(g.a_mn, g.b_mn, ma, mb, mc, mx, a, grid, stream); break;
+    default: launch_bn<64>(g.a_mn, g.b_mn, ma, mb, mc, mx, a, grid, stream); break;
+  }
+}
+
+// Grouped problems: one persistent launch sized for the largest possible row count; the group offsets are
+// read on the device, so nothing here waits for the routing.
+static void gemm_grouped_launch(const GemmProblem& g, cudaStream_t stream) {
+  MESHY_CHECK(g.grp_off != nullptr && g.grp_n > 0, "grouped GEMM: group offsets missing");
+  MESHY_CHECK((reinterpret_cast<uintptr_t>(g.out) & 15) == 0 && (g.ldo * (g.out_f32 ? 4 : 2)) % 16 == 0,
+              "grouped GEMM: output rows must start on 16-byte boundaries");
+  MESHY_CHECK(g.bias == nullptr && g.residual == nullptr, "grouped GEMM: no bias / residual epilogue");
+  const int sms = num_sms();
+  GemmArgs a{};
+  a.N = g.N;
+  a.K = g.K;
+  a.grp_off = g.grp_off;
+  a.grp_n = g.grp_n;
+  a.grp_mode = g.grp_mode;
+  a.epi = g.epi;
+  a.out = g.out; a.ldo = g.ldo; a.out_f32 = g.out_f32;
+  a.aux = g.aux; a.ld_aux = g.ld_aux;
+  a.err = g.err;
+  a.split_k = 1;
+  int BN = g.force_bn;
+  CUtensorMap ma, mb, mc, mx;
+  if (g.grp_mode == GRP_M) {
+    MESHY_CHECK(!g.a_mn && g.M % BM == 0, "GRP_M: A K-major with a row count padded to 128");
+    MESHY_CHECK(g.epi == EPI_STORE || g.epi == EPI_SWIGLU, "GRP_M: store or SwiGLU epilogue");
+    MESHY_CHECK(!g.out_f32, "GRP_M: bf16 output");
+    if (BN == 0) BN = (g.epi == EPI_SWIGLU || g.N >= 256) ? 256 : (g.N >= 128 ? 128 : 64);
+    MESHY_CHECK(g.epi != EPI_SWIGLU || g.N % 128 == 0, "GRP_M SwiGLU: N % 128 == 0");
+    MESHY_CHECK(g.N % BN == 0 || g.epi == EPI_STORE, "GRP_M: N must be a multiple of the tile width");
+    a.M = g.M;
+    a.m_tiles = g.M / BM;
+    a.n_tiles = (g.N + BN - 1) / BN;
+    a.k_blocks = (g.K + BK - 1) / BK;
+    a.kb_per_split = a.k_blocks;
+    a.total_units = a.m_tiles * a.n_tiles;
+    ma = make_map_bf16(g.A, g.M, g.K, g.lda, 64, BM);
+    MESHY_CHECK((g.grp_stride * 2) % 16 == 0 && (g.ldb * 2) % 16 == 0, "GRP_M: B strides must be 16-byte multiples");
+    if (!g.b_mn)  // B_g = [N, K] row-major (row stride ldb), groups grp_stride apart
+      mb = make_map_bf16_3d(g.B, g.K, g.N, g.grp_n, g.ldb * 2, g.grp_stride * 2, 64, BN);
+    else          // B_g = [K, N] row-major
+      mb = make_map_bf16_3d(g.B, g.N, g.K, g.grp_n, g.ldb * 2, g.grp_stride * 2, 64, 64);
+    mc = mx = ma;
+    a.tma_out = 0;
+    if (gemm_tma_out_enabled()) {
+      const bool aux_ok = g.aux == nullptr || ((reinterpret_cast<uintptr_t>(g.aux) & 15) == 0 && (g.ld_aux * 2) % 16 == 0);
+      if (g.epi == EPI_STORE) {
+        mc = make_map_bf16(g.out, g.M, g.N, g.ldo, 64, BM);
+        a.tma_out = 1;
+      } else if (aux_ok) {
+        mc = make_map_bf16(g.out, g.M, g.N / 2, g.ldo, 64, BM);
+        if (g.aux) mx = make_map_bf16(g.aux, g.M, g.N, g.ld_aux, 64, BM);
+        a.tma_out = 1;
+      }
+    }
+  } else {
+    MESHY_CHECK(g.grp_mode == GRP_K && g.a_mn && g.b_mn, "GRP_K: A and B MN-major (token rows as K)");
+    MESHY_CHECK(g.epi == EPI_ACC_F32 && g.out_f32, "GRP_K: fp32 accumulation");
+    MESHY_CHECK(g.M % BM == 0, "GRP_K: rows per group must be a multiple of 128");
+    if (BN == 0) BN = g.N >= 256 ? 256 : (g.N >= 128 ? 128 : 64);
+    a.M = g.M * g.grp_n;
+    a.grp_rows = g.M;
+    a.m_tiles = g.M / BM;
+    a.n_tiles = (g.N + BN - 1) / BN;
+    a.k_blocks = (g.K + BK - 1) / BK;
+    a.kb_per_split = a.k_blocks;
+    a.total_units = g.grp_n * a.m_tiles * a.n_tiles;
+    ma = make_map_bf16(g.A, g.K, g.M, g.lda, 64, 64);
+    mb = make_map_bf16(g.B, g.K, g.N, g.ldb, 64, 64);
+    mx = ma;
+    a.tma_out = gemm_tma_out_enabled() ? 1 : 0;
+    mc = a.tma_out ? make_map_f32(g.out, (int64_t)g.M * g.grp_n, g.N, g.ldo, 32, BM) : ma;
+  }
+  const int grid = std::min(a.total_units, sms);
   switch (BN) {
     case 256: launch_bn<256>(g.a_mn, g.b_mn, ma, mb, mc, mx, a, grid, stream); break;
     case 128: launch_bn<128>(g.a_mn, g.b_mn, ma, mb, mc, mx, a, grid, stream); break;

@@ -9,6 +9,13 @@
 namespace meshy {
 
 enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ACC_F32 = 2, EPI_LSE = 3, EPI_DLOGITS = 4 };
+// Grouped (mixture-of-experts) GEMMs over token rows sorted by group, each group's segment padded to a
+// multiple of 128 rows (device offsets grp_off[0..grp_n]):
+//   GRP_M  out[seg_g] = A[seg_g] . op(B_g)^T   (forward and data gradient; B = [grp_n] matrices at a
+//          stride of grp_stride elements; M = rows allocated, units past grp_off[grp_n] do nothing)
+//   GRP_K  out[g] += A[seg_g]^T . B[seg_g]      (weight gradient; A and B MN-major with the token rows as
+//          K; out = [grp_n * grp_rows, N] fp32, M = grp_rows per group)
+enum GroupMode : int { GRP_NONE = 0, GRP_M = 1, GRP_K = 2 };
 
 struct GemmProblem {
   const void* A = nullptr;  // bf16
@@ -67,6 +74,11 @@ struct GemmProblem {
   bf16* vc = nullptr;
   const int64_t* slots = nullptr;
   int hq = 0, hkv = 0;
+  // grouped problems (see GroupMode)
+  int grp_mode = GRP_NONE;
+  const int* grp_off = nullptr;
+  int grp_n = 0;
+  int64_t grp_stride = 0;   // GRP_M: elements between consecutive groups' B matrices
 };
 constexpr int kSmallPartLd = 256;
 

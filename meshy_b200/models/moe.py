@@ -6,10 +6,12 @@ the reference trains (``TT:torchtitan/models/common/moe.py``).  Experts are
 SwiGLU MLPs stored stacked: ``w13 [E, 2F, D]`` (block-interleaved gate/up, the
 same layout as the dense block) and ``w2 [E, D, F]``.
 
-On CUDA the token permutation, the grouped expert GEMMs and the weighted
-combine run in the native kernels (``moe_*`` in ``meshy_b200._C``); under
-expert parallelism the dispatch/combine all-to-all is fused with them
-(:mod:`meshy_b200.parallel.ep`).  On CPU the loop below is the oracle.
+On CUDA the router (softmax + top-k kernel), the device-side expert plan and
+token gather, the grouped tcgen05 expert GEMMs and the weighted combine run
+in the native kernels (:mod:`meshy_b200.ops.moe`), with no host
+synchronisation. Under expert parallelism the tokens travel to the experts'
+owners as described in :mod:`meshy_b200.parallel.ep`. On CPU the per-expert
+loop of :func:`moe_experts` is the oracle.
 """
 
 from __future__ import annotations
@@ -61,6 +63,19 @@ class MoE(nn.Module):
             nn.init.normal_(self.shared_w2, std=depth_std)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if Fx.native(x):
+            from ..ops import moe as M
+
+            weights, experts = M.route(Fx.linear(x, self.router), self.top_k, self.route_norm)
+            if self.ep_group is not None:
+                from ..parallel.ep import ep_moe_forward
+
+                out = ep_moe_forward(self, x, weights, experts)
+            else:
+                out = M.experts_forward(x, weights, experts, self.w13, self.w2, self.args.swiglu_block)
+            if self.shared_w13 is not None:
+                out = out + Fx.linear(Fx.linear_swiglu(x, self.shared_w13, self.args.swiglu_block), self.shared_w2)
+            return out
         weights, experts = route(x, self.router, self.top_k, self.route_norm)
         if self.ep_group is not None:
             from ..parallel.ep import ep_moe_forward

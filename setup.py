@@ -26,6 +26,7 @@ cuda_sources = [
     "csrc/kernels/attention_tc.cu",
     "csrc/kernels/decode_attn.cu",
     "csrc/kernels/misc.cu",
+    "csrc/kernels/moe.cu",
     "csrc/kernels/decode_noalloc.cu",
     "csrc/kernels/decode_mega.cu",
 ]
