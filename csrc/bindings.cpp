@@ -19,6 +19,7 @@
 #include "kernels/elementwise.h"
 #include "kernels/gemm.h"
 #include "kernels/misc.h"
+#include "kernels/ep.h"
 #include "kernels/moe.h"
 #include "kernels/symm.h"
 
@@ -907,6 +908,78 @@ void gemm_grouped(Tensor a, Tensor b, Tensor out, Tensor off, int64_t mode, bool
   count();
 }
 
+// ─── expert parallelism over peer memory ────────────────────────────────────
+using ull = unsigned long long;
+const ull* tab(const Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == at::kLong && t.is_cuda(), "peer pointer tables are int64 CUDA tensors");
+  return reinterpret_cast<const ull*>(t.data_ptr());
+}
+const ull* otab(const c10::optional<Tensor>& t) { return (t.has_value() && t->defined()) ? tab(*t) : nullptr; }
+
+void ep_dispatch_(Tensor rows, int64_t row_div, Tensor experts, Tensor slot_of, Tensor off, Tensor cnt,
+                  int64_t e_local, int64_t rank, int64_t world, int64_t cap, Tensor recv_x,
+                  c10::optional<Tensor> recv_meta, c10::optional<Tensor> recv_idx, c10::optional<Tensor> recv_cnt) {
+  CHECK_CUDA(rows);
+  CHECK_BF16(rows);
+  CHECK_CONTIG(rows);
+  TORCH_CHECK(off.numel() == world + 1 && cnt.numel() == world, "ep_dispatch: owner plan of world entries");
+  TORCH_CHECK(rows.size(0) * row_div >= experts.numel(), "ep_dispatch: too few rows");
+  const c10::cuda::CUDAGuard guard(rows.device());
+  EpDispatchArgs a;
+  a.rows = ptr<bf16>(rows);
+  a.row_div = (int)row_div;
+  a.experts = ptr<int>(experts);
+  a.n = experts.numel();
+  a.slot_of = ptr<int>(slot_of);
+  a.off = ptr<int>(off);
+  a.cnt = ptr<int>(cnt);
+  a.e_local = (int)e_local;
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.cap = (int)cap;
+  a.D = rows.size(1);
+  a.recv_x = tab(recv_x);
+  a.recv_meta = otab(recv_meta);
+  a.recv_idx = otab(recv_idx);
+  a.recv_cnt = otab(recv_cnt);
+  ep_dispatch(a, cur_stream());
+  count();
+}
+
+void ep_recv_ids_(Tensor meta, Tensor cnt, int64_t world, int64_t cap, int64_t e_local, Tensor ids) {
+  CHECK_CUDA(meta);
+  TORCH_CHECK(meta.numel() >= world * cap && ids.numel() >= world * cap, "ep_recv_ids: sizes");
+  const c10::cuda::CUDAGuard guard(meta.device());
+  ep_recv_ids(ptr<int>(meta), ptr<int>(cnt), (int)world, (int)cap, (int)e_local, ptr<int>(ids), cur_stream());
+  count();
+}
+
+void ep_return_(Tensor y, Tensor ids, Tensor slot_of, Tensor idx, int64_t world, int64_t cap, int64_t n_src_cap,
+                Tensor ret) {
+  CHECK_CUDA(y);
+  CHECK_BF16(y);
+  CHECK_CONTIG(y);
+  TORCH_CHECK(ids.numel() >= world * cap && slot_of.numel() >= world * cap && idx.numel() >= world * cap,
+              "ep_return: sizes");
+  const c10::cuda::CUDAGuard guard(y.device());
+  ep_return(ptr<bf16>(y), y.size(0), ptr<int>(ids), ptr<int>(slot_of), ptr<int>(idx), (int)world, (int)cap,
+            (int)n_src_cap, y.size(1), tab(ret), cur_stream());
+  count();
+}
+
+void gather_rows_(Tensor row_src, Tensor off, Tensor src, Tensor dst) {
+  CHECK_CUDA(src);
+  CHECK_BF16(src);
+  CHECK_BF16(dst);
+  CHECK_CONTIG(src);
+  CHECK_CONTIG(dst);
+  TORCH_CHECK(src.size(1) == dst.size(1) && row_src.numel() >= dst.size(0), "gather_rows: shapes");
+  const c10::cuda::CUDAGuard guard(src.device());
+  gather_rows(ptr<int>(row_src), ptr<int>(off) + (off.numel() - 1), ptr<bf16>(src), src.size(0), src.size(1),
+              ptr<bf16>(dst), dst.size(0), cur_stream());
+  count();
+}
+
 int64_t symm_alloc_(int64_t nbytes) {
   const c10::cuda::CUDAGuard guard(at::cuda::current_device());
   return reinterpret_cast<int64_t>(symm_malloc((size_t)nbytes));
@@ -1103,6 +1176,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine_, "weighted gather-sum of expert outputs per token");
   m.def("moe_combine_bwd", &moe_combine_bwd_, "combine backward: expert-row gradients and routing-weight gradients");
   m.def("gemm_grouped", &gemm_grouped, "grouped tcgen05 GEMM over 128-aligned expert segments");
+  m.def("ep_dispatch", &ep_dispatch_, "expert-parallel dispatch: P2P stores of token rows into the owners' regions");
+  m.def("ep_recv_ids", &ep_recv_ids_, "received rows -> local expert ids (-1 past each source's count)");
+  m.def("ep_return", &ep_return_, "expert-parallel return: P2P stores of expert rows into the sources' buffers");
+  m.def("gather_rows", &gather_rows_, "dst[r] = src[row_src[r]] up to the plan's end (zero padding rows)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd_);
   m.def("rmsnorm_bwd", &rmsnorm_bwd_);
   m.def("qkv_rope_fwd", &qkv_rope_fwd_);

@@ -87,7 +87,10 @@ class PPOTrainer:
         if ep_group is not None and dist.is_initialized() and dist.get_world_size(ep_group) > 1:
             from ..parallel.ep import shard_experts
 
-            shard_experts(model, ep_group)
+            p = self.params
+            # tokens of the largest micro-batch: the peer-memory exchange sizes its receive regions for it
+            max_tokens = p.max_tokens_per_micro or config.seq_len * max(1, p.micro_batch_size or 1)
+            shard_experts(model, ep_group, max_tokens=max_tokens)
         self.model = model
         self.model.activation_checkpoint = config.activation_checkpoint_mode == "full"
         self.flat = FlatParams(self.model, compute_dtype=cdt, device=self.device)

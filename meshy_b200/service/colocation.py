@@ -34,6 +34,8 @@ import queue
 import threading
 import time
 import uuid
+from concurrent.futures import Future
+from concurrent.futures import TimeoutError as FutureTimeout
 from contextlib import contextmanager
 from dataclasses import dataclass, replace
 from enum import Enum
@@ -57,36 +59,42 @@ class RingNode(NamedTuple):
 
 @dataclass(frozen=True)
 class ColocationRing:
+    """Members of one card block in hand-off order; ``ring[0]`` holds the card first."""
+
     group_id: str
     ring: tuple
     poll_interval: float = 1.0
     next_owner_timeout: float = 3.0
 
     def __post_init__(self) -> None:
-        object.__setattr__(self, "ring", tuple(RingNode(n[0], SchedulingMode(n[1])) for n in self.ring))
+        nodes = tuple(RingNode(str(sid), SchedulingMode(mode)) for sid, mode in self.ring)
+        object.__setattr__(self, "ring", nodes)
+        object.__setattr__(self, "_index", {n.service_id: i for i, n in enumerate(nodes)})
+        problems = []
         if not self.group_id:
-            raise ValueError("ColocationRing.group_id must be non-empty")
-        if len(self.ring) < 2:
-            raise ValueError("a colocation ring needs at least two Services")
-        names = [n.service_id for n in self.ring]
-        if any(not n for n in names):
-            raise ValueError("colocation ring service ids must be non-empty")
-        if len(set(names)) != len(names):
-            raise ValueError(f"colocation ring contains duplicates: {names}")
-        if self.poll_interval <= 0:
-            raise ValueError("colocation poll_interval must be positive")
+            problems.append("group_id is empty")
+        if len(nodes) < 2:
+            problems.append(f"{len(nodes)} member(s); a hand-off needs two or more")
+        if any(not n.service_id for n in nodes):
+            problems.append("a member has an empty service id")
+        if len(self._index) != len(nodes):
+            problems.append("a service appears twice: " + ", ".join(n.service_id for n in nodes))
+        if not self.poll_interval > 0:
+            problems.append(f"poll_interval {self.poll_interval} is not positive")
         if self.next_owner_timeout < 0:
-            raise ValueError("colocation next_owner_timeout must be >= 0")
+            problems.append(f"next_owner_timeout {self.next_owner_timeout} is negative")
+        if problems:
+            raise ValueError(f"colocation ring {self.group_id!r}: " + "; ".join(problems))
 
     @property
     def initial_owner(self) -> str:
         return self.ring[0].service_id
 
     def ring_index_for(self, service_id: str) -> int:
-        for i, n in enumerate(self.ring):
-            if n.service_id == service_id:
-                return i
-        raise KeyError(f"service {service_id!r} is not in ring {self.group_id!r}")
+        try:
+            return self._index[service_id]
+        except KeyError:
+            raise KeyError(f"{service_id!r} is not a member of colocation ring {self.group_id!r}") from None
 
     def mode_for(self, service_id: str) -> SchedulingMode:
         return self.ring[self.ring_index_for(service_id)].mode
@@ -229,22 +237,27 @@ class StoreLedger:
         pass
 
 
+GENESIS_SOURCE = "authority"
+
+
 def issue_genesis(config: ColocationRing, ledger: Ledger) -> GpuGrant:
-    req = GpuRequest(config.group_id, config.initial_owner, f"genesis:{config.group_id}", 0, ring_index=0, priority=1,
-                     kind=SchedulingMode.FALLBACK)
-    ledger.create(req)
-    g = GpuGrant(config.group_id, 0, "authority", config.initial_owner, req.request_id, "genesis")
-    ledger.grant(req.request_id, g)
-    return g
+    """Write the ring's first grant (sequence 0, from the authority to ``ring[0]``) into an empty ledger."""
+    owner = config.initial_owner
+    request = GpuRequest(group_id=config.group_id, service_id=owner, request_id="genesis:" + config.group_id,
+                         created_at_ns=0, ring_index=0, priority=1, kind=SchedulingMode.FALLBACK)
+    grant = GpuGrant(group_id=config.group_id, sequence=0, source=GENESIS_SOURCE, target=owner,
+                     request_id=request.request_id, transition="genesis")
+    ledger.create(request)
+    ledger.grant(request.request_id, grant)
+    return grant
 
 
-@dataclass
-class _Cmd:
+class _Command(NamedTuple):
+    """Work handed to the manager thread; the caller waits on ``future``."""
+
     action: str
     payload: Any
-    done: threading.Event
-    result: Any = None
-    error: BaseException | None = None
+    future: Future
 
 
 class ColocationManager:
@@ -260,7 +273,7 @@ class ColocationManager:
         self._ledger_factory = ledger_factory
         self._on_acquire = on_acquire or (lambda g: None)
         self._on_release = on_release or (lambda target: None)
-        self._cmds: queue.Queue[_Cmd] = queue.Queue()
+        self._cmds: queue.Queue[_Command] = queue.Queue()
         self._stop = threading.Event()
         self._started = threading.Event()
         self._thread: threading.Thread | None = None
@@ -342,13 +355,12 @@ class ColocationManager:
             raise RuntimeError("ColocationManager is not started")
         if self._fatal is not None:
             raise RuntimeError("colocation manager failed") from self._fatal
-        cmd = _Cmd(action, payload, threading.Event())
-        self._cmds.put(cmd)
-        if not cmd.done.wait(self.command_timeout):
-            raise TimeoutError(f"colocation command {action!r} timed out")
-        if cmd.error is not None:
-            raise cmd.error
-        return cmd.result
+        fut: Future = Future()
+        self._cmds.put(_Command(action, payload, fut))
+        try:
+            return fut.result(timeout=self.command_timeout)
+        except FutureTimeout:
+            raise TimeoutError(f"colocation command {action!r} timed out") from None
 
     def _run(self) -> None:
         ledger = self._ledger_factory()
@@ -363,11 +375,10 @@ class ColocationManager:
             log.exception("colocation manager %s failed", self.service_id)
             while True:
                 try:
-                    c = self._cmds.get_nowait()
+                    pending = self._cmds.get_nowait()
                 except queue.Empty:
                     break
-                c.error = exc
-                c.done.set()
+                pending.future.set_exception(exc)
             for ev in self._events.values():
                 ev.set()
         finally:
@@ -383,19 +394,19 @@ class ColocationManager:
                 if cmd.action == "request":
                     ledger.create(cmd.payload)
                     self._rows[cmd.payload.request_id] = LedgerRow(cmd.payload)
-                    cmd.result = cmd.payload
+                    result = cmd.payload
                 elif cmd.action == "release":
                     self._reconcile(ledger.scan(), ledger)
-                    transition, ref = cmd.payload
-                    cmd.result = self._transfer(ledger, transition, ref)
+                    result = self._transfer(ledger, *cmd.payload)
                 elif cmd.action == "stop":
                     self._stop.set()
+                    result = None
                 else:
                     raise ValueError(f"unknown colocation command {cmd.action!r}")
-            except BaseException as e:  # noqa: BLE001
-                cmd.error = e
-            finally:
-                cmd.done.set()
+            except BaseException as e:  # noqa: BLE001 - handed to the waiting caller
+                cmd.future.set_exception(e)
+            else:
+                cmd.future.set_result(result)
 
     def _reconcile(self, rows: list[LedgerRow], ledger: Ledger) -> None:
         rows.sort(key=lambda r: r.grant.sequence if r.grant else -1)
@@ -430,7 +441,7 @@ class ColocationManager:
         if g.group_id != self.config.group_id or g.sequence <= self._last_seq:
             return
         if self._last_seq < 0:
-            if g.sequence != 0 or g.source != "authority" or g.target != self.config.initial_owner:
+            if g.sequence != 0 or g.source != GENESIS_SOURCE or g.target != self.config.initial_owner:
                 raise RuntimeError(f"invalid genesis grant: {g}")
         elif g.sequence != self._last_seq + 1 or self._grant is None or g.source != self._grant.target:
             raise RuntimeError(f"non-contiguous GPU grant: last={self._grant}, next={g}")
@@ -464,7 +475,7 @@ class ColocationManager:
         c = self._candidates()
         if c:
             return c[0][4]
-        if self._grant is not None and self._grant.source not in (self.service_id, "authority"):
+        if self._grant is not None and self._grant.source not in (self.service_id, GENESIS_SOURCE):
             # nobody asked: hand the card back to whoever gave it to us
             self._ensure_fallback(ledger, self._grant.source)
             c = self._candidates()

@@ -27,6 +27,7 @@ cuda_sources = [
     "csrc/kernels/decode_attn.cu",
     "csrc/kernels/misc.cu",
     "csrc/kernels/moe.cu",
+    "csrc/kernels/ep.cu",
     "csrc/kernels/decode_noalloc.cu",
     "csrc/kernels/decode_mega.cu",
 ]

@@ -1,69 +1,83 @@
-"""``train_step`` takes the behaviour policy's log-probs before the first optimizer step.
+"""The PPO ratio's denominator is the policy that generated the batch (CPU, real trainer).
 
-Mirrors the reference's snapshot check (``tests/test_old_logprobs_snapshot.py``). With
-``old_logprobs_source="train"`` every mini-batch must train against log-probs of the weights the rollout was
-generated with: taking them inside each mini-batch would use weights already moved by the earlier
-mini-batches, pin the ratio at 1 and switch the PPO clip / TIS off. ``train_step`` runs unbound on a stub, so
-no model, GPU or process group is needed.
+With ``old_logprobs_source="train"`` the trainer recomputes behaviour log-probs itself. They must all be
+taken from the weights the step started with -- before the first mini-batch's optimiser update -- or the
+later mini-batches would see a ratio pinned at 1 and the clip / TIS bounds would never act. A tiny
+fp32 model trains three mini-batches on CPU; what each mini-batch receives as its behaviour log-probs is
+recorded and compared with log-probs computed up front from the starting weights.
 """
 
-from types import SimpleNamespace
+import random
 
-import pytest
 import torch
 
-from meshy_b200.backend import trainer as T
-from meshy_b200.backend.opd import StudentTopKTrainer
+from meshy_b200.backend.trainer import PPOTrainer
+from meshy_b200.config import TrainerConfig, TrainerParamsConfig
 
 
-def _run(source: str, needs: bool = True, n_mini: int = 3):
-    state = {"version": 0, "snapshots": [], "seen": []}
-
-    def compute_old(samples, mini):
-        state["snapshots"].append(state["version"])  # tag the snapshot with the weight version
-        return [torch.tensor(float(state["version"]))]
-
-    def run_mini(samples, mini, timer, old_lps=None):
-        state["seen"].append(None if old_lps is None else float(old_lps[0]))
-        state["version"] += 1  # this mini-batch's optimizer step
-        return {"loss": 0.0}, torch.tensor(1.0)
-
-    stub = SimpleNamespace(
-        timer_enabled=False, needs_behaviour_logprobs=needs, batch_layout="padded", step=0,
-        params=SimpleNamespace(enable_gae=False, old_logprobs_source=source),
-        config=SimpleNamespace(warmup_steps=0, steps=10, lr_decay_ratio=0.0, lr_decay_type="linear",
-                               lr_min_factor=0.0),
-        optimizer=SimpleNamespace(lr=1e-6, base_lr=1e-6),
-        compute_old_logprobs=compute_old, _run_mini_batch=run_mini,
-    )
-    plan = [SimpleNamespace(micros=[0]) for _ in range(n_mini)]
-    mp = pytest.MonkeyPatch()
-    mp.setattr(T, "plan_stats", lambda plan, layout: {})
-    try:
-        out = T.PPOTrainer.train_step(stub, [], plan=plan)
-    finally:
-        mp.undo()
-    assert out["num_mini_batches"] == float(n_mini) and out["step"] == 1
-    return state
+def _batch(n=6, seed=3):
+    rng = random.Random(seed)
+    out = []
+    for i in range(n):
+        p, r = rng.randint(3, 9), rng.randint(5, 20)
+        out.append({"tokens": torch.tensor([rng.randrange(2048) for _ in range(p + r)]),
+                    "mask_assistant": torch.tensor([0] * p + [1] * r, dtype=torch.float32),
+                    "logprobs": torch.tensor([0.0] * p + [-1.5] * r),
+                    "advantage": torch.tensor([1.0 if i % 2 else -1.0]), "reward": torch.tensor([float(i % 2)]),
+                    "weight_version": torch.tensor([0])})
+    return out
 
 
-def test_train_source_snapshots_every_mini_batch_before_any_step():
-    s = _run("train")
-    assert s["snapshots"] == [0, 0, 0]  # all taken at version 0
-    assert s["seen"] == [0.0, 0.0, 0.0]  # later mini-batches still see the version-0 policy
-    assert s["version"] == 3
+def _trainer(source):
+    tc = TrainerConfig(model_name="qwen3", model_flavor="debugmodel", seq_len=64, lr=3e-3, weight_decay=0.0,
+                       max_norm=0.0, dtype="float32")
+    tp = TrainerParamsConfig(mini_batch_size=2, batch_layout="packed", max_tokens_per_micro=64,
+                             old_logprobs_source=source)
+    return PPOTrainer(tc, tp, device="cpu", seed=1, timer_enabled=False)
 
 
-def test_rollout_source_takes_no_snapshot():
-    s = _run("rollout")
-    assert s["snapshots"] == [] and s["seen"] == [None, None, None]
+def _record(trainer):
+    seen = []
+    inner = trainer._run_mini_batch
+
+    def spy(samples, mini, timer, old_lps=None):
+        seen.append(None if old_lps is None else [t.clone() for t in old_lps])
+        return inner(samples, mini, timer, old_lps)
+
+    trainer._run_mini_batch = spy
+    return seen
 
 
-def test_trainer_without_a_ratio_skips_the_snapshot():
-    s = _run("train", needs=False)
-    assert s["snapshots"] == [] and s["seen"] == [None, None, None]
+def test_every_mini_batch_trains_against_the_starting_policy():
+    t = _trainer("train")
+    batch = _batch()
+    full = t.plan_batch(batch, 1)
+    local, plan = full.local_samples(batch, 0), full.per_rank[0]
+    assert len(plan) == 3
+    with torch.no_grad():
+        start = [t.compute_old_logprobs(local, mini) for mini in plan]
+    seen = _record(t)
+    t.train_step(local, plan=plan)
+    assert len(seen) == 3 and all(s is not None for s in seen)
+    for want, got in zip(start, seen):
+        for a, b in zip(want, got):
+            assert torch.allclose(a, b, atol=1e-6)
+    # the weights did move inside the step: the last mini-batch's log-probs under the final weights differ
+    with torch.no_grad():
+        after = t.compute_old_logprobs(local, plan[-1])
+    assert max((a - b).abs().max().item() for a, b in zip(after, start[-1])) > 1e-4
 
 
-def test_distillation_trainer_opts_out():
-    assert T.PPOTrainer.needs_behaviour_logprobs.fget(None) is True
+def test_rollout_source_passes_no_recomputed_logprobs():
+    t = _trainer("rollout")
+    batch = _batch()
+    seen = _record(t)
+    t.train_step(batch)
+    assert seen and all(s is None for s in seen)
+
+
+def test_trainers_without_an_importance_ratio_skip_the_recompute():
+    from meshy_b200.backend.opd import StudentTopKTrainer
+
+    assert PPOTrainer.needs_behaviour_logprobs.fget(None) is True
     assert StudentTopKTrainer.needs_behaviour_logprobs.fget(None) is False
