@@ -82,6 +82,7 @@ def _worker(rank, world, port, q):
             w2.main_grad = torch.zeros(w2.shape, dtype=torch.float32, device="cuda")
             for r in range(world):
                 xr, wr, er, gr = _inputs(r, call, T, D, E, k)
+                xr.requires_grad_(True)  # the other ranks' tokens only feed the expert-weight gradients
                 if r == rank:
                     xr, wr = x2, w2r
                 ref = M.experts_forward(xr, wr, er, w13, w2, 64)
