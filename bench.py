@@ -293,7 +293,7 @@ def main():
     value = tok_all / (ms_max / 1e3)
     e2e_value = tok_all / (e2e_max / 1e3)
     n_params = rl.trainer.model_args.num_params()
-    sync_bytes = rl.trainer.flat.numel * (4 + 2)
+    sync_bytes = rl.trainer.flat.numel * (2 + 2)  # read the bf16 compute weights, write the engine's copy
     meas = os.path.join(ROOT, "MEASURED_PEAKS.json")
     hbm = json.load(open(meas)).get("hbm_gbs", 6650.0) if os.path.exists(meas) else 6650.0
     if rank == 0:
@@ -327,7 +327,7 @@ def main():
             "weight_sync": {"ms": round(sync_max, 3), "bytes": sync_bytes,
                             "roofline_ms": round(sync_bytes / (hbm * 1e9) * 1e3, 3),
                             "frac_of_measured_hbm": round((sync_bytes / (hbm * 1e9) * 1e3) / max(sync_max, 1e-9), 3),
-                            "path": "fp32 master -> bf16 engine buffer, one device cast kernel (colocated)"},
+                            "path": "trainer bf16 compute weights -> engine bf16 buffer, one device copy (colocated)"},
             "e2e": {"value": round(e2e_value, 1), "unit": "trained tokens/s (all GPUs)",
                     "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
             "gpu_launches": launches,

@@ -1002,7 +1002,8 @@ void symm_barrier_(Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch,
   count();
 }
 
-void symm_dp_adamw_(Tensor grad_ptrs, Tensor master_ptrs, c10::optional<Tensor> compute_ptrs, Tensor flag_ptrs,
+void symm_dp_adamw_(Tensor grad_ptrs, c10::optional<Tensor> master_ptrs, c10::optional<Tensor> compute_ptrs,
+                    Tensor flag_ptrs,
                     Tensor slot_ptrs, Tensor master_local, Tensor grad_local, Tensor exp_avg, Tensor exp_avg_sq,
                     Tensor scalars, int64_t rank, int64_t world, int64_t lo, int64_t hi, int64_t epoch, double max_norm,
                     double lr, double b1, double b2, double eps, double wd, int64_t step, double timeout_s) {
@@ -1012,8 +1013,9 @@ void symm_dp_adamw_(Tensor grad_ptrs, Tensor master_ptrs, c10::optional<Tensor> 
   SymmAdamWArgs a;
   auto tab = [](const Tensor& t) { return reinterpret_cast<const unsigned long long*>(t.data_ptr()); };
   a.grad_ptrs = tab(grad_ptrs);
-  a.master_ptrs = tab(master_ptrs);
+  a.master_ptrs = master_ptrs.has_value() && master_ptrs->defined() ? tab(*master_ptrs) : nullptr;
   a.compute_ptrs = compute_ptrs.has_value() && compute_ptrs->defined() ? tab(*compute_ptrs) : nullptr;
+  TORCH_CHECK(a.master_ptrs || a.compute_ptrs, "symm_dp_adamw: a sharded master needs the bf16 compute table");
   a.flag_ptrs = tab(flag_ptrs);
   a.slot_ptrs = tab(slot_ptrs);
   a.master_local = ptr<float>(master_local);

@@ -18,9 +18,12 @@
 //                            global gradient norm (fixed summation order, so
 //                            every rank computes the identical value)
 //   4. symm_adamw_push       clip + AdamW on the shard (moments stay local,
-//                            ZeRO-1 style), then all-gather by P2P stores:
-//                            the new fp32 master and bf16 compute values go
-//                            straight into every rank's buffers
+//                            ZeRO-1 style), then all-gather by P2P stores.
+//                            With a bf16 compute copy the fp32 master is
+//                            sharded too: the shard is written locally and
+//                            only the bf16 values go to every rank (2 bytes
+//                            per parameter cross NVLink instead of 6); with
+//                            fp32 compute the master itself is pushed
 //   5. symm_barrier          nobody reuses its gradient or parameters before
 //                            every peer has finished reading and writing.
 //
@@ -137,7 +140,7 @@ __global__ void symm_norm_exchange_kernel(const unsigned long long* __restrict__
 
 __global__ void symm_adamw_push_kernel(const unsigned long long* __restrict__ master_ptrs,
                                        const unsigned long long* __restrict__ compute_ptrs,
-                                       const float* __restrict__ master_local, int world, long long lo,
+                                       float* __restrict__ master_local, int world, long long lo,
                                        long long hi, const float* __restrict__ g, float* __restrict__ m,
                                        float* __restrict__ v, const float* __restrict__ norm, float max_norm, float lr,
                                        float b1, float b2, float eps, float wd, float bc1, float bc2,
@@ -167,9 +170,16 @@ __global__ void symm_adamw_push_kernel(const unsigned long long* __restrict__ ma
     *reinterpret_cast<float4*>(m + 4 * i) = mm;
     *reinterpret_cast<float4*>(v + 4 * i) = vv;
     const uint2 packed = make_uint2(pack_bf16x2(pp.x, pp.y), pack_bf16x2(pp.z, pp.w));
-    for (int q = 0; q < world; ++q) {
-      *reinterpret_cast<float4*>(reinterpret_cast<float*>(master_ptrs[q]) + e) = pp;
-      if (compute_ptrs) *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(compute_ptrs[q]) + e) = packed;
+    if (master_ptrs == nullptr) {
+      // master weights sharded like the moments: the fp32 shard stays here, only bf16 crosses NVLink
+      *reinterpret_cast<float4*>(master_local + e) = pp;
+      for (int q = 0; q < world; ++q)
+        *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(compute_ptrs[q]) + e) = packed;
+    } else {
+      for (int q = 0; q < world; ++q) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(master_ptrs[q]) + e) = pp;
+        if (compute_ptrs) *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(compute_ptrs[q]) + e) = packed;
+      }
     }
   }
 }

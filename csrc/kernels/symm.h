@@ -20,11 +20,11 @@ void symm_barrier(const unsigned long long* flag_ptrs, int rank, int world, unsi
 
 struct SymmAdamWArgs {
   const unsigned long long* grad_ptrs = nullptr;     // [world] device table
-  const unsigned long long* master_ptrs = nullptr;   // [world]
+  const unsigned long long* master_ptrs = nullptr;   // [world], or null: master sharded (needs compute_ptrs)
   const unsigned long long* compute_ptrs = nullptr;  // [world] or null (no bf16 copy)
   const unsigned long long* flag_ptrs = nullptr;     // [world] u32[world] flag arrays
   const unsigned long long* slot_ptrs = nullptr;     // [world] f32[world] norm slots
-  const float* master_local = nullptr;
+  float* master_local = nullptr;
   float* local_grad = nullptr;
   float* exp_avg = nullptr;     // AdamW moments of this rank's shard only: [hi - lo]
   float* exp_avg_sq = nullptr;  // (ZeRO-1: every rank keeps 1/world of the optimiser state)

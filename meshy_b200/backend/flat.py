@@ -134,8 +134,38 @@ class FlatParams:
                 return buf[s.offset:s.offset + s.numel].view(s.shape)
         raise KeyError(name)
 
-    def state_dict(self) -> dict[str, torch.Tensor]:
-        return {s.name: self.master[s.offset:s.offset + s.numel].view(s.shape) for s in self.slots}
+    def gather_master(self) -> None:
+        """Make every element of the fp32 master current on this rank when an optimiser shards it (a
+        collective over the shard group: every rank of it must call this); a no-op otherwise."""
+        shard = getattr(self, "master_shard", None)
+        if shard is None:
+            return
+        import torch.distributed as dist
+
+        lo, hi, group, per = shard
+        world = dist.get_world_size(group)
+        mine = torch.zeros(per, dtype=torch.float32, device=self.master.device)
+        mine[:hi - lo].copy_(self.master[lo:hi])
+        parts = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(parts, mine, group=group)
+        with torch.no_grad():
+            self.master.copy_(torch.cat(parts)[:self.numel])
+
+    def state_dict(self, source: str = "master") -> dict[str, torch.Tensor]:
+        """Weights by parameter name. ``source="master"``: the fp32 master (gathered first when sharded, a
+        collective); ``"compute"``: the compute-dtype copy, which is complete on every rank."""
+        if source == "compute":
+            buf = self.compute
+        else:
+            self.gather_master()
+            buf = self.master
+        return {s.name: buf[s.offset:s.offset + s.numel].view(s.shape) for s in self.slots}
+
+    @property
+    def sync_source(self) -> torch.Tensor:
+        """The buffer a weight sync reads: the compute-dtype copy (complete on every rank, and what the
+        inference engines hold) when there is one, else the fp32 master."""
+        return self.compute if self.separate_compute else self.master
 
     def load_state_dict(self, sd: dict[str, torch.Tensor]) -> None:
         with torch.no_grad():

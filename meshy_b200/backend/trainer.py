@@ -132,7 +132,9 @@ class PPOTrainer:
 
             self.optimizer = FusedDPAdamW(self.flat, self.loss_group, lr=config.lr, betas=(config.beta1, config.beta2),
                                           eps=config.eps, weight_decay=config.weight_decay, max_norm=config.max_norm)
-            self.flat.resident = ("master", "grad", "compute")
+            # heap-resident buffers stay mapped while the trainer is offloaded (the fp32 master stays only
+            # when it is the replicated weight buffer, i.e. without a bf16 compute copy)
+            self.flat.resident = ("grad", "compute") if self.flat.separate_compute else ("master", "grad", "compute")
             self.reducer.backend = "none"
             self.fused_dp = True
         self.h2d_bytes = 0
@@ -349,7 +351,8 @@ class PPOTrainer:
     def export_hf(self, output_dir: str) -> str:
         from ..models.hf import save_hf_checkpoint
 
-        return save_hf_checkpoint(self.model_args, self.flat.state_dict(), output_dir)
+        # the replicated compute weights: valid on every rank, whatever shards the fp32 master
+        return save_hf_checkpoint(self.model_args, self.flat.state_dict(source="compute"), output_dir)
 
     def offload_to_cpu(self) -> None:
         """Colocation hand-off: move every flat buffer to pinned host memory."""

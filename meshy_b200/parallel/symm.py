@@ -131,9 +131,15 @@ class FusedDPAdamW:
         self.hi = min(n, self.lo + per)
         n_pad = per * world
         sep = flat.separate_compute
-        need = _align(n_pad * 4) * 2 + (_align(n_pad * 2) if sep else 0) + 2 * _align(world * 4) + 4096
+        # with a bf16 compute copy the fp32 master is sharded like the moments: it stays a local buffer of
+        # which only [lo, hi) is kept current, and only the bf16 copy is replicated (by the push); without
+        # one the master itself is the replicated weight buffer and lives in the heap
+        need = _align(n_pad * 4) * (1 if sep else 2) + (_align(n_pad * 2) if sep else 0) + 2 * _align(world * 4) \
+            + 4096
         self.heap = SymmetricHeap(need, group, dev)
-        master, self.master_tab = self.heap.alloc(n_pad, torch.float32)
+        self.master_tab = None
+        if not sep:
+            master, self.master_tab = self.heap.alloc(n_pad, torch.float32)
         grad, self.grad_tab = self.heap.alloc(n_pad, torch.float32)
         self.compute_tab = None
         if sep:
@@ -141,15 +147,17 @@ class FusedDPAdamW:
         _, self.flag_tab = self.heap.alloc(world, torch.int32)
         _, self.slot_tab = self.heap.alloc(world, torch.float32)
         with torch.no_grad():
-            master[:n].copy_(flat.master)
             grad[:n].copy_(flat.grad)
             if sep:
                 compute[:n].copy_(flat.compute)
-        flat.master = master[:n]
+            else:
+                master[:n].copy_(flat.master)
         flat.grad = grad[:n]
         if sep:
             flat.compute = compute[:n]
+            flat.master_shard = (self.lo, self.hi, group, per)
         else:
+            flat.master = master[:n]
             flat.compute = flat.master
         for s, p in zip(flat.slots, flat.params):
             p.data = flat.compute[s.offset:s.offset + s.numel].view(s.shape)

@@ -11,8 +11,9 @@ without any process or network hop inside a rank:
 3. the :class:`~meshy_b200.backend.trainer.PPOTrainer` recomputes behaviour
    log-probs, runs the PPO mini-batches with the DDP gradient reduction, and
    steps AdamW;
-4. weight sync: the fp32 master weights are cast straight into the engine's
-   bf16 weight buffer (same flat layout; one kernel, no disk, no gather).
+4. weight sync: the trainer's bf16 compute weights (what AdamW just wrote)
+   are copied into the engine's bf16 weight buffer (same flat layout; one
+   device copy, no disk, no gather).
 
 Across ranks only the gradient reduction and the loss denominators travel.
 The service-based path (launcher → TransferQueue → workers) drives the same
@@ -87,12 +88,12 @@ class ColocatedGRPO:
         if self.device.type == "cuda":
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            self.engine.update_weights_from_flat(self.trainer.flat.master, version=getattr(self, "version", 0))
+            self.engine.update_weights_from_flat(self.trainer.flat.sync_source, version=getattr(self, "version", 0))
             e.record()
             e.synchronize()
             return s.elapsed_time(e)
         t0 = time.perf_counter()
-        self.engine.update_weights_from_flat(self.trainer.flat.master, version=getattr(self, "version", 0))
+        self.engine.update_weights_from_flat(self.trainer.flat.sync_source, version=getattr(self, "version", 0))
         return (time.perf_counter() - t0) * 1e3
 
     def rollout(self, prompts: Sequence[Sequence[int]], max_new_tokens: Sequence[int] | int):

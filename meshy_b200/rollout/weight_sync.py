@@ -4,11 +4,11 @@ Trainer and engines lay parameters out identically in one flat buffer
 (:func:`meshy_b200.backend.flat.flatten_module`), so a sync never re-keys or
 re-shapes anything. Three routes, fastest first:
 
-* same process (:class:`~meshy_b200.rl.ColocatedGRPO`): one cast kernel from
-  the fp32 master buffer into the engine's bf16 buffer;
+* same process (:class:`~meshy_b200.rl.ColocatedGRPO`): one device copy of
+  the trainer's bf16 compute weights into the engine's bf16 buffer;
 * same node, other processes (the launcher's services, any DP size): every
   trainer rank keeps a bf16 snapshot of its weights in the engines' layout
-  (:class:`DevicePublisher`; one cast kernel per publish) and exports a CUDA
+  (:class:`DevicePublisher`; one device copy per publish) and exports a CUDA
   IPC handle of it. Rank 0 gathers the handles, keyed by GPU UUID, into one
   ``ipc-set:`` reference (:func:`encode_handle_set`) that travels through the
   colocation ring as ``payload_ref``. Each engine server maps the handle of
@@ -54,7 +54,8 @@ def device_uuid(device: torch.device | int | None = None) -> str:
 class DevicePublisher:
     """One trainer rank's published weights: two bf16 snapshots used alternately.
 
-    ``publish(version)`` casts the fp32 master weights into the snapshot of
+    ``publish(version)`` copies the trainer's compute weights (bf16; the fp32
+    master is cast when there is no bf16 copy) into the snapshot of
     ``version % 2`` and returns ``(gpu_uuid, version, handle)``. Two buffers let
     an engine still copying version ``v`` overlap the trainer publishing
     ``v + 1``. The snapshots stay on the GPU while the trainer is offloaded
@@ -72,10 +73,12 @@ class DevicePublisher:
         if self._bufs[i] is None:
             self._bufs[i] = torch.empty(self.flat.numel, dtype=torch.bfloat16, device=self.device)
             self._handles[i] = export_ipc_flat(self._bufs[i])
-        src = self.flat.master
+        src = self.flat.sync_source
         from ..ops.functional import native
 
-        if native(src):
+        if src.dtype == self._bufs[i].dtype:
+            self._bufs[i].copy_(src)
+        elif native(src):
             from ..ops._ext import ext
 
             ext().cast_copy(src, self._bufs[i])
