@@ -17,6 +17,13 @@ B200 layout: the backbone lives in flat buffers (bf16 compute, fp32 master,
 gradients accumulated by the wgrad GEMM epilogues, one AdamW kernel); the
 fp32 value head has its own tiny optimiser; the DP gradient reduction is the
 same flat-buffer reducer the actor uses.
+
+Optimiser grouping follows the reference critic (``critic/engine.py:158-168``,
+``vapo.py:44-50``): without ``optimizer_kwargs`` one AdamW group with PyTorch's
+defaults (weight decay 0.01 on every parameter); with them, a decay group
+(matrices, ``weight_decay`` from the kwargs, default 0.01) and a no-decay group
+(vectors and biases), and those explicit settings stay authoritative when a
+checkpoint with another grouping is restored (:meth:`load_state`).
 """
 
 from __future__ import annotations
@@ -38,7 +45,7 @@ from .model import CriticModel
 class CriticTrainer:
     def __init__(self, args: ModelArgs, *, device="cpu", lr: float = 5e-6, warmup_steps: int = 10,
                  max_norm: float = 1.0, value_clip: float | None = None, gamma: float = 1.0,
-                 weight_decay: float = 0.0, betas=(0.9, 0.999), eps: float = 1e-8, seq_len: int = 8192,
+                 optimizer_kwargs: dict | None = None, seq_len: int = 8192,
                  max_tokens_per_micro: int | None = None, dp_group=None, train_backbone: bool = True, seed: int = 0,
                  model: CriticModel | None = None):
         self.args = args
@@ -55,9 +62,21 @@ class CriticTrainer:
         self.model = model if model is not None else CriticModel(args, seed=seed, device=self.device)
         cdt = torch.bfloat16 if self.device.type == "cuda" else torch.float32
         self.flat = FlatParams(self.model.backbone, compute_dtype=cdt, device=self.device)
-        self.opt = FlatAdamW(self.flat, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, max_norm=0.0)
-        self.head_opt = torch.optim.AdamW([self.model.value_head, self.model.value_bias], lr=lr, betas=betas,
-                                          eps=eps, weight_decay=0.0)
+        opts = dict(optimizer_kwargs or {})
+        wd = float(opts.pop("weight_decay", 0.01))
+        betas = tuple(opts.pop("betas", (0.9, 0.999)))
+        eps = float(opts.pop("eps", 1e-8))
+        #: explicit optimiser settings win over a restored checkpoint's (grouping and hyperparameters)
+        self.restore_optimizer_config = optimizer_kwargs is not None
+        self.grouped = optimizer_kwargs is not None
+        self.opt = FlatAdamW(self.flat, lr=lr, betas=betas, eps=eps, weight_decay=wd, max_norm=0.0)
+        if self.grouped:
+            self.opt.set_decay_slots(s.name for s in self.flat.slots if len(s.shape) >= 2)
+            head_groups = [{"params": [self.model.value_head], "weight_decay": wd},
+                           {"params": [self.model.value_bias], "weight_decay": 0.0}]
+        else:
+            head_groups = [{"params": [self.model.value_head, self.model.value_bias], "weight_decay": wd}]
+        self.head_opt = torch.optim.AdamW(head_groups, lr=lr, betas=betas, eps=eps)
         self.reducer = GradReducer(self.flat, dp_group)
         self.train_steps = 0
 
@@ -168,6 +187,135 @@ class CriticTrainer:
         window_loss = float(self._all_sum(torch.tensor(float(num))) / denom)
         return window_loss, values, {"critic/value_loss": window_loss, "critic/grad_norm": gn, "critic/lr": lr,
                                      "critic/tokens": denom}
+
+    # ------------------------------------------------------------------ DCP state (reference layout)
+    def _fqn_slots(self):
+        """(torchtitan FQN, backbone slot, piece shape) of every backbone tensor, in slot order."""
+        from ...models.titan_names import titan_pieces
+
+        out = []
+        for s in self.flat.slots:
+            for fqn, t in titan_pieces(self.args, s.name, torch.empty(s.shape, device="meta")):
+                out.append((fqn, s, tuple(t.shape)))
+        return out
+
+    def _pieces(self, buf: torch.Tensor, s):
+        from ...models.titan_names import titan_pieces
+
+        return [t for _, t in titan_pieces(self.args, s.name, buf[s.offset:s.offset + s.numel].view(s.shape))]
+
+    def _groups_doc(self) -> list[dict]:
+        """param_groups as PyTorch's FQN-keyed state dict writes them."""
+        o = self.opt
+        base = {"lr": float(o.lr), "betas": tuple(float(b) for b in o.betas), "eps": float(o.eps), "amsgrad": False,
+                "maximize": False}
+        fqns = [(q, s, None) for q, s, _ in self._fqn_slots()]
+        if not self.grouped:
+            return [dict(base, weight_decay=float(o.weight_decay),
+                         params=[q for q, _, _ in fqns] + ["value_head.weight", "value_head.bias"])]
+        decay = set(o.decay_names or [])
+        return [dict(base, weight_decay=float(o.weight_decay),
+                     params=[q for q, s, _ in fqns if s.name in decay] + ["value_head.weight"]),
+                dict(base, weight_decay=0.0, params=[q for q, s, _ in fqns if s.name not in decay] +
+                     ["value_head.bias"])]
+
+    def save_state(self, path: str) -> None:
+        """The critic's value net and AdamW state as DCP ``{"model": ..., "optim": {"state", "param_groups"}}``
+        under torchtitan FQNs (``value_head.weight`` / ``value_head.bias`` for the head), as the reference
+        critic writes it. Collective over the DP group: each rank writes the parameters it owns."""
+        import torch.distributed.checkpoint as dcp
+
+        from ..checkpoint import _owners
+
+        self.flat.gather_master()
+        world = self.dp_world
+        rank = dist.get_rank(self.dp_group) if world > 1 else 0
+        owner = _owners(self.flat.slots, world)
+        f, n = self.flat, float(self.opt.step_count)
+        model, state = {}, {}
+        names_of: dict = {}
+        for q, s, _ in self._fqn_slots():
+            names_of.setdefault(s.name, []).append(q)
+        for s, who in zip(f.slots, owner):
+            if who != rank:
+                continue
+            for q, w, m, v in zip(names_of[s.name], self._pieces(f.master, s), self._pieces(f.exp_avg, s),
+                                  self._pieces(f.exp_avg_sq, s)):
+                model[q] = w.detach().float().cpu().contiguous()
+                state[q] = {"step": torch.tensor(n), "exp_avg": m.detach().float().cpu().contiguous(),
+                            "exp_avg_sq": v.detach().float().cpu().contiguous()}
+        if rank == 0:
+            head = {"value_head.weight": self.model.value_head, "value_head.bias": self.model.value_bias}
+            for q, p in head.items():
+                model[q] = p.detach().float().cpu().clone()
+                st = self.head_opt.state.get(p, {})
+                state[q] = {"step": torch.tensor(float(st["step"]) if "step" in st else 0.0),
+                            "exp_avg": st.get("exp_avg", torch.zeros_like(p)).detach().float().cpu().clone(),
+                            "exp_avg_sq": st.get("exp_avg_sq", torch.zeros_like(p)).detach().float().cpu().clone()}
+        doc = {"model": model, "optim": {"state": state}}
+        if rank == 0:
+            doc["optim"]["param_groups"] = self._groups_doc()
+        group = self.dp_group if world > 1 else None
+        dcp.save(doc, checkpoint_id=path, process_group=group, no_dist=group is None)
+
+    def load_state(self, path: str) -> None:
+        """Restore what :meth:`save_state` wrote (or the reference critic's checkpoint). Moments and steps are
+        matched by parameter name, whatever grouping the checkpoint had. With explicit ``optimizer_kwargs`` the
+        current groups and hyperparameters stay; without them the saved hyperparameters are applied."""
+        import os
+
+        import torch.distributed.checkpoint as dcp
+
+        from ...models.titan_names import join_pieces
+
+        if not os.path.isdir(path):
+            raise FileNotFoundError(f"not a critic checkpoint directory: {path}")
+        f = self.flat
+        plan: dict = {}
+        want_model, want_state = {}, {}
+        for q, s, shape in self._fqn_slots():
+            plan.setdefault(s.name, (s, []))[1].append(q)
+            want_model[q] = torch.empty(shape, dtype=torch.float32)
+            want_state[q] = {"step": torch.tensor(0.0), "exp_avg": torch.empty(shape, dtype=torch.float32),
+                             "exp_avg_sq": torch.empty(shape, dtype=torch.float32)}
+        for q, p in (("value_head.weight", self.model.value_head), ("value_head.bias", self.model.value_bias)):
+            want_model[q] = torch.empty(p.shape, dtype=torch.float32)
+            want_state[q] = {"step": torch.tensor(0.0), "exp_avg": torch.empty(p.shape, dtype=torch.float32),
+                             "exp_avg_sq": torch.empty(p.shape, dtype=torch.float32)}
+        doc = {"model": want_model, "optim": {"state": want_state}}
+        if not self.restore_optimizer_config:
+            from torch.distributed.checkpoint import FileSystemReader
+
+            meta = FileSystemReader(path).read_metadata().state_dict_metadata
+            if any(k.startswith("optim.param_groups") for k in meta):
+                doc["optim"]["param_groups"] = self._groups_doc()
+        group = self.dp_group if self.dp_world > 1 else None
+        dcp.load(doc, checkpoint_id=path, process_group=group, no_dist=group is None)
+        steps = 0
+        with torch.no_grad():
+            for name, (s, qs) in plan.items():
+                f.master[s.offset:s.offset + s.numel].copy_(join_pieces(self.args, name, [want_model[q] for q in qs])
+                                                            .reshape(-1))
+                f.exp_avg[s.offset:s.offset + s.numel].copy_(
+                    join_pieces(self.args, name, [want_state[q]["exp_avg"] for q in qs]).reshape(-1))
+                f.exp_avg_sq[s.offset:s.offset + s.numel].copy_(
+                    join_pieces(self.args, name, [want_state[q]["exp_avg_sq"] for q in qs]).reshape(-1))
+                steps = max(steps, int(float(want_state[qs[0]]["step"])))
+            f.recast()
+            for q, p in (("value_head.weight", self.model.value_head), ("value_head.bias", self.model.value_bias)):
+                p.copy_(want_model[q].reshape(p.shape))
+                st = want_state[q]
+                self.head_opt.state[p] = {"step": st["step"].clone(), "exp_avg": st["exp_avg"].to(p.device).clone(),
+                                          "exp_avg_sq": st["exp_avg_sq"].to(p.device).clone()}
+        self.opt.step_count = steps
+        groups = doc["optim"].get("param_groups")
+        if groups and not self.restore_optimizer_config:
+            g0 = groups[0]
+            self.opt.betas = tuple(g0["betas"])
+            self.opt.eps = float(g0["eps"])
+            self.opt.weight_decay = float(g0["weight_decay"])
+            for hg in self.head_opt.param_groups:
+                hg["betas"], hg["eps"] = tuple(g0["betas"]), float(g0["eps"])
 
     # ------------------------------------------------------------------ state
     def state_dict(self) -> dict:

@@ -208,10 +208,41 @@ class FlatAdamW:
         self.step_count = 0
         self.mirror: torch.Tensor | None = None
 
+    def set_decay_slots(self, names) -> None:
+        """Apply weight decay only to the named parameters (a decay / no-decay grouping); ``None`` restores
+        decay on every parameter."""
+        if names is None:
+            self.decay_names = None
+            return
+        wanted = set(names)
+        self.decay_names = [s.name for s in self.flat.slots if s.name in wanted]
+
+    def _decay_views(self):
+        f = self.flat
+        by_name = {s.name: s for s in f.slots}
+        return [f.master[by_name[n].offset:by_name[n].offset + by_name[n].numel] for n in self.decay_names]
+
     def step(self, grad_norm: torch.Tensor | None = None) -> torch.Tensor:
         f = self.flat
         if grad_norm is None:
             grad_norm = f.grad_norm()
+        if getattr(self, "decay_names", None) is not None:
+            # grouped decay: the decoupled factor (1 - lr * wd) multiplies the decaying parameters before an
+            # update without decay -- the same result as AdamW with per-group weight decay
+            wd = self.weight_decay
+            self.weight_decay = 0.0
+            try:
+                with torch.no_grad():
+                    views = self._decay_views()
+                    if views and wd:
+                        torch._foreach_mul_(views, 1.0 - self.lr * wd)
+                return self._step(grad_norm)
+            finally:
+                self.weight_decay = wd
+        return self._step(grad_norm)
+
+    def _step(self, grad_norm: torch.Tensor) -> torch.Tensor:
+        f = self.flat
         self.step_count += 1
         b1, b2 = self.betas
         if f.grad.is_cuda and not native(f.grad):

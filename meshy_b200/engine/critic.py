@@ -48,11 +48,9 @@ class CriticSpmdEngine(SpmdEngine):
         c = self.cfg
         tc = c.trainer_config
         args = get_model_args(tc.model_name, tc.model_flavor)
-        opt = dict(c.optimizer_kwargs or {})
         self.trainer = CriticTrainer(
             args, device=self.device, lr=c.lr, warmup_steps=c.warmup_steps, max_norm=c.max_norm,
-            value_clip=c.value_clip, gamma=c.gamma, weight_decay=opt.get("weight_decay", 0.0),
-            betas=tuple(opt.get("betas", (0.9, 0.999))), eps=opt.get("eps", 1e-8), seq_len=tc.seq_len,
+            value_clip=c.value_clip, gamma=c.gamma, optimizer_kwargs=c.optimizer_kwargs, seq_len=tc.seq_len,
             max_tokens_per_micro=c.max_tokens_per_micro, dp_group=self.compute_group if self.world_size > 1 else None,
             train_backbone=c.train_backbone)
         if c.model_path and os.path.isdir(c.model_path):
@@ -159,8 +157,8 @@ class CriticSpmdEngine(SpmdEngine):
         store = self.runtime.state_store()
         d = store.shard_dir(self.service_name, step)
         os.makedirs(d, exist_ok=True)
+        self.trainer.save_state(d)  # collective: every rank writes its share
         if self.rank == 0:
-            torch.save(self.trainer.state_dict(), os.path.join(d, "critic.pt"))
             store.write_meta(self.service_name, step, {"windows": self.windows, "train_steps": self.trainer.train_steps})
             store.mark_complete(self.service_name, step)
             store.prune(self.service_name, self.checkpoint.keep_latest_k)
@@ -172,9 +170,8 @@ class CriticSpmdEngine(SpmdEngine):
         store = self.runtime.state_store()
         if not store.is_complete(self.service_name, resume_step):
             raise FileNotFoundError(f"no critic shard at global step {resume_step}")
-        sd = torch.load(os.path.join(store.shard_dir(self.service_name, resume_step), "critic.pt"),
-                        map_location="cpu", weights_only=False)
-        self.trainer.load_state_dict(sd)
+        self.trainer.load_state(store.shard_dir(self.service_name, resume_step))
+        self.trainer.train_steps = int(store.payload(self.service_name, resume_step).get("train_steps", 0))
         self.windows = int(store.payload(self.service_name, resume_step)["windows"])
         return True
 
