@@ -47,7 +47,7 @@ class CriticTrainer:
                  max_norm: float = 1.0, value_clip: float | None = None, gamma: float = 1.0,
                  optimizer_kwargs: dict | None = None, seq_len: int = 8192,
                  max_tokens_per_micro: int | None = None, dp_group=None, train_backbone: bool = True, seed: int = 0,
-                 model: CriticModel | None = None):
+                 model: CriticModel | None = None, cp_group=None, loss_group=None):
         self.args = args
         self.device = torch.device(device)
         self.dp_group = dp_group
@@ -77,7 +77,15 @@ class CriticTrainer:
         else:
             head_groups = [{"params": [self.model.value_head, self.model.value_bias], "weight_decay": wd}]
         self.head_opt = torch.optim.AdamW(head_groups, lr=lr, betas=betas, eps=eps)
-        self.reducer = GradReducer(self.flat, dp_group)
+        # context parallelism: every row of a micro-batch is padded to a multiple of 2 x cp and split head-tail
+        # over the CP group (reference ``critic/engine.py:561-618``); gradients then sum over DP x CP
+        self.cp = None
+        if cp_group is not None and dist.is_initialized() and dist.get_world_size(cp_group) > 1:
+            from ...parallel.cp import CpSharder
+
+            self.cp = CpSharder(cp_group)
+        self.loss_group = loss_group if loss_group is not None else dp_group
+        self.reducer = GradReducer(self.flat, self.loss_group)
         self.train_steps = 0
 
     # ------------------------------------------------------------------ helpers
@@ -87,11 +95,12 @@ class CriticTrainer:
             return 1
         return dist.get_world_size(self.dp_group)
 
-    def _all_sum(self, x: torch.Tensor) -> torch.Tensor:
-        if self.dp_world > 1:
-            dev = self.device if dist.get_backend(self.dp_group) == "nccl" else torch.device("cpu")
+    def _all_sum(self, x: torch.Tensor, group=None) -> torch.Tensor:
+        g = self.dp_group if group is None else group
+        if g is not None and dist.is_initialized() and dist.get_world_size(g) > 1:
+            dev = self.device if dist.get_backend(g) == "nccl" else torch.device("cpu")
             y = x.detach().to(dev).clone()
-            dist.all_reduce(y, group=self.dp_group)
+            dist.all_reduce(y, group=g)
             return y.to(x.device)
         return x
 
@@ -100,7 +109,45 @@ class CriticTrainer:
 
     def _forward(self, mb: CriticMicro) -> torch.Tensor:
         d = self.device
+        if getattr(mb, "cp_layout", None) is not None:
+            from ...parallel.cp import cp_attention
+
+            with cp_attention(self.cp, mb.cp_layout):
+                return self.model(mb.input_ids.to(d), mb.positions.to(d), mb.cu_seqlens.to(d), mb.max_seqlen)
         return self.model(mb.input_ids.to(d), mb.positions.to(d), mb.cu_seqlens.to(d), mb.max_seqlen)
+
+    def _cp_shard(self, mb: CriticMicro) -> CriticMicro:
+        """Pad every row of a packed micro-batch to one length divisible by 2 x cp and keep this CP rank's
+        head-tail chunks (ids, positions, mask and returns alike)."""
+        from ...parallel.cp import CpLayout
+
+        rows = len(mb.rows)
+        div = 2 * self.cp.size
+        S = -(-mb.max_seqlen // div) * div
+        def pad(t, fill=0):
+            out = torch.full((rows, S), fill, dtype=t.dtype)
+            off = 0
+            for r, L in enumerate(mb.lengths):
+                out[r, :L] = t[off:off + L]
+                off += L
+            return out
+        ids, msk, ret = pad(mb.input_ids), pad(mb.mask), pad(mb.returns)
+        pos = torch.arange(S, dtype=torch.int32).repeat(rows, 1)
+        ids, pos, msk, ret = self.cp.shard_seq(ids, pos, msk, ret)
+        L = ids.shape[1]
+        sh = CriticMicro(mb.rows, ids.reshape(-1), pos.reshape(-1),
+                         torch.arange(0, rows * L + 1, L, dtype=torch.int32), L, msk.reshape(-1), ret.reshape(-1),
+                         list(mb.lengths))
+        sh.cp_layout = CpLayout(rows, S, S // div)
+        return sh
+
+    def _values_of(self, mb: CriticMicro, v: torch.Tensor) -> dict[int, torch.Tensor]:
+        """Per-row values of a micro-batch (a CP micro gathers the full rows from the CP group first)."""
+        if getattr(mb, "cp_layout", None) is None:
+            return self._split_values(mb, v)
+        rows = len(mb.rows)
+        (full,) = self.cp.gather_seq(v.detach().view(rows, -1))
+        return {r: full[j, :L].float().cpu() for j, (r, L) in enumerate(zip(mb.rows, mb.lengths))}
 
     def _split_values(self, mb: CriticMicro, v: torch.Tensor) -> dict[int, torch.Tensor]:
         out, off = {}, 0
@@ -114,7 +161,9 @@ class CriticTrainer:
     def predict(self, samples: Sequence[TrajectorySample], rows: Sequence[int]) -> dict[int, torch.Tensor]:
         out: dict[int, torch.Tensor] = {}
         for mb in self._micros(samples, rows):
-            out.update(self._split_values(mb, self._forward(mb)))
+            if self.cp is not None:
+                mb = self._cp_shard(mb)
+            out.update(self._values_of(mb, self._forward(mb)))
         return out
 
     def _apply_warmup(self) -> float:
@@ -132,8 +181,11 @@ class CriticTrainer:
         self.train_steps += 1
         lr = self._apply_warmup()
         micros = self._micros(samples, rows)
+        # the denominator counts every response token of the window once (full rows, summed over DP)
         local_cnt = torch.tensor(float(sum(float(mb.mask.sum()) for mb in micros)))
         denom = float(self._all_sum(local_cnt).clamp(min=1.0))
+        if self.cp is not None:
+            micros = [self._cp_shard(mb) for mb in micros]
         self.flat.zero_grad()
         self.head_opt.zero_grad(set_to_none=False)
         for p in (self.model.value_head, self.model.value_bias):
@@ -152,6 +204,8 @@ class CriticTrainer:
                                                        mb.cu_seqlens.to(d), mb.max_seqlen)
                     v = (h.float() @ self.model.value_head.t()).squeeze(-1) + self.model.value_bias
                 old = None
+                if old_values is not None and self.cp is not None:
+                    raise NotImplementedError("explicit old values with context parallelism")
                 if old_values is not None:
                     old = torch.cat([old_values[r][:L] for r, L in zip(mb.rows, mb.lengths)]).to(d)
                 elif self.value_clip is not None:
@@ -163,12 +217,12 @@ class CriticTrainer:
                     raise RuntimeError(f"non-finite critic loss: {float(loss)}")
                 loss.backward()
             num += float(numer.detach())
-            values.update(self._split_values(mb, v))
+            values.update(self._values_of(mb, v))
         self.flat.collect_cpu_grads()
         if self.train_backbone:
             self.reducer.finish()
         head = torch.cat([self.model.value_head.grad.reshape(-1), self.model.value_bias.grad.reshape(-1)])
-        head = self._all_sum(head)
+        head = self._all_sum(head, self.loss_group)
         self.model.value_head.grad.copy_(head[:-1].view_as(self.model.value_head))
         self.model.value_bias.grad.copy_(head[-1:])
         gn_bb = self.flat.grad_norm().float().cpu() if self.train_backbone else torch.zeros(())
@@ -184,7 +238,7 @@ class CriticTrainer:
             self.model.value_head.grad.mul_(scale)
             self.model.value_bias.grad.mul_(scale)
         self.head_opt.step()
-        window_loss = float(self._all_sum(torch.tensor(float(num))) / denom)
+        window_loss = float(self._all_sum(torch.tensor(float(num)), self.loss_group) / denom)
         return window_loss, values, {"critic/value_loss": window_loss, "critic/grad_norm": gn, "critic/lr": lr,
                                      "critic/tokens": denom}
 
@@ -228,6 +282,8 @@ class CriticTrainer:
         from ..checkpoint import _owners
 
         self.flat.gather_master()
+        if self.cp is not None and self.cp.rank != 0:
+            return  # CP ranks hold the same weights; the first rank of each CP group writes
         world = self.dp_world
         rank = dist.get_rank(self.dp_group) if world > 1 else 0
         owner = _owners(self.flat.slots, world)

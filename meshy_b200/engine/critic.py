@@ -48,11 +48,19 @@ class CriticSpmdEngine(SpmdEngine):
         c = self.cfg
         tc = c.trainer_config
         args = get_model_args(tc.model_name, tc.model_flavor)
+        groups = {"dp_group": self.compute_group if self.world_size > 1 else None}
+        cp = max(1, int(getattr(tc, "cp_degree", 1)))
+        if cp > 1 and self.world_size > 1:
+            # critic grouping: DP x CP (no TP / EP for the value net); rows are dealt over the DP index only
+            from ..parallel.mesh import build_parallel_dims
+
+            pd = build_parallel_dims(self.world_size, self.rank, dp_replicate=-1, dp_shard=1, cp=cp)
+            self.parallel_dims = pd
+            groups = {"dp_group": pd.batch_group, "cp_group": pd.cp_group, "loss_group": pd.loss_group}
         self.trainer = CriticTrainer(
             args, device=self.device, lr=c.lr, warmup_steps=c.warmup_steps, max_norm=c.max_norm,
             value_clip=c.value_clip, gamma=c.gamma, optimizer_kwargs=c.optimizer_kwargs, seq_len=tc.seq_len,
-            max_tokens_per_micro=c.max_tokens_per_micro, dp_group=self.compute_group if self.world_size > 1 else None,
-            train_backbone=c.train_backbone)
+            max_tokens_per_micro=c.max_tokens_per_micro, train_backbone=c.train_backbone, **groups)
         if c.model_path and os.path.isdir(c.model_path):
             from ..models.hf import load_hf_checkpoint
 
@@ -80,6 +88,9 @@ class CriticSpmdEngine(SpmdEngine):
         n = len(samples)
         lens = [len(s.tokens) for s in samples]
         order = sorted(range(n), key=lambda i: (-lens[i], i))
+        pd = getattr(self, "parallel_dims", None)
+        if pd is not None:  # CP ranks of one DP index share its rows
+            return list(snake_deal(order, pd.dp)[pd.dp_rank])
         return list(snake_deal(order, self.world_size)[self.rank]) if self.world_size > 1 else list(range(n))
 
     def _gather(self, obj):
