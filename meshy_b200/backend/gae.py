@@ -18,6 +18,8 @@ the oracle for the kernel.
 
 from __future__ import annotations
 
+import math
+
 from typing import Any, Sequence
 
 import numpy as np
@@ -142,7 +144,9 @@ def attach_gae(samples: Sequence[Any], seq_len: int, *, gamma: float, alpha: flo
 
 
 def whiten(adv: torch.Tensor, mask: torch.Tensor, group=None, cp_degree: int = 1) -> torch.Tensor:
-    """Global mean/variance whitening over masked tokens (reference ``vapo.py:6-32``)."""
+    """Whitening over the masked tokens of every rank of ``group``: ``(a - mean) / sqrt(var + 1e-8)`` with the
+    unbiased variance (reference ``vapo.py:6-32``); unmasked tokens become 0. ``cp_degree``: ranks of the
+    group that hold replicas of the same full sequences (CP ranks before sharding), counted once."""
     stats = torch.tensor([float((adv * mask).sum()), float((adv * adv * mask).sum()), float(mask.sum())],
                          dtype=torch.float64)
     if group is not None and dist.is_initialized() and dist.get_world_size(group) > 1:
@@ -151,10 +155,12 @@ def whiten(adv: torch.Tensor, mask: torch.Tensor, group=None, cp_degree: int = 1
         dist.all_reduce(st, group=group)
         stats = st.cpu() / cp_degree
     s, s2, n = stats.tolist()
-    n = max(n, 1.0)
-    mean = s / n
-    var = max(s2 / n - mean * mean, 0.0)
-    return ((adv - mean) / (var ** 0.5 + 1e-8)) * mask
+    count = max(n, 1.0)
+    mean = s / count
+    var = max(s2 / count - mean * mean, 0.0)
+    if n >= 2:
+        var *= n / (n - 1)
+    return torch.where(mask > 0, (adv - mean) / math.sqrt(var + 1e-8), torch.zeros_like(adv))
 
 
 __all__ = [
