@@ -908,6 +908,18 @@ void gemm_grouped(Tensor a, Tensor b, Tensor out, Tensor off, int64_t mode, bool
   count();
 }
 
+void filtered_sample_(Tensor logits, double temperature, int64_t top_k, double top_p, int64_t seed,
+                      c10::optional<Tensor> step, Tensor tok, Tensor lp) {
+  CHECK_CUDA(logits);
+  CHECK_F32(logits);
+  CHECK_CONTIG(logits);
+  TORCH_CHECK(tok.scalar_type() == at::kLong && lp.scalar_type() == at::kFloat, "tok int64, lp fp32");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  filtered_sample(ptr<float>(logits), logits.size(0), logits.size(1), (float)temperature, (int)top_k, (float)top_p,
+                  (uint64_t)seed, optr<int64_t>(step), ptr<int64_t>(tok), ptr<float>(lp), cur_stream());
+  count();
+}
+
 // ─── expert parallelism over peer memory ────────────────────────────────────
 using ull = unsigned long long;
 const ull* tab(const Tensor& t) {
@@ -1171,6 +1183,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_small_config", [](int64_t enabled, int64_t cluster) { gemm_small_config((int)enabled, (int)cluster); },
         "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");
   m.def("swiglu_bwd", &swiglu_bwd_);
+  m.def("filtered_sample", &filtered_sample_, "top-k / top-p / temperature sampling over fp32 logits");
   m.def("moe_route", &moe_route_, "router softmax + top-k (+ renormalisation)");
   m.def("moe_route_bwd", &moe_route_bwd_, "router backward: d logits from d weights");
   m.def("moe_plan", &moe_plan_, "device-side expert plan: counts, 128-aligned offsets, slots, gather");

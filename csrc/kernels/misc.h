@@ -21,4 +21,9 @@ void sample_advance(const float* part, int n_parts, int64_t* tok_in, int* pos, i
                     const int* max_new, int* done, int64_t* slot, const int* bt, const int* req, int64_t* out_tok,
                     float* out_lp, const int64_t* eos, int n_eos, int B, int max_pages, int cap, int page,
                     int64_t* step, cudaStream_t st);
+// Top-k / top-p (and temperature) sampling over fp32 logits [B, V], one CTA per row (sampling.cu): token and
+// its log-probability under the filtered, tempered distribution; temperature 0 is greedy.
+void filtered_sample(const float* logits, int B, int V, float temperature, int top_k, float top_p, uint64_t seed,
+                     const int64_t* step_ptr, int64_t* tok, float* lp, cudaStream_t st);
+
 }  // namespace meshy

@@ -15,7 +15,8 @@
   tcgen05 tiles, keeps an online log-sum-exp and a Gumbel-max argmax per row,
   and a final pass merges the per-CTA partials.  Temperature-only sampling
   (every shipped recipe: temperature 1, top_p 1, top_k -1) takes this path;
-  top-k / top-p materialise logits and filter them.
+  top-k / top-p write fp32 logits with the tcgen05 GEMM and filter and draw
+  in one kernel per row (``_C.filtered_sample``), still without a host sync.
 * :func:`decode_advance` — per-row bookkeeping after sampling (append token,
   bump lengths, recompute the next cache slot, finish flags), so a whole
   decode step can be replayed from a CUDA graph with no host work.
@@ -170,6 +171,16 @@ def sample(h, w, temperature: float, *, top_k: int = -1, top_p: float = 1.0, see
         tok = torch.empty(B, dtype=torch.int64, device=h.device)
         lp = torch.empty(B, dtype=torch.float32, device=h.device)
         ext().lmhead_sample(h, w, tok, lp, float(temperature), int(seed), step)
+        return tok, lp
+    if native(h):  # top-k / top-p or greedy: fp32 logits from the tcgen05 GEMM, then the filtered sampler
+        from ._ext import ext
+
+        B, V = h.shape[0], w.shape[0]
+        logits = torch.empty(B, V, dtype=torch.float32, device=h.device)
+        ext().gemm(h.contiguous(), w, logits, False, False, None, None, None, 0, False, 0)
+        tok = torch.empty(B, dtype=torch.int64, device=h.device)
+        lp = torch.empty(B, dtype=torch.float32, device=h.device)
+        ext().filtered_sample(logits, float(temperature), int(top_k), float(top_p), int(seed), step, tok, lp)
         return tok, lp
     if h.is_cuda and temperature > 0 and top_k <= 0 and top_p >= 1.0:
         return _library_sample(h, w, temperature)

@@ -28,6 +28,7 @@ cuda_sources = [
     "csrc/kernels/misc.cu",
     "csrc/kernels/moe.cu",
     "csrc/kernels/ep.cu",
+    "csrc/kernels/sampling.cu",
     "csrc/kernels/decode_noalloc.cu",
     "csrc/kernels/decode_mega.cu",
 ]

@@ -37,15 +37,27 @@ def test_launcher_colocated_grpo_with_device_weight_sync(tmp_path):
                XRL_SMOKE_WEIGHT_SYNC="device", PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0",
                XRL_PORT_OFFSET=str(100 + (_free_port() % 400) * 10))
     rt = tmp_path / "rt"
-    r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
-                        "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
-                       capture_output=True, text=True, timeout=840)
+    proc = subprocess.Popen([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
+                             "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
+                            stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, start_new_session=True)
+    timed_out = False
+    try:
+        out, _ = proc.communicate(timeout=int(os.environ.get("MESHY_LAUNCH_GPU_TIMEOUT", "600")))
+    except subprocess.TimeoutExpired:
+        timed_out = True
+        import signal
+
+        os.killpg(proc.pid, signal.SIGTERM)
+        out, _ = proc.communicate(timeout=60)
     logs = rt / "logs"
-    detail = r.stdout[-2000:] + r.stderr[-2000:]
+    detail = (out or "")[-3000:]
     if logs.exists():
         for f in sorted(logs.iterdir()):
-            detail += f"\n==== {f.name}\n" + f.read_text(errors="replace")[-2000:]
-    assert r.returncode == 0, detail
+            detail += f"\n==== {f.name}\n" + f.read_text(errors="replace")[-2500:]
+    if timed_out or proc.returncode != 0:
+        print(detail)
+    assert not timed_out, "launcher run timed out\n" + detail
+    assert proc.returncode == 0, detail
     rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
     assert len(rows) == 3, detail
     # every engine loaded versions 1..3 from the trainer snapshot on its own GPU, with no disk export

@@ -127,46 +127,59 @@ def test_expert_layer_is_graph_capturable():
     assert _rel(eager, again) > 1e-2  # the replay saw the new input
 
 
-def test_qwen3_moe_model_native_matches_torch_path():
+def test_qwen3_moe_model_native_matches_fp32_torch_path():
+    """The whole Qwen3-MoE model: native bf16 log-probs and gradients against the PyTorch path run in fp32 on
+    the same weights (the experts chosen by the native router are used on both sides, so near-equal bf16
+    router logits cannot send a token to different experts in the two runs)."""
     from meshy_b200.models import build_model, get_model_args
     from meshy_b200.ops import functional as Fx
+    import meshy_b200.models.moe as moe_mod
 
     args = get_model_args("qwen3", "debugmodel_moe")
     torch.manual_seed(0)
     model = build_model(args, seed=0, device=DEV, dtype=torch.bfloat16)
+    ref = build_model(args, seed=0, device=DEV, dtype=torch.float32)
+    with torch.no_grad():
+        for (n, p), (_, q) in zip(model.named_parameters(), ref.named_parameters()):
+            q.copy_(p.float())
     lens = [37, 100, 3]
     T = sum(lens)
     ids = torch.randint(0, args.vocab_size, (T,), device=DEV)
     labels = torch.randint(0, args.vocab_size, (T,), device=DEV)
     pos = torch.cat([torch.arange(L, device=DEV) for L in lens]).int()
     cu = torch.tensor([0, 37, 137, 140], dtype=torch.int32, device=DEV)
-    lp, _ = model.logprobs(ids, labels, pos, cu, max(lens))
-    lp.sum().backward()
-    g_native = {n: p.grad.float().clone() for n, p in model.named_parameters() if p.grad is not None}
-    model.zero_grad(set_to_none=True)
-    # the PyTorch path routes with the experts the kernel picked: near-equal bf16 router logits may be ordered
-    # differently by torch.topk, which would make the two paths train different experts for those tokens
-    import meshy_b200.models.moe as moe_mod
+    picks = []
+    real_route = M.route
 
-    def same_experts(x, w_router, top_k, route_norm):
-        logits = Fx.linear(x, w_router)
-        with torch.no_grad():
-            _, e = M.route(logits.detach(), top_k, route_norm)
-        w = torch.softmax(logits.float(), -1).gather(-1, e.long())
-        if route_norm:
-            w = w / w.sum(-1, keepdim=True)
-        return w, e.long()
+    def recording_route(logits, k, norm):
+        w, e = real_route(logits, k, norm)
+        picks.append(e.detach().long())
+        return w, e
 
     mp = pytest.MonkeyPatch()
-    mp.setattr(moe_mod, "route", same_experts)
+    mp.setattr(M, "route", recording_route)
     try:
-        with Fx.torch_baseline(True):
-            lp_t, _ = model.logprobs(ids, labels, pos, cu, max(lens))
-            lp_t.sum().backward()
+        lp, _ = model.logprobs(ids, labels, pos, cu, max(lens))
+        lp.sum().backward()
     finally:
         mp.undo()
-    assert _rel(lp, lp_t) < 2e-2
-    for n, p in model.named_parameters():
-        if p.grad is None or n not in g_native:
-            continue
-        assert _rel(g_native[n], p.grad) < 6e-2, n
+    calls = iter(picks)
+
+    def replay_route(x, w_router, top_k, route_norm):
+        e = next(calls)
+        w = torch.softmax(Fx.linear(x, w_router).float(), -1).gather(-1, e)
+        if route_norm:
+            w = w / w.sum(-1, keepdim=True)
+        return w, e
+
+    mp.setattr(moe_mod, "route", replay_route)
+    try:
+        with Fx.torch_baseline(True):  # fp32 PyTorch ops on the GPU
+            lp_ref, _ = ref.logprobs(ids, labels, pos, cu, max(lens))
+            lp_ref.sum().backward()
+    finally:
+        mp.undo()
+    assert _rel(lp, lp_ref) < 2e-2
+    for (n, p), (_, q) in zip(model.named_parameters(), ref.named_parameters()):
+        assert p.grad is not None and q.grad is not None, n
+        assert _rel(p.grad, q.grad) < 6e-2, n

@@ -61,6 +61,8 @@ def _numerics(rank, world, port, q):
         gn = opt.step()
         torch.cuda.synchronize()
         opt.check()
+        # the fp32 master is sharded like the moments (only bf16 is replicated by the step): gather it to compare
+        flat.gather_master()
         assert abs(float(gn) - norm) <= 1e-4 * norm, (float(gn), norm)
         err = (flat.master - ref_p).abs().max().item()
         assert err < 1e-6, err
