@@ -920,6 +920,32 @@ void filtered_sample_(Tensor logits, double temperature, int64_t top_k, double t
   count();
 }
 
+void value_head_fwd_(Tensor h, Tensor w, Tensor b, Tensor ret, Tensor mask, c10::optional<Tensor> old, double clip,
+                     double inv_denom, Tensor v, Tensor dv, Tensor num) {
+  CHECK_CUDA(h);
+  CHECK_BF16(h);
+  CHECK_CONTIG(h);
+  CHECK_F32(w);
+  const int T = h.size(0), D = h.size(1);
+  TORCH_CHECK(w.numel() == D && ret.numel() == T && mask.numel() == T && v.numel() == T && dv.numel() == T,
+              "value_head_fwd: shapes");
+  const c10::cuda::CUDAGuard guard(h.device());
+  value_head_fwd(ptr<bf16>(h), ptr<float>(w), ptr<float>(b), T, D, ptr<float>(ret), ptr<float>(mask), optr<float>(old),
+                 (float)clip, (float)inv_denom, ptr<float>(v), ptr<float>(dv), ptr<float>(num), cur_stream());
+  count();
+}
+
+void value_head_bwd_(Tensor h, Tensor w, Tensor dv, Tensor dh, Tensor dw, Tensor db) {
+  CHECK_CUDA(h);
+  CHECK_BF16(h);
+  CHECK_BF16(dh);
+  CHECK_F32(dw);
+  const c10::cuda::CUDAGuard guard(h.device());
+  value_head_bwd(ptr<bf16>(h), ptr<float>(w), ptr<float>(dv), h.size(0), h.size(1), ptr<bf16>(dh), ptr<float>(dw),
+                 ptr<float>(db), cur_stream());
+  count();
+}
+
 // ─── expert parallelism over peer memory ────────────────────────────────────
 using ull = unsigned long long;
 const ull* tab(const Tensor& t) {
@@ -1184,6 +1210,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "small-M GEMM switches: enabled (1/0, -1 keep), cluster split-K size (0 auto, -1 keep)");
   m.def("swiglu_bwd", &swiglu_bwd_);
   m.def("filtered_sample", &filtered_sample_, "top-k / top-p / temperature sampling over fp32 logits");
+  m.def("value_head_fwd", &value_head_fwd_, "critic value head + clipped value loss (values, dL/dv, loss sum)");
+  m.def("value_head_bwd", &value_head_bwd_, "critic value head backward: dh, dw, db");
   m.def("moe_route", &moe_route_, "router softmax + top-k (+ renormalisation)");
   m.def("moe_route_bwd", &moe_route_bwd_, "router backward: d logits from d weights");
   m.def("moe_plan", &moe_plan_, "device-side expert plan: counts, 128-aligned offsets, slots, gather");

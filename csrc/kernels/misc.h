@@ -26,4 +26,11 @@ void sample_advance(const float* part, int n_parts, int64_t* tok_in, int* pos, i
 void filtered_sample(const float* logits, int B, int V, float temperature, int top_k, float top_p, uint64_t seed,
                      const int64_t* step_ptr, int64_t* tok, float* lp, cudaStream_t st);
 
+// Critic value head fused with the clipped value loss (value_head.cu). fwd: v = h w + b, num += sum(err *
+// mask), dv = mask * d err / dv / denom; bwd: dh = dv w^T (bf16), dw += dv^T h, db += sum dv (fp32).
+void value_head_fwd(const bf16* h, const float* w, const float* b, int T, int D, const float* ret, const float* mask,
+                    const float* old, float clip, float inv_denom, float* v, float* dv, float* num, cudaStream_t st);
+void value_head_bwd(const bf16* h, const float* w, const float* dv, int T, int D, bf16* dh, float* dw, float* db,
+                    cudaStream_t st);
+
 }  // namespace meshy

@@ -37,9 +37,8 @@ import torch.distributed as dist
 from ...models.args import ModelArgs
 from ...parallel.ddp import GradReducer
 from ..flat import FlatAdamW, FlatParams
-from ..vapo import clipped_value_error
 from .data import CriticMicro, TrajectorySample, pack_micros
-from .model import CriticModel
+from .model import CriticModel, value_head_loss
 
 
 class CriticTrainer:
@@ -115,6 +114,17 @@ class CriticTrainer:
             with cp_attention(self.cp, mb.cp_layout):
                 return self.model(mb.input_ids.to(d), mb.positions.to(d), mb.cu_seqlens.to(d), mb.max_seqlen)
         return self.model(mb.input_ids.to(d), mb.positions.to(d), mb.cu_seqlens.to(d), mb.max_seqlen)
+
+    def _hidden(self, mb: CriticMicro) -> torch.Tensor:
+        """Final normed hidden states of a micro-batch (the value head's input)."""
+        d = self.device
+        args = (mb.input_ids.to(d), mb.positions.to(d), mb.cu_seqlens.to(d), mb.max_seqlen)
+        if getattr(mb, "cp_layout", None) is not None:
+            from ...parallel.cp import cp_attention
+
+            with cp_attention(self.cp, mb.cp_layout):
+                return self.model.backbone.hidden(*args)
+        return self.model.backbone.hidden(*args)
 
     def _cp_shard(self, mb: CriticMicro) -> CriticMicro:
         """Pad every row of a packed micro-batch to one length divisible by 2 x cp and keep this CP rank's
@@ -196,27 +206,24 @@ class CriticTrainer:
         d = self.device
         for mb in micros:
             with torch.set_grad_enabled(True):
-                if self.train_backbone:
-                    v = self._forward(mb)
-                else:
-                    with torch.no_grad():
-                        h = self.model.backbone.hidden(mb.input_ids.to(d), mb.positions.to(d),
-                                                       mb.cu_seqlens.to(d), mb.max_seqlen)
-                    v = (h.float() @ self.model.value_head.t()).squeeze(-1) + self.model.value_bias
+                with torch.set_grad_enabled(self.train_backbone):
+                    h = self._hidden(mb)
                 old = None
                 if old_values is not None and self.cp is not None:
                     raise NotImplementedError("explicit old values with context parallelism")
                 if old_values is not None:
                     old = torch.cat([old_values[r][:L] for r, L in zip(mb.rows, mb.lengths)]).to(d)
                 elif self.value_clip is not None:
-                    old = v.detach()
-                err = clipped_value_error(v, mb.returns.to(d), old, self.value_clip) * mb.mask.to(d)
-                numer = err.sum()
-                loss = numer / denom
+                    # this window's own forward is the old value of its clipping (pre-update weights)
+                    with torch.no_grad():
+                        _, old = value_head_loss(h.detach(), self.model.value_head, self.model.value_bias,
+                                                 mb.returns.to(d), mb.mask.to(d), None, None, 1.0)
+                loss, v = value_head_loss(h, self.model.value_head, self.model.value_bias, mb.returns.to(d),
+                                          mb.mask.to(d), old, self.value_clip, denom)
                 if not torch.isfinite(loss):
                     raise RuntimeError(f"non-finite critic loss: {float(loss)}")
                 loss.backward()
-            num += float(numer.detach())
+            num += float(loss.detach()) * denom
             values.update(self._values_of(mb, v))
         self.flat.collect_cpu_grads()
         if self.train_backbone:

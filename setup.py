@@ -29,6 +29,7 @@ cuda_sources = [
     "csrc/kernels/moe.cu",
     "csrc/kernels/ep.cu",
     "csrc/kernels/sampling.cu",
+    "csrc/kernels/value_head.cu",
     "csrc/kernels/decode_noalloc.cu",
     "csrc/kernels/decode_mega.cu",
 ]
