@@ -946,6 +946,53 @@ void value_head_bwd_(Tensor h, Tensor w, Tensor dv, Tensor dh, Tensor dw, Tensor
   count();
 }
 
+void topk_logprobs_(Tensor z, int64_t k, Tensor ids, Tensor lp, c10::optional<Tensor> lse) {
+  CHECK_CUDA(z);
+  CHECK_F32(z);
+  TORCH_CHECK(z.dim() == 2 && z.stride(1) == 1, "topk_logprobs: z [T, V] row-major");
+  const int T = z.size(0);
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.numel() == (int64_t)T * k,
+              "topk_logprobs: ids [T, K] int64");
+  TORCH_CHECK(lp.scalar_type() == at::kFloat && lp.is_contiguous() && lp.numel() == (int64_t)T * k,
+              "topk_logprobs: lp [T, K] fp32");
+  TORCH_CHECK(!lse || (lse->scalar_type() == at::kFloat && lse->numel() == T), "topk_logprobs: lse [T] fp32");
+  const c10::cuda::CUDAGuard guard(z.device());
+  topk_logprobs(ptr<float>(z), z.stride(0), T, z.size(1), (int)k, ptr<int64_t>(ids), ptr<float>(lp), optr<float>(lse),
+                cur_stream());
+  count();
+}
+
+void gather_logprobs_(Tensor h, Tensor w, Tensor ids, Tensor lse, Tensor lp) {
+  CHECK_CUDA(h);
+  CHECK_BF16(h);
+  CHECK_BF16(w);
+  TORCH_CHECK(h.dim() == 2 && w.dim() == 2 && h.stride(1) == 1 && w.stride(1) == 1 && h.size(1) == w.size(1),
+              "gather_logprobs: h [T, D], w [V, D] row-major");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == h.size(0),
+              "gather_logprobs: ids [T, K] int64");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == h.size(0), "gather_logprobs: lse [T] fp32");
+  TORCH_CHECK(lp.scalar_type() == at::kFloat && lp.is_contiguous() && lp.numel() == ids.numel(),
+              "gather_logprobs: lp [T, K] fp32");
+  const c10::cuda::CUDAGuard guard(h.device());
+  gather_logprobs(ptr<bf16>(h), h.stride(0), ptr<bf16>(w), w.stride(0), h.size(0), h.size(1), w.size(0),
+                  ptr<int64_t>(ids), ids.size(1), ptr<float>(lse), ptr<float>(lp), cur_stream());
+  count();
+}
+
+void scatter_add_rows_(Tensor dz, Tensor ids, Tensor g) {
+  CHECK_CUDA(dz);
+  CHECK_BF16(dz);
+  TORCH_CHECK(dz.dim() == 2 && dz.stride(1) == 1, "scatter_add_rows: dz [T, V] row-major");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == dz.size(0),
+              "scatter_add_rows: ids [T, K] int64");
+  TORCH_CHECK(g.scalar_type() == at::kFloat && g.is_contiguous() && g.numel() == ids.numel(),
+              "scatter_add_rows: g [T, K] fp32");
+  const c10::cuda::CUDAGuard guard(dz.device());
+  scatter_add_rows(ptr<bf16>(dz), dz.stride(0), dz.size(0), dz.size(1), ptr<int64_t>(ids), ptr<float>(g),
+                   ids.size(1), cur_stream());
+  count();
+}
+
 // ─── expert parallelism over peer memory ────────────────────────────────────
 using ull = unsigned long long;
 const ull* tab(const Tensor& t) {
@@ -1212,6 +1259,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("filtered_sample", &filtered_sample_, "top-k / top-p / temperature sampling over fp32 logits");
   m.def("value_head_fwd", &value_head_fwd_, "critic value head + clipped value loss (values, dL/dv, loss sum)");
   m.def("value_head_bwd", &value_head_bwd_, "critic value head backward: dh, dw, db");
+  m.def("topk_logprobs", &topk_logprobs_, "K largest fp32 logits per row (sorted), log-probabilities, lse");
+  m.def("gather_logprobs", &gather_logprobs_, "log-probabilities of given ids from hidden rows and the LM head");
+  m.def("scatter_add_rows", &scatter_add_rows_, "dz[t, ids[t, k]] += g[t, k] on bf16 logit gradients");
   m.def("moe_route", &moe_route_, "router softmax + top-k (+ renormalisation)");
   m.def("moe_route_bwd", &moe_route_bwd_, "router backward: d logits from d weights");
   m.def("moe_plan", &moe_plan_, "device-side expert plan: counts, 128-aligned offsets, slots, gather");

@@ -47,6 +47,7 @@ constexpr int W_TILE_BYTES = 128 * SBK * 2;
 struct SmallArgs {
   int M, N, K;
   int n_tiles, k_blocks, kb_per, cs;
+  int stages;  // depth of the shared-memory stage ring of this launch (<= SCfg::STAGES)
   int epi;
   void* out;
   int ldo;
@@ -108,9 +109,17 @@ struct SCfg {
   // after the barriers: rstd [MP], 16 floats of cross-warp sums, then the QKV epilogue's row exchange
   // [4][128] or the sampler's cross-warp statistics [4][MP][5]
   static constexpr int XCH_FLOATS = (MP <= 64 && 20 * MP > 4 * 128) ? 20 * MP : 4 * 128;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + (MP + 16 + XCH_FLOATS) * 4;
+  static constexpr int FIXED_BYTES = 1024 + BAR_BYTES + (MP + 16 + XCH_FLOATS) * 4;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + FIXED_BYTES;
+  // the split-K partials alias the ring after the K loop: the ring is never shallower than this
+  static constexpr int RED_STAGES = (RED_BYTES + STAGE_BYTES - 1) / STAGE_BYTES;
+  // deepest ring with which two CTAs fit in one SM's 228 KB (1 KB of it reserved per CTA)
+  static constexpr int PAIR_STAGES_FIT = (113 * 1024 - FIXED_BYTES) / STAGE_BYTES;
+  static constexpr int PAIR_STAGES = PAIR_STAGES_FIT < RED_STAGES ? RED_STAGES : PAIR_STAGES_FIT;
   static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "reduction buffer must fit in the stage ring");
+  static_assert(STAGES <= 8, "the barrier block holds 8 stages");
   static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
+  static constexpr int smem_bytes(int stages) { return stages * STAGE_BYTES + FIXED_BYTES; }
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
@@ -188,7 +197,7 @@ __device__ __forceinline__ void norm_stages(const SmallArgs& p, uint8_t* smem, u
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     if (lane == 0) mbar_arrive(&normed[stage]);
-    if (++stage == C::STAGES) {
+    if (++stage == p.stages) {
       stage = 0;
       phase ^= 1;
     }
@@ -352,21 +361,22 @@ __device__ __forceinline__ void lse_epilogue(const SmallArgs& p, uint32_t t_lane
 }
 
 template <int MP, bool PERSIST>
-__global__ void __launch_bounds__(kSmallThreads, 1)
+__global__ void __launch_bounds__(kSmallThreads, 2)
     gemm_small_kernel(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapX,
                       SmallArgs p) {
   using C = SCfg<MP, PERSIST>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* tfull = empty + C::STAGES;
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* normed = drain + 1;  // [STAGES]: X tile of the stage normalised (fused RMSNorm)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(normed + C::STAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(normed + S);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* rstd_s = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+  float* rstd_s = reinterpret_cast<float*>(smem + S * C::STAGE_BYTES + C::BAR_BYTES);
   const bool fuse_norm = p.norm_w != nullptr;
 
   const int warp = threadIdx.x / 32;
@@ -378,7 +388,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
 
   if (threadIdx.x == 0) {
     SMALL_TRACE(0);
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -387,7 +397,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       mbar_init(&tempty[i], 128);
     }
     mbar_init(drain, 1);
-    for (int s = 0; s < C::STAGES; ++s) mbar_init(&normed[s], 4);
+    for (int s = 0; s < S; ++s) mbar_init(&normed[s], 4);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&mapW);
@@ -419,7 +429,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       // The weights do not depend on the kernel before this one: under programmatic dependent
       // launch the first STAGES weight tiles stream in while that kernel finishes; the activation
       // tiles of those stages follow once it has completed.
-      const int npre = first < p.n_tiles ? min(kb1 - kb0, C::STAGES) : 0;
+      const int npre = first < p.n_tiles ? min(kb1 - kb0, S) : 0;
       for (int j = 0; j < npre; ++j) {
         mbar_arrive_expect_tx(&full[j], C::STAGE_BYTES);
         tma_load_2d(smem + j * C::STAGE_BYTES, &mapW, &full[j], (kb0 + j) * SBK, first * 128);
@@ -432,8 +442,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         issued = npre;
         last_stage = npre - 1;
         last_phase = 0;
-        stage = npre % C::STAGES;
-        phase = (npre == C::STAGES) ? 1u : 0u;
+        stage = npre % S;
+        phase = (npre == S) ? 1u : 0u;
       }
       for (int nt = first; nt < p.n_tiles && !*abort_flag; nt += stride) {
         for (int kb = (nt == first ? kb0 + npre : kb0); kb < kb1; ++kb) {
@@ -445,7 +455,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
           issued++;
           last_stage = stage;
           last_phase = phase;
-          if (++stage == C::STAGES) {
+          if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
@@ -488,7 +498,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
           }
           mma_commit(&empty[stage]);
           any = true;
-          if (++stage == C::STAGES) {
+          if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
@@ -828,10 +838,34 @@ int sm_count() {
   return n;
 }
 
+// Pair-sized rings (MESHY_GEMM_SMALL_PAIR, default on; read once).
+bool pair_rings() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MESHY_GEMM_SMALL_PAIR");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Ring depth of a launch. A split-K CTA never needs more stages than its k-blocks, and with a ring small
+// enough for two CTAs per SM (registers allow two: __launch_bounds__(192, 2)) the next kernel of a decode
+// chain becomes resident under programmatic dependent launch and streams its weights while this one
+// finishes. The persistent schedule (LM head) keeps the full ring.
 template <int MP, bool PERSIST>
-void launch_small(const CUtensorMap& mw, const CUtensorMap& mx, const SmallArgs& a, int grid, int cs,
+int ring_stages(int kb_per) {
+  using C = SCfg<MP, PERSIST>;
+  if (PERSIST) return C::STAGES;
+  const int cap = pair_rings() ? std::min(C::STAGES, C::PAIR_STAGES) : C::STAGES;
+  return std::max(C::RED_STAGES, std::min(cap, kb_per));
+}
+
+template <int MP, bool PERSIST>
+void launch_small(const CUtensorMap& mw, const CUtensorMap& mx, const SmallArgs& args, int grid, int cs,
                   cudaStream_t st) {
   using C = SCfg<MP, PERSIST>;
+  SmallArgs a = args;
+  a.stages = ring_stages<MP, PERSIST>(a.kb_per);
   auto k = gemm_small_kernel<MP, PERSIST>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -842,7 +876,7 @@ void launch_small(const CUtensorMap& mw, const CUtensorMap& mx, const SmallArgs&
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kSmallThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.dynamicSmemBytes = C::smem_bytes(a.stages);
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -33,4 +33,14 @@ void value_head_fwd(const bf16* h, const float* w, const float* b, int T, int D,
 void value_head_bwd(const bf16* h, const float* w, const float* dv, int T, int D, bf16* dh, float* dw, float* db,
                     cudaStream_t st);
 
+// Top-K distillation (topk.cu): the K largest fp32 logits of each row (sorted) with their log-probabilities
+// and the row's log-sum-exp; log-probabilities of given ids from the hidden rows and the LM-head weight
+// (needs lse); dz[t, ids[t, k]] += g[t, k] on bf16 logit gradients.
+void topk_logprobs(const float* z, long long ldz, int T, int V, int K, int64_t* ids, float* lp, float* lse,
+                   cudaStream_t st);
+void gather_logprobs(const bf16* h, long long ldh, const bf16* w, long long ldw, int T, int D, int V,
+                     const int64_t* ids, int K, const float* lse, float* lp, cudaStream_t st);
+void scatter_add_rows(bf16* dz, long long ldz, int T, int V, const int64_t* ids, const float* g, int K,
+                      cudaStream_t st);
+
 }  // namespace meshy

@@ -66,8 +66,13 @@ def save_trainer_state(trainer, path: str, step: int, ntokens_seen: int = 0) -> 
     group = _group(trainer)
     world = dist.get_world_size(group) if group is not None else 1
     rank = dist.get_rank(group) if group is not None else 0
-    f.gather_master()
-    m, v = _moments(trainer)
+    full = getattr(f, "full_buffer", None)  # sharded parameters: re-assemble the global layout
+    if full is not None:
+        master, m, v = full("master"), full("exp_avg"), full("exp_avg_sq")
+    else:
+        f.gather_master()
+        master = f.master
+        m, v = _moments(trainer)
     owner = _owners(f.slots, world)
     n_steps = torch.tensor(float(trainer.optimizer.step_count))
     hyper = _hyper(trainer)
@@ -76,7 +81,7 @@ def save_trainer_state(trainer, path: str, step: int, ntokens_seen: int = 0) -> 
     for s, who in zip(f.slots, owner):
         if who != rank:
             continue
-        views = [buf[s.offset:s.offset + s.numel].view(s.shape) for buf in (f.master, m, v)]
+        views = [buf[s.offset:s.offset + s.numel].view(s.shape) for buf in (master, m, v)]
         for (fqn, w), (_, a), (_, b) in zip(*(titan_pieces(args, s.name, x) for x in views)):
             sd[fqn] = w.detach().float().cpu().contiguous()
             sd["optimizer"]["state"][fqn] = {"exp_avg": a.detach().float().cpu().contiguous(),
@@ -92,8 +97,11 @@ def load_trainer_state(trainer, path: str) -> None:
     args = trainer.model_args
     group = _group(trainer)
     dev = f.master.device
-    moments = (torch.zeros(f.numel, dtype=torch.float32, device=dev),
-               torch.zeros(f.numel, dtype=torch.float32, device=dev))
+    sharded = getattr(f, "set_full", None)
+    n_full = f.global_numel if sharded is not None else f.numel
+    master = torch.zeros(n_full, dtype=torch.float32, device=dev) if sharded is not None else f.master
+    moments = (torch.zeros(n_full, dtype=torch.float32, device=dev),
+               torch.zeros(n_full, dtype=torch.float32, device=dev))
     # receive buffers for every key (every rank holds the whole model)
     want: dict = {"train_state": {"step": 0, "ntokens_seen": 0, "meshy_trainer_step": 0},
                   "optimizer": {"state": {}}}
@@ -111,15 +119,19 @@ def load_trainer_state(trainer, path: str) -> None:
     with torch.no_grad():
         for s, fqns in plan:
             st = want["optimizer"]["state"]
-            f.master[s.offset:s.offset + s.numel].copy_(join_pieces(args, s.name, [want[q] for q in fqns]).reshape(-1))
+            master[s.offset:s.offset + s.numel].copy_(join_pieces(args, s.name, [want[q] for q in fqns]).reshape(-1))
             moments[0][s.offset:s.offset + s.numel].copy_(
                 join_pieces(args, s.name, [st[q]["exp_avg"] for q in fqns]).reshape(-1))
             moments[1][s.offset:s.offset + s.numel].copy_(
                 join_pieces(args, s.name, [st[q]["exp_avg_sq"] for q in fqns]).reshape(-1))
             steps = max(steps, int(float(st[fqns[0]]["step"])))
-    sharded = getattr(trainer.optimizer, "set_full_moments", None)
+    opt_sharded = getattr(trainer.optimizer, "set_full_moments", None)
     if sharded is not None:
-        sharded(*moments)
+        sharded("master", master)
+        sharded("exp_avg", moments[0])
+        sharded("exp_avg_sq", moments[1])
+    elif opt_sharded is not None:
+        opt_sharded(*moments)
     else:
         f.exp_avg.copy_(moments[0])
         f.exp_avg_sq.copy_(moments[1])

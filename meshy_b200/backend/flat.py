@@ -184,7 +184,7 @@ class FlatParams:
             out = torch.zeros(1, dtype=torch.float32, device=self.device)
             ext().sq_norm(self.grad, out)
             return out.sqrt().reshape(())
-        return self.grad.norm()
+        return self.grad.double().norm().float()  # fp64 accumulation: the CPU oracle's norm is exact to fp32
 
 
 class FlatAdamW:
@@ -219,10 +219,20 @@ class FlatAdamW:
 
     def _decay_views(self):
         f = self.flat
+        if hasattr(f, "shard_views"):  # sharded parameters: this rank's pieces of them
+            return f.shard_views(f.master, self.decay_names)
         by_name = {s.name: s for s in f.slots}
         return [f.master[by_name[n].offset:by_name[n].offset + by_name[n].numel] for n in self.decay_names]
 
     def step(self, grad_norm: torch.Tensor | None = None) -> torch.Tensor:
+        try:
+            return self._grouped_step(grad_norm)
+        finally:
+            changed = getattr(self.flat, "weights_changed", None)
+            if changed is not None:  # sharded parameters: gathered copies are stale now
+                changed()
+
+    def _grouped_step(self, grad_norm: torch.Tensor | None) -> torch.Tensor:
         f = self.flat
         if grad_norm is None:
             grad_norm = f.grad_norm()

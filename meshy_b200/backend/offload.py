@@ -23,6 +23,8 @@ def restore(trainer) -> None:
 
 def offload_flat(f) -> None:
     """Move every flat buffer of a :class:`~.flat.FlatParams` to pinned host memory."""
+    if getattr(f, "sharded", False):
+        return f.offload()
     if f.master is None or f.master.device.type != "cuda":
         return
     host = {}
@@ -49,6 +51,8 @@ def offload_flat(f) -> None:
 
 def restore_flat(f) -> None:
     """Inverse of :func:`offload_flat`: buffers back on the device, parameter views re-pointed."""
+    if getattr(f, "sharded", False):
+        return f.restore()
     host = getattr(f, "_host", None)
     if not host:
         return

@@ -58,6 +58,8 @@ class PPOTrainer:
         loss_group=None,
         ep_group=None,
         tp_group=None,
+        fsdp_group=None,
+        replicate_group=None,
     ):
         self.config = config
         self.params = params or TrainerParamsConfig()
@@ -93,7 +95,18 @@ class PPOTrainer:
             shard_experts(model, ep_group, max_tokens=max_tokens)
         self.model = model
         self.model.activation_checkpoint = config.activation_checkpoint_mode == "full"
-        self.flat = FlatParams(self.model, compute_dtype=cdt, device=self.device)
+        # fully sharded parameters (FSDP over fsdp_group, HSDP with a replicate group on top)
+        self.fsdp = (fsdp_group is not None and dist.is_initialized() and dist.get_world_size(fsdp_group) > 1)
+        if self.fsdp:
+            if self.ep_group is not None or (self.tp_group is not None and dist.get_world_size(self.tp_group) > 1):
+                raise ValueError("sharded parameters combine with data and context parallelism only")
+            from ..parallel.fsdp import ShardedFlat
+
+            self.flat = ShardedFlat(self.model, fsdp_group, compute_dtype=cdt, device=self.device,
+                                    replicate_group=replicate_group)
+            self.model.fsdp = self.flat
+        else:
+            self.flat = FlatParams(self.model, compute_dtype=cdt, device=self.device)
         if cdt != torch.float32:
             torch.cuda.empty_cache()
         self.optimizer = FlatAdamW(self.flat, lr=config.lr, betas=(config.beta1, config.beta2), eps=config.eps,
@@ -118,7 +131,13 @@ class PPOTrainer:
 
         expert_slots = [(sl.offset, sl.numel) for sl in self.flat.slots
                         if ".moe.w13" in sl.name or ".moe.w2" in sl.name] if self.ep_group is not None else []
-        self.reducer = GradReducer(self.flat, self.loss_group, skip=expert_slots)
+        if self.fsdp:
+            # the gradient shards are reduced inside backward; replicas of a shard sum theirs here
+            rg = replicate_group if (replicate_group is not None and dist.get_world_size(replicate_group) > 1) \
+                else None
+            self.reducer = GradReducer(self.flat, rg, backend=None if rg is not None else "none")
+        else:
+            self.reducer = GradReducer(self.flat, self.loss_group, skip=expert_slots)
         # under TP the per-head QK-norm gains are replicated but each rank's gradient covers only its
         # heads: those slots are summed over the TP group before the DP reduction
         self.tp_partial = [(sl.offset, sl.numel) for sl in self.flat.slots
@@ -142,7 +161,7 @@ class PPOTrainer:
     def _use_fused_dp(self) -> bool:
         import os
 
-        if os.environ.get("MESHY_DP_FUSED", "auto") == "0" or self.device.type != "cuda":
+        if os.environ.get("MESHY_DP_FUSED", "auto") == "0" or self.device.type != "cuda" or self.fsdp:
             return False
         from ..ops.functional import native
 

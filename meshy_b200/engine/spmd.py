@@ -47,6 +47,10 @@ class SpmdEngine:
             os.environ.pop(v, None)
         os.environ["MASTER_ADDR"] = self.master_addr
         os.environ["MASTER_PORT"] = str(self.master_port)
+        if self.device.type == "cuda":
+            # collectives that stage through the current device (all_gather_object and friends) must
+            # see the device the process group was bound to
+            torch.cuda.set_device(self.device)
         if not dist.is_initialized():
             backend = "nccl" if self.device.type == "cuda" else "gloo"
             kw = {"device_id": self.device} if backend == "nccl" else {}

@@ -129,13 +129,20 @@ class DecoderLM(nn.Module):
     # ------------------------------------------------------------------
     def hidden(self, input_ids, positions, cu_seqlens, max_seqlen) -> torch.Tensor:
         """Final-norm hidden states ``[T, D]`` of a packed token stream."""
+        fs = getattr(self, "fsdp", None)  # sharded parameters: per-block gather / reduce hooks
+        if fs is not None:
+            fs.begin_forward()
         x = Fx.embedding(input_ids, self.embed)
         ckpt = self.activation_checkpoint and torch.is_grad_enabled()
-        for layer in self.layers:
+        for i, layer in enumerate(self.layers):
+            if fs is not None:
+                x = fs.pre_block(i, x)
             if ckpt:
                 x = checkpoint(layer, x, positions, cu_seqlens, max_seqlen, use_reentrant=False)
             else:
                 x = layer(x, positions, cu_seqlens, max_seqlen)
+            if fs is not None:
+                x = fs.post_block(i, x)
         return Fx.rmsnorm(x, self.norm, self.args.norm_eps)
 
     def logprobs(self, input_ids, labels, positions, cu_seqlens, max_seqlen, *, with_entropy=False,

@@ -312,9 +312,9 @@ def flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen: int, scale: float | None 
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if native(q):
         return _FlashAttnVarlen.apply(q, k, v, cu_seqlens, max_seqlen, scale)
-    if q.is_cuda:  # torch baseline: PyTorch's FlashAttention varlen kernel
+    if q.is_cuda and q.dtype != torch.float32:  # torch baseline: PyTorch's FlashAttention varlen kernel
         return _torch_varlen(q, k, v, cu_seqlens, max_seqlen, scale)
-    return _RefAttn.apply(q, k, v, cu_seqlens, scale)
+    return _RefAttn.apply(q, k, v, cu_seqlens, scale)  # CPU, and fp32 oracles on the GPU
 
 
 def _torch_varlen(q, k, v, cu, max_seqlen, scale):

@@ -30,6 +30,7 @@ cuda_sources = [
     "csrc/kernels/ep.cu",
     "csrc/kernels/sampling.cu",
     "csrc/kernels/value_head.cu",
+    "csrc/kernels/topk.cu",
     "csrc/kernels/decode_noalloc.cu",
     "csrc/kernels/decode_mega.cu",
 ]
