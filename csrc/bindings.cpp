@@ -946,6 +946,34 @@ void value_head_bwd_(Tensor h, Tensor w, Tensor dv, Tensor dh, Tensor dw, Tensor
   count();
 }
 
+void l2_prefetch_(std::vector<Tensor> ts) {
+  TORCH_CHECK(!ts.empty() && ts.size() <= 4, "l2_prefetch: 1 to 4 tensors");
+  const void* ptrs[4];
+  long long bytes[4];
+  for (size_t i = 0; i < ts.size(); ++i) {
+    CHECK_CUDA(ts[i]);
+    TORCH_CHECK(ts[i].is_contiguous(), "l2_prefetch: contiguous tensors");
+    ptrs[i] = ts[i].data_ptr();
+    bytes[i] = ts[i].numel() * ts[i].element_size();
+  }
+  const c10::cuda::CUDAGuard guard(ts[0].device());
+  l2_prefetch(ptrs, bytes, (int)ts.size(), cur_stream());
+  count();
+}
+
+void kv_prefetch_(Tensor bt, Tensor seq_lens, Tensor kc, Tensor vc, int64_t page) {
+  CHECK_CUDA(bt);
+  TORCH_CHECK(bt.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt && bt.dim() == 2 &&
+                  bt.stride(1) == 1 && seq_lens.numel() >= bt.size(0),
+              "kv_prefetch: bt [B, max_pages] int32, seq_lens [B] int32");
+  TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous() && kc.size(0) == vc.size(0), "kv_prefetch: caches");
+  const int64_t page_bytes = kc.numel() / kc.size(0) * kc.element_size();
+  const c10::cuda::CUDAGuard guard(bt.device());
+  kv_prefetch(bt.data_ptr<int>(), seq_lens.data_ptr<int>(), bt.size(0), bt.stride(0), (int)page, kc.data_ptr(),
+              vc.data_ptr(), page_bytes, kc.size(0), cur_stream());
+  count();
+}
+
 void topk_logprobs_(Tensor z, int64_t k, Tensor ids, Tensor lp, c10::optional<Tensor> lse) {
   CHECK_CUDA(z);
   CHECK_F32(z);
@@ -1084,6 +1112,26 @@ void symm_barrier_(Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch,
   TORCH_CHECK(flag_ptrs.scalar_type() == at::kLong && flag_ptrs.is_cuda(), "flag_ptrs: int64 CUDA tensor");
   symm_barrier(reinterpret_cast<const unsigned long long*>(flag_ptrs.data_ptr()), (int)rank, (int)world,
                (unsigned)epoch, timeout_s, ptr<int>(scratch(0, 0).err), cur_stream());
+  count();
+}
+
+void fsdp_gather_(Tensor ptrs, int64_t off_bytes, int64_t bytes, Tensor dst) {
+  TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.is_cuda(), "ptrs: int64 CUDA tensor");
+  TORCH_CHECK(dst.is_cuda() && dst.is_contiguous() && dst.numel() * dst.element_size() >= ptrs.numel() * bytes,
+              "fsdp_gather: dst holds world x bytes");
+  const c10::cuda::CUDAGuard guard(dst.device());
+  fsdp_gather(reinterpret_cast<const unsigned long long*>(ptrs.data_ptr()), off_bytes, bytes, (int)ptrs.numel(),
+              dst.data_ptr(), cur_stream());
+  count();
+}
+
+void fsdp_reduce_(Tensor ptrs, int64_t off_bytes, int64_t n, int64_t rank, Tensor dst) {
+  TORCH_CHECK(ptrs.scalar_type() == at::kLong && ptrs.is_cuda(), "ptrs: int64 CUDA tensor");
+  CHECK_F32(dst);
+  TORCH_CHECK(dst.is_contiguous() && dst.numel() >= n, "fsdp_reduce: dst holds n fp32");
+  const c10::cuda::CUDAGuard guard(dst.device());
+  fsdp_reduce(reinterpret_cast<const unsigned long long*>(ptrs.data_ptr()), off_bytes, n, (int)rank,
+              (int)ptrs.numel(), ptr<float>(dst), cur_stream());
   count();
 }
 
@@ -1259,6 +1307,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("filtered_sample", &filtered_sample_, "top-k / top-p / temperature sampling over fp32 logits");
   m.def("value_head_fwd", &value_head_fwd_, "critic value head + clipped value loss (values, dL/dv, loss sum)");
   m.def("value_head_bwd", &value_head_bwd_, "critic value head backward: dh, dw, db");
+  m.def("kv_prefetch", &kv_prefetch_, "ask the L2 for the K/V cache pages of the rows' block tables");
+  m.def("l2_prefetch", &l2_prefetch_, "ask the L2 for the bytes of up to 4 tensors (no wait)");
   m.def("topk_logprobs", &topk_logprobs_, "K largest fp32 logits per row (sorted), log-probabilities, lse");
   m.def("gather_logprobs", &gather_logprobs_, "log-probabilities of given ids from hidden rows and the LM head");
   m.def("scatter_add_rows", &scatter_add_rows_, "dz[t, ids[t, k]] += g[t, k] on bf16 logit gradients");
@@ -1313,6 +1363,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close_);
   m.def("symm_view", &symm_view_, "non-owning tensor view into a symmetric-heap buffer");
   m.def("symm_barrier", &symm_barrier_, "device barrier over the ranks' flag arrays (bounded wait)");
+  m.def("fsdp_gather", &fsdp_gather_, "gather every rank's shard of a symmetric region (peer loads)");
+  m.def("fsdp_reduce", &fsdp_reduce_, "this rank's shard of the sum of the ranks' fp32 regions (peer loads)");
   m.def("symm_dp_adamw", &symm_dp_adamw_,
         "fused DP optimiser step over NVLink: reduce-scatter + grad norm + AdamW + all-gather by P2P stores");
   m.def("device_error", &device_error);

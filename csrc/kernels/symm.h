@@ -41,4 +41,14 @@ struct SymmAdamWArgs {
 
 void symm_dp_adamw_step(const SymmAdamWArgs& a, cudaStream_t st);
 
+// Sharded-parameter collectives over peer memory (fsdp.cu); ``ptrs`` is the [world] device table of the
+// ranks' heap addresses of one symmetric region, ``off_bytes`` an offset inside it.
+constexpr int kMaxPeers = 8;
+// dst[r * bytes .. (r + 1) * bytes) = rank r's bytes at off_bytes, for every rank r.
+void fsdp_gather(const unsigned long long* ptrs, long long off_bytes, long long bytes, int world, void* dst,
+                 cudaStream_t st);
+// dst[j] += sum_r (rank r's fp32 region at off_bytes)[rank * n + j], j < n.
+void fsdp_reduce(const unsigned long long* ptrs, long long off_bytes, long long n, int rank, int world, float* dst,
+                 cudaStream_t st);
+
 }  // namespace meshy

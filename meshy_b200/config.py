@@ -97,6 +97,10 @@ class TrainerConfig:
     lr_min_factor: float = 0.0
     dp_shard_degree: int = -1
     dp_replicate_degree: int = 1
+    # parameter sharding over the dp_shard ranks: "on" always (FSDP; HSDP with dp_replicate_degree > 1),
+    # "off" never (parameters replicated, AdamW state and fp32 master sharded inside the fused DP step),
+    # "auto" when the replicated training state would take more than 40 % of a device's memory
+    shard_params: Literal["auto", "on", "off"] = "auto"
     tp_degree: int = 1
     cp_degree: int = 1
     ep_degree: int = 1
@@ -119,6 +123,8 @@ class TrainerConfig:
             raise ValueError(f"lr_decay_type must be 'linear', 'sqrt' or 'cosine', got {self.lr_decay_type!r}")
         if not (0.0 <= self.lr_min_factor <= 1.0):
             raise ValueError(f"lr_min_factor must be within [0, 1], got {self.lr_min_factor!r}")
+        if self.shard_params not in ("auto", "on", "off"):
+            raise ValueError(f"shard_params must be 'auto', 'on' or 'off', got {self.shard_params!r}")
         for name in ("tp_degree", "cp_degree", "ep_degree", "dp_replicate_degree"):
             if getattr(self, name) <= 0:
                 raise ValueError(f"{name} must be positive")

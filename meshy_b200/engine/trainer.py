@@ -72,6 +72,13 @@ class TrainerEngine(SpmdEngine):
         tc = self.tc
         cp = max(1, int(getattr(tc, "cp_degree", 1)))
         ep = max(1, int(getattr(tc, "ep_degree", 1)))
+        if self.shard_parameters():
+            rep = max(1, int(getattr(tc, "dp_replicate_degree", 1)))
+            pd = build_parallel_dims(self.world_size, self.rank, dp_replicate=rep, dp_shard=-1, cp=cp,
+                                     tp=max(1, int(getattr(tc, "tp_degree", 1))))
+            self.parallel_dims = pd
+            return {"dp_group": pd.batch_group, "cp_group": pd.cp_group, "loss_group": pd.loss_group,
+                    "tp_group": pd.tp_group, "fsdp_group": pd.shard_group, "replicate_group": pd.replicate_group}
         if cp == 1 and int(getattr(tc, "tp_degree", 1)) <= 1:
             out = {"dp_group": self.compute_group}
             if ep > 1:
@@ -84,6 +91,21 @@ class TrainerEngine(SpmdEngine):
         self.parallel_dims = pd
         return {"dp_group": pd.batch_group, "cp_group": pd.cp_group, "loss_group": pd.loss_group,
                 "tp_group": pd.tp_group}
+
+    def shard_parameters(self) -> bool:
+        """Whether this replica shards its parameters (``shard_params``; "auto": the replicated state -- bf16
+        weights, fp32 gradients, and the fp32 master and moments split over the ranks -- above 40 % of HBM)."""
+        mode = getattr(self.tc, "shard_params", "auto")
+        if mode != "auto" or self.world_size == 1:
+            return mode == "on" and self.world_size > 1
+        if self.device.type != "cuda" or int(getattr(self.tc, "ep_degree", 1)) > 1 \
+                or int(getattr(self.tc, "tp_degree", 1)) > 1:
+            return False
+        from ..models import get_model_args
+
+        n = get_model_args(self.tc.model_name, self.tc.model_flavor).num_params()
+        need = n * (2 + 4 + 12 / self.world_size)
+        return need > 0.4 * torch.cuda.get_device_properties(self.device).total_memory
 
     @property
     def global_step(self) -> int:

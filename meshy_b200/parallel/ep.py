@@ -121,94 +121,138 @@ def ext():
     return _e()
 
 
+# ─── the three phases of each direction (source → owner → source), between device barriers ───────────
+# They are separate functions so one process can also play every rank in turn against local regions (the
+# kernels only read and store through address tables; nothing in them waits on another rank).
+
+def _fwd_dispatch(x, experts, xch, E_local):
+    """Source: plan this rank's assignments per owner and store the token rows into the owners' regions."""
+    k = experts.shape[1]
+    ex = experts.reshape(-1).contiguous()
+    slot_o, off_o, cnt_o = xch.owner_plan(ex, E_local)
+    ext().ep_dispatch(x.contiguous(), k, ex, slot_o, off_o, cnt_o, E_local, xch.rank, xch.world, xch.cap,
+                      xch.t_recv_x, xch.t_recv_meta, xch.t_recv_idx, xch.t_recv_cnt)
+    return ex, slot_o, off_o, cnt_o
+
+
+def _fwd_owner(xch, w13, w2):
+    """Owner: local plan over everything received, grouped GEMMs on local memory, rows stored back to their
+    sources' return regions."""
+    from ..ops import moe as M
+
+    C = ext()
+    W, cap = xch.world, xch.cap
+    E_local, F2 = w13.shape[0], w13.shape[1]
+    D = xch.dim
+    dev, dt = xch.recv_x.device, xch.recv_x.dtype
+    ids = torch.empty(W * cap, dtype=torch.int32, device=dev)
+    C.ep_recv_ids(xch.recv_meta, xch.recv_cnt, W, cap, E_local, ids)
+    rows = M.plan_rows(W * cap, E_local)
+    cnt = torch.empty(E_local, dtype=torch.int32, device=dev)
+    off = torch.empty(E_local + 1, dtype=torch.int32, device=dev)
+    slot = torch.empty(W * cap, dtype=torch.int32, device=dev)
+    row_src = torch.empty(rows, dtype=torch.int32, device=dev)
+    xp = torch.empty(rows, D, dtype=dt, device=dev)
+    C.moe_plan(ids.view(-1, 1), cnt, off, slot, row_src, xch.recv_x, xp)
+    idx = xch.recv_idx.clone()
+    h = torch.empty(rows, F2, dtype=dt, device=dev)
+    act = torch.empty(rows, F2 // 2, dtype=dt, device=dev)
+    C.gemm_grouped(xp, w13, act, off, M.GRP_M, False, M.EPI_SWIGLU, h)
+    y = torch.empty(rows, D, dtype=dt, device=dev)
+    C.gemm_grouped(act, w2, y, off, M.GRP_M, False, M.EPI_STORE, None)
+    C.ep_return(y, ids, slot, idx, W, cap, xch.cap, xch.t_ret)
+    return ids, slot, off, cnt, row_src, idx, xp, h, act
+
+
+def _fwd_collect(xch, n, weights, T):
+    """Source: weighted sum of the returned rows (assignment i came back to ret[i])."""
+    y_src = xch.ret[:n].clone()
+    ident = torch.arange(n, dtype=torch.int32, device=y_src.device)
+    out = torch.empty(T, xch.dim, dtype=y_src.dtype, device=y_src.device)
+    ext().moe_combine(y_src, ident, weights.contiguous(), out)
+    return out, y_src, ident
+
+
+def _bwd_dispatch(dout, y_src, ident, weights, ex, slot_o, off_o, cnt_o, E_local, xch):
+    """Source: gradients of the returned rows and of the routing weights; the row gradients go to the owners."""
+    T, D = dout.shape
+    n = ident.numel()
+    dret = torch.empty(n, D, dtype=dout.dtype, device=dout.device)
+    dw = torch.empty(T, n // T, dtype=torch.float32, device=dout.device)
+    ext().moe_combine_bwd(dout.contiguous(), y_src, ident, weights, dret, dw)
+    ext().ep_dispatch(dret, 1, ex, slot_o, off_o, cnt_o, E_local, xch.rank, xch.world, xch.cap, xch.t_recv_x,
+                      None, None, None)
+    return dw
+
+
+def _bwd_owner(xch, ids, slot, off, row_src, idx, xp, h, act, w13, w2, block):
+    """Owner: the experts' backward on its rows (weight gradients into main_grad when there is one); the input
+    row gradients are stored back to their sources."""
+    from ..ops import moe as M
+
+    C = ext()
+    W, cap = xch.world, xch.cap
+    E_local, F2 = w13.shape[0], w13.shape[1]
+    D = xch.dim
+    rows = xp.shape[0]
+    dev, dt = xp.device, xp.dtype
+    dy = torch.empty(rows, D, dtype=dt, device=dev)
+    C.gather_rows(row_src, off, xch.recv_x, dy)
+    dact = torch.empty(rows, F2 // 2, dtype=dt, device=dev)
+    C.gemm_grouped(dy, w2, dact, off, M.GRP_M, True, M.EPI_STORE, None)
+    g2 = w2.main_grad if getattr(w2, "main_grad", None) is not None else torch.zeros(
+        w2.shape, dtype=torch.float32, device=dev)
+    C.gemm_grouped(dy, act, g2.view(E_local * D, F2 // 2), off, M.GRP_K, True, M.EPI_STORE, None)
+    dh = torch.empty_like(h)
+    C.swiglu_bwd(h, dact, dh, block)
+    dxp = torch.empty(rows, D, dtype=dt, device=dev)
+    C.gemm_grouped(dh, w13, dxp, off, M.GRP_M, True, M.EPI_STORE, None)
+    g13 = w13.main_grad if getattr(w13, "main_grad", None) is not None else torch.zeros(
+        w13.shape, dtype=torch.float32, device=dev)
+    C.gemm_grouped(dh, xp, g13.view(E_local * F2, D), off, M.GRP_K, True, M.EPI_STORE, None)
+    C.ep_return(dxp, ids, slot, idx, W, cap, xch.cap, xch.t_ret)
+    return g13, g2
+
+
+def _bwd_collect(xch, ident, T):
+    """Source: token gradient = sum over its k returned rows."""
+    n = ident.numel()
+    dx = torch.empty(T, xch.dim, dtype=xch.ret.dtype, device=xch.ret.device)
+    ext().moe_combine(xch.ret[:n].contiguous(), ident, None, dx)
+    return dx
+
+
 class _PeerExperts(torch.autograd.Function):
     """Expert-parallel routed-expert output over peer memory (see :class:`PeerExchange`)."""
 
     @staticmethod
     def forward(ctx, x, weights, experts, w13, w2, xch: PeerExchange, block: int):
-        from ..ops import moe as M
-
-        C = ext()
-        T, D = x.shape
-        k = experts.shape[1]
-        n = T * k
+        T = x.shape[0]
+        n = T * experts.shape[1]
         if n > xch.cap:
             raise RuntimeError(f"expert-parallel layer got {n} assignments; the receive regions hold {xch.cap}")
-        E_local, F2 = w13.shape[0], w13.shape[1]
-        ex = experts.reshape(-1).contiguous()
-        slot_o, off_o, cnt_o = xch.owner_plan(ex, E_local)
-        C.ep_dispatch(x.contiguous(), k, ex, slot_o, off_o, cnt_o, E_local, xch.rank, xch.world, xch.cap,
-                      xch.t_recv_x, xch.t_recv_meta, xch.t_recv_idx, xch.t_recv_cnt)
+        E_local = w13.shape[0]
+        ex, slot_o, off_o, cnt_o = _fwd_dispatch(x, experts, xch, E_local)
         xch.barrier()
-        # owner: local plan over everything received, grouped GEMMs on local memory
-        W, cap = xch.world, xch.cap
-        ids = torch.empty(W * cap, dtype=torch.int32, device=x.device)
-        C.ep_recv_ids(xch.recv_meta, xch.recv_cnt, W, cap, E_local, ids)
-        rows = M.plan_rows(W * cap, E_local)
-        cnt = torch.empty(E_local, dtype=torch.int32, device=x.device)
-        off = torch.empty(E_local + 1, dtype=torch.int32, device=x.device)
-        slot = torch.empty(W * cap, dtype=torch.int32, device=x.device)
-        row_src = torch.empty(rows, dtype=torch.int32, device=x.device)
-        xp = torch.empty(rows, D, dtype=x.dtype, device=x.device)
-        C.moe_plan(ids.view(-1, 1), cnt, off, slot, row_src, xch.recv_x, xp)
-        idx = xch.recv_idx.clone()
-        h = torch.empty(rows, F2, dtype=x.dtype, device=x.device)
-        act = torch.empty(rows, F2 // 2, dtype=x.dtype, device=x.device)
-        C.gemm_grouped(xp, w13, act, off, M.GRP_M, False, M.EPI_SWIGLU, h)
-        y = torch.empty(rows, D, dtype=x.dtype, device=x.device)
-        C.gemm_grouped(act, w2, y, off, M.GRP_M, False, M.EPI_STORE, None)
-        C.ep_return(y, ids, slot, idx, W, cap, xch.cap, xch.t_ret)
+        ids, slot, off, cnt, row_src, idx, xp, h, act = _fwd_owner(xch, w13, w2)
         xch.barrier()
-        # source: weighted sum of the returned rows (assignment i came back to ret[i])
-        y_src = xch.ret[:n].clone()
-        ident = torch.arange(n, dtype=torch.int32, device=x.device)
-        out = torch.empty(T, D, dtype=x.dtype, device=x.device)
-        C.moe_combine(y_src, ident, weights.contiguous(), out)
+        out, y_src, ident = _fwd_collect(xch, n, weights, T)
         ctx.save_for_backward(ex, slot_o, off_o, cnt_o, ids, slot, off, cnt, row_src, idx, xp, h, act, y_src, ident,
                               weights, w13, w2)
-        ctx.xch, ctx.block, ctx.k = xch, block, k
+        ctx.xch, ctx.block = xch, block
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        from ..ops import moe as M
-
-        C = ext()
         (ex, slot_o, off_o, cnt_o, ids, slot, off, cnt, row_src, idx, xp, h, act, y_src, ident, weights, w13,
          w2) = ctx.saved_tensors
-        xch, k = ctx.xch, ctx.k
-        T, D = dout.shape
-        n = T * k
-        W, cap = xch.world, xch.cap
-        E_local, F2 = w13.shape[0], w13.shape[1]
-        rows = xp.shape[0]
-        dev = dout.device
-        # source: gradients of the returned rows and of the routing weights, sent to the owners
-        dret = torch.empty(n, D, dtype=dout.dtype, device=dev)
-        dw = torch.empty(T, k, dtype=torch.float32, device=dev)
-        C.moe_combine_bwd(dout.contiguous(), y_src, ident, weights, dret, dw)
-        C.ep_dispatch(dret, 1, ex, slot_o, off_o, cnt_o, E_local, xch.rank, W, cap, xch.t_recv_x, None, None, None)
+        xch = ctx.xch
+        T = dout.shape[0]
+        dw = _bwd_dispatch(dout, y_src, ident, weights, ex, slot_o, off_o, cnt_o, w13.shape[0], xch)
         xch.barrier()
-        # owner: expert backward on its own rows
-        dy = torch.empty(rows, D, dtype=dout.dtype, device=dev)
-        C.gather_rows(row_src, off, xch.recv_x, dy)
-        dact = torch.empty(rows, F2 // 2, dtype=dout.dtype, device=dev)
-        C.gemm_grouped(dy, w2, dact, off, M.GRP_M, True, M.EPI_STORE, None)
-        g2 = w2.main_grad if getattr(w2, "main_grad", None) is not None else torch.zeros(
-            w2.shape, dtype=torch.float32, device=dev)
-        C.gemm_grouped(dy, act, g2.view(E_local * D, F2 // 2), off, M.GRP_K, True, M.EPI_STORE, None)
-        dh = torch.empty_like(h)
-        C.swiglu_bwd(h, dact, dh, ctx.block)
-        dxp = torch.empty(rows, D, dtype=dout.dtype, device=dev)
-        C.gemm_grouped(dh, w13, dxp, off, M.GRP_M, True, M.EPI_STORE, None)
-        g13 = w13.main_grad if getattr(w13, "main_grad", None) is not None else torch.zeros(
-            w13.shape, dtype=torch.float32, device=dev)
-        C.gemm_grouped(dh, xp, g13.view(E_local * F2, D), off, M.GRP_K, True, M.EPI_STORE, None)
-        C.ep_return(dxp, ids, slot, idx, W, cap, xch.cap, xch.t_ret)
+        g13, g2 = _bwd_owner(xch, ids, slot, off, row_src, idx, xp, h, act, w13, w2, ctx.block)
         xch.barrier()
-        # source: token gradient = sum over its k returned rows
-        dx = torch.empty(T, D, dtype=dout.dtype, device=dev)
-        C.moe_combine(xch.ret[:n].contiguous(), ident, None, dx)
+        dx = _bwd_collect(xch, ident, T)
         gw13 = None if getattr(w13, "main_grad", None) is not None else g13.to(w13.dtype)
         gw2 = None if getattr(w2, "main_grad", None) is not None else g2.to(w2.dtype)
         return dx, dw, None, gw13, gw2, None, None

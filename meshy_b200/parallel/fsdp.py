@@ -23,14 +23,21 @@ the root module, ``TT:torchtitan/models/llama4/parallelize.py:170-240``, driven 
 * **HSDP**: with a replicate group, the gradient shards are all-reduced across it before the step (the
   trainer's gradient reducer runs over the replicate group on the shard buffer).
 
-The collectives are NCCL's ``all_gather_into_tensor`` / ``reduce_scatter_tensor`` (gloo on the CPU).
-A weight sync and a checkpoint read the full model through :meth:`ShardedFlat.full_buffer`, which
-re-assembles the global flat layout -- the shard -> replica reshard an inference engine needs.
+Collectives. On one node with peer-capable GPUs (the default there) the compute shards and the full-size
+gradient buffers live in a symmetric heap (CUDA IPC, :class:`~meshy_b200.parallel.symm.SymmetricHeap`):
+a gather is one kernel that reads every rank's shard over NVLink into the local full-size buffer, and a
+reduce-scatter is one kernel that sums this rank's slice of every rank's gradient buffer into the local
+gradient shard (``csrc/kernels/fsdp.cu``), bracketed by bounded device barriers; the first gather after an
+optimiser step waits at a barrier for every rank's step. Elsewhere (and on the CPU, with gloo) they are
+``all_gather_into_tensor`` / ``reduce_scatter_tensor``. A weight sync and a checkpoint read the full model
+through :meth:`ShardedFlat.full_buffer`, which re-assembles the global flat layout -- the shard -> replica
+reshard an inference engine needs.
 """
 
 from __future__ import annotations
 
 import contextlib
+import os
 
 import torch
 import torch.distributed as dist
@@ -129,6 +136,8 @@ class ShardedFlat:
         self.exp_avg_sq = torch.zeros(self.numel, dtype=f32, device=dev)
         self.compute = torch.zeros(self.numel, dtype=compute_dtype, device=dev) if self.separate_compute \
             else self.master
+        self.peer = self._peer_capable()
+        self.heap = None
         self._alloc_full()
         # shards from the (identical on every rank) initial values; parameter views into the full buffers
         with torch.no_grad():
@@ -147,14 +156,50 @@ class ShardedFlat:
         self.comm_bytes = 0
 
     # ------------------------------------------------------------------ layout
+    def _peer_capable(self) -> bool:
+        if self.device.type != "cuda" or not self.separate_compute or os.environ.get("MESHY_FSDP_PEER", "1") == "0":
+            return False
+        if not native(self.master) or dist.get_backend(self.group) != "nccl":
+            return False
+        from .symm import SymmetricHeap
+
+        return SymmetricHeap.supported(self.group) and self.world <= 8
+
     def _alloc_full(self) -> None:
-        """Full-size buffers: the root unit's weights and gradients, two blocks' worth of each."""
+        """Full-size buffers: the root unit's weights and gradients, two blocks' worth of each. In peer mode the
+        compute shard and the gradient buffers are carved from a symmetric heap (mapped by every rank)."""
         dev, f32 = self.device, torch.float32
         bmax = max((u.full for u in self.blocks), default=ALIGN)
         self.root_w = torch.zeros(self.root.full, dtype=self.compute_dtype, device=dev)
-        self.root_g = torch.zeros(self.root.full, dtype=f32, device=dev)
         self.block_w = [torch.zeros(bmax, dtype=self.compute_dtype, device=dev) for _ in range(2)]
-        self.block_g = [torch.zeros(bmax, dtype=f32, device=dev) for _ in range(2)]
+        if self.peer:
+            from .symm import SymmetricHeap
+
+            if self.heap is None:
+                nbytes = self.numel * 2 + (self.root.full + 2 * bmax) * 4 + 8 * 1024
+                self.heap = SymmetricHeap(nbytes, self.group, dev)
+                shard, self.t_compute = self.heap.alloc(self.numel, self.compute_dtype)
+                self.root_g, self.t_root_g = self.heap.alloc(self.root.full, f32)
+                g0, t0 = self.heap.alloc(bmax, f32)
+                g1, t1 = self.heap.alloc(bmax, f32)
+                self._heap_g = [g0, g1]
+                self.t_block_g = [t0, t1]
+                self._flags, self.t_flags = self.heap.alloc(self.world, torch.int32)
+                self._flags.zero_()
+                self._heap_compute = shard
+                self.epoch = 0
+                self.timeout_s = float(os.environ.get("MESHY_SYMM_TIMEOUT_S", "30"))
+            self._heap_compute.copy_(self.compute)
+            self.compute = self._heap_compute
+            self.root_g.zero_()
+            for g in self._heap_g:
+                g.zero_()
+            self.block_g = list(self._heap_g)
+            torch.cuda.synchronize(dev)
+            dist.barrier(group=self.group)  # every region is mapped and initialised everywhere
+        else:
+            self.root_g = torch.zeros(self.root.full, dtype=f32, device=dev)
+            self.block_g = [torch.zeros(bmax, dtype=f32, device=dev) for _ in range(2)]
         self._rs_tmp = torch.zeros(max([u.shard for u in self.blocks] + [self.root.shard]), dtype=f32, device=dev)
         self._holder = [None, None]  # (block, version) held by each block buffer
         self._root_version = -1
@@ -202,15 +247,28 @@ class ShardedFlat:
             self._ev[key] = ev
 
     # ------------------------------------------------------------------ collectives
+    def _barrier(self) -> None:
+        self.epoch += 1
+        ext().symm_barrier(self.t_flags, self.rank, self.world, self.epoch, self.timeout_s)
+
     def _gather(self, u: _Unit, out: torch.Tensor) -> None:
-        shard = self._shard(self.compute, u)
-        dist.all_gather_into_tensor(out[:u.full], shard, group=self.group)
+        if self.peer:
+            es = self.compute.element_size()
+            ext().fsdp_gather(self.t_compute, u.shard_off * es, u.shard * es, out)
+        else:
+            shard = self._shard(self.compute, u)
+            dist.all_gather_into_tensor(out[:u.full], shard, group=self.group)
         self.comm_bytes += u.full * out.element_size()
 
-    def _reduce(self, u: _Unit, full: torch.Tensor) -> None:
-        tmp = self._rs_tmp[:u.shard]
-        dist.reduce_scatter_tensor(tmp, full[:u.full], group=self.group)
-        self._shard(self.grad, u).add_(tmp)
+    def _reduce(self, u: _Unit, full: torch.Tensor, table=None) -> None:
+        if self.peer:
+            self._barrier()  # every rank's gradients of this unit are complete
+            ext().fsdp_reduce(table, 0, u.shard, self.rank, self._shard(self.grad, u))
+            self._barrier()  # every rank has read this rank's buffer
+        else:
+            tmp = self._rs_tmp[:u.shard]
+            dist.reduce_scatter_tensor(tmp, full[:u.full], group=self.group)
+            self._shard(self.grad, u).add_(tmp)
         full[:u.full].zero_()
         self.comm_bytes += u.full * 4
 
@@ -219,6 +277,9 @@ class ShardedFlat:
         if self._cuda:  # buffers may still be read by work queued before this forward
             self._side.wait_stream(torch.cuda.current_stream(self.device))
         if self._root_version != self.version:
+            if self.peer:  # every rank has finished the step that rewrote its shards
+                with self._side_ctx():
+                    self._barrier()
             with self._side_ctx():
                 self._gather(self.root, self.root_w)
             self._side_record(("root",))
@@ -272,7 +333,7 @@ class ShardedFlat:
         if self._cuda:
             self._side_wait(("bwd", i))
         with self._side_ctx():
-            self._reduce(u, self.block_g[i % 2])
+            self._reduce(u, self.block_g[i % 2], self.t_block_g[i % 2] if self.peer else None)
         self._side_record(("rs", i))
 
     def _fold(self, u: _Unit, full: torch.Tensor) -> None:
@@ -289,7 +350,7 @@ class ShardedFlat:
         if self._cuda:
             self._side.wait_stream(torch.cuda.current_stream(self.device))
         with self._side_ctx():
-            self._reduce(self.root, self.root_g)
+            self._reduce(self.root, self.root_g, self.t_root_g if self.peer else None)
         if self._cuda:
             torch.cuda.current_stream(self.device).wait_stream(self._side)
         self._ev.clear()
@@ -372,6 +433,18 @@ class ShardedFlat:
         self.set_full("master", full)
         self.recast()
 
+    def check(self) -> None:
+        """Raise if a bounded device wait of the peer collectives timed out (reads the device error word)."""
+        err = int(ext().device_error()) if self.peer else 0
+        if err:
+            raise RuntimeError(f"sharded-parameter collective failed on rank {self.rank}: device error code {err}")
+
+    def close(self) -> None:
+        if self.heap is not None:
+            torch.cuda.synchronize(self.device)
+            self.heap.close()
+            self.heap = None
+
     # ------------------------------------------------------------------ colocation hand-off
     _SHARDS = ("master", "grad", "exp_avg", "exp_avg_sq", "compute")
 
@@ -381,7 +454,7 @@ class ShardedFlat:
             return
         host = {}
         for name in self._SHARDS:
-            if name == "compute" and not self.separate_compute:
+            if name == "compute" and (not self.separate_compute or self.peer):  # heap memory stays mapped
                 continue
             t = getattr(self, name)
             h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
@@ -389,10 +462,15 @@ class ShardedFlat:
             host[name] = h
         torch.cuda.synchronize()
         self._host = host
-        for name in self._SHARDS:
+        for name in host:
             setattr(self, name, None)
-        self.root_w = self.root_g = self._rs_tmp = None
-        self.block_w = self.block_g = [None, None]
+        if not self.separate_compute:
+            self.compute = None
+        self.root_w = self._rs_tmp = None
+        self.block_w = [None, None]
+        if not self.peer:
+            self.root_g = None
+            self.block_g = [None, None]
         for p in self.params:
             p.data = torch.empty(0, dtype=p.dtype, device=p.device)
             p.main_grad = None

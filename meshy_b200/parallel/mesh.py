@@ -32,6 +32,8 @@ class ParallelDims:
     cp_group: object = None
     tp_group: object = None
     loss_group: object = None
+    shard_group: object = None      # ranks that shard one replica's parameters (dp_shard x cp)
+    replicate_group: object = None  # ranks that hold the same shard in different replicas
 
     @property
     def world(self) -> int:
@@ -108,6 +110,20 @@ def build_parallel_dims(world: int, rank: int, *, dp_replicate: int = -1, dp_sha
         g = dist.new_group(ranks, **kw) if dp * cp > 1 else None
         if rank in ranks:
             pd.loss_group = g
+    # replica-major DP index: d = rep * dp_shard + shard
+    for rep in range(dp_replicate):
+        for t in range(tp):
+            ranks = [((rep * dp_shard + sh) * cp + c) * tp + t for sh in range(dp_shard) for c in range(cp)]
+            g = dist.new_group(ranks, **kw) if dp_shard * cp > 1 else None
+            if rank in ranks:
+                pd.shard_group = g
+    for sh in range(dp_shard):
+        for c in range(cp):
+            for t in range(tp):
+                ranks = [((rep * dp_shard + sh) * cp + c) * tp + t for rep in range(dp_replicate)]
+                g = dist.new_group(ranks, **kw) if dp_replicate > 1 else None
+                if rank in ranks:
+                    pd.replicate_group = g
     return pd
 
 

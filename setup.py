@@ -34,7 +34,7 @@ cuda_sources = [
     "csrc/kernels/decode_noalloc.cu",
     "csrc/kernels/decode_mega.cu",
 ]
-extra_cuda = [s for s in ("csrc/kernels/symm.cu",) if os.path.exists(os.path.join(ROOT, s))]
+extra_cuda = [s for s in ("csrc/kernels/symm.cu", "csrc/kernels/fsdp.cu") if os.path.exists(os.path.join(ROOT, s))]
 
 native_sources = [s for s in ("csrc/native/bindings.cpp", "csrc/native/column_store.cpp")
                   if os.path.exists(os.path.join(ROOT, s))]

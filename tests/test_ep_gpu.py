@@ -127,3 +127,77 @@ def test_expert_parallel_over_peer_memory_matches_local_layer():
         assert err == 0, (rank, err)
         assert worst["out"] < 1e-2 and worst["dx"] < 2e-2 and worst["dw"] < 2e-2, (rank, worst)
         assert worst["dw13"] < 2e-2 and worst["dw2"] < 2e-2, (rank, worst)
+
+
+class _EmulatedExchange:
+    """One emulated rank's view of the exchange: its own regions, and address tables that list every emulated
+    rank's regions (all on this GPU)."""
+
+    def __init__(self, rank, world, dim, cap, regions, tables):
+        self.rank, self.world, self.dim, self.cap = rank, world, dim, cap
+        for name, bufs in regions.items():
+            setattr(self, name, bufs[rank])
+        for name, tab in tables.items():
+            setattr(self, "t_" + name, tab)
+
+    def owner_plan(self, experts, e_local):
+        from meshy_b200.parallel.ep import PeerExchange
+
+        return PeerExchange.owner_plan(self, experts, e_local)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_kernels_emulated_on_one_gpu(world):
+    """Every rank's phases run in turn on one GPU (dispatch for all, then the owners, then the sources): the
+    dispatch / return kernels only store through address tables and never wait on another rank, so the
+    exchange is exercised without a second GPU. Same oracle as the 2-GPU test."""
+    from meshy_b200.ops import moe as M
+    from meshy_b200.parallel import ep as EP
+
+    E, D, F, k, T = 8, 256, 128, 2, 300
+    w13, w2 = _weights(E, D, F)
+    n_l = E // world
+    cap = (T + 5 * (world - 1)) * k
+    dev = "cuda"
+    regions = {
+        "recv_x": [torch.zeros(world * cap, D, dtype=torch.bfloat16, device=dev) for _ in range(world)],
+        "recv_meta": [torch.zeros(world * cap, dtype=torch.int32, device=dev) for _ in range(world)],
+        "recv_idx": [torch.zeros(world * cap, dtype=torch.int32, device=dev) for _ in range(world)],
+        "recv_cnt": [torch.zeros(world, dtype=torch.int32, device=dev) for _ in range(world)],
+        "ret": [torch.zeros(cap, D, dtype=torch.bfloat16, device=dev) for _ in range(world)],
+    }
+    tables = {name: torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=dev)
+              for name, bufs in regions.items()}
+    xs = [_EmulatedExchange(r, world, D, cap, regions, tables) for r in range(world)]
+    w13_l = [w13[r * n_l:(r + 1) * n_l].clone() for r in range(world)]
+    w2_l = [w2[r * n_l:(r + 1) * n_l].clone() for r in range(world)]
+    for r in range(world):
+        w13_l[r].main_grad = torch.zeros(w13_l[r].shape, dtype=torch.float32, device=dev)
+        w2_l[r].main_grad = torch.zeros(w2_l[r].shape, dtype=torch.float32, device=dev)
+    inp = [_inputs(r, 0, T, D, E, k) for r in range(world)]
+    # forward: sources, owners, sources
+    disp = [EP._fwd_dispatch(inp[r][0], inp[r][2], xs[r], n_l) for r in range(world)]
+    own = [EP._fwd_owner(xs[r], w13_l[r], w2_l[r]) for r in range(world)]
+    col = [EP._fwd_collect(xs[r], inp[r][0].shape[0] * k, inp[r][1], inp[r][0].shape[0]) for r in range(world)]
+    # backward
+    dws = [EP._bwd_dispatch(inp[r][3], col[r][1], col[r][2], inp[r][1], *disp[r], n_l, xs[r]) for r in range(world)]
+    for r in range(world):
+        ids, slot, off, cnt, row_src, idx, xp, h, act = own[r]
+        EP._bwd_owner(xs[r], ids, slot, off, row_src, idx, xp, h, act, w13_l[r], w2_l[r], 64)
+    dxs = [EP._bwd_collect(xs[r], col[r][2], inp[r][0].shape[0]) for r in range(world)]
+    torch.cuda.synchronize()
+    # oracle: the local layer with every expert, rank by rank
+    w13.main_grad = torch.zeros(w13.shape, dtype=torch.float32, device=dev)
+    w2.main_grad = torch.zeros(w2.shape, dtype=torch.float32, device=dev)
+    for r in range(world):
+        x, w, e, gout = inp[r]
+        x1, w1 = x.clone().requires_grad_(True), w.clone().requires_grad_(True)
+        ref = M.experts_forward(x1, w1, e, w13, w2, 64)
+        ref.backward(gout)
+        assert _rel(col[r][0], ref) < 1e-2
+        assert _rel(dxs[r], x1.grad) < 2e-2
+        assert _rel(dws[r], w1.grad) < 2e-2
+    for r in range(world):
+        assert _rel(w13_l[r].main_grad, w13.main_grad[r * n_l:(r + 1) * n_l]) < 2e-2
+        assert _rel(w2_l[r].main_grad, w2.main_grad[r * n_l:(r + 1) * n_l]) < 2e-2

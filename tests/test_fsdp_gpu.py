@@ -1,0 +1,144 @@
+"""Sharded parameters on 2 GPUs (one process per GPU, NCCL).
+
+The sharded trainer -- with its collectives over peer memory (gather and reduce-scatter kernels between
+bounded device barriers) and with NCCL's -- takes the same optimiser steps as the replicated trainer with
+the fused data-parallel step, on bf16 compute: several micro-batches per mini-batch, two mini-batches,
+behaviour log-probs from a no-grad forward, clipping and weight decay. The gathered global layout (the
+weight-sync source) equals the replicated trainer's compute buffer. The peer kernels alone also run on one
+GPU, against a table of local regions standing in for the ranks.
+"""
+
+import os
+import random
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+NEED = 2
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _samples(rank, seed=0, n=6):
+    rng = random.Random(seed * 100 + rank)
+    out = []
+    for i in range(n):
+        P, R = rng.randint(16, 64), rng.randint(32, 160)
+        toks = [rng.randrange(2048) for _ in range(P + R)]
+        out.append({"tokens": torch.tensor(toks), "mask_assistant": torch.tensor([0] * P + [1] * R),
+                    "logprobs": torch.tensor([0.0] * P + [-2.0] * R), "advantage": torch.tensor([1.0 - 0.3 * i]),
+                    "reward": torch.tensor([float(i % 2)]), "weight_version": torch.tensor([0])})
+    return out
+
+
+def _trainer(group, fsdp):
+    from meshy_b200.backend.trainer import PPOTrainer
+    from meshy_b200.config import TrainerConfig, TrainerParamsConfig
+
+    tc = TrainerConfig(model_name="qwen3", model_flavor="debugmodel", seq_len=256, lr=1e-3, weight_decay=0.1,
+                       max_norm=0.5, dtype="bfloat16")
+    tp = TrainerParamsConfig(mini_batch_size=3, batch_layout="packed", max_tokens_per_micro=256,
+                             old_logprobs_source="train")
+    return PPOTrainer(tc, tp, device="cuda", seed=0, dp_group=group, loss_group=group, timer_enabled=False,
+                      fsdp_group=group if fsdp else None)
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_WORLD_SIZE=str(world))
+        torch.cuda.set_device(rank)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                                timeout=timedelta(seconds=120))
+        g = dist.group.WORLD
+        rep = _trainer(g, False)
+        assert rep.fused_dp
+        os.environ["MESHY_FSDP_PEER"] = "1"
+        peer = _trainer(g, True)
+        os.environ["MESHY_FSDP_PEER"] = "0"
+        nccl = _trainer(g, True)
+        assert peer.flat.peer and not nccl.flat.peer
+        out = {}
+        for step in range(2):
+            ms = [t.train_step(_samples(rank, step)) for t in (rep, peer, nccl)]
+            out[step] = [(m["grad_norm"], m["pg_loss"]) for m in ms]
+        peer.flat.check()
+        rep.flat.gather_master()
+        want = rep.flat.master
+        out["err"] = [float((t.flat.full_buffer("master") - want).abs().max()) for t in (peer, nccl)]
+        out["sync_err"] = [float((t.flat.sync_source.float() - rep.flat.sync_source.float()).abs().max())
+                           for t in (peer, nccl)]
+        out["bytes"] = peer.flat.comm_bytes
+        torch.cuda.synchronize()
+        peer.flat.close()
+        q.put((rank, out))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < NEED, reason="needs 2 GPUs")
+@pytest.mark.timeout(600)
+def test_sharded_trainer_matches_replicated_on_gpus():
+    port = _port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_worker, args=(r, NEED, port, q)) for r in range(NEED)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=540) for _ in range(NEED)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, out in res:
+        assert not isinstance(out, str), out
+        for step in range(2):
+            (gn0, l0), *others = out[step]
+            for gn, lo in others:
+                assert abs(gn - gn0) <= 2e-3 * max(1.0, gn0), (step, out[step])
+                assert abs(lo - l0) <= 2e-3 * max(1.0, abs(l0)), (step, out[step])
+        for e in out["err"]:
+            assert e < 2e-4, out["err"]
+        for e in out["sync_err"]:
+            assert e < 1e-2, out["sync_err"]
+        assert out["bytes"] > 0
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_kernels_on_one_gpu(world):
+    """The gather and reduce kernels read ranks' regions through a table of addresses; on one GPU a table of
+    ``world`` local regions stands in for the peers (the kernels never wait on another rank)."""
+    from meshy_b200.ops._ext import ext
+
+    C = ext()
+    shard = 4096 + 64
+    off = 1024  # elements into each region
+    gen = torch.Generator(device="cuda").manual_seed(world)
+    regions = [torch.randn(off + shard, device="cuda", generator=gen).bfloat16() for _ in range(world)]
+    table = torch.tensor([r.data_ptr() for r in regions], dtype=torch.int64, device="cuda")
+    out = torch.empty(world * shard, dtype=torch.bfloat16, device="cuda")
+    C.fsdp_gather(table, off * 2, shard * 2, out)
+    want = torch.cat([r[off:] for r in regions])
+    assert torch.equal(out, want)
+    grads = [torch.randn(world * shard, device="cuda", generator=gen) for _ in range(world)]
+    gtab = torch.tensor([g.data_ptr() for g in grads], dtype=torch.int64, device="cuda")
+    for rank in range(world):
+        dst = torch.randn(shard, device="cuda", generator=gen)
+        ref = dst.clone()
+        for g in grads:  # rank order, as the kernel sums
+            ref = ref + g[rank * shard:(rank + 1) * shard]
+        C.fsdp_reduce(gtab, 0, shard, rank, dst)
+        assert torch.allclose(dst, ref, rtol=0, atol=1e-5)
