@@ -33,7 +33,7 @@ from ..utils.timer import TimerStats
 from .batch import ADVANTAGE_TOKENS, Batch, build_micro_batch
 from .flat import FlatAdamW, FlatParams, lr_lambda
 from .loss import LossConfig, ppo_clip_loss, reduce_sums
-from .plan import MiniPlan, Plan, PlannerConfig, build_plan, plan_stats, resolve_align
+from .plan import MiniPlan, Plan, PlannerConfig, build_plan, filler_micro, plan_stats, resolve_align
 
 
 @dataclass
@@ -253,6 +253,8 @@ class PPOTrainer:
                 full = self.plan_batch(samples, 1)
                 samples = full.local_samples(samples, 0)
                 plan = full.per_rank[0]
+        if self.fsdp:
+            plan = self._equalize_micros(plan)
         gae_metrics: dict[str, float] = {}
         if self.params.enable_gae:
             with timer.timer("train/gae"):
@@ -324,6 +326,28 @@ class PPOTrainer:
         with timer.timer("train/optim_step"):
             gn = self.optimizer.step(self._ep_grad_norm() if self.reducer.skip else None)
         return reduce_sums(sums, self.loss_group), gn
+
+    def _equalize_micros(self, plan: Sequence[MiniPlan]) -> list[MiniPlan]:
+        """Sharded parameters gather and reduce inside every micro-batch, so every rank of the shard group
+        must run the same number of them: pad each mini-batch with empty filler micros up to the group's
+        largest count (a rank-local plan, as the lock-step loop builds, can differ from rank to rank)."""
+        g = self.flat.group
+        dev = self.device if dist.get_backend(g) == "nccl" else torch.device("cpu")
+        n = torch.tensor([len(plan), -len(plan)], dtype=torch.int64, device=dev)
+        dist.all_reduce(n, op=dist.ReduceOp.MAX, group=g)
+        if int(n[0]) != -int(n[1]):
+            raise ValueError(f"ranks of the shard group planned {-int(n[1])} to {int(n[0])} mini-batches; sharded "
+                             "parameters need the same number on every rank")
+        counts = torch.tensor([len(m.micros) for m in plan] or [0], dtype=torch.int64, device=dev)
+        dist.all_reduce(counts, op=dist.ReduceOp.MAX, group=g)
+        filler = filler_micro(self.planner_config)
+        out = []
+        for m, c in zip(plan, counts.tolist()):
+            if c > len(m.micros):
+                m = MiniPlan(tuple(m.micros) + (filler,) * (c - len(m.micros)), m.n_docs_global, m.n_tokens_global,
+                             m.tokens_per_rank)
+            out.append(m)
+        return out
 
     def _ep_grad_norm(self) -> torch.Tensor:
         """Global gradient norm under expert parallelism: the dense part is replicated (counted once),

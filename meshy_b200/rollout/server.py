@@ -183,10 +183,10 @@ def build_app(runner: EngineRunner, model_name: str = ""):
 
         def do():
             nonlocal local
-            handle = body.get("handle")
+            handle, uuid = body.get("handle"), body.get("gpu_uuid")
             if handle is None:
-                handle, local = pick_handle(body["handles"], device_uuid(eng.device))
-            src = open_ipc_flat(handle)
+                handle, local, uuid = pick_handle(body["handles"], device_uuid(eng.device))
+            src = open_ipc_flat(handle, uuid)
             eng.update_weights_from_flat(src, body.get("weight_version"))
             if eng.cuda:
                 import torch

@@ -41,9 +41,30 @@ def export_ipc_flat(flat: torch.Tensor) -> str:
     return base64.b64encode(pickle.dumps(reduce_tensor(flat))).decode()
 
 
-def open_ipc_flat(handle: str) -> torch.Tensor:
+def open_ipc_flat(handle: str, uuid: str | None = None) -> torch.Tensor:
+    """Map an exported tensor. The handle names the exporter's device by ITS ordinal, which means nothing in a
+    process with another ``CUDA_VISIBLE_DEVICES``; with ``uuid`` (the exporting GPU) the tensor is opened on
+    this process's ordinal of that GPU."""
     fn, args = pickle.loads(base64.b64decode(handle.encode()))
+    if uuid is not None:
+        import inspect
+
+        names = list(inspect.signature(fn).parameters)
+        if "storage_device" in names:
+            ordinal = local_ordinal(uuid)
+            if ordinal is None:
+                raise ValueError(f"GPU {uuid} is not visible in this process; cannot map its weights")
+            args = list(args)
+            args[names.index("storage_device")] = ordinal
     return fn(*args)
+
+
+def local_ordinal(uuid: str) -> int | None:
+    """This process's device ordinal of the GPU with ``uuid`` (None when it is not visible)."""
+    for i in range(torch.cuda.device_count()):
+        if device_uuid(i) == uuid:
+            return i
+    return None
 
 
 def device_uuid(device: torch.device | int | None = None) -> str:
@@ -103,15 +124,17 @@ def decode_handle_set(ref: str) -> dict:
     return json.loads(ref[len("ipc-set:"):])
 
 
-def pick_handle(handles: dict[str, str], my_uuid: str) -> tuple[str, bool]:
-    """The handle exported on this engine's GPU if there is one (``local=True``), else a peer GPU's (read
-    over NVLink; any DDP rank's snapshot holds the same weights)."""
+def pick_handle(handles: dict[str, str], my_uuid: str) -> tuple[str, bool, str]:
+    """The handle exported on this engine's GPU if there is one (``local=True``), else a visible peer GPU's
+    (read over NVLink; any DDP rank's snapshot holds the same weights). Returns ``(handle, local, uuid)``."""
     if my_uuid in handles:
-        return handles[my_uuid], True
+        return handles[my_uuid], True, my_uuid
     if not handles:
         raise ValueError("empty handle set")
-    return handles[sorted(handles)[0]], False
+    visible = [u for u in sorted(handles) if local_ordinal(u) is not None]
+    u = visible[0] if visible else sorted(handles)[0]
+    return handles[u], False, u
 
 
 __all__ = ["DevicePublisher", "decode_handle_set", "device_uuid", "encode_handle_set", "export_ipc_flat",
-           "open_ipc_flat", "pick_handle"]
+           "local_ordinal", "open_ipc_flat", "pick_handle"]

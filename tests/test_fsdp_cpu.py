@@ -22,7 +22,8 @@ def _samples(rank, seed=0, n=4):
     rng = random.Random(seed * 100 + rank)
     out = []
     for i in range(n):
-        P, R = rng.randint(4, 12), rng.randint(6, 30)
+        # rank 0's short documents share micro-batches, rank 1's long ones do not: unequal micro counts
+        P, R = (rng.randint(3, 5), rng.randint(4, 8)) if rank == 0 else (rng.randint(4, 12), rng.randint(56, 70))
         toks = [rng.randrange(2048) for _ in range(P + R)]
         out.append({"tokens": torch.tensor(toks), "mask_assistant": torch.tensor([0] * P + [1] * R),
                     "logprobs": torch.tensor([0.0] * P + [-2.0] * R), "advantage": torch.tensor([1.0 - 0.5 * i]),
@@ -36,7 +37,7 @@ def _trainer(group, fsdp, ckpt_mode="none"):
 
     tc = TrainerConfig(model_name="qwen3", model_flavor="debugmodel", seq_len=64, lr=1e-3, weight_decay=0.1,
                        max_norm=0.5, dtype="float32", activation_checkpoint_mode=ckpt_mode)
-    tp = TrainerParamsConfig(mini_batch_size=2, batch_layout="packed", max_tokens_per_micro=48,
+    tp = TrainerParamsConfig(mini_batch_size=2, batch_layout="packed", max_tokens_per_micro=96,
                              old_logprobs_source="train")
     return PPOTrainer(tc, tp, device="cpu", seed=0, dp_group=group, loss_group=group, timer_enabled=False,
                       fsdp_group=group if fsdp else None)
@@ -52,16 +53,20 @@ def _worker(rank, world, port, q, tmp):
             sh = _trainer(g, True, ckpt_mode)
             rep = _trainer(g, False, ckpt_mode)
             assert sh.flat.numel < rep.flat.numel  # this rank holds about half of the state
+            w0 = rep.flat.master.clone()
             for step in range(2):
                 m1 = sh.train_step(_samples(rank, step))
                 m2 = rep.train_step(_samples(rank, step))
                 out[(ckpt_mode, step)] = (m1["grad_norm"], m2["grad_norm"], m1["pg_loss"], m2["pg_loss"])
-            a = sh.flat.state_dict("master")
-            b = rep.flat.state_dict("master")
-            out[(ckpt_mode, "err")] = max(float((a[k] - b[k]).abs().max()) for k in b)
+            # AdamW's first steps move every weight by about lr * sign(g): a gradient that is zero up to rounding
+            # can flip sign between the two reduction orders, so compare the updates as a whole
+            full = sh.flat.full_buffer("master")
+            out[(ckpt_mode, "err")] = float((full - rep.flat.master).norm() / (rep.flat.master - w0).norm())
         # global layout of the gathered weights == the replicated trainer's flat buffer
         full = sh.flat.full_buffer("master")
-        out["layout_err"] = float((full - rep.flat.master).abs().max())
+        sd = sh.flat.state_dict("master")
+        out["layout_err"] = max(float((sd[sl.name].reshape(-1) - full[sl.offset:sl.offset + sl.numel]).abs().max())
+                                for sl in sh.flat.slots)
         # checkpoint round trip into a fresh sharded trainer
         path = os.path.join(tmp, "ckpt")
         sh.save_checkpoint(path, step=2)
@@ -101,8 +106,8 @@ def test_sharded_trainer_matches_replicated(tmp_path):
                 gn1, gn2, l1, l2 = out[(mode, step)]
                 assert abs(gn1 - gn2) <= 1e-5 * max(1.0, gn2), (mode, step, gn1, gn2)
                 assert abs(l1 - l2) <= 1e-6 * max(1.0, abs(l2)), (mode, step, l1, l2)
-            assert out[(mode, "err")] < 1e-5, (mode, out[(mode, "err")])  # 1 % of one AdamW step
-        assert out["layout_err"] < 1e-5
+            assert out[(mode, "err")] < 1e-3, (mode, out[(mode, "err")])
+        assert out["layout_err"] == 0.0
         assert out["restore_err"] == 0.0
         l1, l2, werr = out["resume"]
         assert l1 == l2 and werr == 0.0

@@ -32,7 +32,7 @@ def _samples(rank, seed=0, n=6):
     rng = random.Random(seed * 100 + rank)
     out = []
     for i in range(n):
-        P, R = rng.randint(16, 64), rng.randint(32, 160)
+        P, R = rng.randint(16, 64), rng.randint(32, 160) + 60 * rank  # rank 1 packs more micro-batches
         toks = [rng.randrange(2048) for _ in range(P + R)]
         out.append({"tokens": torch.tensor(toks), "mask_assistant": torch.tensor([0] * P + [1] * R),
                     "logprobs": torch.tensor([0.0] * P + [-2.0] * R), "advantage": torch.tensor([1.0 - 0.3 * i]),
@@ -54,15 +54,18 @@ def _trainer(group, fsdp):
 
 def _worker(rank, world, port, q):
     try:
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_WORLD_SIZE=str(world))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_WORLD_SIZE=str(world),
+                          MESHY_SYMM_TIMEOUT_S="5")
         torch.cuda.set_device(rank)
         from datetime import timedelta
 
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
-                                timeout=timedelta(seconds=120))
+                                timeout=timedelta(seconds=60))
         g = dist.group.WORLD
         rep = _trainer(g, False)
         assert rep.fused_dp
+        rep.flat.gather_master()
+        w0 = rep.flat.master.clone()
         os.environ["MESHY_FSDP_PEER"] = "1"
         peer = _trainer(g, True)
         os.environ["MESHY_FSDP_PEER"] = "0"
@@ -75,7 +78,9 @@ def _worker(rank, world, port, q):
         peer.flat.check()
         rep.flat.gather_master()
         want = rep.flat.master
-        out["err"] = [float((t.flat.full_buffer("master") - want).abs().max()) for t in (peer, nccl)]
+        # AdamW's first steps move weights by about lr * sign(g), and a gradient that is zero up to rounding can
+        # flip sign between reduction orders: compare the updates as a whole
+        out["err"] = [float((t.flat.full_buffer("master") - want).norm() / (want - w0).norm()) for t in (peer, nccl)]
         out["sync_err"] = [float((t.flat.sync_source.float() - rep.flat.sync_source.float()).abs().max())
                            for t in (peer, nccl)]
         out["bytes"] = peer.flat.comm_bytes
@@ -91,7 +96,7 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < NEED, reason="needs 2 GPUs")
-@pytest.mark.timeout(600)
+@pytest.mark.timeout(400)
 def test_sharded_trainer_matches_replicated_on_gpus():
     port = _port()
     ctx = mp.get_context("spawn")
@@ -99,7 +104,7 @@ def test_sharded_trainer_matches_replicated_on_gpus():
     ps = [ctx.Process(target=_worker, args=(r, NEED, port, q)) for r in range(NEED)]
     for p in ps:
         p.start()
-    res = [q.get(timeout=540) for _ in range(NEED)]
+    res = [q.get(timeout=300) for _ in range(NEED)]
     for p in ps:
         p.join(timeout=60)
     for rank, out in res:
@@ -110,7 +115,7 @@ def test_sharded_trainer_matches_replicated_on_gpus():
                 assert abs(gn - gn0) <= 2e-3 * max(1.0, gn0), (step, out[step])
                 assert abs(lo - l0) <= 2e-3 * max(1.0, abs(l0)), (step, out[step])
         for e in out["err"]:
-            assert e < 2e-4, out["err"]
+            assert e < 1e-2, out["err"]
         for e in out["sync_err"]:
             assert e < 1e-2, out["sync_err"]
         assert out["bytes"] > 0
