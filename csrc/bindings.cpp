@@ -946,34 +946,6 @@ void value_head_bwd_(Tensor h, Tensor w, Tensor dv, Tensor dh, Tensor dw, Tensor
   count();
 }
 
-void l2_prefetch_(std::vector<Tensor> ts) {
-  TORCH_CHECK(!ts.empty() && ts.size() <= 4, "l2_prefetch: 1 to 4 tensors");
-  const void* ptrs[4];
-  long long bytes[4];
-  for (size_t i = 0; i < ts.size(); ++i) {
-    CHECK_CUDA(ts[i]);
-    TORCH_CHECK(ts[i].is_contiguous(), "l2_prefetch: contiguous tensors");
-    ptrs[i] = ts[i].data_ptr();
-    bytes[i] = ts[i].numel() * ts[i].element_size();
-  }
-  const c10::cuda::CUDAGuard guard(ts[0].device());
-  l2_prefetch(ptrs, bytes, (int)ts.size(), cur_stream());
-  count();
-}
-
-void kv_prefetch_(Tensor bt, Tensor seq_lens, Tensor kc, Tensor vc, int64_t page) {
-  CHECK_CUDA(bt);
-  TORCH_CHECK(bt.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt && bt.dim() == 2 &&
-                  bt.stride(1) == 1 && seq_lens.numel() >= bt.size(0),
-              "kv_prefetch: bt [B, max_pages] int32, seq_lens [B] int32");
-  TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous() && kc.size(0) == vc.size(0), "kv_prefetch: caches");
-  const int64_t page_bytes = kc.numel() / kc.size(0) * kc.element_size();
-  const c10::cuda::CUDAGuard guard(bt.device());
-  kv_prefetch(bt.data_ptr<int>(), seq_lens.data_ptr<int>(), bt.size(0), bt.stride(0), (int)page, kc.data_ptr(),
-              vc.data_ptr(), page_bytes, kc.size(0), cur_stream());
-  count();
-}
-
 void topk_logprobs_(Tensor z, int64_t k, Tensor ids, Tensor lp, c10::optional<Tensor> lse) {
   CHECK_CUDA(z);
   CHECK_F32(z);
@@ -1290,6 +1262,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_norm_scaled", &gemm_norm_scaled, "decode: GEMM on a prepared RMSNorm input, rows scaled by rstd");
   m.def("gemm_qkv_rope", &gemm_qkv_rope, "decode: QKV GEMM with RoPE / QK-norm and the KV-cache write fused");
   m.def("gemm_norm", &gemm_norm, "decode: fused input RMSNorm + small-M GEMM (returns False if not eligible)");
+  m.def("paged_decode_trace",
+        [](c10::optional<Tensor> buf) {
+          if (buf && buf->defined()) {
+            TORCH_CHECK(buf->scalar_type() == at::kLong && buf->is_cuda() && buf->dim() == 3 && buf->size(-1) == 8 &&
+                            buf->size(-2) == 1024,
+                        "paged_decode_trace: int64 [slots, 1024, 8]");
+            paged_decode_trace(reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>()), (int)buf->size(0));
+          } else {
+            paged_decode_trace(nullptr, 0);
+          }
+        },
+        "record per-CTA timelines of the decode-attention launches (None stops)", py::arg("buf") = py::none());
   m.def("gemm_small_trace",
         [](c10::optional<Tensor> buf) {
           if (buf.has_value() && buf->defined()) {
@@ -1307,8 +1291,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("filtered_sample", &filtered_sample_, "top-k / top-p / temperature sampling over fp32 logits");
   m.def("value_head_fwd", &value_head_fwd_, "critic value head + clipped value loss (values, dL/dv, loss sum)");
   m.def("value_head_bwd", &value_head_bwd_, "critic value head backward: dh, dw, db");
-  m.def("kv_prefetch", &kv_prefetch_, "ask the L2 for the K/V cache pages of the rows' block tables");
-  m.def("l2_prefetch", &l2_prefetch_, "ask the L2 for the bytes of up to 4 tensors (no wait)");
   m.def("topk_logprobs", &topk_logprobs_, "K largest fp32 logits per row (sorted), log-probabilities, lse");
   m.def("gather_logprobs", &gather_logprobs_, "log-probabilities of given ids from hidden rows and the LM head");
   m.def("scatter_add_rows", &scatter_add_rows_, "dz[t, ids[t, k]] += g[t, k] on bf16 logit gradients");

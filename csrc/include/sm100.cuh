@@ -199,6 +199,9 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of cluster_sync_all, for work between the arrival and the wait (warp-uniform calls).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // Address of the same shared-memory offset in CTA ``rank`` of this cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   uint32_t r;

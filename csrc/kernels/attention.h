@@ -45,6 +45,9 @@ constexpr int kMaxClusterSplits = 16;
 int paged_decode_tma_splits(int B, int Hkv, int max_pages);
 int paged_decode_max_cluster();  // kMaxClusterSplits, or 8 where the device cannot place 16-CTA clusters
 void paged_decode_force_splits(int n);  // tests: 0 restores the heuristic
+// Timeline capture of the TMA decode-attention launches: launch i writes slot i of buf [slots][1024][8]
+// (global-timer ns per CTA, see decode_attn.cu); null stops it.
+void paged_decode_trace(unsigned long long* buf, int slots);
 // ``decode_step``: the kernel before this one in the stream wrote, of this cache, at most the row of each
 // sequence's last position (seq_lens[b] - 1) and nothing of bt / seq_lens. Pages before a sequence's last
 // one are then loaded before the programmatic-dependent-launch wait, under that kernel's tail.

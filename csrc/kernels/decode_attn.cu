@@ -81,7 +81,8 @@ template <int HD, bool CLUSTER>
 __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
     const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV, const bf16* __restrict__ Q,
     const int* __restrict__ bt, const int* __restrict__ seq_lens, bf16* __restrict__ O, float* __restrict__ part,
-    int Hq, int Hkv, int max_pages, int n_split, float scale, int* err, int early, unsigned* __restrict__ ctr) {
+    int Hq, int Hkv, int max_pages, int n_split, float scale, int* err, int early, unsigned* __restrict__ ctr,
+    unsigned long long* __restrict__ trace) {
   using C = DCfg<HD>;
   extern __shared__ __align__(1024) uint8_t smraw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
@@ -92,6 +93,15 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
 
   const int b = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
   const int rep = Hq / Hkv;
+  // optional timeline, [CTA][8] global-timer ns: entry, past the dependency wait, Q staged, first page
+  // consumed (warp 0), last page consumed (warp 0), CTA merge done, cluster merge done, exit
+  unsigned long long* tr =
+      trace ? trace + (((size_t)b * gridDim.y + hk) * gridDim.z + sp) * 8 : nullptr;
+#define DEC_TRACE(k)                                     \
+  do {                                                   \
+    if (tr && threadIdx.x == 0) tr[(k)] = globaltimer_ns(); \
+  } while (0)
+  DEC_TRACE(0);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const float sl2 = scale * kLog2eD;
 
@@ -131,6 +141,7 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
     }
     pdl_wait();  // Q and the newest K/V rows come from the kernel before
   }
+  DEC_TRACE(1);
   pdl_trigger();
   // query rows of this GQA group → Qs[16][HD] (XOR swizzle of 16-byte chunks), rows >= rep zero
   for (int i = threadIdx.x; i < 16 * HD / 8; i += kThreadsDec) {
@@ -141,6 +152,7 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
     *reinterpret_cast<uint4*>(Qs + r * HD + ch * 8) = val;
   }
   __syncthreads();
+  DEC_TRACE(2);
 
   float o[HD / 8][4];
 #pragma unroll
@@ -257,11 +269,13 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
+      if (pi == p0) DEC_TRACE(3);
       if (++stage == C::STAGES) {
         stage = 0;
         phase ^= 1;
       }
     }
+    DEC_TRACE(4);
   }
   __syncthreads();  // every page consumed: the stage ring is free for the merge buffers
 
@@ -318,6 +332,7 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
       }
     }
   }
+  DEC_TRACE(5);
   if constexpr (!CLUSTER) {
     if (n_split > 1 && ctr != nullptr) {
       // the last split of (b, hk) to finish merges all splits' partials (no second kernel); it resets
@@ -370,33 +385,47 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
       const uint32_t base_m = smem_u32(cm), base_l = smem_u32(cl), base_o = smem_u32(co);
       for (int idx = sp * kThreadsDec + threadIdx.x; idx < rep * HD; idx += n_split * kThreadsDec) {
         int row = idx / HD, c = idx % HD;
-        float ms[kMaxClusterSplits];
-        float M = -INFINITY;
-        for (int r = 0; r < n_split; ++r) {
-          float v;
-          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(mapa_shared(base_m + row * 4, r)) : "memory");
-          ms[r] = v;
-          M = fmaxf(M, v);
+        // every peer's (m, l, o) is loaded before any of them is used, so the DSMEM round trips overlap
+        // (one load in flight at a time cost ~0.1 us each, 3 x n_split of them per output)
+        float ms[kMaxClusterSplits], ls[kMaxClusterSplits], os[kMaxClusterSplits];
+#pragma unroll
+        for (int r = 0; r < kMaxClusterSplits; ++r) {
+          if (r < n_split) {
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ms[r]) : "r"(mapa_shared(base_m + row * 4, r)));
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ls[r]) : "r"(mapa_shared(base_l + row * 4, r)));
+            asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                         : "=f"(os[r])
+                         : "r"(mapa_shared(base_o + (row * HD + c) * 4, r)));
+          }
         }
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kMaxClusterSplits; ++r)
+          if (r < n_split) M = fmaxf(M, ms[r]);
         float Ls = 0.f, acc = 0.f;
-        for (int r = 0; r < n_split; ++r) {
-          float f = (ms[r] == -INFINITY) ? 0.f : exp2f(ms[r] - M);
-          float lv, ov;
-          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(lv) : "r"(mapa_shared(base_l + row * 4, r)) : "memory");
-          asm volatile("ld.shared::cluster.f32 %0, [%1];"
-                       : "=f"(ov)
-                       : "r"(mapa_shared(base_o + (row * HD + c) * 4, r))
-                       : "memory");
-          Ls += lv * f;
-          acc += ov * f;
+#pragma unroll
+        for (int r = 0; r < kMaxClusterSplits; ++r) {
+          if (r < n_split) {
+            const float f = (ms[r] == -INFINITY) ? 0.f : exp2f(ms[r] - M);
+            Ls += ls[r] * f;
+            acc += os[r] * f;
+          }
         }
         O[((size_t)b * Hq + hk * rep + row) * HD + c] = __float2bfloat16(Ls > 0.f ? acc / Ls : 0.f);
       }
+      DEC_TRACE(6);
       __syncwarp();
       cluster_sync_all();
     }
   }
+  DEC_TRACE(7);
+#undef DEC_TRACE
 }
+
+// Timeline capture (tests / benchmarks): launch i writes slot i of [slots][kDecTraceCtas][8].
+constexpr int kDecTraceCtas = 1024;
+unsigned long long* g_dec_trace = nullptr;
+int g_dec_trace_slots = 0, g_dec_trace_next = 0;
 
 template <int HD, bool CLUSTER>
 void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, const int* bt, const int* seq_lens,
@@ -404,6 +433,10 @@ void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, con
                 bool early, unsigned* ctr, cudaStream_t st) {
   using C = DCfg<HD>;
   auto k = paged_decode_tma_kernel<HD, CLUSTER>;
+  unsigned long long* trace = nullptr;
+  const size_t ctas = (size_t)B * Hkv * n_split;
+  if (g_dec_trace && g_dec_trace_next < g_dec_trace_slots && ctas <= (size_t)kDecTraceCtas)
+    trace = g_dec_trace + (size_t)(g_dec_trace_next++) * kDecTraceCtas * 8;
   static bool attr_set = false;
   if (!attr_set) {
     MESHY_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
@@ -425,7 +458,7 @@ void launch_dec(const CUtensorMap& mk, const CUtensorMap& mv, const bf16* q, con
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   MESHY_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, mk, mv, q, bt, seq_lens, o, part, Hq, Hkv, max_pages, n_split, scale,
-                                      err, early ? 1 : 0, ctr));
+                                      err, early ? 1 : 0, ctr, trace));
 }
 
 }  // namespace
@@ -461,6 +494,12 @@ static int dec_max_cluster() {
 }
 
 int paged_decode_max_cluster() { return dec_max_cluster(); }
+
+void paged_decode_trace(unsigned long long* buf, int slots) {
+  g_dec_trace = buf;
+  g_dec_trace_slots = buf ? slots : 0;
+  g_dec_trace_next = 0;
+}
 
 static int g_force_splits = 0;
 void paged_decode_force_splits(int n) { g_force_splits = n < 0 ? 0 : n; }

@@ -636,6 +636,12 @@ __global__ void __launch_bounds__(kSmallThreads, 2)
       const uint32_t red_addr = smem_u32(smem);
       const bool swiglu = p.epi == EPI_SWIGLU;
       constexpr int G = MP / 4;
+      // The closing cluster barrier only guards the peers' reads of this CTA's partials: a warp arrives as soon
+      // as its last group's partials are summed and waits only before the CTA exits, so the epilogue math and
+      // stores run inside the barrier interval instead of before it (the loop bounds are warp-uniform).
+      int g_last = -1;
+      for (int g = (int)rank; g < G && 4 * g < p.M && !(swiglu && f >= 64); g += p.cs) g_last = g;
+      if (g_last < 0) cluster_arrive();
       for (int g = (int)rank; g < G; g += p.cs) {
         if (4 * g >= p.M) break;
         if (swiglu && f >= 64) break;
@@ -681,6 +687,7 @@ __global__ void __launch_bounds__(kSmallThreads, 2)
         }
         float av[4] = {a.x, a.y, a.z, a.w};
         float bv[4] = {b.x, b.y, b.z, b.w};
+        if (g == g_last) cluster_arrive();  // every read of a peer's shared memory by this warp is done
         if (p.part_in) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -818,7 +825,8 @@ __global__ void __launch_bounds__(kSmallThreads, 2)
     }
     if (threadIdx.x == 64) SMALL_TRACE(6);
     __syncwarp();
-    cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
+    if (warp < 2) cluster_arrive();
+    cluster_wait();  // no CTA leaves while a peer may still read its shared memory
     if (threadIdx.x == 64) SMALL_TRACE(7);
   }
 

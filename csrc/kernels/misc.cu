@@ -404,78 +404,4 @@ void sample_advance(const float* part, int n_parts, int64_t* tok_in, int* pos, i
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 
-// ─── L2 prefetch of decode weights ───────────────────────────────────────────
-// A decode layer's attention phase (QKV GEMM, paged attention, o_proj) is latency-bound and leaves HBM mostly
-// idle; the MLP GEMMs that follow stream most of the layer's bytes. Launched on a side stream at the start of
-// the layer, this kernel asks the L2 for the MLP weights (cp.async.bulk.prefetch.L2: no registers, no shared
-// memory, nothing waits for it), so the MLP GEMMs' TMA loads hit in L2.
-namespace {
-constexpr long long kPrefetchChunk = 16 * 1024;
-
-struct PrefetchRanges {
-  const char* p[4];
-  long long bytes[4];
-  int n;
-};
-
-__global__ void l2_prefetch_kernel(PrefetchRanges r) {
-  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long nth = (long long)gridDim.x * blockDim.x;
-  for (int k = 0; k < r.n; ++k) {
-    const long long chunks = (r.bytes[k] + kPrefetchChunk - 1) / kPrefetchChunk;
-    for (long long c = tid; c < chunks; c += nth) {
-      const long long off = c * kPrefetchChunk;
-      long long sz = r.bytes[k] - off;
-      if (sz > kPrefetchChunk) sz = kPrefetchChunk;
-      sz &= ~15ll;
-      if (sz <= 0) continue;
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(r.p[k] + off), "r"((unsigned)sz) : "memory");
-    }
-  }
-}
-}  // namespace
-
-namespace {
-// one CTA per row: ask the L2 for the K and V pages of the row's block-table entries that hold tokens
-__global__ void kv_prefetch_kernel(const int* __restrict__ bt, const int* __restrict__ seq_lens, int max_pages,
-                                   int page, const char* kc, const char* vc, long long page_bytes, int n_cache_pages) {
-  const int r = blockIdx.x;
-  const int n = min((seq_lens[r] + page - 1) / page, max_pages);
-  for (int i = threadIdx.x; i < 2 * n; i += blockDim.x) {
-    const int id = bt[(size_t)r * max_pages + (i >> 1)];
-    if (id < 0 || id >= n_cache_pages) continue;
-    const char* base = (i & 1) ? vc : kc;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + (size_t)id * page_bytes),
-                 "r"((unsigned)page_bytes) : "memory");
-  }
-}
-}  // namespace
-
-void kv_prefetch(const int* bt, const int* seq_lens, int B, int max_pages, int page, const void* kc, const void* vc,
-                 long long page_bytes, int n_cache_pages, cudaStream_t st) {
-  MESHY_CHECK(page_bytes % 16 == 0 && page_bytes < (1ll << 31), "kv_prefetch: page bytes");
-  if (B == 0) return;
-  kv_prefetch_kernel<<<B, 128, 0, st>>>(bt, seq_lens, max_pages, page, static_cast<const char*>(kc),
-                                        static_cast<const char*>(vc), page_bytes, n_cache_pages);
-  MESHY_CUDA_CHECK(cudaGetLastError());
-}
-
-void l2_prefetch(const void* const* ptrs, const long long* bytes, int n, cudaStream_t st) {
-  MESHY_CHECK(n >= 1 && n <= 4, "l2_prefetch: 1 to 4 ranges");
-  PrefetchRanges r{};
-  r.n = n;
-  long long total = 0;
-  for (int i = 0; i < n; ++i) {
-    MESHY_CHECK((reinterpret_cast<uintptr_t>(ptrs[i]) & 15) == 0, "l2_prefetch: 16-byte aligned ranges");
-    r.p[i] = static_cast<const char*>(ptrs[i]);
-    r.bytes[i] = bytes[i];
-    total += bytes[i];
-  }
-  if (total <= 0) return;
-  const long long chunks = (total + kPrefetchChunk - 1) / kPrefetchChunk;
-  const int blocks = (int)std::min<long long>(8, (chunks + 255) / 256);
-  l2_prefetch_kernel<<<std::max(1, blocks), 256, 0, st>>>(r);
-  MESHY_CUDA_CHECK(cudaGetLastError());
-}
-
 }  // namespace meshy

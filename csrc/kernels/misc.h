@@ -33,12 +33,6 @@ void value_head_fwd(const bf16* h, const float* w, const float* b, int T, int D,
 void value_head_bwd(const bf16* h, const float* w, const float* dv, int T, int D, bf16* dh, float* dw, float* db,
                     cudaStream_t st);
 
-// Ask the L2 for up to 4 byte ranges (16-byte aligned) without waiting for them (misc.cu).
-void l2_prefetch(const void* const* ptrs, const long long* bytes, int n, cudaStream_t st);
-// The same for the K and V cache pages of B rows' block tables (pages of page_bytes each).
-void kv_prefetch(const int* bt, const int* seq_lens, int B, int max_pages, int page, const void* kc, const void* vc,
-                 long long page_bytes, int n_cache_pages, cudaStream_t st);
-
 // Top-K distillation (topk.cu): the K largest fp32 logits of each row (sorted) with their log-probabilities
 // and the row's log-sum-exp; log-probabilities of given ids from the hidden rows and the LM-head weight
 // (needs lse); dz[t, ids[t, k]] += g[t, k] on bf16 logit gradients.

@@ -524,29 +524,7 @@ class RolloutEngine:
         xg, parts = self._norm_ws() if split else (None, None)
         prep = None
         L = len(m.layers)
-        # L2 prefetch: while a layer's latency-bound attention phase runs, a side-stream kernel asks the L2
-        # for the layer's MLP weights (and, during the MLP, for the next layer's attention weights). Only
-        # for few rows: with many rows the KV pages would evict the prefetched lines before their use.
-        pf = None
-        if self.cuda and b <= int(os.environ.get("MESHY_L2_PREFETCH_ROWS", "16")):
-            if getattr(self, "_pf_stream", None) is None:
-                self._pf_stream = torch.cuda.Stream(device=self.device)
-            pf, cur = self._pf_stream, torch.cuda.current_stream(self.device)
-            from ..ops._ext import ext as _ext
-
-        pf_kv = os.environ.get("MESHY_L2_PREFETCH_KV", "1") != "0"
-
-        def prefetch(ts, li=None):
-            pf.wait_stream(cur)
-            with torch.cuda.stream(pf):
-                if li is not None:  # this layer's K/V pages first: attention reads them right after QKV
-                    _ext().kv_prefetch(st["block_table"][:b], st["seq_lens"][:b], self.kv[li, 0], self.kv[li, 1],
-                                       self.page_size)
-                _ext().l2_prefetch(ts)
-
         for li, layer in enumerate(m.layers):
-            if pf is not None and layer.moe is None:
-                prefetch([layer.w13, layer.w2], li if pf_kv else None)
             q = None
             if prep is not None and fuse_rope:
                 q = D.qkv_rope_fused(xg[:b], layer.wqkv, layer.bqkv, pos, layer.q_norm, layer.k_norm, a.n_heads,
@@ -572,9 +550,6 @@ class RolloutEngine:
             if prep is None:
                 x = Fx.linear(o, layer.wo, residual=x)
             if layer.moe is None:
-                if pf is not None and li + 1 < L and os.environ.get("MESHY_L2_PREFETCH_NEXT", "1") != "0":
-                    nxt = m.layers[li + 1]
-                    prefetch([nxt.wqkv, nxt.wo])
                 act = None
                 if prep is not None:
                     act = D.linear_norm_scaled(xg[:b], layer.w13, None, prep, a.dim, a.norm_eps,
@@ -592,8 +567,6 @@ class RolloutEngine:
             else:
                 prep = None
                 x = self._mlp(layer, Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps), x)
-        if pf is not None:
-            cur.wait_stream(pf)
         if final_split and prep is not None:
             return xg[:b], prep
         return Fx.rmsnorm(x, m.norm, a.norm_eps)
