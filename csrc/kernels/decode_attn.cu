@@ -279,7 +279,11 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
   }
   __syncthreads();  // every page consumed: the stage ring is free for the merge buffers
 
-  // merge the 4 consumer warps: rows lane/4 (+8)
+  // merge the 4 consumer warps. Every warp holds the same (row, column) positions per lane, for its own
+  // tokens: all four leave their fragments in shared memory (float4 per lane and column octet) with their
+  // row maxima and sums, then warp w combines the four for its quarter of the columns (octets i in
+  // [w HD/32, (w + 1) HD/32)) and writes the CTA's state for rows < rep.
+  constexpr int IQ = HD / 32;  // column octets per warp
   float* rm = reinterpret_cast<float*>(ring);
   float* rl = rm + 64;
   float* ro = rm + 128;
@@ -287,48 +291,79 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
   float* cl = cm + 16;
   float* co = cm + 32;
   if (warp < 4) {
+    if (lane % 4 == 0) {
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      int row = lane / 4 + 8 * r;
-      if (lane % 4 == 0) {
-        rm[warp * 16 + row] = m_r[r];
-        rl[warp * 16 + row] = l_r[r];
-      }
-#pragma unroll
-      for (int i = 0; i < HD / 8; ++i) {
-        int c = i * 8 + 2 * (lane % 4);
-        ro[(warp * 16 + row) * HD + c] = o[i][2 * r];
-        ro[(warp * 16 + row) * HD + c + 1] = o[i][2 * r + 1];
+      for (int r = 0; r < 2; ++r) {
+        rm[warp * 16 + lane / 4 + 8 * r] = m_r[r];
+        rl[warp * 16 + lane / 4 + 8 * r] = l_r[r];
       }
     }
+    // [warp][i][lane] float4: consecutive lanes hit consecutive 16-byte words (no bank conflicts)
+    float4* dst = reinterpret_cast<float4*>(ro) + warp * (HD / 8) * 32 + lane;
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) dst[i * 32] = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < rep * HD; idx += kThreadsDec) {
-    int row = idx / HD, c = idx % HD;
-    float M = -INFINITY;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, rm[w * 16 + row]);
-    float Ls = 0.f, acc = 0.f;
-    for (int w = 0; w < 4; ++w) {
-      float mw = rm[w * 16 + row];
-      float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-      Ls += rl[w * 16 + row] * f;
-      acc += ro[(w * 16 + row) * HD + c] * f;
-    }
-    const int h = hk * rep + row;
-    if (n_split == 1) {
-      O[((size_t)b * Hq + h) * HD + c] = __float2bfloat16(Ls > 0.f ? acc / Ls : 0.f);
-    } else if (CLUSTER) {
-      co[row * HD + c] = acc;
-      if (c == 0) {
-        cm[row] = M;
-        cl[row] = Ls;
+  if (warp < 4) {
+    float f[4][2], Mr[2], Lr[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = lane / 4 + 8 * r;
+      float mw[4], lw[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        mw[w] = rm[w * 16 + row];
+        lw[w] = rl[w * 16 + row];
       }
-    } else {
-      float* pp = part + (((size_t)b * Hq + h) * n_split + sp) * (HD + 2);
-      pp[c] = acc;
-      if (c == 0) {
-        pp[HD] = M;
-        pp[HD + 1] = Ls;
+      Mr[r] = fmaxf(fmaxf(mw[0], mw[1]), fmaxf(mw[2], mw[3]));
+      Lr[r] = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        f[w][r] = (mw[w] == -INFINITY) ? 0.f : exp2f(mw[w] - Mr[r]);
+        Lr[r] += lw[w] * f[w][r];
+      }
+    }
+    float4 x[4][IQ];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float4* src = reinterpret_cast<const float4*>(ro) + (w * (HD / 8) + warp * IQ) * 32 + lane;
+#pragma unroll
+      for (int k = 0; k < IQ; ++k) x[w][k] = src[k * 32];
+    }
+#pragma unroll
+    for (int k = 0; k < IQ; ++k) {
+      const int i = warp * IQ + k;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int r = t >> 1, row = lane / 4 + 8 * r;
+        if (row >= rep) continue;
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) acc += (&x[w][k].x)[t] * f[w][r];
+        const int c = i * 8 + 2 * (lane % 4) + (t & 1);
+        const int h = hk * rep + row;
+        if (n_split == 1) {
+          O[((size_t)b * Hq + h) * HD + c] = __float2bfloat16(Lr[r] > 0.f ? acc / Lr[r] : 0.f);
+        } else if (CLUSTER) {
+          co[row * HD + c] = acc;
+        } else {
+          part[(((size_t)b * Hq + h) * n_split + sp) * (HD + 2) + c] = acc;
+        }
+      }
+    }
+    if (warp == 0 && lane % 4 == 0 && n_split > 1) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = lane / 4 + 8 * r;
+        if (row >= rep) continue;
+        if (CLUSTER) {
+          cm[row] = Mr[r];
+          cl[row] = Lr[r];
+        } else {
+          float* pp = part + (((size_t)b * Hq + hk * rep + row) * n_split + sp) * (HD + 2);
+          pp[HD] = Mr[r];
+          pp[HD + 1] = Lr[r];
+        }
       }
     }
   }
@@ -386,7 +421,6 @@ __global__ void __launch_bounds__(kThreadsDec) paged_decode_tma_kernel(
       for (int idx = sp * kThreadsDec + threadIdx.x; idx < rep * HD; idx += n_split * kThreadsDec) {
         int row = idx / HD, c = idx % HD;
         // every peer's (m, l, o) is loaded before any of them is used, so the DSMEM round trips overlap
-        // (one load in flight at a time cost ~0.1 us each, 3 x n_split of them per output)
         float ms[kMaxClusterSplits], ls[kMaxClusterSplits], os[kMaxClusterSplits];
 #pragma unroll
         for (int r = 0; r < kMaxClusterSplits; ++r) {

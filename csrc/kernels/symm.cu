@@ -218,10 +218,14 @@ void symm_close(void* p) {
   if (p) MESHY_CUDA_CHECK(cudaIpcCloseMemHandle(p));
 }
 
+// The SM clock rate is read once per device: the attribute query costs milliseconds of host time on this
+// driver, which stalled every optimiser step (and every barrier) while the GPU waited for the next launch.
 static long long cycles_for(double seconds) {
-  int dev = 0, khz = 0;
+  static int khz_of[64] = {};
+  int dev = 0;
   MESHY_CUDA_CHECK(cudaGetDevice(&dev));
-  MESHY_CUDA_CHECK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev));
+  int& khz = khz_of[dev & 63];
+  if (khz == 0) MESHY_CUDA_CHECK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev));
   return (long long)(seconds * (double)khz * 1000.0);
 }
 
