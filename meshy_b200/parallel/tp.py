@@ -64,35 +64,58 @@ def reduce_from_tp(x, group):
     return _ReduceFromTP.apply(x, group)
 
 
+def _check_divisible(a, tp: int) -> None:
+    if a.n_heads % tp or a.n_kv_heads % tp or (2 * a.ffn_dim) % (128 * tp):
+        raise ValueError(f"TP={tp} must divide the heads ({a.n_heads}/{a.n_kv_heads}) and the 128-row gate/up "
+                         f"blocks of 2F={2 * a.ffn_dim}")
+
+
+def local_args(a, tp: int):
+    """The block arguments one of ``tp`` ranks sees (its share of the heads and of the FFN width)."""
+    _check_divisible(a, tp)
+    return dataclasses.replace(a, n_heads=a.n_heads // tp, n_kv_heads=a.n_kv_heads // tp, ffn_dim=a.ffn_dim // tp)
+
+
+def tp_shard_param(name: str, full: torch.Tensor, a, tp: int, t: int) -> torch.Tensor:
+    """Rank ``t``'s slice of the block parameter ``name`` (its last dotted component: ``wqkv``, ``bqkv``,
+    ``wo``, ``w13``, ``w2``; anything else is replicated and returned as is) from the full tensor."""
+    leaf = name.rsplit(".", 1)[-1]
+    hd = a.head_dim
+    hq, hkv = a.n_heads // tp, a.n_kv_heads // tp
+    dev = full.device
+    if leaf in ("wqkv", "bqkv"):
+        q_rows = torch.arange(t * hq * hd, (t + 1) * hq * hd)
+        k_rows = a.n_heads * hd + torch.arange(t * hkv * hd, (t + 1) * hkv * hd)
+        v_rows = (a.n_heads + a.n_kv_heads) * hd + torch.arange(t * hkv * hd, (t + 1) * hkv * hd)
+        return full.index_select(0, torch.cat([q_rows, k_rows, v_rows]).to(dev))
+    if leaf == "wo":
+        return full[:, t * hq * hd:(t + 1) * hq * hd]
+    if leaf == "w13" and ".moe." not in name:
+        return full[t * 2 * a.ffn_dim // tp:(t + 1) * 2 * a.ffn_dim // tp]
+    if leaf == "w2" and ".moe." not in name:
+        f0, f1 = t * 2 * a.ffn_dim // tp, (t + 1) * 2 * a.ffn_dim // tp
+        cols = torch.cat([torch.arange(b * 64, (b + 1) * 64) for b in range(f0 // 128, f1 // 128)])
+        return full.index_select(1, cols.to(dev))
+    return full
+
+
 def shard_model_tp(model, group) -> None:
     """Slice every block of ``model`` (a :class:`~meshy_b200.models.transformer.DecoderLM`) in place."""
     tp = dist.get_world_size(group)
     t = dist.get_rank(group)
     a = model.args
-    if a.n_heads % tp or a.n_kv_heads % tp or (2 * a.ffn_dim) % (128 * tp):
-        raise ValueError(f"TP={tp} must divide the heads ({a.n_heads}/{a.n_kv_heads}) and the 128-row gate/up "
-                         f"blocks of 2F={2 * a.ffn_dim}")
-    hd = a.head_dim
-    hq, hkv = a.n_heads // tp, a.n_kv_heads // tp
-    la = dataclasses.replace(a, n_heads=hq, n_kv_heads=hkv, ffn_dim=a.ffn_dim // tp)
-    q_rows = torch.arange(t * hq * hd, (t + 1) * hq * hd)
-    k_rows = a.n_heads * hd + torch.arange(t * hkv * hd, (t + 1) * hkv * hd)
-    v_rows = (a.n_heads + a.n_kv_heads) * hd + torch.arange(t * hkv * hd, (t + 1) * hkv * hd)
-    qkv_rows = torch.cat([q_rows, k_rows, v_rows])
-    f_slice = slice(t * 2 * a.ffn_dim // tp, (t + 1) * 2 * a.ffn_dim // tp)
-    w2_cols = torch.cat([torch.arange(b * 64, (b + 1) * 64) for b in range(f_slice.start // 128, f_slice.stop // 128)])
+    la = local_args(a, tp)
     with torch.no_grad():
         for blk in model.layers:
-            dev = blk.wqkv.device
-            blk.wqkv = nn.Parameter(blk.wqkv.index_select(0, qkv_rows.to(dev)).clone())
-            if blk.bqkv is not None:
-                blk.bqkv = nn.Parameter(blk.bqkv.index_select(0, qkv_rows.to(dev)).clone())
-            blk.wo = nn.Parameter(blk.wo[:, t * hq * hd:(t + 1) * hq * hd].clone())
+            for leaf in ("wqkv", "bqkv", "wo"):
+                w = getattr(blk, leaf)
+                if w is not None:
+                    setattr(blk, leaf, nn.Parameter(tp_shard_param(leaf, w, a, tp, t).clone()))
             if blk.moe is None:
-                blk.w13 = nn.Parameter(blk.w13[f_slice].clone())
-                blk.w2 = nn.Parameter(blk.w2.index_select(1, w2_cols.to(dev)).clone())
+                blk.w13 = nn.Parameter(tp_shard_param("w13", blk.w13, a, tp, t).clone())
+                blk.w2 = nn.Parameter(tp_shard_param("w2", blk.w2, a, tp, t).clone())
             blk.args = la
             blk.tp_group = group
 
 
-__all__ = ["copy_to_tp", "reduce_from_tp", "shard_model_tp"]
+__all__ = ["copy_to_tp", "local_args", "reduce_from_tp", "shard_model_tp", "tp_shard_param"]

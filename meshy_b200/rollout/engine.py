@@ -102,8 +102,9 @@ class RolloutEngine:
         eos_token_ids: Sequence[int] = (),
         prefill_chunk_tokens: int = 32768,
         mem_fraction: float = 0.5,
+        tp_group=None,
     ):
-        from ..backend.flat import flatten_module
+        from ..backend.flat import Slot, _align, flatten_module
 
         self.args = args
         self.device = torch.device(device)
@@ -113,6 +114,25 @@ class RolloutEngine:
             from ..models import build_model
 
             model = build_model(args, seed=seed, device=self.device, dtype=self.dtype)
+        # tensor parallelism: this rank keeps its heads and FFN slice of every dense block (the embedding, the
+        # norms, the LM head and MoE experts stay whole); the row-parallel outputs are summed over tp_group
+        import torch.distributed as dist
+
+        self.tp_group = tp_group if (tp_group is not None and dist.is_initialized()
+                                     and dist.get_world_size(tp_group) > 1) else None
+        self.tp, self.tp_rank = 1, 0
+        self.local_args = args
+        self.full_slots = None
+        if self.tp_group is not None:
+            from ..parallel.tp import local_args, shard_model_tp
+
+            self.tp, self.tp_rank = dist.get_world_size(self.tp_group), dist.get_rank(self.tp_group)
+            off, self.full_slots = 0, []
+            for name, p in model.named_parameters():  # the trainer's (unsharded) flat layout
+                self.full_slots.append(Slot(name, off, p.numel(), tuple(p.shape)))
+                off += _align(p.numel())
+            shard_model_tp(model, self.tp_group)
+            self.local_args = local_args(args, self.tp)
         self.model = model.eval()
         for p in self.model.parameters():
             p.requires_grad_(False)
@@ -138,7 +158,7 @@ class RolloutEngine:
         if max_total_tokens is None:
             if self.cuda:
                 free, _ = torch.cuda.mem_get_info(self.device)
-                max_total_tokens = int(free * mem_fraction) // max(1, args.kv_bytes_per_token(2))
+                max_total_tokens = int(free * mem_fraction) // max(1, self.local_args.kv_bytes_per_token(2))
             else:
                 max_total_tokens = 64 * 1024
         n_pages = max(1, max_total_tokens // page_size)
@@ -164,7 +184,7 @@ class RolloutEngine:
         self._mega = None
         self._mega_rows = 0
         self.mega_reason = "not on CUDA"
-        if self.cuda:
+        if self.cuda and self.tp_group is None:
             from .mega import MAX_ROWS, MegaDecoder
 
             self.mega_reason = MegaDecoder.reason(self.model, self.page_size)
@@ -174,7 +194,7 @@ class RolloutEngine:
 
     # ------------------------------------------------------------------ memory
     def _alloc_kv(self):
-        a = self.args
+        a = self.local_args  # this rank's KV heads
         shape = [a.n_layers, 2, self.n_pages, a.n_kv_heads, self.page_size, a.head_dim]
         if not self.cuda:
             self.kv = torch.zeros(*shape, dtype=self.dtype, device=self.device)
@@ -263,9 +283,14 @@ class RolloutEngine:
 
     # ------------------------------------------------------------------ weights
     def update_weights_from_flat(self, src: torch.Tensor, version: int | None = None) -> None:
-        """Device weight sync: ``src`` is a flat buffer in the same layout."""
+        """Device weight sync: ``src`` is a flat buffer in the trainer's layout (with tensor parallelism the
+        full model's; this rank takes its slices)."""
         with self.lock:
             self._check_resident(("weights",))
+            if self.full_slots is not None:
+                self._load_full(lambda s: src[s.offset:s.offset + s.numel].view(s.shape))
+                self.weight_version = self.weight_version + 1 if version is None else int(version)
+                return
             if src.numel() != self.weight_flat.numel():
                 raise ValueError("flat weight layout mismatch")
             if src.dtype == self.weight_flat.dtype:
@@ -281,10 +306,38 @@ class RolloutEngine:
     def update_weights_from_state_dict(self, sd: dict[str, torch.Tensor], version: int | None = None) -> None:
         with self.lock:
             self._check_resident(("weights",))
-            with torch.no_grad():
-                for s in self.weight_slots:
-                    self.weight_flat[s.offset:s.offset + s.numel].copy_(sd[s.name].reshape(-1))
+            if self.full_slots is not None:
+                self._load_full(lambda s: sd[s.name].reshape(s.shape))
+            else:
+                with torch.no_grad():
+                    for s in self.weight_slots:
+                        self.weight_flat[s.offset:s.offset + s.numel].copy_(sd[s.name].reshape(-1))
             self.weight_version = self.weight_version + 1 if version is None else int(version)
+
+    @torch.no_grad()
+    def _load_full(self, full_of) -> None:
+        """Tensor parallelism: every local parameter from its full tensor (``full_of(full_slot)``), sliced for
+        this rank -- the replica -> tensor-parallel reshard of a weight sync."""
+        from ..parallel.tp import tp_shard_param
+
+        local = {s.name: s for s in self.weight_slots}
+        for fs in self.full_slots:
+            ls = local[fs.name]
+            part = tp_shard_param(fs.name, full_of(fs), self.args, self.tp, self.tp_rank)
+            self.weight_flat[ls.offset:ls.offset + ls.numel].view(ls.shape).copy_(part)
+
+    def update_weights_from_ipc(self, handles: dict, version: int | None = None) -> bool:
+        """``handles``: ``{gpu_uuid: handle}`` of the trainer ranks' published bf16 snapshots; this engine maps the
+        one exported on its own GPU (else a visible peer's). Returns whether the handle was local."""
+        from .weight_sync import device_uuid, open_ipc_flat, pick_handle
+
+        handle, local, uuid = pick_handle(handles, device_uuid(self.device))
+        src = open_ipc_flat(handle, uuid)
+        self.update_weights_from_flat(src, version)
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+        del src
+        return local
 
     def update_weights_from_disk(self, path: str, version: int | None = None) -> None:
         from ..models.hf import load_hf_checkpoint
@@ -418,15 +471,16 @@ class RolloutEngine:
         cu = torch.tensor([0] + list(itertools.accumulate(lens)), dtype=torch.int32)
         toks, pos, slots, cu = (t.to(dev, non_blocking=True) for t in (toks, pos, slots, cu))
         m = self.model
+        la = self.local_args
         x = Fx.embedding(toks, m.embed)
         for li, layer in enumerate(m.layers):
             h = Fx.rmsnorm(x, layer.attn_norm, a.norm_eps)
             qkv = Fx.linear(h, layer.wqkv, layer.bqkv)
-            q, k, v = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads, a.head_dim,
-                                          a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1], slots,
+            q, k, v = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, la.n_heads, la.n_kv_heads,
+                                          a.head_dim, a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1], slots,
                                           keep_kv=True)
             o = Fx.flash_attn_varlen(q, k, v, cu, max(lens))
-            x = Fx.linear(o.reshape(T, a.q_dim), layer.wo, residual=x)
+            x = self._row_parallel(o.reshape(T, la.q_dim), layer.wo, x)
             h = Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps)
             x = self._mlp(layer, h, x)
         last = (cu[1:] - 1).long()
@@ -467,8 +521,25 @@ class RolloutEngine:
     def _mlp(self, layer, h, x):
         a = self.args
         if layer.moe is None:
-            return Fx.linear(Fx.linear_swiglu(h, layer.w13, a.swiglu_block), layer.w2, residual=x)
+            return self._row_parallel(Fx.linear_swiglu(h, layer.w13, a.swiglu_block), layer.w2, x)
         return x + layer.moe(h)
+
+    def _row_parallel(self, h, w, residual):
+        """``residual + h @ w.T``; with tensor parallelism ``w`` holds this rank's input columns, and the
+        partial products are summed over the TP group in fp32 before the residual is added once."""
+        if self.tp_group is None:
+            return Fx.linear(h, w, residual=residual)
+        import torch.distributed as dist
+
+        if Fx.native(h):
+            from ..ops._ext import ext
+
+            y = torch.empty(h.shape[0], w.shape[0], dtype=torch.float32, device=h.device)
+            ext().gemm(h, w, y, False, False, None, None, None, Fx.EPI_NONE, False, 0)
+        else:
+            y = torch.nn.functional.linear(h.float(), w.float())
+        dist.all_reduce(y, group=self.tp_group)
+        return (residual.float() + y).to(residual.dtype)
 
     def _sample_rows(self, h, reqs: Sequence[Request]):
         r0 = reqs[0]
@@ -514,12 +585,14 @@ class RolloutEngine:
         result is ``(xg [b, D], part)`` for a consumer that applies ``rstd`` itself (the LM-head
         sampler) instead of the normed hidden states."""
         a, m, st = self.args, self.model, self.st
+        la = self.local_args
         x = Fx.embedding(st["tok_in"][:b], m.embed)
         pos = st["pos"][:b]
         # RMSNorm split across GEMMs: the residual GEMM producing x writes bf16(g_next * x) and per-tile
         # sums of squares, the consuming GEMM scales its rows by rstd (no normalisation kernels).
         # ``prep`` is the part buffer the next norm can use (None: run the unfused norm).
-        split = self.cuda and os.environ.get("MESHY_SPLIT_NORM", "1") != "0"
+        # (the split norm needs the whole row-parallel output in one epilogue: off under tensor parallelism)
+        split = self.cuda and os.environ.get("MESHY_SPLIT_NORM", "1") != "0" and self.tp_group is None
         fuse_rope = os.environ.get("MESHY_FUSED_QKV_ROPE", "1") != "0"
         xg, parts = self._norm_ws() if split else (None, None)
         prep = None
@@ -536,19 +609,19 @@ class RolloutEngine:
                     qkv = D.linear_norm_scaled(xg[:b], layer.wqkv, layer.bqkv, prep, a.dim, a.norm_eps)
                 if qkv is None:
                     qkv = Fx.rmsnorm_linear(x, layer.attn_norm, a.norm_eps, layer.wqkv, layer.bqkv)
-                q, _, _ = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, a.n_heads, a.n_kv_heads,
+                q, _, _ = D.qkv_rope_to_cache(qkv, pos, layer.q_norm, layer.k_norm, la.n_heads, la.n_kv_heads,
                                               a.head_dim, a.rope_theta, a.norm_eps, self.kv[li, 0], self.kv[li, 1],
                                               st["slot"][:b])
             o = D.paged_attention(q, self.kv[li, 0], self.kv[li, 1], st["block_table"][:b], st["seq_lens"][:b],
                                   decode_step=True)
-            o = o.reshape(b, a.q_dim)
+            o = o.reshape(b, la.q_dim)
             prep = None
             if layer.moe is None and split:
                 xn = D.linear_norm_prep(o, layer.wo, x, layer.mlp_norm, xg, parts[1])
                 if xn is not None:
                     x, prep = xn, parts[1]
             if prep is None:
-                x = Fx.linear(o, layer.wo, residual=x)
+                x = self._row_parallel(o, layer.wo, x)
             if layer.moe is None:
                 act = None
                 if prep is not None:
@@ -563,7 +636,7 @@ class RolloutEngine:
                     if xn is not None:
                         x, prep = xn, parts[0]
                 if prep is None:
-                    x = Fx.linear(act, layer.w2, residual=x)
+                    x = self._row_parallel(act, layer.w2, x)
             else:
                 prep = None
                 x = self._mlp(layer, Fx.rmsnorm(x, layer.mlp_norm, a.norm_eps), x)

@@ -176,17 +176,19 @@ def build_app(runner: EngineRunner, model_name: str = ""):
         """``{handle}``: one exported buffer; ``{handles: {gpu_uuid: handle}}``: one per trainer rank, of
         which this server maps the one exported on its own GPU (see ``weight_sync.pick_handle``)."""
         body = await req.json()
-        from .weight_sync import device_uuid, open_ipc_flat, pick_handle
+        from .weight_sync import open_ipc_flat
 
         t0 = time.perf_counter()
         local = True
 
         def do():
             nonlocal local
-            handle, uuid = body.get("handle"), body.get("gpu_uuid")
-            if handle is None:
-                handle, local, uuid = pick_handle(body["handles"], device_uuid(eng.device))
-            src = open_ipc_flat(handle, uuid)
+            if body.get("handle") is None:  # one handle per trainer rank: every engine rank maps its own GPU's
+                local = eng.update_weights_from_ipc(body["handles"], body.get("weight_version"))
+                return
+            if getattr(eng, "tp", 1) > 1:
+                raise ValueError("a tensor-parallel replica needs the per-GPU handle set ('handles')")
+            src = open_ipc_flat(body["handle"], body.get("gpu_uuid"))
             eng.update_weights_from_flat(src, body.get("weight_version"))
             if eng.cuda:
                 import torch
@@ -232,19 +234,86 @@ def main(argv=None):
     p.add_argument("--eos", type=int, nargs="*", default=[])
     p.add_argument("--tp-size", type=int, default=1, help="tensor-parallel degree of this replica")
     p.add_argument("--ep-size", type=int, default=1, help="expert-parallel degree of this replica")
+    p.add_argument("--dist-port", type=int, default=0, help="rendezvous port of the TP ranks (0: free port)")
     a = p.parse_args(argv)
-    if a.tp_size > 1 or a.ep_size > 1:
-        raise SystemExit("this server runs one card per replica (tp_size = ep_size = 1); use more replicas")
+    if a.ep_size > 1:
+        raise SystemExit("expert-parallel decoding is not supported: MoE replicas keep every expert (one card "
+                         "holds Qwen3-30B-A3B), or split the experts' FFN width with --tp-size")
+    if a.tp_size > 1:
+        return _serve_tp(a)
+    eng = _build_engine(a)
+    if a.model_path:
+        eng.update_weights_from_disk(a.model_path, 0)
+    serve(eng, a.host, a.port, a.model_path or a.model)
+
+
+def _build_engine(a, device=None, tp_group=None):
     from ..models import get_model_args
     from .engine import RolloutEngine
 
     name, flavor = a.model.split(":")
-    eng = RolloutEngine(get_model_args(name, flavor), device=a.device, max_running=a.max_running,
-                        max_total_tokens=a.max_total_tokens, max_seq_len=a.max_seq_len, mem_fraction=a.mem_fraction,
-                        seed=a.seed, eos_token_ids=a.eos)
+    return RolloutEngine(get_model_args(name, flavor), device=device or a.device, max_running=a.max_running,
+                         max_total_tokens=a.max_total_tokens, max_seq_len=a.max_seq_len,
+                         mem_fraction=a.mem_fraction, seed=a.seed, eos_token_ids=a.eos, tp_group=tp_group)
+
+
+def _tp_rank_setup(a, rank: int):
+    """Process group of one TP replica (NCCL on the GPU for the partial sums, gloo for the control channel)."""
+    import os
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(a.dist_port))
+    cuda = a.device.startswith("cuda")
+    device = torch.device("cuda", rank) if cuda else torch.device("cpu")
+    kw = {"device_id": device} if cuda else {}
+    if cuda:
+        torch.cuda.set_device(device)
+    dist.init_process_group("nccl" if cuda else "gloo", rank=rank, world_size=a.tp_size,
+                            timeout=timedelta(seconds=600), **kw)
+    ctrl = dist.new_group(backend="gloo") if cuda else dist.group.WORLD
+    return device, dist.group.WORLD, ctrl
+
+
+def _tp_follower(a, rank: int) -> None:
+    from .spmd import follow
+
+    import torch.distributed as dist
+
+    device, group, ctrl = _tp_rank_setup(a, rank)
+    eng = _build_engine(a, device=str(device), tp_group=group)
+    follow(eng, ctrl)
+    eng._graphs.clear()  # captured graphs hold NCCL calls: release them before the process group
+    dist.destroy_process_group()
+
+
+def _serve_tp(a) -> None:
+    """Rank 0 serves HTTP and drives ``tp_size - 1`` follower processes (one per further visible GPU)."""
+    import multiprocessing as mp
+    import socket
+
+    from .spmd import EngineLeader
+
+    if not a.dist_port:
+        with socket.socket() as s_:
+            s_.bind(("127.0.0.1", 0))
+            a.dist_port = s_.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_tp_follower, args=(a, r), daemon=True) for r in range(1, a.tp_size)]
+    for p_ in procs:
+        p_.start()
+    device, group, ctrl = _tp_rank_setup(a, 0)
+    eng = EngineLeader(_build_engine(a, device=str(device), tp_group=group), ctrl)
     if a.model_path:
         eng.update_weights_from_disk(a.model_path, 0)
-    serve(eng, a.host, a.port, a.model_path or a.model)
+    try:
+        serve(eng, a.host, a.port, a.model_path or a.model)
+    finally:
+        eng.stop()
+        for p_ in procs:
+            p_.join(timeout=30)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,149 @@
+"""Tensor-parallel rollout engine on CPU (gloo, 2 ranks).
+
+* engine level: rank 0 drives the replica through :class:`EngineLeader`, rank 1 follows; greedy generations
+  equal a single-rank engine's on the same weights (token ids exact, log-probs to fp32 summation order), and
+  so do they after a weight update from a full state dict (the replica -> tensor-parallel reshard);
+* server level: ``python -m meshy_b200.rollout.server --tp-size 2`` spawns its follower and answers
+  ``/generate`` with the single-card server's tokens.
+"""
+
+import os
+import socket
+import subprocess
+import sys
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PROMPTS = [[3, 14, 15, 92, 65, 35], [8, 97, 93, 23, 84, 62, 64, 33, 83, 27], [2, 71]]
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _engine(group=None, seed=0):
+    from meshy_b200.models import get_model_args
+    from meshy_b200.rollout.engine import RolloutEngine
+
+    return RolloutEngine(get_model_args("qwen3", "debugmodel"), device="cpu", max_running=8, max_seq_len=128,
+                         seed=seed, sync_every=4, tp_group=group)
+
+
+def _run(eng):
+    gens = eng.generate(PROMPTS, [12, 7, 20], temperature=0.0, ignore_eos=True)
+    return [(g.output_ids, g.output_logprobs) for g in gens]
+
+
+def _worker(rank, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=2)
+        from meshy_b200.rollout.spmd import EngineLeader, follow
+
+        g = dist.group.WORLD
+        eng = _engine(g)
+        assert eng.tp == 2 and eng.local_args.n_heads * 2 == eng.args.n_heads
+        if rank == 1:
+            follow(eng, g)
+            q.put((rank, "ok"))
+        else:
+            lead = EngineLeader(eng, g)
+            out = {"first": _run(lead)}
+            # a different model, sent as a full state dict: every rank takes its slices
+            from meshy_b200.models import build_model
+
+            other = build_model(eng.args, seed=7, device="cpu", dtype=torch.float32)
+            sd = {k: v.detach().clone() for k, v in other.named_parameters()}
+            lead.update_weights_from_state_dict(sd, 3)
+            out["second"] = _run(lead)
+            lead.stop()
+            # single-rank references (tp_group=None)
+            ref = _engine(None)
+            out["ref_first"] = _run(ref)
+            ref.update_weights_from_state_dict(sd, 3)
+            out["ref_second"] = _run(ref)
+            q.put((rank, out))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+
+
+def _same(a, b, tol=1e-4):
+    for (ta, la), (tb, lb) in zip(a, b):
+        assert ta == tb
+        assert max(abs(x - y) for x, y in zip(la, lb)) < tol
+
+
+@pytest.mark.timeout(300)
+def test_tp_engine_matches_single_rank():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert not (isinstance(v, str) and v != "ok"), v
+    out = res[0]
+    _same(out["first"], out["ref_first"])
+    _same(out["second"], out["ref_second"])
+    assert out["first"][0][0] != out["second"][0][0] or out["first"][1][0] != out["second"][1][0]
+
+
+def _server(tp, port):
+    env = dict(os.environ, PYTHONPATH=ROOT)
+    cmd = [sys.executable, "-m", "meshy_b200.rollout.server", "--model", "qwen3:debugmodel", "--device", "cpu",
+           "--port", str(port), "--max-running", "8", "--max-seq-len", "128", "--tp-size", str(tp)]
+    return subprocess.Popen(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                            start_new_session=True)
+
+
+def _wait(port, proc, timeout=120):
+    import requests
+
+    end = time.time() + timeout
+    while time.time() < end:
+        assert proc.poll() is None, proc.stdout.read().decode()[-3000:]
+        try:
+            if requests.get(f"http://127.0.0.1:{port}/health", timeout=2).ok:
+                return
+        except Exception:
+            time.sleep(0.5)
+    raise AssertionError("server did not come up")
+
+
+@pytest.mark.timeout(300)
+def test_tp_server_answers_like_single_card_server():
+    import requests
+
+    outs = []
+    for tp in (1, 2):
+        port = _port()
+        proc = _server(tp, port)
+        try:
+            _wait(port, proc)
+            body = {"input_ids": PROMPTS[1], "sampling_params": {"max_new_tokens": 9, "temperature": 0.0,
+                                                                 "ignore_eos": True}, "return_logprob": True}
+            r = requests.post(f"http://127.0.0.1:{port}/generate", json=body, timeout=120)
+            r.raise_for_status()
+            outs.append(r.json())
+        finally:
+            os.killpg(proc.pid, 15)
+            proc.wait(timeout=30)
+    assert outs[0]["output_ids"] == outs[1]["output_ids"] and len(outs[0]["output_ids"]) == 9
+    la = [x[0] for x in outs[0]["meta_info"]["output_token_logprobs"]]
+    lb = [x[0] for x in outs[1]["meta_info"]["output_token_logprobs"]]
+    assert max(abs(x - y) for x, y in zip(la, lb)) < 1e-4
