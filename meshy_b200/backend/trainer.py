@@ -96,7 +96,7 @@ class PPOTrainer:
         self.model = model
         self.model.activation_checkpoint = config.activation_checkpoint_mode == "full"
         # fully sharded parameters (FSDP over fsdp_group, HSDP with a replicate group on top)
-        self.fsdp = (fsdp_group is not None and dist.is_initialized() and dist.get_world_size(fsdp_group) > 1)
+        self.fsdp = fsdp_group is not None and dist.is_initialized()
         if self.fsdp:
             if self.ep_group is not None or (self.tp_group is not None and dist.get_world_size(self.tp_group) > 1):
                 raise ValueError("sharded parameters combine with data and context parallelism only")

@@ -147,3 +147,46 @@ def test_peer_kernels_on_one_gpu(world):
             ref = ref + g[rank * shard:(rank + 1) * shard]
         C.fsdp_reduce(gtab, 0, shard, rank, dst)
         assert torch.allclose(dst, ref, rtol=0, atol=1e-5)
+
+
+def _single_worker(port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_WORLD_SIZE="1")
+        torch.cuda.set_device(0)
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+        g = dist.group.WORLD
+        plain = _trainer(None, False)
+        sharded = _trainer(g, True)
+        assert sharded.fsdp and not sharded.flat.peer
+        w0 = plain.flat.master.clone()
+        out = []
+        for step in range(2):
+            m1 = plain.train_step(_samples(0, step))
+            m2 = sharded.train_step(_samples(0, step))
+            out.append((m1["grad_norm"], m2["grad_norm"], m1["pg_loss"], m2["pg_loss"]))
+        full = sharded.flat.full_buffer("master")
+        err = float((full - plain.flat.master).norm() / (plain.flat.master - w0).norm())
+        q.put(("ok", out, err))
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        q.put((traceback.format_exc(), None, None))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.timeout(300)
+def test_sharded_trainer_on_one_gpu_matches_unsharded():
+    """One rank shards over itself: the per-block gathers, boundary hooks, side-stream reduce-scatters and shard
+    optimiser must reproduce the plain trainer's steps on the native kernels."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_single_worker, args=(_port(), q))
+    p.start()
+    status, out, err = q.get(timeout=240)
+    p.join(timeout=60)
+    assert status == "ok", status
+    for gn1, gn2, l1, l2 in out:
+        assert abs(gn1 - gn2) <= 2e-3 * max(1.0, gn1), out
+        assert abs(l1 - l2) <= 2e-3 * max(1.0, abs(l1)), out
+    assert err < 1e-2, err
