@@ -191,7 +191,8 @@ class FusedDPAdamW:
                             float(self.weight_decay), int(self.step_count), self.timeout_s)
         if self.mirror is not None:
             self.mirror.copy_(f.compute if f.separate_compute else f.master)
-        return self.scalars[1]
+        # a copy: the scalar buffer is rewritten by the next step, and callers keep the norms of several steps
+        return self.scalars[1].clone()
 
     def check(self) -> None:
         """Raise if a bounded wait of the step timed out (reads the device error word: a host sync)."""
