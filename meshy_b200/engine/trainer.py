@@ -179,11 +179,23 @@ class TrainerEngine(SpmdEngine):
         if self.runtime is None:
             return None
         path = self.runtime.checkpoint_path(self.service_name, self.version)
+        self._export_hf(path)
         if self.rank == 0:
-            self.trainer.export_hf(path)
             self.prune_weights()
         self.barrier()
         return path
+
+    def _export_hf(self, path: str) -> None:
+        """HF safetensors export, written by rank 0. With sharded parameters every rank takes part in gathering
+        the full weights first (a collective), then rank 0 writes them."""
+        if getattr(self.trainer.flat, "sharded", False):
+            from ..models.hf import save_hf_checkpoint
+
+            sd = self.trainer.flat.state_dict(source="compute")
+            if self.rank == 0:
+                save_hf_checkpoint(self.trainer.model_args, sd, path)
+        elif self.rank == 0:
+            self.trainer.export_hf(path)
 
     def _replicated_weights(self) -> bool:
         """Whether every rank holds the whole model (DP / CP): expert- or tensor-parallel ranks hold parts."""
@@ -239,9 +251,11 @@ class TrainerEngine(SpmdEngine):
         # a resumed run boots its engines from the HF export of the checkpointed weight version; with
         # device weight sync no per-step export exists, so the checkpoint writes that one
         path = self.runtime.checkpoint_path(self.service_name, self.version)
-        if self.rank == 0 and not os.path.isdir(path):
-            self.trainer.export_hf(path)
-            self.prune_weights()
+        missing = self.broadcast_object(not os.path.isdir(path) if self.rank == 0 else None)
+        if missing:
+            self._export_hf(path)
+            if self.rank == 0:
+                self.prune_weights()
         self.trainer.save_checkpoint(store.shard_dir(self.service_name, step), step)
         if self.rank == 0:
             store.write_meta(self.service_name, step, {"step_index": self.step_index, "weight_version": self.version,

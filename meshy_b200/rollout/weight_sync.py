@@ -92,7 +92,9 @@ class DevicePublisher:
     def publish(self, version: int) -> tuple[str, int, str]:
         i = version % 2
         if self._bufs[i] is None:
-            self._bufs[i] = torch.empty(self.flat.numel, dtype=torch.bfloat16, device=self.device)
+            # the engines' (full) layout: a sharded trainer's own buffers hold only its shards
+            n = getattr(self.flat, "global_numel", self.flat.numel)
+            self._bufs[i] = torch.empty(n, dtype=torch.bfloat16, device=self.device)
             self._handles[i] = export_ipc_flat(self._bufs[i])
         src = self.flat.sync_source
         from ..ops.functional import native

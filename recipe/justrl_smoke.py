@@ -28,9 +28,14 @@ SYNC = os.environ.get("XRL_SMOKE_WEIGHT_SYNC", "auto")
 CKPT = GlobalCheckpointConfig(enabled=os.environ.get("XRL_SMOKE_CKPT", "0") == "1", interval=1, keep_latest_k=2)
 
 
+SHARD = os.environ.get("XRL_SMOKE_SHARD", "0") == "1"  # FSDP over the trainer's cards instead of DDP
+
+
 def _trainer_config() -> TrainerConfig:
+    par = dict(shard_params="on", dp_shard_degree=-1, dp_replicate_degree=1) if SHARD else \
+        dict(dp_replicate_degree=CARDS)
     return TrainerConfig(model_name="qwen3", model_flavor="debugmodel", seq_len=512, lr=1e-5, weight_decay=0.0,
-                         max_norm=1.0, steps=1000, dtype="bfloat16", dp_replicate_degree=CARDS)
+                         max_norm=1.0, steps=1000, dtype="bfloat16", **par)
 
 
 SERVICE_GROUPS = [

@@ -55,6 +55,30 @@ def test_launcher_runs_colocated_grpo_on_cpu(tmp_path):
 
 
 @pytest.mark.timeout(600)
+def test_launcher_runs_sharded_trainer_on_cpu(tmp_path):
+    """The same ring with the trainer's parameters sharded over its two ranks (FSDP): weights still reach
+    the engines every step (gathered into the full layout) and the run checkpoints and finishes."""
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", XRL_SMOKE_CKPT="1", XRL_SMOKE_SHARD="1",
+               PYTHONPATH=ROOT, XRL_PORT_OFFSET=_port_offset())
+    port = _free_port()
+    rt = tmp_path / "rt"
+    r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
+                        "--runtime-dir", str(rt), "--master-port", str(port)], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=540)
+    logs = rt / "logs"
+    detail = r.stdout[-2000:] + r.stderr[-2000:]
+    if logs.exists():
+        for f in sorted(logs.iterdir()):
+            detail += f"\n==== {f.name}\n" + f.read_text(errors="replace")[-1500:]
+    assert r.returncode == 0, detail
+    rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
+    assert len(rows) == 2, detail
+    ign = (logs / "ignitor-0.log").read_text()
+    assert ign.count("colocation transfer actor_infer -> actor_train") == 2, detail
+    assert (rt / "state" / "actor_train-0").exists(), detail
+
+
+@pytest.mark.timeout(600)
 def test_launcher_runs_critic_ppo_on_cpu(tmp_path):
     """Ring of inference → critic → trainer on one card: the critic cold-starts for one window (it raises
     the gate itself), then publishes values that the trainer turns into VAPO-GAE advantages."""
