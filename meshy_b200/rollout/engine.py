@@ -323,7 +323,8 @@ class RolloutEngine:
         local = {s.name: s for s in self.weight_slots}
         for fs in self.full_slots:
             ls = local[fs.name]
-            part = tp_shard_param(fs.name, full_of(fs), self.args, self.tp, self.tp_rank)
+            full = full_of(fs).to(self.weight_flat.device)  # sources may sit on the CPU or another device
+            part = tp_shard_param(fs.name, full, self.args, self.tp, self.tp_rank)
             self.weight_flat[ls.offset:ls.offset + ls.numel].view(ls.shape).copy_(part)
 
     def update_weights_from_ipc(self, handles: dict, version: int | None = None) -> bool:

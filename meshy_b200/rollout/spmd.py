@@ -25,6 +25,20 @@ LOCKSTEP = frozenset({
 })
 
 
+def _to_host(obj):
+    """Tensors in a broadcast call go by value through host memory: a pickled CUDA tensor would be rebuilt on
+    rank 0's device in the follower's process."""
+    import torch
+
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().cpu()
+    if isinstance(obj, dict):
+        return {k: _to_host(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_to_host(v) for v in obj)
+    return obj
+
+
 class EngineLeader:
     """Rank 0's engine handle: lock-step calls are broadcast to the followers before they run here; everything
     else (attributes, read-only helpers) is the local engine's."""
@@ -35,7 +49,7 @@ class EngineLeader:
         self._order = threading.RLock()  # one broadcast + local call at a time, in one order for every rank
 
     def _broadcast(self, obj) -> None:
-        dist.broadcast_object_list([obj], src=0, group=self._group)
+        dist.broadcast_object_list([_to_host(obj)], src=0, group=self._group)
 
     def __getattr__(self, name: str) -> Any:
         attr = getattr(self._engine, name)
