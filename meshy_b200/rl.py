@@ -64,8 +64,12 @@ class ColocatedGRPO:
         reward_fn: Callable[[Sequence[int], Sequence[int]], float] = parity_reward,
         engine_kwargs: dict | None = None,
         ignore_eos: bool = True,
+        release_kv_for_training: bool = True,
     ):
         self.device = torch.device(device)
+        # the engine's KV pages are idle while the trainer runs: releasing them (virtual addresses kept, so the
+        # decode graphs stay valid) gives the training activations that much more headroom
+        self.release_kv = release_kv_for_training
         self.trainer = PPOTrainer(trainer_config, trainer_params, device=self.device, dp_group=dp_group, seed=seed)
         ek = dict(engine_kwargs or {})
         self.engine = RolloutEngine(self.trainer.model_args, device=self.device, seed=seed + 1000 * self.rank,
@@ -152,11 +156,15 @@ class ColocatedGRPO:
         with nvtx_range("rl/rollout"):
             samples = self.rollout(prompts, max_new_tokens)
         times["rollout_s"] = time.perf_counter() - t0
+        if self.release_kv:
+            self.engine.release_memory(("kv_cache",))
         t1 = time.perf_counter()
         with nvtx_range("rl/train"):
             local, minis = self.plan_local(samples)
             metrics = self.trainer.train_step(local, plan=minis)
         times["train_s"] = time.perf_counter() - t1
+        if self.release_kv:
+            self.engine.resume_memory(("kv_cache",))
         times["wait_s"] = getattr(self, "last_wait_s", 0.0)
         times["optim_s"] = float(metrics.get("time/train/optim_step", 0.0)) + float(
             metrics.get("time/train/grad_reduce", 0.0))
