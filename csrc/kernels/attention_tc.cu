@@ -109,8 +109,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int doc = blockIdx.x / max_blocks;
-  const int qb = max_blocks - 1 - blockIdx.x % max_blocks;  // longest causal rows first
+  // query-tile-major dispatch, the longest causal rows (highest tile) of every document first
+  const int n_docs = gridDim.x / max_blocks;
+  const int doc = blockIdx.x % n_docs;
+  const int qb = max_blocks - 1 - blockIdx.x / n_docs;
   const int h = blockIdx.y, hk = h / (Hq / Hkv);
   const int s = cu[doc], e = cu[doc + 1], L = e - s;
   const int ks = NP > 1 ? 0 : (cu_k ? cu_k[doc] : s);
@@ -388,8 +390,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* ld_s = reinterpret_cast<float*>(sm + kBK_LD);  // [buf][LSE | D][64]
 
-  const int doc = blockIdx.x / max_blocks;
-  const int kb = blockIdx.x % max_blocks;
+  // key tile kb of a causal document meets the query tiles from kb on, so low kb carries the most work:
+  // CTAs are dispatched key-tile-major (every document's tile 0 first), the heaviest first, so the last wave
+  // holds the light tiles
+  const int n_docs = gridDim.x / max_blocks;
+  const int doc = blockIdx.x % n_docs;
+  const int kb = blockIdx.x / n_docs;
   const int hk = blockIdx.y, rep = Hq / Hkv;
   const int s = cu[doc], e = cu[doc + 1], L = e - s;
   const int ks = cu_k ? cu_k[doc] : s, ke = cu_k ? cu_k[doc + 1] : e, Lk = ke - ks;
@@ -635,8 +641,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int doc = blockIdx.x / max_blocks;
-  const int qb = max_blocks - 1 - blockIdx.x % max_blocks;
+  const int n_docs = gridDim.x / max_blocks;  // query-tile-major, longest causal rows first (as the forward)
+  const int doc = blockIdx.x % n_docs;
+  const int qb = max_blocks - 1 - blockIdx.x / n_docs;
   const int h = blockIdx.y, hk = h / (Hq / Hkv);
   const int s = cu[doc], e = cu[doc + 1], L = e - s;
   const int ks = cu_k ? cu_k[doc] : s, ke = cu_k ? cu_k[doc + 1] : e, Lk = ke - ks;

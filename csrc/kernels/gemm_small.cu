@@ -48,6 +48,7 @@ struct SmallArgs {
   int M, N, K;
   int n_tiles, k_blocks, kb_per, cs;
   int stages;  // depth of the shared-memory stage ring of this launch (<= SCfg::STAGES)
+  int early_arrive;  // closing cluster barrier: arrive once the partials are read (1) or after the epilogue (0)
   int epi;
   void* out;
   int ldo;
@@ -636,12 +637,14 @@ __global__ void __launch_bounds__(kSmallThreads, 2)
       const uint32_t red_addr = smem_u32(smem);
       const bool swiglu = p.epi == EPI_SWIGLU;
       constexpr int G = MP / 4;
-      // The closing cluster barrier only guards the peers' reads of this CTA's partials: a warp arrives as soon
-      // as its last group's partials are summed and waits only before the CTA exits, so the epilogue math and
-      // stores run inside the barrier interval instead of before it (the loop bounds are warp-uniform).
+      // The closing cluster barrier only guards the peers' reads of this CTA's partials. With early_arrive a warp
+      // arrives as soon as its last group's partials are summed and waits only before the CTA exits, so the
+      // epilogue runs inside the barrier interval (the loop bounds are warp-uniform); otherwise every warp
+      // arrives after its epilogue.
       int g_last = -1;
       for (int g = (int)rank; g < G && 4 * g < p.M && !(swiglu && f >= 64); g += p.cs) g_last = g;
-      if (g_last < 0) cluster_arrive();
+      if (!p.early_arrive) g_last = -2;  // arrive after the epilogue instead (below)
+      if (g_last == -1) cluster_arrive();
       for (int g = (int)rank; g < G; g += p.cs) {
         if (4 * g >= p.M) break;
         if (swiglu && f >= 64) break;
@@ -825,7 +828,7 @@ __global__ void __launch_bounds__(kSmallThreads, 2)
     }
     if (threadIdx.x == 64) SMALL_TRACE(6);
     __syncwarp();
-    if (warp < 2) cluster_arrive();
+    if (warp < 2 || !p.early_arrive) cluster_arrive();
     cluster_wait();  // no CTA leaves while a peer may still read its shared memory
     if (threadIdx.x == 64) SMALL_TRACE(7);
   }
@@ -874,6 +877,13 @@ void launch_small(const CUtensorMap& mw, const CUtensorMap& mx, const SmallArgs&
   using C = SCfg<MP, PERSIST>;
   SmallArgs a = args;
   a.stages = ring_stages<MP, PERSIST>(a.kb_per);
+  // early arrival (MESHY_GEMM_SMALL_EARLY_ARRIVE=1) measured 1-4 % slower at 16-64 rows on the same box (its
+  // release fence stalls the epilogue warps), and ~1 % faster at 1 row: off by default
+  static const int early = [] {
+    const char* e = std::getenv("MESHY_GEMM_SMALL_EARLY_ARRIVE");
+    return (e && e[0] == '1') ? 1 : 0;
+  }();
+  a.early_arrive = early;
   auto k = gemm_small_kernel<MP, PERSIST>;
   static bool attr_set = false;
   if (!attr_set) {

@@ -64,11 +64,12 @@ class ColocatedGRPO:
         reward_fn: Callable[[Sequence[int], Sequence[int]], float] = parity_reward,
         engine_kwargs: dict | None = None,
         ignore_eos: bool = True,
-        release_kv_for_training: bool = True,
+        release_kv_for_training: bool = False,
     ):
         self.device = torch.device(device)
-        # the engine's KV pages are idle while the trainer runs: releasing them (virtual addresses kept, so the
-        # decode graphs stay valid) gives the training activations that much more headroom
+        # the engine's KV pages are idle while the trainer runs; releasing them (virtual addresses kept, so the
+        # decode graphs stay valid) frees their memory for the trainer, but the release also empties the
+        # allocator's cache, and the trainer's next forward re-allocates everything (measured slower: off)
         self.release_kv = release_kv_for_training
         self.trainer = PPOTrainer(trainer_config, trainer_params, device=self.device, dp_group=dp_group, seed=seed)
         ek = dict(engine_kwargs or {})
