@@ -53,6 +53,9 @@ class MoE(nn.Module):
         #: local expert range under expert parallelism (set by parallel.ep)
         self.expert_offset = 0
         self.ep_group = None
+        #: inference expert parallelism over ranks that hold the same tokens (a tensor-parallel replica): each
+        #: rank runs the assignments of its own experts and the outputs are summed over this group
+        self.ep_tokens_group = None
 
     def reset_parameters(self, std: float, depth_std: float) -> None:
         nn.init.normal_(self.router, std=std)
@@ -62,7 +65,39 @@ class MoE(nn.Module):
             nn.init.normal_(self.shared_w13, std=std)
             nn.init.normal_(self.shared_w2, std=depth_std)
 
+    def _replicated_token_experts(self, x, weights, experts):
+        """Expert parallelism when every rank holds every token: assignments to other ranks' experts get weight 0
+        (and a local expert id, so the device plan needs no host synchronisation), then the outputs of the ranks
+        are summed."""
+        import torch.distributed as dist
+
+        e_local = self.w13.shape[0]
+        local = experts.long() - self.expert_offset
+        mine = (local >= 0) & (local < e_local)
+        w = torch.where(mine, weights, torch.zeros_like(weights))
+        e = torch.where(mine, local, torch.zeros_like(local)).to(experts.dtype)
+        if Fx.native(x):
+            from ..ops import moe as M
+
+            out = M.experts_forward(x, w, e, self.w13, self.w2, self.args.swiglu_block)
+        else:
+            out = moe_experts(x, w, e, self.w13, self.w2, self.args.swiglu_block)
+        out = out.float()
+        dist.all_reduce(out, group=self.ep_tokens_group)
+        return out.to(x.dtype)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.ep_tokens_group is not None:
+            if Fx.native(x):
+                from ..ops import moe as M
+
+                weights, experts = M.route(Fx.linear(x, self.router), self.top_k, self.route_norm)
+            else:
+                weights, experts = route(x, self.router, self.top_k, self.route_norm)
+            out = self._replicated_token_experts(x, weights, experts)
+            if self.shared_w13 is not None:
+                out = out + Fx.linear(Fx.linear_swiglu(x, self.shared_w13, self.args.swiglu_block), self.shared_w2)
+            return out
         if Fx.native(x):
             from ..ops import moe as M
 

@@ -76,10 +76,15 @@ def local_args(a, tp: int):
     return dataclasses.replace(a, n_heads=a.n_heads // tp, n_kv_heads=a.n_kv_heads // tp, ffn_dim=a.ffn_dim // tp)
 
 
-def tp_shard_param(name: str, full: torch.Tensor, a, tp: int, t: int) -> torch.Tensor:
+def tp_shard_param(name: str, full: torch.Tensor, a, tp: int, t: int, ep: bool = False) -> torch.Tensor:
     """Rank ``t``'s slice of the block parameter ``name`` (its last dotted component: ``wqkv``, ``bqkv``,
-    ``wo``, ``w13``, ``w2``; anything else is replicated and returned as is) from the full tensor."""
+    ``wo``, ``w13``, ``w2``; anything else is replicated and returned as is) from the full tensor. With ``ep``
+    the MoE experts (``...moe.w13`` / ``...moe.w2``) are split over the ranks by expert: rank ``t`` keeps
+    experts ``[t E/tp, (t + 1) E/tp)``."""
     leaf = name.rsplit(".", 1)[-1]
+    if ep and ".moe." in name and leaf in ("w13", "w2"):
+        n = full.shape[0] // tp
+        return full[t * n:(t + 1) * n]
     hd = a.head_dim
     hq, hkv = a.n_heads // tp, a.n_kv_heads // tp
     dev = full.device
@@ -99,8 +104,10 @@ def tp_shard_param(name: str, full: torch.Tensor, a, tp: int, t: int) -> torch.T
     return full
 
 
-def shard_model_tp(model, group) -> None:
-    """Slice every block of ``model`` (a :class:`~meshy_b200.models.transformer.DecoderLM`) in place."""
+def shard_model_tp(model, group, ep: bool = False) -> None:
+    """Slice every block of ``model`` (a :class:`~meshy_b200.models.transformer.DecoderLM`) in place. With ``ep``
+    (inference) each rank also keeps only its share of every MoE layer's experts; the MoE output is then summed
+    over ``group`` (every rank holds every token)."""
     tp = dist.get_world_size(group)
     t = dist.get_rank(group)
     a = model.args
@@ -114,6 +121,14 @@ def shard_model_tp(model, group) -> None:
             if blk.moe is None:
                 blk.w13 = nn.Parameter(tp_shard_param("w13", blk.w13, a, tp, t).clone())
                 blk.w2 = nn.Parameter(tp_shard_param("w2", blk.w2, a, tp, t).clone())
+            elif ep:
+                moe = blk.moe
+                if moe.n_experts % tp:
+                    raise ValueError(f"EP={tp} must divide the {moe.n_experts} experts")
+                moe.w13 = nn.Parameter(tp_shard_param(".moe.w13", moe.w13, a, tp, t, ep=True).clone())
+                moe.w2 = nn.Parameter(tp_shard_param(".moe.w2", moe.w2, a, tp, t, ep=True).clone())
+                moe.expert_offset = t * (moe.n_experts // tp)
+                moe.ep_tokens_group = group
             blk.args = la
             blk.tp_group = group
 

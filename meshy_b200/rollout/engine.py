@@ -103,6 +103,7 @@ class RolloutEngine:
         prefill_chunk_tokens: int = 32768,
         mem_fraction: float = 0.5,
         tp_group=None,
+        ep: bool = False,
     ):
         from ..backend.flat import Slot, _align, flatten_module
 
@@ -121,6 +122,7 @@ class RolloutEngine:
         self.tp_group = tp_group if (tp_group is not None and dist.is_initialized()
                                      and dist.get_world_size(tp_group) > 1) else None
         self.tp, self.tp_rank = 1, 0
+        self.ep = bool(ep) and self.tp_group is not None  # MoE experts split over the TP ranks too
         self.local_args = args
         self.full_slots = None
         if self.tp_group is not None:
@@ -131,7 +133,7 @@ class RolloutEngine:
             for name, p in model.named_parameters():  # the trainer's (unsharded) flat layout
                 self.full_slots.append(Slot(name, off, p.numel(), tuple(p.shape)))
                 off += _align(p.numel())
-            shard_model_tp(model, self.tp_group)
+            shard_model_tp(model, self.tp_group, ep=self.ep)
             self.local_args = local_args(args, self.tp)
         self.model = model.eval()
         for p in self.model.parameters():
@@ -324,7 +326,7 @@ class RolloutEngine:
         for fs in self.full_slots:
             ls = local[fs.name]
             full = full_of(fs).to(self.weight_flat.device)  # sources may sit on the CPU or another device
-            part = tp_shard_param(fs.name, full, self.args, self.tp, self.tp_rank)
+            part = tp_shard_param(fs.name, full, self.args, self.tp, self.tp_rank, ep=self.ep)
             self.weight_flat[ls.offset:ls.offset + ls.numel].view(ls.shape).copy_(part)
 
     def update_weights_from_ipc(self, handles: dict, version: int | None = None) -> bool:

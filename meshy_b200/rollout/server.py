@@ -236,9 +236,9 @@ def main(argv=None):
     p.add_argument("--ep-size", type=int, default=1, help="expert-parallel degree of this replica")
     p.add_argument("--dist-port", type=int, default=0, help="rendezvous port of the TP ranks (0: free port)")
     a = p.parse_args(argv)
-    if a.ep_size > 1:
-        raise SystemExit("expert-parallel decoding is not supported: MoE replicas keep every expert (one card "
-                         "holds Qwen3-30B-A3B), or split the experts' FFN width with --tp-size")
+    if a.ep_size > 1 and a.ep_size != a.tp_size:
+        raise SystemExit("--ep-size splits the MoE experts over the ranks of a tensor-parallel replica: it must "
+                         "equal --tp-size (or be 1: every rank keeps every expert)")
     if a.tp_size > 1:
         return _serve_tp(a)
     eng = _build_engine(a)
@@ -254,7 +254,8 @@ def _build_engine(a, device=None, tp_group=None):
     name, flavor = a.model.split(":")
     return RolloutEngine(get_model_args(name, flavor), device=device or a.device, max_running=a.max_running,
                          max_total_tokens=a.max_total_tokens, max_seq_len=a.max_seq_len,
-                         mem_fraction=a.mem_fraction, seed=a.seed, eos_token_ids=a.eos, tp_group=tp_group)
+                         mem_fraction=a.mem_fraction, seed=a.seed, eos_token_ids=a.eos, tp_group=tp_group,
+                         ep=a.ep_size > 1)
 
 
 def _tp_rank_setup(a, rank: int):

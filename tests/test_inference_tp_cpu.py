@@ -3,6 +3,8 @@
 * engine level: rank 0 drives the replica through :class:`EngineLeader`, rank 1 follows; greedy generations
   equal a single-rank engine's on the same weights (token ids exact, log-probs to fp32 summation order), and
   so do they after a weight update from a full state dict (the replica -> tensor-parallel reshard);
+* expert parallelism inside the replica (Qwen3-MoE, ``ep=True``): each rank keeps half of the experts, the
+  routed outputs are summed over the ranks, and generations again equal the single-rank engine's;
 * server level: ``python -m meshy_b200.rollout.server --tp-size 2`` spawns its follower and answers
   ``/generate`` with the single-card server's tokens.
 """
@@ -28,12 +30,12 @@ def _port():
         return s.getsockname()[1]
 
 
-def _engine(group=None, seed=0):
+def _engine(group=None, seed=0, flavor="debugmodel", ep=False):
     from meshy_b200.models import get_model_args
     from meshy_b200.rollout.engine import RolloutEngine
 
-    return RolloutEngine(get_model_args("qwen3", "debugmodel"), device="cpu", max_running=8, max_seq_len=128,
-                         seed=seed, sync_every=4, tp_group=group)
+    return RolloutEngine(get_model_args("qwen3", flavor), device="cpu", max_running=8, max_seq_len=128,
+                         seed=seed, sync_every=4, tp_group=group, ep=ep)
 
 
 def _run(eng):
@@ -82,6 +84,60 @@ def _same(a, b, tol=1e-4):
     for (ta, la), (tb, lb) in zip(a, b):
         assert ta == tb
         assert max(abs(x - y) for x, y in zip(la, lb)) < tol
+
+
+def _ep_worker(rank, port, q):
+    """Qwen3-MoE replica with attention split over 2 ranks and the experts too (4 of 8 each)."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=2)
+        from meshy_b200.rollout.spmd import EngineLeader, follow
+
+        g = dist.group.WORLD
+        eng = _engine(g, flavor="debugmodel_moe", ep=True)
+        moe = eng.model.layers[0].moe
+        assert moe.w13.shape[0] * 2 == moe.n_experts and moe.expert_offset == rank * moe.n_experts // 2
+        if rank == 1:
+            follow(eng, g)
+            q.put((rank, "ok"))
+        else:
+            lead = EngineLeader(eng, g)
+            out = {"ep": _run(lead)}
+            from meshy_b200.models import build_model
+
+            other = build_model(eng.args, seed=7, device="cpu", dtype=torch.float32)
+            sd = {k: v.detach().clone() for k, v in other.named_parameters()}
+            lead.update_weights_from_state_dict(sd, 2)  # each rank keeps its experts' slices
+            out["ep2"] = _run(lead)
+            lead.stop()
+            ref = _engine(None, flavor="debugmodel_moe")
+            out["ref"] = _run(ref)
+            ref.update_weights_from_state_dict(sd, 2)
+            out["ref2"] = _run(ref)
+            q.put((rank, out))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.timeout(300)
+def test_tp_ep_moe_engine_matches_single_rank():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_ep_worker, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+    for v in res.values():
+        assert not (isinstance(v, str) and v != "ok"), v
+    _same(res[0]["ep"], res[0]["ref"])
+    _same(res[0]["ep2"], res[0]["ref2"])
 
 
 @pytest.mark.timeout(300)
