@@ -235,12 +235,20 @@ def main(argv=None):
     p.add_argument("--tp-size", type=int, default=1, help="tensor-parallel degree of this replica")
     p.add_argument("--ep-size", type=int, default=1, help="expert-parallel degree of this replica")
     p.add_argument("--dist-port", type=int, default=0, help="rendezvous port of the TP ranks (0: free port)")
+    p.add_argument("--nnodes", type=int, default=1, help="nodes the replica's TP ranks span")
+    p.add_argument("--node-rank", type=int, default=0, help="this node's index among them (0 serves HTTP)")
+    p.add_argument("--dist-init-addr", default="", help="host:port of the TP rendezvous (multi-node replicas)")
     a = p.parse_args(argv)
     if a.ep_size > 1 and a.ep_size != a.tp_size:
         raise SystemExit("--ep-size splits the MoE experts over the ranks of a tensor-parallel replica: it must "
                          "equal --tp-size (or be 1: every rank keeps every expert)")
+    if a.nnodes < 1 or a.tp_size % a.nnodes or not 0 <= a.node_rank < a.nnodes:
+        raise SystemExit(f"--tp-size {a.tp_size} must split evenly over --nnodes {a.nnodes}, and --node-rank "
+                         f"must be below it")
+    if a.nnodes > 1 and not a.dist_init_addr:
+        raise SystemExit("a replica over several nodes needs --dist-init-addr host:port (node 0's address)")
     if a.tp_size > 1:
-        return _serve_tp(a)
+        return _serve_tp(a) if a.node_rank == 0 else _serve_tp_node(a)
     eng = _build_engine(a)
     if a.model_path:
         eng.update_weights_from_disk(a.model_path, 0)
@@ -258,17 +266,33 @@ def _build_engine(a, device=None, tp_group=None):
                          ep=a.ep_size > 1)
 
 
+def _rendezvous(a) -> tuple[str, int]:
+    if a.dist_init_addr:
+        host, port = a.dist_init_addr.rsplit(":", 1)
+        return host, int(port)
+    return "127.0.0.1", a.dist_port
+
+
+def _local_ranks(a) -> range:
+    """Global TP ranks run on this node: ``tp_size / nnodes`` consecutive ones, node 0 first (as SGLang's
+    ``--nnodes``/``--node-rank`` place them)."""
+    per = a.tp_size // a.nnodes
+    return range(a.node_rank * per, (a.node_rank + 1) * per)
+
+
 def _tp_rank_setup(a, rank: int):
-    """Process group of one TP replica (NCCL on the GPU for the partial sums, gloo for the control channel)."""
+    """Process group of one TP replica (NCCL on the GPU for the partial sums, gloo for the control channel).
+    ``rank`` is the global TP rank; its GPU is the node-local index among the visible devices."""
     import os
     from datetime import timedelta
 
     import torch
     import torch.distributed as dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(a.dist_port))
+    host, port = _rendezvous(a)
+    os.environ.update(MASTER_ADDR=host, MASTER_PORT=str(port))
     cuda = a.device.startswith("cuda")
-    device = torch.device("cuda", rank) if cuda else torch.device("cpu")
+    device = torch.device("cuda", rank - _local_ranks(a).start) if cuda else torch.device("cpu")
     kw = {"device_id": device} if cuda else {}
     if cuda:
         torch.cuda.set_device(device)
@@ -290,21 +314,42 @@ def _tp_follower(a, rank: int) -> None:
     dist.destroy_process_group()
 
 
-def _serve_tp(a) -> None:
-    """Rank 0 serves HTTP and drives ``tp_size - 1`` follower processes (one per further visible GPU)."""
+def _spawn_followers(a, ranks) -> list:
     import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_tp_follower, args=(a, r), daemon=True) for r in ranks]
+    for p_ in procs:
+        p_.start()
+    return procs
+
+
+def _serve_tp_node(a) -> None:
+    """A further node of a multi-node replica: every local rank is a follower; the process ends when node 0's
+    leader stops the replica."""
+    import sys
+
+    procs = _spawn_followers(a, _local_ranks(a))
+    for p_ in procs:
+        p_.join()
+    bad = [p_.exitcode for p_ in procs if p_.exitcode]
+    if bad:
+        sys.exit(f"tensor-parallel follower exited with {bad}")
+
+
+def _serve_tp(a) -> None:
+    """Rank 0 serves HTTP and drives the replica's other ranks: ``tp_size / nnodes - 1`` follower processes
+    here (one per further visible GPU) and, for a multi-node replica, those that the other nodes' servers
+    start (``_serve_tp_node``)."""
     import socket
 
     from .spmd import EngineLeader
 
-    if not a.dist_port:
+    if not a.dist_port and not a.dist_init_addr:
         with socket.socket() as s_:
             s_.bind(("127.0.0.1", 0))
             a.dist_port = s_.getsockname()[1]
-    ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_tp_follower, args=(a, r), daemon=True) for r in range(1, a.tp_size)]
-    for p_ in procs:
-        p_.start()
+    procs = _spawn_followers(a, _local_ranks(a)[1:])
     device, group, ctrl = _tp_rank_setup(a, 0)
     eng = EngineLeader(_build_engine(a, device=str(device), tp_group=group), ctrl)
     if a.model_path:

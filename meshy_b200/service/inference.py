@@ -68,6 +68,13 @@ class InferenceService(Service):
         self.rank_in_replica = ranks.index(rank) if rank in ranks else 0
         self.my_gpu = info.replica_gpus[self.rank_in_replica]
         self.is_master = self.rank_in_replica == 0
+        # a replica's cards by node, in node order; the lowest global rank of each node starts that node's server
+        by_node: dict[int, list] = {}
+        for g in info.replica_gpus:
+            by_node.setdefault(g.node_rank, []).append(g)
+        self.nodes = sorted(by_node)
+        self.node_gpus = sorted(by_node[self.my_gpu.node_rank], key=lambda g: g.global_rank)
+        self.is_node_leader = self.my_gpu.global_rank == self.node_gpus[0].global_rank
         self.processes: list = []
         self.client = None
 
@@ -111,18 +118,27 @@ class InferenceService(Service):
         boot = self._boot_model_path()
         if boot:
             cmd += ["--model-path", boot]
-        return cmd + server_args_to_cli(args)
+        # the replica's cards set its tensor-parallel degree, whatever server_args say (as the reference's
+        # SGLang launch does); a replica over several nodes rendezvouses at the master card's host
+        args["tp_size"] = len(self.info.replica_gpus)
+        cmd += server_args_to_cli(args)
+        if len(self.nodes) > 1:
+            cmd += ["--nnodes", str(len(self.nodes)), "--node-rank", str(self.nodes.index(self.my_gpu.node_rank)),
+                    "--dist-init-addr", f"{self.info.replica_gpus[0].host}:{self.info.dist_port}"]
+        elif len(self.info.replica_gpus) > 1:
+            cmd += ["--dist-port", str(self.info.dist_port)]
+        return cmd
 
     def ignite(self) -> None:
-        if not self.is_master:
+        if not self.is_node_leader:
             return
         env = dict(os.environ)
         for v in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT", "GROUP_RANK",
                   "TORCHELASTIC_RUN_ID", "LOCAL_WORLD_SIZE"):
             env.pop(v, None)
         if env.get("XRL_DEVICE", "cuda") == "cuda":
-            env["CUDA_VISIBLE_DEVICES"] = ",".join(str(g.local_rank) for g in self.info.replica_gpus)
-        log_path = self.runtime.process_log_path(self.name, 0)
+            env["CUDA_VISIBLE_DEVICES"] = ",".join(str(g.local_rank) for g in self.node_gpus)
+        log_path = self.runtime.process_log_path(self.name, self.rank_in_replica)
         self._log = open(log_path, "ab")
         # own session (killpg on terminate) + PR_SET_PDEATHSIG so a dead ignitor takes the server with it
         self.proc = subprocess.Popen(self.command(), stdout=self._log, stderr=subprocess.STDOUT, env=env,

@@ -6,7 +6,10 @@
 * expert parallelism inside the replica (Qwen3-MoE, ``ep=True``): each rank keeps half of the experts, the
   routed outputs are summed over the ranks, and generations again equal the single-rank engine's;
 * server level: ``python -m meshy_b200.rollout.server --tp-size 2`` spawns its follower and answers
-  ``/generate`` with the single-card server's tokens.
+  ``/generate`` with the single-card server's tokens; so does a replica over two "nodes" (two server processes,
+  ``--nnodes 2 --node-rank 0/1 --dist-init-addr``), the second of which runs only its follower rank;
+* service level: an inference replica's server command takes its TP degree from the replica's cards and, over
+  several nodes, the node count, this node's index and the master card's rendezvous address.
 """
 
 import os
@@ -159,10 +162,10 @@ def test_tp_engine_matches_single_rank():
     assert out["first"][0][0] != out["second"][0][0] or out["first"][1][0] != out["second"][1][0]
 
 
-def _server(tp, port):
+def _server(tp, port, extra=()):
     env = dict(os.environ, PYTHONPATH=ROOT)
     cmd = [sys.executable, "-m", "meshy_b200.rollout.server", "--model", "qwen3:debugmodel", "--device", "cpu",
-           "--port", str(port), "--max-running", "8", "--max-seq-len", "128", "--tp-size", str(tp)]
+           "--port", str(port), "--max-running", "8", "--max-seq-len", "128", "--tp-size", str(tp), *extra]
     return subprocess.Popen(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
                             start_new_session=True)
 
@@ -181,25 +184,68 @@ def _wait(port, proc, timeout=120):
     raise AssertionError("server did not come up")
 
 
-@pytest.mark.timeout(300)
+@pytest.mark.timeout(420)
 def test_tp_server_answers_like_single_card_server():
     import requests
 
     outs = []
-    for tp in (1, 2):
+    for case in ("tp1", "tp2", "tp2-2nodes"):
         port = _port()
-        proc = _server(tp, port)
+        if case == "tp2-2nodes":
+            rdv = f"127.0.0.1:{_port()}"
+            procs = [_server(2, port if n == 0 else _port(),
+                             ["--nnodes", "2", "--node-rank", str(n), "--dist-init-addr", rdv]) for n in (0, 1)]
+        else:
+            procs = [_server(1 if case == "tp1" else 2, port)]
         try:
-            _wait(port, proc)
+            _wait(port, procs[0])
+            assert all(p.poll() is None for p in procs)
             body = {"input_ids": PROMPTS[1], "sampling_params": {"max_new_tokens": 9, "temperature": 0.0,
                                                                  "ignore_eos": True}, "return_logprob": True}
             r = requests.post(f"http://127.0.0.1:{port}/generate", json=body, timeout=120)
             r.raise_for_status()
             outs.append(r.json())
         finally:
-            os.killpg(proc.pid, 15)
-            proc.wait(timeout=30)
-    assert outs[0]["output_ids"] == outs[1]["output_ids"] and len(outs[0]["output_ids"]) == 9
-    la = [x[0] for x in outs[0]["meta_info"]["output_token_logprobs"]]
-    lb = [x[0] for x in outs[1]["meta_info"]["output_token_logprobs"]]
-    assert max(abs(x - y) for x, y in zip(la, lb)) < 1e-4
+            for p in procs:
+                os.killpg(p.pid, 15)
+            for p in procs:
+                p.wait(timeout=30)
+    for o in outs[1:]:
+        assert outs[0]["output_ids"] == o["output_ids"] and len(o["output_ids"]) == 9
+        la = [x[0] for x in outs[0]["meta_info"]["output_token_logprobs"]]
+        lb = [x[0] for x in o["meta_info"]["output_token_logprobs"]]
+        assert max(abs(x - y) for x, y in zip(la, lb)) < 1e-4
+
+
+def _service(gpus, me):
+    from meshy_b200.config import InferenceServiceConfig
+    from meshy_b200.service.inference import InferenceService
+    from meshy_b200.service.topology import ServiceInfo
+
+    cfg = InferenceServiceConfig(server_args={"model": "qwen3:debugmodel", "tp_size": 1, "ep_size": len(gpus)})
+    info = ServiceInfo("actor_infer-0", "actor_infer", "inference", True, 0, gpus[0].host, 30000, 40000, gpus,
+                       False, None, config=cfg)
+    return InferenceService(info, None, None, my_gpu=me)
+
+
+def _flag(cmd, name):
+    return cmd[cmd.index(name) + 1] if name in cmd else None
+
+
+def test_inference_service_command_sets_tp_from_replica_cards():
+    from meshy_b200.service.base import GPU
+
+    one = [GPU(r, "10.0.0.1", r, 0) for r in range(4)]
+    svc = _service(one, one[2])
+    assert svc.is_node_leader is False and svc.is_master is False
+    cmd = _service(one, one[0]).command()
+    assert _flag(cmd, "--tp-size") == "4" and _flag(cmd, "--ep-size") == "4"  # server_args' tp_size is overridden
+    assert _flag(cmd, "--dist-port") == "40000" and "--nnodes" not in cmd
+    two = [GPU(r, f"10.0.0.{1 + r // 2}", r % 2, r // 2) for r in range(4)]
+    lead0, lead1, other = _service(two, two[0]), _service(two, two[2]), _service(two, two[3])
+    assert lead0.is_node_leader and lead1.is_node_leader and not other.is_node_leader
+    assert [g.local_rank for g in lead1.node_gpus] == [0, 1]
+    c0, c1 = lead0.command(), lead1.command()
+    for c, n in ((c0, "0"), (c1, "1")):
+        assert _flag(c, "--tp-size") == "4" and _flag(c, "--nnodes") == "2" and _flag(c, "--node-rank") == n
+        assert _flag(c, "--dist-init-addr") == "10.0.0.1:40000"
