@@ -144,20 +144,9 @@ class MemoryLedger:
     def __init__(self):
         self._rows: dict[str, LedgerRow] = {}
         self._lock = threading.Lock()
-        self.dropped_writes = 0
-        self.drop_next = 0  # fault injection: silently drop this many upcoming writes
-
-    def _maybe_drop(self) -> bool:
-        if self.drop_next > 0:
-            self.drop_next -= 1
-            self.dropped_writes += 1
-            return True
-        return False
 
     def create(self, request: GpuRequest) -> None:
         with self._lock:
-            if self._maybe_drop():
-                return
             self._rows[request.request_id] = LedgerRow(request)
 
     def grant(self, request_id: str, grant: GpuGrant) -> None:

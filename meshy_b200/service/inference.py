@@ -176,12 +176,13 @@ class InferenceService(Service):
         from ..engine.rollout_client import EngineClient
         from ..tq.client import connect
         from .colocation import ColocationManager, StoreLedger
+        from ..utils.faults import inject
 
         ring = self.info.colocation
         group = EngineClient([s.endpoint for s in self.topology.group(self.info.group_id)])
         ref = os.environ.get("XRL_TQ_ENDPOINTS")
         self.colocation_manager = ColocationManager(
-            ring, self.info.group_id, lambda: StoreLedger(connect(ref), ring.group_id),
+            ring, self.info.group_id, lambda: inject(StoreLedger(connect(ref), ring.group_id), "ledger"),
             on_acquire=group.on_colocate_acquire, on_release=group.on_colocate_release)
         self.colocation_manager.start()
 

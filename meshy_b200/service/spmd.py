@@ -94,9 +94,10 @@ class SpmdService(Service):
     def _ledger_factory(self, ring):
         from ..tq.client import connect
         from .colocation import StoreLedger
+        from ..utils.faults import inject
 
         ref = self.runtime_tq_ref()
-        return lambda: StoreLedger(connect(ref), ring.group_id)
+        return lambda: inject(StoreLedger(connect(ref), ring.group_id), "ledger")
 
     def runtime_tq_ref(self) -> str | None:
         cfg = self.info.config

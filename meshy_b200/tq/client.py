@@ -173,18 +173,22 @@ class RemoteClient(_Base):
 
 def connect(ref: str | None = None) -> _Base:
     """``tcp://host:port`` / ``host:port`` → RemoteClient; ``store://key`` reads the
-    endpoint from the bootstrap store; ``None`` → a fresh in-process store."""
+    endpoint from the bootstrap store; ``None`` → a fresh in-process store. The client
+    goes through :func:`meshy_b200.utils.faults.inject` (scope ``tq``), a no-op unless a
+    fault plan names that scope."""
+    from ..utils.faults import inject
+
     if ref is None or ref == "local":
-        return LocalClient()
+        return inject(LocalClient(), "tq")
     if ref.startswith("store://"):
         from ..service.bootstrap import get_store
 
         key = ref[len("store://"):]
         endpoint = get_store().get(key).decode()
-        return RemoteClient(endpoint)
+        return inject(RemoteClient(endpoint), "tq")
     if ref.startswith("tcp://"):
         ref = ref[len("tcp://"):]
-    return RemoteClient(ref)
+    return inject(RemoteClient(ref), "tq")
 
 
 __all__ = ["BatchMeta", "Columns", "LocalClient", "RemoteClient", "connect"]
