@@ -156,6 +156,8 @@ class PPOTrainer:
             self.flat.resident = ("grad", "compute") if self.flat.separate_compute else ("master", "grad", "compute")
             self.reducer.backend = "none"
             self.fused_dp = True
+        if not self.fsdp and self.reducer.overlapping:
+            self.model.block_hooks = self.reducer  # per-block all-reduce during the last micro's backward
         self.h2d_bytes = 0
 
     def _use_fused_dp(self) -> bool:
@@ -320,9 +322,9 @@ class PPOTrainer:
                 self.flat.collect_cpu_grads()  # PyTorch paths only: fold .grad into the fp32 buffer
             sums = mb_sums if sums is None else {k: sums[k] + v for k, v in mb_sums.items()}
         with timer.timer("train/grad_reduce"):
+            self.reducer.finish()  # first: it waits for the reductions the backward started
             for off, n in self.tp_partial:
                 dist.all_reduce(self.flat.grad[off:off + n], group=self.tp_group)
-            self.reducer.finish()
         with timer.timer("train/optim_step"):
             gn = self.optimizer.step(self._ep_grad_norm() if self.reducer.skip else None)
         return reduce_sums(sums, self.loss_group), gn

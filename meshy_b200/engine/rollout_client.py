@@ -167,6 +167,10 @@ class EngineClient(_Base):
     def pause_generation(self) -> None:
         self._mgmt("POST", "/pause_generation", json={"mode": "abort"})
 
+    def weight_versions(self) -> list:
+        """The weight version each endpoint serves."""
+        return [(d or {}).get("weight_version") for d in self._mgmt("GET", "/get_model_info", timeout=30.0)]
+
     def continue_generation(self) -> None:
         self._mgmt("POST", "/continue_generation", json={})
 
@@ -240,6 +244,9 @@ class LocalEngineClient(_Base):
 
     def pause_generation(self) -> None:
         self.runner.pause("abort")
+
+    def weight_versions(self) -> list:
+        return [self.engine.weight_version]
 
     def continue_generation(self) -> None:
         self.runner.resume()

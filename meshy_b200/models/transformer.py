@@ -129,7 +129,9 @@ class DecoderLM(nn.Module):
     # ------------------------------------------------------------------
     def hidden(self, input_ids, positions, cu_seqlens, max_seqlen) -> torch.Tensor:
         """Final-norm hidden states ``[T, D]`` of a packed token stream."""
-        fs = getattr(self, "fsdp", None)  # sharded parameters: per-block gather / reduce hooks
+        # per-block hooks: the sharded-parameter engine (gathers / reduce-scatters) or the data-parallel
+        # reducer (gradient all-reduce overlapped with the backward)
+        fs = getattr(self, "fsdp", None) or getattr(self, "block_hooks", None)
         if fs is not None:
             fs.begin_forward()
         x = Fx.embedding(input_ids, self.embed)

@@ -64,8 +64,9 @@ class _Unit:
         self.full = self.shard * world
 
 
-class _Boundary(torch.autograd.Function):
-    """Identity whose backward tells the sharding engine that a block's backward begins or ends."""
+class BlockBoundary(torch.autograd.Function):
+    """Identity whose backward tells ``engine`` (the sharding engine, or the data-parallel reducer) that a
+    block's backward begins (``where="out"``) or ends (``where="in"``)."""
 
     @staticmethod
     def forward(ctx, x, engine, i, where):
@@ -309,13 +310,13 @@ class ShardedFlat:
         if i + 1 < self.n_blocks:
             self._fetch(i + 1, after=("fwd", i - 1))
         if torch.is_grad_enabled() and x.requires_grad:
-            x = _Boundary.apply(x, self, i, "in")
+            x = BlockBoundary.apply(x, self, i, "in")
         return x
 
     def post_block(self, i: int, x: torch.Tensor) -> torch.Tensor:
         self._record(("fwd", i))
         if torch.is_grad_enabled() and x.requires_grad:
-            x = _Boundary.apply(x, self, i, "out")
+            x = BlockBoundary.apply(x, self, i, "out")
         return x
 
     # ------------------------------------------------------------------ backward hooks

@@ -367,11 +367,43 @@ class RolloutWorker(TQWorker):
         while not self.stopped:
             n = await self.tq_call(lambda: self._aclient.num_rows(part))
             if n == 0:
-                return
+                break
             if deadline is not None and time.monotonic() > deadline:
                 log.warning("drain: %d rows still unconsumed in %s", n, part)
                 return
             await asyncio.sleep(self.poll_interval)
+        await self.await_final_weights()
+
+    async def await_final_weights(self, timeout: float | None = None) -> None:
+        """After the last step: wait until every engine serves the trainer's final weights. The trainer hands
+        them over after clearing its batch (through the card's colocation ring when colocated), so ending the
+        run at once would tear the engines down in the middle of that hand-over."""
+        timeout = float(os.environ.get("XRL_FINAL_SYNC_TIMEOUT", "60")) if timeout is None else timeout
+        versions = getattr(self.engine, "weight_versions", None)
+        if versions is None or timeout <= 0:
+            return
+        while not self.stopped:  # the gates raised since the last generation slot (no snapshot: the run ends)
+            data = await self.read_tq_control("gen_gate")
+            if data is None:
+                break
+            self.gates_seen += 1
+            self.weight_version = int(data["weight_version"][0].reshape(-1)[0])
+        want = self.weight_version
+        if want is None:
+            return
+        deadline = time.monotonic() + timeout
+        have = None
+        while not self.stopped:
+            try:
+                have = await asyncio.to_thread(versions)
+            except Exception as e:  # noqa: BLE001 - an engine that is down ends the wait at the deadline
+                have = repr(e)
+            if isinstance(have, list) and all(v is not None and int(v) >= want for v in have):
+                return
+            if time.monotonic() > deadline:
+                log.warning("final weights v%d not on every engine after %.0f s (engines: %s)", want, timeout, have)
+                return
+            await asyncio.sleep(min(self.poll_interval, 0.5))
 
 
 __all__ = ["GRPO_FIELDS", "GRPO_FIELDS_NO_ADVANTAGE", "RAW_REWARD_FIELD", "RolloutWorker", "TrajectoryLogger",
