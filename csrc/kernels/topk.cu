@@ -3,9 +3,9 @@
 //   topk_logprobs   per row of fp32 logits z [T, V]: the K largest entries (sorted, largest first) and their
 //                   log-probabilities z - logsumexp(z). One CTA per row. The K-th largest value is found
 //                   exactly by a 4-pass radix select over the order-preserving integer image of the floats
-//                   (8-bit digits, 256-bin shared-memory histograms; the first pass also folds the row's max
-//                   and sum of exponentials), then one pass collects the K winners and a bitonic sort in
-//                   shared memory orders them.
+//                   (8-bit digits, 256-bin shared-memory histograms with warp-aggregated counts; the first
+//                   pass also folds the row's max and sum of exponentials), then one pass collects the K
+//                   winners and a bitonic sort in shared memory orders them.
 //   gather_logprobs z[t, ids[t, k]] - lse[t] without the logits: one warp per (t, k) takes the dot product of
 //                   the hidden row and the vocabulary row of the weight (fp32 accumulation of bf16 products).
 //   scatter_add_rows  dz[t, ids[t, k]] += g[t, k] in bf16 (one thread per row, so repeated ids in a row add
@@ -27,6 +27,35 @@ __device__ __forceinline__ uint32_t okey(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// One element's share of a radix pass: the row's online max / sum of exponentials on the first pass, and a
+// count in the histogram bin of its digit when it still matches the selected prefix. Lanes of a warp whose
+// elements fall in the same bin add once, through their lowest lane: logits occupy few exponent bins, so
+// one shared-memory atomic per lane would serialise up to 32-fold on one address. All 32 lanes call this
+// together (``valid`` false for the lanes past the row's end).
+__device__ __forceinline__ void radix_count(float v, bool valid, bool first, uint32_t prefix, uint32_t pmask,
+                                            int shift, float& m, float& s, unsigned* hist, int lane) {
+  bool take = false;
+  uint32_t bin = 0u;
+  if (valid) {
+    if (first) {
+      if (v > m) {
+        s = s * __expf(m - v) + 1.f;
+        m = v;
+      } else {
+        s += __expf(v - m);
+      }
+    }
+    const uint32_t u = okey(v);
+    take = (u & pmask) == prefix;
+    bin = (u >> shift) & 255u;
+  }
+  const unsigned takers = __ballot_sync(0xffffffffu, take);
+  if (take) {
+    const unsigned peers = __match_any_sync(takers, bin);
+    if (__ffs(peers) - 1 == lane) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+  }
+}
+
 __global__ void __launch_bounds__(kTopkThreads)
     topk_logprobs_kernel(const float* __restrict__ z, long long ldz, int V, int K, int64_t* __restrict__ ids,
                          float* __restrict__ lp, float* __restrict__ lse_out) {
@@ -44,22 +73,31 @@ __global__ void __launch_bounds__(kTopkThreads)
   uint32_t prefix = 0u, pmask = 0u;
   int kr = K;  // how many of the remaining candidates (those matching the prefix) are still to be taken
   float m = -INFINITY, s = 0.f;
+  // 16-byte loads when the rows allow them (blockDim.x is a multiple of 32, so every warp runs the same
+  // number of iterations and stays converged at the warp votes in radix_count)
+  const bool vec = (ldz % 4 == 0) && (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(z) & 15u) == 0u);
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0u;
     __syncthreads();
-    for (int i = tid; i < V; i += blockDim.x) {
-      const float v = zr[i];
-      if (shift == 24) {
-        // online max / sum of exponentials for the row's log-sum-exp
-        if (v > m) {
-          s = s * __expf(m - v) + 1.f;
-          m = v;
-        } else {
-          s += __expf(v - m);
-        }
+    const bool first = shift == 24;
+    if (vec) {
+      const float4* z4 = reinterpret_cast<const float4*>(zr);
+      const int V4 = V / 4;
+      for (int j0 = 0; j0 < V4; j0 += blockDim.x) {
+        const int j = j0 + tid;
+        const bool ok = j < V4;
+        const float4 q = ok ? z4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        radix_count(q.x, ok, first, prefix, pmask, shift, m, s, hist, lane);
+        radix_count(q.y, ok, first, prefix, pmask, shift, m, s, hist, lane);
+        radix_count(q.z, ok, first, prefix, pmask, shift, m, s, hist, lane);
+        radix_count(q.w, ok, first, prefix, pmask, shift, m, s, hist, lane);
       }
-      const uint32_t u = okey(v);
-      if ((u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
+    } else {
+      for (int i0 = 0; i0 < V; i0 += blockDim.x) {
+        const int i = i0 + tid;
+        const bool ok = i < V;
+        radix_count(ok ? zr[i] : 0.f, ok, first, prefix, pmask, shift, m, s, hist, lane);
+      }
     }
     __syncthreads();
     if (warp == 0) {
