@@ -85,6 +85,8 @@ class CriticTrainer:
             self.cp = CpSharder(cp_group)
         self.loss_group = loss_group if loss_group is not None else dp_group
         self.reducer = GradReducer(self.flat, self.loss_group)
+        if self.reducer.overlapping and self.train_backbone:
+            self.model.backbone.block_hooks = self.reducer  # per-block all-reduce in the last micro's backward
         self.train_steps = 0
 
     # ------------------------------------------------------------------ helpers
@@ -192,8 +194,12 @@ class CriticTrainer:
         lr = self._apply_warmup()
         micros = self._micros(samples, rows)
         # the denominator counts every response token of the window once (full rows, summed over DP)
-        local_cnt = torch.tensor(float(sum(float(mb.mask.sum()) for mb in micros)))
-        denom = float(self._all_sum(local_cnt).clamp(min=1.0))
+        # with it, how many DP ranks have a micro-batch: the per-block gradient all-reduces started inside the
+        # last micro's backward only line up across ranks when every rank runs one
+        local = torch.tensor([float(sum(float(mb.mask.sum()) for mb in micros)), 1.0 if micros else 0.0])
+        tot = self._all_sum(local)
+        denom = float(tot[0].clamp(min=1.0))
+        overlap = self.train_backbone and self.reducer.overlapping and int(tot[1]) == self.dp_world
         if self.cp is not None:
             micros = [self._cp_shard(mb) for mb in micros]
         self.flat.zero_grad()
@@ -204,7 +210,9 @@ class CriticTrainer:
         values: dict[int, torch.Tensor] = {}
         num = torch.zeros((), dtype=torch.float64)
         d = self.device
-        for mb in micros:
+        for i, mb in enumerate(micros):
+            if overlap and i == len(micros) - 1:
+                self.reducer.arm()
             with torch.set_grad_enabled(True):
                 with torch.set_grad_enabled(self.train_backbone):
                     h = self._hidden(mb)
