@@ -4,7 +4,8 @@ A recipe is a module exporting ``SERVICE_GROUPS``, ``COLOCATIONS`` and
 ``main()`` (reference ``recipe/justrl.py:154-167``).  Most recipes are one of
 three graphs, which :func:`grpo_graph` builds:
 
-* **colocated** (``colocate=True``): ``n_infer`` single-card inference replicas
+* **colocated** (``colocate=True``): ``n_infer`` single-card inference replicas (or ``n_infer / infer_tp``
+  tensor-parallel ones)
   and one trainer replica on the same cards, handing them over through a
   FALLBACK (inference) / ON_DEMAND (trainer [, critic]) ring;
 * **disaggregated** (``colocate=False``): inference on the first ``n_infer``
@@ -40,12 +41,15 @@ def grpo_graph(*, model: str, model_path: str | None, trainer_config: TrainerCon
                oversample_factor: float = 1.0, num_epochs: int = 1,
                trainer_service: type = TrainingServiceConfig, trainer_extra: dict | None = None,
                extra_groups: list[ServiceGroup] | None = None, ring_extra: list[tuple[str, Any]] | None = None,
-               critic_colocate: bool | None = None, n_critic: int | None = None, rollout_extra: dict | None = None):
+               critic_colocate: bool | None = None, n_critic: int | None = None, rollout_extra: dict | None = None,
+               infer_tp: int = 1):
     """Service groups and colocation rings of one GRPO / PPO run (see the module docstring).
 
     ``critic_colocate=False`` gives the critic its own ``n_critic`` cards (declared after the
     inference cards, so they follow them); ``rollout_extra`` passes further
     :class:`RolloutServiceConfig` fields (``advantage_kwargs``, ``verbose_trajectory_log`` ...).
+    ``infer_tp`` > 1 makes each inference replica a tensor-parallel group of that many cards (the ``n_infer``
+    cards then hold ``n_infer / infer_tp`` replicas).
     """
     if stream_minibatch and colocate:
         raise ValueError("stream_minibatch needs disaggregated cards (it is incompatible with colocation)")
@@ -53,7 +57,10 @@ def grpo_graph(*, model: str, model_path: str | None, trainer_config: TrainerCon
     ckpt = checkpoint or GlobalCheckpointConfig()
     sargs = {"model": model, "tp_size": 1}
     sargs.update(server_args or {})
-    infer = ServiceGroup(id="actor_infer", n_replicas=n_infer, n_gpus_per_replica=1,
+    if infer_tp < 1 or n_infer % infer_tp:
+        raise ValueError(f"{n_infer} inference cards do not split into replicas of {infer_tp}")
+    sargs["tp_size"] = infer_tp
+    infer = ServiceGroup(id="actor_infer", n_replicas=n_infer // infer_tp, n_gpus_per_replica=infer_tp,
                          config=InferenceServiceConfig(model_path=model_path, server_args=sargs))
     groups = [infer]
     ring = [("actor_infer", SchedulingMode.FALLBACK)]
@@ -100,6 +107,36 @@ def grpo_graph(*, model: str, model_path: str | None, trainer_config: TrainerCon
 __all__ = ["grpo_graph"]
 
 
+def model_from_env(name: str, flavor: str, *, path_env: str = "XRL_MODEL") -> tuple[str, str, str | None]:
+    """``(registry name, flavor, checkpoint dir or None)`` of a recipe's model, with the reference recipes'
+    variables: ``XRL_MODEL`` names the checkpoint (a local directory; a hub id without a local copy gives
+    random-init weights of the architecture, there being no network), ``XRL_MODEL_NAME`` / ``XRL_MODEL_FLAVOR``
+    the architecture. ``XRL_MODEL=name:flavor`` (a registry spec, no such directory) also selects the
+    architecture; ``MODEL_PATH`` is accepted as the checkpoint too."""
+    import os
+
+    spec = os.environ.get(path_env, "")
+    path = os.environ.get("MODEL_PATH") or None
+    if spec and ":" in spec and "/" not in spec and not os.path.isdir(spec):
+        name, flavor = spec.split(":", 1)
+    elif spec:
+        path = spec
+    name = os.environ.get("XRL_MODEL_NAME", name)
+    flavor = os.environ.get("XRL_MODEL_FLAVOR", flavor)
+    path = os.path.abspath(os.path.expanduser(path)) if path and os.path.isdir(os.path.expanduser(path)) else None
+    return name, flavor, path
+
+
+def checkpoint_from_env(interval: int = 10, keep_latest_k: int = 2, enabled: bool = True) -> GlobalCheckpointConfig:
+    """Global checkpoint policy with the reference recipes' switches: ``XRL_CHECKPOINT`` (``0`` / ``false`` /
+    empty turn it off), ``XRL_CHECKPOINT_INTERVAL``, ``XRL_CHECKPOINT_KEEP``."""
+    import os
+
+    on = os.environ.get("XRL_CHECKPOINT", "1" if enabled else "0").strip().lower() not in ("0", "false", "")
+    return GlobalCheckpointConfig(enabled=on, interval=int(os.environ.get("XRL_CHECKPOINT_INTERVAL", interval)),
+                                  keep_latest_k=int(os.environ.get("XRL_CHECKPOINT_KEEP", keep_latest_k)))
+
+
 def local_model_path(env: str = "MINICPM5_LOCAL_PATH", default: str | None = None) -> str | None:
     """Checkpoint directory from ``env`` (``None``: random-init weights of the named architecture)."""
     import os
@@ -108,4 +145,4 @@ def local_model_path(env: str = "MINICPM5_LOCAL_PATH", default: str | None = Non
     return os.path.abspath(os.path.expanduser(p)) if p else None
 
 
-__all__.append("local_model_path")
+__all__ += ["checkpoint_from_env", "local_model_path", "model_from_env"]

@@ -12,9 +12,9 @@ from __future__ import annotations
 
 import os
 
-from meshy_b200.config import (CriticServiceConfig, GlobalCheckpointConfig, SamplingParams, TrainerConfig,
+from meshy_b200.config import (CriticServiceConfig, SamplingParams, TrainerConfig,
                                TrainerParamsConfig)
-from meshy_b200.recipe_lib import grpo_graph, local_model_path
+from meshy_b200.recipe_lib import checkpoint_from_env, grpo_graph, local_model_path
 from meshy_b200.service.ignite import Ignitor
 
 MODEL_PATH = local_model_path()
@@ -26,7 +26,7 @@ BATCH_SIZE = ROLLOUT_BATCH * GROUP_SIZE
 SEQ_LEN = 4096
 MAX_NEW_TOKENS = 1024
 COLD_START_WINDOWS = int(os.environ.get("XRL_COLD_START_WINDOWS", "2"))
-CHECKPOINT = GlobalCheckpointConfig(enabled=True, interval=10, keep_latest_k=2)
+CHECKPOINT = checkpoint_from_env(interval=10, keep_latest_k=3)  # XRL_CHECKPOINT / _INTERVAL / _KEEP
 
 
 def _tc(folder: str, ckpt: str = "selective", shard: int = NUM_INFERENCE_ENGINES) -> TrainerConfig:

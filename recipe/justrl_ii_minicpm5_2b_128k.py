@@ -20,9 +20,9 @@ from __future__ import annotations
 
 import os
 
-from meshy_b200.config import (CriticServiceConfig, GlobalCheckpointConfig, SamplingParams, TrainerConfig,
+from meshy_b200.config import (CriticServiceConfig, SamplingParams, TrainerConfig,
                                TrainerParamsConfig)
-from meshy_b200.recipe_lib import grpo_graph, local_model_path
+from meshy_b200.recipe_lib import checkpoint_from_env, grpo_graph, local_model_path
 from meshy_b200.service.ignite import Ignitor
 
 SEQ_LEN = 131072
@@ -51,7 +51,7 @@ def trainer_params() -> TrainerParamsConfig:
 def build(ngpus: int = 8, critic_colocate: bool = True, n_critic: int | None = None):
     cold = int(os.environ.get("XRL_COLD_START_WINDOWS", "20"))
     score_batch = int(os.environ.get("XRL_CRITIC_SCORE_BATCH", str(BATCH_SIZE)))
-    ckpt = GlobalCheckpointConfig(enabled=True, interval=10, keep_latest_k=2)
+    ckpt = checkpoint_from_env(interval=10, keep_latest_k=3)  # XRL_CHECKPOINT / _INTERVAL / _KEEP
     path = local_model_path()
     n_critic = n_critic or ngpus
     if ngpus % CP or n_critic % CP:

@@ -41,8 +41,8 @@ SCORE_BATCH = int(os.environ.get("XRL_SCORE_BATCH", str(BATCH_SIZE)))
 
 def _tc(name: str, flavor: str, folder: str) -> TrainerConfig:
     return TrainerConfig(model_name=name, model_flavor=flavor, seq_len=SEQ_LEN, lr=float(os.environ.get("XRL_LR", "1e-6")),
-                         weight_decay=0.0, dtype="bfloat16", dp_shard_degree=-1, dp_replicate_degree=1,
-                         dump_folder=folder)
+                         steps=int(os.environ.get("XRL_STEPS", "1000")), weight_decay=0.0, dtype="bfloat16",
+                         dp_shard_degree=-1, dp_replicate_degree=1, dump_folder=folder)
 
 
 def _teacher() -> OPDTeacherConfig:
@@ -85,8 +85,16 @@ def build_service_groups() -> list[ServiceGroup]:
         rest = NGPUS - n_teacher
         if rest < 2:
             raise ValueError(f"disaggregate needs at least 2 cards besides the teacher's {n_teacher}")
-        n_infer = int(os.environ.get("XRL_INFER_GPUS", str(rest // 2)))
-        n_train = rest - n_infer
+        # the reference's split: XRL_TRAIN_GPUS trainer cards (default half, rounded down), the rest inference;
+        # XRL_INFER_GPUS sets the inference side instead
+        if "XRL_INFER_GPUS" in os.environ and "XRL_TRAIN_GPUS" not in os.environ:
+            n_infer = int(os.environ["XRL_INFER_GPUS"])
+            n_train = rest - n_infer
+        else:
+            n_train = int(os.environ.get("XRL_TRAIN_GPUS", str(max(1, rest // 2))))
+            n_infer = rest - n_train
+        if n_infer < 1 or n_train < 1:
+            raise ValueError(f"disaggregate needs at least 1 inference and 1 trainer card (got {n_infer} / {n_train})")
         return [ServiceGroup(id="actor_infer", n_replicas=n_infer, n_gpus_per_replica=1, config=_infer(n_infer)),
                 ServiceGroup(id="teacher", n_replicas=1, n_gpus_per_replica=n_teacher, wait_until=["actor_infer"],
                              config=_teacher()),
