@@ -10,9 +10,13 @@ Inside, the B200 design:
 
 * parameters, gradients and optimiser states are flat buffers
   (:mod:`.flat`); kernels accumulate weight gradients in fp32 directly;
-* the data-parallel gradient reduction is one bucketed collective over the
-  flat gradient (:mod:`meshy_b200.parallel.ddp`: the fused NVLink kernel on a
-  single node, NCCL otherwise), overlapped with the tail of backward;
+* the data-parallel gradient reduction works on the flat gradient: on one
+  node the fused NVLink optimiser step (:mod:`meshy_b200.parallel.symm`:
+  reduce-scatter, norm, AdamW on the shard, all-gather) runs after the
+  backward; otherwise per-block NCCL all-reduces start inside the last
+  micro-batch's backward (:mod:`meshy_b200.parallel.ddp`); with sharded
+  parameters (:mod:`meshy_b200.parallel.fsdp`) each block's gradient is
+  reduce-scattered as its backward ends;
 * the log-prob head is the fused LM-head kernel (no ``[T, V]`` logits), the
   loss is the fused PPO kernel, the step is one AdamW kernel that can also
   write the bf16 weights of a colocated rollout engine (weight sync).
