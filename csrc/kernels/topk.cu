@@ -5,7 +5,8 @@
 //                   exactly by a 4-pass radix select over the order-preserving integer image of the floats
 //                   (8-bit digits, 256-bin shared-memory histograms with warp-aggregated counts; the first
 //                   pass also folds the row's max and sum of exponentials), then one pass collects the K
-//                   winners and a bitonic sort in shared memory orders them.
+//                   winners and a bitonic sort in shared memory orders them. For K <= 8 one read of the row
+//                   suffices: per-thread register lists of the 8 largest, merged by warp maxima.
 //   gather_logprobs z[t, ids[t, k]] - lse[t] without the logits: one warp per (t, k) takes the dot product of
 //                   the hidden row and the vocabulary row of the weight (fp32 accumulation of bf16 products).
 //   scatter_add_rows  dz[t, ids[t, k]] += g[t, k] in bf16 (one thread per row, so repeated ids in a row add
@@ -209,6 +210,120 @@ __global__ void __launch_bounds__(kTopkThreads)
   if (lse_out && tid == 0) lse_out[row] = lse;
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// Small K (K <= kSmallK): one read of the row. Every thread keeps the kSmallK largest of the elements it visits
+// as 64-bit keys (order-preserving image of the value in the high half, 0x7fffffff - index in the low half,
+// so equal values rank by ascending index and every key is unique), then warps and finally warp 0 merge the
+// per-thread lists by repeated warp maxima. The row's log-sum-exp is folded into the same read.
+
+constexpr int kSmallK = 8;
+
+__device__ __forceinline__ unsigned long long topk_key(float v, int i) {
+  return (static_cast<unsigned long long>(okey(v)) << 32) | static_cast<unsigned>(0x7fffffff - i);
+}
+
+__device__ __forceinline__ float key_value(unsigned long long k) {
+  const uint32_t u = static_cast<uint32_t>(k >> 32);
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
+__device__ __forceinline__ void small_visit(float v, int i, float& m, float& s, unsigned long long (&keys)[kSmallK]) {
+  if (v > m) {
+    s = s * __expf(m - v) + 1.f;
+    m = v;
+  } else {
+    s += __expf(v - m);
+  }
+  unsigned long long k = topk_key(v, i);
+  if (k > keys[kSmallK - 1]) {  // rare once the list has filled: insert, carrying the displaced key down
+#pragma unroll
+    for (int j = 0; j < kSmallK; ++j) {
+      if (k > keys[j]) {
+        const unsigned long long t = keys[j];
+        keys[j] = k;
+        k = t;
+      }
+    }
+  }
+}
+
+// The warp's kSmallK largest keys (each lane's list sorted descending) into out[0..kSmallK) by lane 0.
+__device__ __forceinline__ void warp_merge_keys(unsigned long long (&keys)[kSmallK], unsigned long long* out,
+                                                int lane) {
+#pragma unroll
+  for (int r = 0; r < kSmallK; ++r) {
+    unsigned long long best = keys[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) out[r] = best;
+    if (best != 0ull && keys[0] == best) {  // keys are unique: exactly one lane pops its head
+#pragma unroll
+      for (int j = 0; j < kSmallK - 1; ++j) keys[j] = keys[j + 1];
+      keys[kSmallK - 1] = 0ull;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kTopkThreads)
+    topk_small_kernel(const float* __restrict__ z, long long ldz, int V, int K, int64_t* __restrict__ ids,
+                      float* __restrict__ lp, float* __restrict__ lse_out) {
+  __shared__ unsigned long long wtop[32][kSmallK];
+  __shared__ unsigned long long top[kSmallK];
+  __shared__ float red_m[32], red_s[32];
+  const int row = blockIdx.x;
+  const float* zr = z + (size_t)row * ldz;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nwarps = blockDim.x / 32;
+  unsigned long long keys[kSmallK];
+#pragma unroll
+  for (int j = 0; j < kSmallK; ++j) keys[j] = 0ull;  // below every real key (okey(-inf) > 0)
+  float m = -INFINITY, s = 0.f;
+  if ((ldz % 4 == 0) && (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(z) & 15u) == 0u)) {
+    const float4* z4 = reinterpret_cast<const float4*>(zr);
+    for (int j = tid; j < V / 4; j += blockDim.x) {
+      const float4 q = z4[j];
+      small_visit(q.x, 4 * j, m, s, keys);
+      small_visit(q.y, 4 * j + 1, m, s, keys);
+      small_visit(q.z, 4 * j + 2, m, s, keys);
+      small_visit(q.w, 4 * j + 3, m, s, keys);
+    }
+  } else {
+    for (int i = tid; i < V; i += blockDim.x) small_visit(zr[i], i, m, s, keys);
+  }
+  warp_merge_keys(keys, wtop[warp], lane);
+  {
+    float mm = m;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+    float ss = (m == -INFINITY) ? 0.f : s * __expf(m - mm);
+    ss = warp_sum(ss);
+    if (lane == 0) {
+      red_m[warp] = mm;
+      red_s[warp] = ss;
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  unsigned long long k2[kSmallK];
+#pragma unroll
+  for (int j = 0; j < kSmallK; ++j) k2[j] = lane < nwarps ? wtop[lane][j] : 0ull;
+  warp_merge_keys(k2, top, lane);
+  float gm = -INFINITY;
+  for (int w = 0; w < nwarps; ++w) gm = fmaxf(gm, red_m[w]);
+  float gs = 0.f;
+  for (int w = 0; w < nwarps; ++w) gs += (red_m[w] == -INFINITY) ? 0.f : red_s[w] * __expf(red_m[w] - gm);
+  const float lse = gm + __logf(gs);
+  __syncwarp();
+  if (lane < K) {
+    const unsigned long long k = top[lane];
+    ids[(size_t)row * K + lane] = 0x7fffffff - static_cast<int>(k & 0xffffffffull);
+    lp[(size_t)row * K + lane] = key_value(k) - lse;
+  }
+  if (lse_out && lane == 0) lse_out[row] = lse;
+}
+
 __global__ void gather_logprobs_kernel(const bf16* __restrict__ h, long long ldh, const bf16* __restrict__ w,
                                        long long ldw, int D, int V, const int64_t* __restrict__ ids, int TK,
                                        int K, const float* __restrict__ lse, float* __restrict__ lp) {
@@ -255,7 +370,10 @@ void topk_logprobs(const float* z, long long ldz, int T, int V, int K, int64_t* 
                    cudaStream_t st) {
   MESHY_CHECK(K >= 1 && K <= kTopkMax && K <= V, "topk_logprobs: need 1 <= K <= min(1024, V)");
   if (T == 0) return;
-  topk_logprobs_kernel<<<T, kTopkThreads, 0, st>>>(z, ldz, V, K, ids, lp, lse);
+  if (K <= kSmallK)
+    topk_small_kernel<<<T, kTopkThreads, 0, st>>>(z, ldz, V, K, ids, lp, lse);
+  else
+    topk_logprobs_kernel<<<T, kTopkThreads, 0, st>>>(z, ldz, V, K, ids, lp, lse);
   MESHY_CUDA_CHECK(cudaGetLastError());
 }
 
