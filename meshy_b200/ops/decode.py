@@ -39,6 +39,9 @@ from .functional import native
 
 def kv_write(k, v, k_cache, v_cache, slot_mapping):
     """``k/v [B, Hkv, hd]`` → cache ``[n_pages, Hkv, page, hd]`` at ``slot_mapping [B]``."""
+    from .checks import check_range
+
+    check_range("KV-cache slots", slot_mapping, 0, k_cache.shape[0] * k_cache.shape[2])
     if native(k):
         from ._ext import ext
 
@@ -61,7 +64,9 @@ def qkv_rope_to_cache(qkv, positions, q_norm, k_norm, n_heads, n_kv, hd, theta, 
     T = qkv.shape[0]
     if native(qkv):
         from ._ext import ext
+        from .checks import check_range
 
+        check_range("KV-cache slots", slot_mapping, 0, k_cache.shape[0] * k_cache.shape[2])
         q = torch.empty(T, n_heads, hd, dtype=qkv.dtype, device=qkv.device)
         k = torch.empty(T, n_kv, hd, dtype=qkv.dtype, device=qkv.device) if keep_kv else None
         v = torch.empty(T, n_kv, hd, dtype=qkv.dtype, device=qkv.device) if keep_kv else None
@@ -116,7 +121,9 @@ def qkv_rope_fused(x, w, bias, positions, q_norm, k_norm, n_heads, n_kv, theta, 
     if not native(x) or w.shape[0] != (n_heads + 2 * n_kv) * 128 or k_cache.shape[-1] != 128:
         return None
     from ._ext import ext
+    from .checks import check_range
 
+    check_range("KV-cache slots", slot_mapping, 0, k_cache.shape[0] * k_cache.shape[2])
     T = x.shape[0]
     q = torch.empty(T, n_heads, 128, dtype=x.dtype, device=x.device)
     ok = ext().gemm_qkv_rope(x, w, bias, part, (d + 127) // 128 if part is not None else 0, float(d), float(eps),
@@ -129,6 +136,9 @@ def paged_attention(q, k_cache, v_cache, block_table, seq_lens, scale=None, work
     """Decode attention of ``q [B, Hq, hd]`` over each row's paged K/V. ``decode_step``: the op just
     before wrote only each row's newest K/V row (its position ``seq_lens - 1``) and neither the block
     table nor the lengths, so the kernel may load the older pages before that op has finished."""
+    from .checks import check_paged
+
+    check_paged("paged attention", block_table, seq_lens, k_cache.shape[0], k_cache.shape[2])
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if native(q):
         from ._ext import ext

@@ -439,6 +439,9 @@ class _LMHeadLogprob(torch.autograd.Function):
 
 
 def lm_head_logprobs(h, w, labels, with_entropy: bool = True, chunk: int = 4096):
+    from .checks import check_range
+
+    check_range("LM-head labels", labels, 0, w.shape[0])
     if native(h):
         return _LMHeadLogprob.apply(h, w, labels, with_entropy, chunk)
     if h.is_cuda:  # torch baseline
@@ -489,6 +492,9 @@ class _Embedding(torch.autograd.Function):
 
 
 def embedding(ids, w):
+    from .checks import check_range
+
+    check_range("embedding token ids", ids, 0, w.shape[0])
     if native(w):
         return _Embedding.apply(ids, w)
     return F.embedding(ids, w)

@@ -140,6 +140,9 @@ class _Experts(torch.autograd.Function):
 
 def experts_forward(x, weights, experts, w13, w2, block: int):
     """Routed-expert output ``sum_j w[t, j] * SwiGLU_{e_tj}(x[t])`` on the native kernels."""
+    from .checks import check_range
+
+    check_range("MoE expert ids", experts, 0, w13.shape[0])
     return _Experts.apply(x, weights, experts, w13, w2, block)
 
 
