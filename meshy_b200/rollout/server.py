@@ -291,6 +291,7 @@ def _tp_rank_setup(a, rank: int):
 
     host, port = _rendezvous(a)
     os.environ.update(MASTER_ADDR=host, MASTER_PORT=str(port))
+    os.environ.pop("TORCHELASTIC_USE_AGENT_STORE", None)  # rank 0 hosts this rendezvous itself
     cuda = a.device.startswith("cuda")
     device = torch.device("cuda", rank - _local_ranks(a).start) if cuda else torch.device("cpu")
     kw = {"device_id": device} if cuda else {}
@@ -357,7 +358,10 @@ def _serve_tp(a) -> None:
     try:
         serve(eng, a.host, a.port, a.model_path or a.model)
     finally:
-        eng.stop()
+        try:
+            eng.stop()
+        except Exception:  # noqa: BLE001 - at teardown the followers got the same signal and are gone already
+            pass
         for p_ in procs:
             p_.join(timeout=30)
 

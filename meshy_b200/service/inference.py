@@ -30,6 +30,10 @@ from .base import Service, die_with_parent
 
 log = logging.getLogger(__name__)
 
+_TORCHRUN_VARS = frozenset({"RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "GROUP_WORLD_SIZE",
+                            "ROLE_RANK", "ROLE_WORLD_SIZE", "ROLE_NAME", "MASTER_ADDR", "MASTER_PORT",
+                            "TORCH_NCCL_ASYNC_ERROR_HANDLING"})
+
 # SGLang-style server_args key -> rollout.server flag
 _ARG_MAP = {
     "max_running_requests": "--max-running",
@@ -132,10 +136,11 @@ class InferenceService(Service):
     def ignite(self) -> None:
         if not self.is_node_leader:
             return
-        env = dict(os.environ)
-        for v in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT", "GROUP_RANK",
-                  "TORCHELASTIC_RUN_ID", "LOCAL_WORLD_SIZE"):
-            env.pop(v, None)
+        # none of the ignitor's torchrun variables reach the server: with TORCHELASTIC_USE_AGENT_STORE set, a
+        # tensor-parallel replica's rank 0 would wait for an agent store on its rendezvous port instead of
+        # hosting it
+        env = {k: v for k, v in os.environ.items()
+               if k not in _TORCHRUN_VARS and not k.startswith("TORCHELASTIC_")}
         if env.get("XRL_DEVICE", "cuda") == "cuda":
             env["CUDA_VISIBLE_DEVICES"] = ",".join(str(g.local_rank) for g in self.node_gpus)
         log_path = self.runtime.process_log_path(self.name, self.rank_in_replica)

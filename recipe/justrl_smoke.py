@@ -1,7 +1,8 @@
 """Smoke recipe: the JustRL service graph on a tiny Qwen3 (2 cards, CPU or GPU).
 
-Same shape as ``recipe.justrl`` -- per-card inference replicas colocated with
-one DDP trainer in a FALLBACK / ON_DEMAND ring, plus the CPU rollout driver --
+Same shape as ``recipe.justrl`` -- per-card inference replicas (``XRL_SMOKE_INFER_TP`` cards each:
+tensor-parallel replicas) colocated with one DDP trainer in a FALLBACK / ON_DEMAND ring, plus the CPU
+rollout driver --
 on ``qwen3:debugmodel`` with synthetic token prompts and the parity reward,
 for a few steps.  ``XRL_DEVICE=cpu`` runs it without a GPU (gloo):
 
@@ -29,6 +30,7 @@ CKPT = GlobalCheckpointConfig(enabled=os.environ.get("XRL_SMOKE_CKPT", "0") == "
 
 
 SHARD = os.environ.get("XRL_SMOKE_SHARD", "0") == "1"  # FSDP over the trainer's cards instead of DDP
+INFER_TP = int(os.environ.get("XRL_SMOKE_INFER_TP", "1"))  # cards per inference replica (tensor parallel)
 
 
 def _trainer_config() -> TrainerConfig:
@@ -39,7 +41,7 @@ def _trainer_config() -> TrainerConfig:
 
 
 SERVICE_GROUPS = [
-    ServiceGroup(id="actor_infer", n_replicas=CARDS, n_gpus_per_replica=1,
+    ServiceGroup(id="actor_infer", n_replicas=CARDS // INFER_TP, n_gpus_per_replica=INFER_TP,
                  config=InferenceServiceConfig(model_path=None, server_args={
                      "model": MODEL, "max_running_requests": 16, "max_total_tokens": 8192, "context_length": 512})),
     ServiceGroup(id="actor_train", n_replicas=1, n_gpus_per_replica=CARDS, colocate_with="actor_infer",

@@ -55,6 +55,29 @@ def test_launcher_runs_colocated_grpo_on_cpu(tmp_path):
 
 
 @pytest.mark.timeout(600)
+def test_launcher_runs_tensor_parallel_inference_replica_on_cpu(tmp_path):
+    """The ring with ONE inference replica over both cards (``--tp-size 2``: the service starts the server,
+    which spawns its follower rank): the replica serves the rollout, releases and restores its memory in
+    lock-step, loads every weight version and the run finishes."""
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", XRL_SMOKE_INFER_TP="2", PYTHONPATH=ROOT,
+               XRL_PORT_OFFSET=_port_offset())
+    rt = tmp_path / "rt"
+    r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
+                        "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=540)
+    logs = rt / "logs"
+    detail = r.stdout[-2000:] + r.stderr[-2000:]
+    if logs.exists():
+        for f in sorted(logs.iterdir()):
+            detail += f"\n==== {f.name}\n" + f.read_text(errors="replace")[-1500:]
+    assert r.returncode == 0, detail
+    rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
+    assert len(rows) == 2, detail
+    assert (logs / "actor_infer-0-0.log").exists() and not (logs / "actor_infer-1-0.log").exists(), detail
+    assert (logs / "ignitor-0.log").read_text().count("colocation transfer actor_infer -> actor_train") == 2, detail
+
+
+@pytest.mark.timeout(600)
 def test_launcher_runs_sharded_trainer_on_cpu(tmp_path):
     """The same ring with the trainer's parameters sharded over its two ranks (FSDP): weights still reach
     the engines every step (gathered into the full layout) and the run checkpoints and finishes."""
