@@ -112,7 +112,12 @@ def main(argv=None) -> int:
         store.wait([ENDPOINT_KEY])
         os.environ["XRL_TQ_ENDPOINTS"] = store.get(ENDPOINT_KEY).decode()
 
-    proc = subprocess.Popen(torchrun_cmd(args, nproc), env=dict(os.environ), start_new_session=True)
+    from .service.base import die_with_parent
+
+    # torchrun gets SIGTERM if this launcher dies without forwarding a signal (SIGKILL, a crash): it then
+    # stops its ignitors, whose engines and servers follow them the same way
+    proc = subprocess.Popen(torchrun_cmd(args, nproc), env=dict(os.environ), start_new_session=True,
+                            preexec_fn=lambda: die_with_parent(signal.SIGTERM))
 
     def forward(signum, frame):
         try:
@@ -125,6 +130,12 @@ def main(argv=None) -> int:
     try:
         return proc.wait()
     finally:
+        if proc.poll() is None:  # leaving on an exception: take the run down with us
+            forward(signal.SIGTERM, None)
+            try:
+                proc.wait(timeout=60)
+            except subprocess.TimeoutExpired:
+                forward(signal.SIGKILL, None)
         if cluster is not None:
             cluster.stop()
 
