@@ -7,7 +7,8 @@
   point back to the newest step that every participant committed;
 * the engine client against a server that is down retries a bounded number of times and then raises; against a
   server that fails twice it succeeds on the third attempt; a server returning non-finite log-probs is rejected;
-  an aborted generation is continued from where it stopped.
+  an aborted generation is continued from where it stopped;
+* a launcher killed with SIGKILL takes torchrun, the ignitors and the engine servers down with it.
 """
 
 import asyncio
@@ -200,3 +201,39 @@ def test_engine_client_bounded_retries_and_continuation():
             _run(gen(EngineClient(s.url, attempts=1, backoff=0.01), [1], {"max_new_tokens": 1}))
     finally:
         s.close()
+
+
+@pytest.mark.timeout(240)
+def test_killed_launcher_takes_its_run_down(tmp_path):
+    """SIGKILL of the launcher (no chance to forward a signal) still ends torchrun, the ignitors and the
+    engine servers they started: each child dies with its parent."""
+    import signal
+    import subprocess
+    import sys
+
+    psutil = pytest.importorskip("psutil")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="50", PYTHONPATH=root,
+               XRL_PORT_OFFSET=str(100 + (_port() % 400) * 10))
+    p = subprocess.Popen([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
+                          "--runtime-dir", str(tmp_path / "rt"), "--master-port", str(_port())], cwd=root, env=env,
+                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+    kids = []
+    deadline = time.monotonic() + 120
+    while time.monotonic() < deadline:  # until the engine servers are up (launcher > torchrun > ignitor > server)
+        try:
+            kids = psutil.Process(p.pid).children(recursive=True)
+        except psutil.NoSuchProcess:
+            break
+        if sum("rollout.server" in " ".join(k.cmdline()) for k in kids if k.is_running()) >= 2:
+            break
+        time.sleep(1)
+    assert len(kids) >= 4, [" ".join(k.cmdline()) for k in kids]
+    p.send_signal(signal.SIGKILL)
+    p.wait()
+    gone, alive = psutil.wait_procs(kids, timeout=60)
+    try:
+        assert not alive, [" ".join(k.cmdline()) for k in alive]
+    finally:
+        for k in alive:
+            k.kill()
