@@ -78,6 +78,33 @@ def test_launcher_runs_tensor_parallel_inference_replica_on_cpu(tmp_path):
 
 
 @pytest.mark.timeout(600)
+def test_two_node_launch_with_an_inference_replica_across_the_nodes(tmp_path):
+    """Two launchers (``--nnodes 2``, one card each, on this host) run one job: the data plane and bootstrap
+    store live on node 0, the trainer spans both nodes, and the single inference replica spans them too
+    (node 0's server serves HTTP and rendezvouses with node 1's follower through ``--dist-init-addr``)."""
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", XRL_SMOKE_INFER_TP="2", PYTHONPATH=ROOT,
+               XRL_PORT_OFFSET=_port_offset())
+    rt = tmp_path / "rt"
+    port = str(_free_port())
+    procs = [subprocess.Popen([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
+                               "--runtime-dir", str(rt), "--nnodes", "2", "--node-rank", str(n),
+                               "--nproc-per-node", "1", "--master-port", port], cwd=ROOT, env=env,
+                              stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True) for n in (0, 1)]
+    outs = [p.communicate(timeout=540)[0] for p in procs]
+    logs = rt / "logs"
+    detail = "".join(o[-1500:] for o in outs)
+    if logs.exists():
+        for f in sorted(logs.iterdir()):
+            detail += f"\n==== {f.name}\n" + f.read_text(errors="replace")[-1500:]
+    assert [p.returncode for p in procs] == [0, 0], detail
+    rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
+    assert len(rows) == 2, detail
+    # one server per node for the one replica
+    assert (logs / "actor_infer-0-0.log").exists() and (logs / "actor_infer-0-1.log").exists(), detail
+    assert (logs / "ignitor-0.log").read_text().count("colocation transfer actor_infer -> actor_train") == 2, detail
+
+
+@pytest.mark.timeout(600)
 def test_launcher_runs_sharded_trainer_on_cpu(tmp_path):
     """The same ring with the trainer's parameters sharded over its two ranks (FSDP): weights still reach
     the engines every step (gathered into the full layout) and the run checkpoints and finishes."""
