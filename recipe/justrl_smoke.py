@@ -19,7 +19,7 @@ from meshy_b200.service.base import ServiceGroup
 from meshy_b200.service.colocation import ColocationRing, SchedulingMode
 from meshy_b200.service.ignite import Ignitor
 
-MODEL = "qwen3:debugmodel"
+MODEL = os.environ.get("XRL_SMOKE_MODEL", "qwen3:debugmodel")  # qwen3:debugmodel_moe for the MoE path
 CARDS = int(os.environ.get("XRL_SMOKE_CARDS", "2"))
 PROMPTS = int(os.environ.get("XRL_SMOKE_PROMPTS", "4"))
 GROUP = 2
@@ -31,19 +31,22 @@ CKPT = GlobalCheckpointConfig(enabled=os.environ.get("XRL_SMOKE_CKPT", "0") == "
 
 SHARD = os.environ.get("XRL_SMOKE_SHARD", "0") == "1"  # FSDP over the trainer's cards instead of DDP
 INFER_TP = int(os.environ.get("XRL_SMOKE_INFER_TP", "1"))  # cards per inference replica (tensor parallel)
+INFER_EP = int(os.environ.get("XRL_SMOKE_INFER_EP", "1"))  # = INFER_TP: the replica's ranks split the experts
+_NAME, _FLAVOR = MODEL.split(":")
 
 
 def _trainer_config() -> TrainerConfig:
     par = dict(shard_params="on", dp_shard_degree=-1, dp_replicate_degree=1) if SHARD else \
         dict(dp_replicate_degree=CARDS)
-    return TrainerConfig(model_name="qwen3", model_flavor="debugmodel", seq_len=512, lr=1e-5, weight_decay=0.0,
+    return TrainerConfig(model_name=_NAME, model_flavor=_FLAVOR, seq_len=512, lr=1e-5, weight_decay=0.0,
                          max_norm=1.0, steps=1000, dtype="bfloat16", **par)
 
 
 SERVICE_GROUPS = [
     ServiceGroup(id="actor_infer", n_replicas=CARDS // INFER_TP, n_gpus_per_replica=INFER_TP,
                  config=InferenceServiceConfig(model_path=None, server_args={
-                     "model": MODEL, "max_running_requests": 16, "max_total_tokens": 8192, "context_length": 512})),
+                     "model": MODEL, "max_running_requests": 16, "max_total_tokens": 8192, "context_length": 512,
+                     **({"ep_size": INFER_EP} if INFER_EP > 1 else {})})),
     ServiceGroup(id="actor_train", n_replicas=1, n_gpus_per_replica=CARDS, colocate_with="actor_infer",
                  wait_until=["actor_infer"],
                  config=TrainingServiceConfig(

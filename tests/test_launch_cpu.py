@@ -55,12 +55,16 @@ def test_launcher_runs_colocated_grpo_on_cpu(tmp_path):
 
 
 @pytest.mark.timeout(600)
-def test_launcher_runs_tensor_parallel_inference_replica_on_cpu(tmp_path):
+@pytest.mark.parametrize("moe", [False, True], ids=["dense-tp2", "moe-tp2-ep2"])
+def test_launcher_runs_tensor_parallel_inference_replica_on_cpu(tmp_path, moe):
     """The ring with ONE inference replica over both cards (``--tp-size 2``: the service starts the server,
     which spawns its follower rank): the replica serves the rollout, releases and restores its memory in
-    lock-step, loads every weight version and the run finishes."""
+    lock-step, loads every weight version and the run finishes. With the MoE model the replica's ranks also
+    split the experts (``--ep-size 2``) and each loads only its experts' slices of every weight version."""
     env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="2", XRL_SMOKE_INFER_TP="2", PYTHONPATH=ROOT,
                XRL_PORT_OFFSET=_port_offset())
+    if moe:
+        env.update(XRL_SMOKE_MODEL="qwen3:debugmodel_moe", XRL_SMOKE_INFER_EP="2")
     rt = tmp_path / "rt"
     r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
                         "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
