@@ -109,6 +109,38 @@ def test_two_node_launch_with_an_inference_replica_across_the_nodes(tmp_path):
 
 
 @pytest.mark.timeout(600)
+@pytest.mark.parametrize("mode", ["bounded-off-policy", "fully-async-stream"])
+def test_launcher_pacing_modes_on_cpu(tmp_path, mode):
+    """The two non-lock-step pacing modes end to end. Bounded off-policy (colocated, ``pacing_window=2``):
+    the rollout runs one window ahead, so the first two batches are generated with version 0 and the third
+    with version 1. Fully asynchronous (disaggregated cards, no gate, ``stream_minibatch``): the trainer takes
+    each 2-sample mini-batch as it arrives, syncing weights once per 8-sample batch."""
+    env = dict(os.environ, XRL_DEVICE="cpu", XRL_SMOKE_STEPS="3", PYTHONPATH=ROOT, XRL_PORT_OFFSET=_port_offset())
+    if mode == "bounded-off-policy":
+        env.update(XRL_SMOKE_PACING="2")
+    else:
+        env.update(XRL_SMOKE_TOPOLOGY="disaggregate", XRL_SMOKE_PACING="none", XRL_SMOKE_STREAM="1")
+    rt = tmp_path / "rt"
+    r = subprocess.run([sys.executable, "-m", "meshy_b200.launch", "--recipe", "recipe.justrl_smoke",
+                        "--runtime-dir", str(rt), "--master-port", str(_free_port())], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=540)
+    logs = rt / "logs"
+    detail = r.stdout[-2000:] + r.stderr[-2000:]
+    if logs.exists():
+        for f in sorted(logs.iterdir()):
+            detail += f"\n==== {f.name}\n" + f.read_text(errors="replace")[-1500:]
+    assert r.returncode == 0, detail
+    rows = [json.loads(l) for l in (rt / "tensorboard" / "actor_train-0" / "metrics.jsonl").read_text().splitlines()]
+    versions = [json.loads(l)["weight_version"] for l in (rt / "trajectories.jsonl").read_text().splitlines()]
+    assert len(versions) == 24, detail
+    if mode == "bounded-off-policy":
+        assert len(rows) == 3 and sorted(versions) == [0] * 16 + [1] * 8, (versions, detail)
+    else:
+        assert len(rows) == 12 and rows[-1]["step"] == 3, ([r_.get("step") for r_ in rows], detail)
+        assert max(versions) <= 2  # generated ahead of the trainer, never ahead of its weights
+
+
+@pytest.mark.timeout(600)
 def test_launcher_runs_sharded_trainer_on_cpu(tmp_path):
     """The same ring with the trainer's parameters sharded over its two ranks (FSDP): weights still reach
     the engines every step (gathered into the full layout) and the run checkpoints and finishes."""
