@@ -37,11 +37,22 @@ class TrainingService(SpmdService):
 
         cfg = self.info.config
         eng = TrainerEngine(cfg.trainer_config, cfg.trainer_params, service_name=self.name, runtime=self.runtime,
-                            checkpoint=cfg.checkpoint, weight_sync_mode=cfg.weight_sync_mode,
+                            checkpoint=cfg.checkpoint, weight_sync_mode=self.weight_sync_mode(),
                             weights_keep_latest_k=cfg.weights_keep_latest_k,
                             critic_cold_start_windows=self._critic_cold_start(), model_path=cfg.model_path,
                             **self.engine_kwargs())
         return eng
+
+    def weight_sync_mode(self) -> str:
+        """``auto`` becomes ``disk`` when the trainer's cards and the inference engines' cards are not all on
+        one host: CUDA IPC handles only open on the node that exported them."""
+        mode = self.info.config.weight_sync_mode
+        if mode != "auto" or self.topology is None:
+            return mode
+        hosts = {g.host for g in self.info.replica_gpus}
+        for svc in self.topology.inference_services():
+            hosts |= {g.host for g in svc.replica_gpus}
+        return "disk" if len(hosts) > 1 else mode
 
     def _chunk(self) -> int | None:
         cfg = self.info.config

@@ -249,3 +249,20 @@ def test_inference_service_command_sets_tp_from_replica_cards():
     for c, n in ((c0, "0"), (c1, "1")):
         assert _flag(c, "--tp-size") == "4" and _flag(c, "--nnodes") == "2" and _flag(c, "--node-rank") == n
         assert _flag(c, "--dist-init-addr") == "10.0.0.1:40000"
+
+
+def test_trainer_syncs_through_disk_when_engines_are_on_another_host():
+    from types import SimpleNamespace
+
+    from meshy_b200.service.base import GPU
+    from meshy_b200.service.training import TrainingService
+
+    def svc(mode, train_hosts, infer_hosts):
+        info = SimpleNamespace(config=SimpleNamespace(weight_sync_mode=mode),
+                               replica_gpus=[GPU(i, h, i, 0) for i, h in enumerate(train_hosts)])
+        infer = [SimpleNamespace(replica_gpus=[GPU(10 + i, h, i, 0)]) for i, h in enumerate(infer_hosts)]
+        return SimpleNamespace(info=info, topology=SimpleNamespace(inference_services=lambda: infer))
+
+    assert TrainingService.weight_sync_mode(svc("auto", ["a", "a"], ["a", "a"])) == "auto"
+    assert TrainingService.weight_sync_mode(svc("auto", ["a", "a"], ["a", "b"])) == "disk"  # IPC is node-local
+    assert TrainingService.weight_sync_mode(svc("device", ["a"], ["b"])) == "device"  # explicit choice stands
