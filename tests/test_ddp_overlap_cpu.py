@@ -107,3 +107,34 @@ def test_overlapped_reduction_equals_reduction_after_backward():
             armed = o["armed_blocks"]
             assert len(armed) % L == 0 and armed[:L] == list(range(L - 1, -1, -1)), armed
             assert o["unarmed"] == []  # without overlap no boundary is inserted
+
+
+def test_range_arithmetic_with_skipped_expert_slices():
+    """Blocks reduced from their hooks plus what ``finish`` reduces cover every non-skipped element exactly
+    once (expert slices that differ per rank are never summed)."""
+    from types import SimpleNamespace
+
+    from meshy_b200.parallel.ddp import GradReducer, _subtract
+
+    assert list(_subtract(0, 10, [(2, 4), (6, 7)])) == [(0, 2), (4, 6), (7, 10)]
+    assert list(_subtract(3, 5, [(0, 10)])) == [] and list(_subtract(0, 4, [])) == [(0, 4)]
+    names = ["embed", "layers.0.wqkv", "layers.0.moe.w13", "layers.0.w2", "layers.1.wqkv", "layers.1.moe.w13",
+             "norm", "output"]
+    slots, off = [], 0
+    for n in names:
+        slots.append(SimpleNamespace(name=n, offset=off, numel=10))
+        off += 10
+    flat = SimpleNamespace(slots=slots, params=[None] * len(slots), grad=None)
+    skip = [(s.offset, s.numel) for s in slots if ".moe." in s.name]
+    r = GradReducer(flat, None, skip=skip, overlap=True)
+    assert {i: (lo, hi) for i, (lo, hi, _) in r._blocks.items()} == {0: (10, 40), 1: (40, 60)}
+    covered = []
+    for i in (1, 0):  # hooks fire in backward order
+        lo, hi, _ = r._blocks[i]
+        covered += list(_subtract(lo, hi, r._holes))
+    done = sorted((r._blocks[i][0], r._blocks[i][1]) for i in (0, 1))
+    for lo, hi in r._ranges(off):
+        covered += list(_subtract(lo, hi, done))
+    elems = sorted(x for a, b in covered for x in range(a, b))
+    want = [x for x in range(off) if not any(o <= x < o + n for o, n in skip)]
+    assert elems == want
